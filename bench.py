@@ -1,0 +1,389 @@
+"""Decode throughput of the B200 backend on BASELINE's headline workload: Qwen3-0.6B shape, FP8 weights in the
+engine's format, a 512-token random prompt, then greedy decode.
+
+A step is one greedy decode step of every sequence on the GPU (batch 1 by default, --batch 64 for the batched
+variant). One process per GPU; sequences are independent, so N GPUs run N replicas with the same per-GPU work
+(weak scaling, no collective on the data path).
+
+Printed line (rank 0): value = decode tok/s of the device-resident loop (tokens, positions and argmax stay in
+HBM; one CUDA graph per step); e2e = the same through the engine-facing host API (neko_model_decode: host token
+ids in, host logits out every step, like Model::forward); roofline = the dequant GEMV over every weight matrix of
+one step, timed with CUDA events; cpu_baseline = the reference engine's CPU backend (compiled from its sources in
+oracle/_ref) on this host's cores.
+
+    python bench.py [--gpus N --steps K --warmup W --batch B --impl ours|reference]
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SHAPE = "qwen3-0.6b"
+FMT = 1  # FP8
+METRIC = "Qwen3-0.6B FP8 decode tok/s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=256)
+    p.add_argument("--warmup", type=int, default=8)
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--prompt", type=int, default=512)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--profile", action="store_true", help="small case for ncu: short prompt, few steps, no extras")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------------------------- clocks (NVML)
+class ClockSampler:
+    """Samples SM clock and throttle reasons every few ms on a thread while the timed region runs."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.stop_ev = [], set(), threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+
+    def _run(self):
+        while not self.stop_ev.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self.stop_ev.set()
+        if self.ok:
+            self.t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------------------------- helpers
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def reduce_max(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    import torch
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def gemv_roofline(model, s, stream, reps=3):
+    """Every packed weight matrix of one decode step (28 layers x {qkv, o, gate|up, down} + LM head, 633 MB for
+    FP8 at 0.6B: far above the 126 MB L2, so each launch streams from HBM) through the GEMV kernel at M = 1,
+    launched back to back with programmatic dependent launch as in the step. Returns (algorithmic bytes per
+    launch, mean launch time in s, launches)."""
+    import torch
+    from nekochat_b200 import ops, workload
+    mats = []
+    for l in range(s["layers"]):
+        for w in ("wqkv", "wo", "wgu", "wdown"):
+            mats.append(model.matrix(f"layers.{l}.{w}"))
+    mats.append(model.matrix("head"))
+    kmax = max(c for _, _, c, _ in mats)
+    nmax = max(r for _, r, _, _ in mats)
+    x = torch.randn(kmax, device="cuda")
+    y = torch.empty(nmax, device="cuda")
+    lib = __import__("nekochat_b200").lib()
+    import ctypes as C
+    nbytes = 0
+    for p, r, c, f in mats:
+        nbytes += r * workload.row_bytes(f, c) + c * 4 + r * 4
+    def run():
+        for p, r, c, f in mats:
+            rc = lib.neko_op_matmul(f, C.c_void_p(x.data_ptr()), 1, c, C.c_void_p(p), r, None,
+                                    C.c_void_p(y.data_ptr()), r, 0, 256, C.c_void_p(stream.cuda_stream))
+            if rc:
+                raise RuntimeError(lib.neko_last_error().decode())
+    with torch.cuda.stream(stream):
+        run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            run()
+        e1.record(stream)
+        e1.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / (reps * len(mats))
+    return nbytes / len(mats), t, reps * len(mats)
+
+
+def cpu_baseline(args, s, tmpdir, h16, steps=8, prompt=32):
+    """The reference engine's CPU backend on this host (oracle/_ref/libneko_ref.so): loadModel with all host
+    threads (the engine's pool caps at 16), a short prompt, then `steps` timed greedy decode steps."""
+    from oracle.checkpoint import write_model
+    from oracle.oracle import Reference
+    ref = Reference()
+    folder = write_model(os.path.join(tmpdir, "ckpt"), s, h16, dtype=np.float16)
+    threads = min(16, os.cpu_count() or 1)
+    m = ref.load_model(folder, FMT, threads=threads)
+    from nekochat_b200 import workload
+    toks = workload.prompt(s, prompt)
+    logits = m.forward(toks, 0)
+    tok, pos = int(np.argmax(logits)), prompt
+    logits = m.forward(np.array([tok], np.int32), pos)  # warm-up step
+    tok, pos = int(np.argmax(logits)), pos + 1
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        logits = m.forward(np.array([tok], np.int32), pos)
+        tok, pos = int(np.argmax(logits)), pos + 1
+    dt = time.perf_counter() - t0
+    m.close()
+    return {"value": steps / dt, "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"reference CPU engine (x86 scalar path, {threads} threads), batch 1, {prompt}-token prompt, "
+                      f"{steps} timed greedy decode steps after 1 warm-up; the engine has no multi-sequence "
+                      f"batching, so its aggregate rate equals this single-sequence rate"}
+
+
+# ---------------------------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from nekochat_b200 import workload
+    s = workload.shape(SHAPE)
+    import torch
+    with tempfile.TemporaryDirectory() as tmp:
+        # weights: N(0, 0.02) f16 checkpoint from torch's seeded CPU generator (numpy's is ~10x slower here)
+        g = torch.Generator().manual_seed(0)
+        h16 = []
+        for name, shp, kind in workload.tensor_specs(s):
+            if kind == "w":
+                a = (torch.randn(shp, generator=g) * 0.02).half().numpy()
+            else:
+                a = (np.ones if kind == "g" else np.zeros)(shp, np.float16)
+            h16.append((name, a))
+        n_prompt = 32
+        steps, warm = args.steps, args.warmup
+        from oracle.checkpoint import write_model
+        from oracle.oracle import Reference
+        ref = Reference()
+        folder = write_model(os.path.join(tmp, "ckpt"), s, h16, dtype=np.float16)
+        del h16
+        threads = min(16, os.cpu_count() or 1)
+        m = ref.load_model(folder, FMT, threads=threads)
+        toks = workload.prompt(s, n_prompt)
+        logits = m.forward(toks, 0)
+        tok, pos = int(np.argmax(logits)), n_prompt
+        # bounded sample: at most 24 timed steps per run so K/W-sized runs finish in minutes
+        k = min(steps, 24)
+        w = min(warm, 3)
+        for _ in range(w):
+            logits = m.forward(np.array([tok], np.int32), pos)
+            tok, pos = int(np.argmax(logits)), pos + 1
+        t0 = time.perf_counter()
+        for _ in range(k):
+            logits = m.forward(np.array([tok], np.int32), pos)
+            tok, pos = int(np.argmax(logits)), pos + 1
+        dt = time.perf_counter() - t0
+        m.close()
+    v = k / dt
+    sample = (f"reference CPU engine (oracle/_ref, x86 scalar path, {threads} threads), batch 1, {n_prompt}-token "
+              f"prompt, {w} warm-up + {k} timed greedy decode steps (bounded sample of the {args.steps}-step run); "
+              f"the engine runs sequences one at a time, so this is also its aggregate rate")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world, "steps": k,
+        "warmup": w, "ms_per_step": dt / k * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "qwen3-0.6b fp8 greedy decode, batch 1", "batch": 1, "prompt": n_prompt},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    from nekochat_b200 import model as nmodel, workload
+    world, rank, local = dist_setup(args)
+    s = workload.shape(SHAPE)
+    B = args.batch
+    prompt_len = 32 if args.profile else args.prompt
+    steps, warm = (4, 3) if args.profile else (args.steps, args.warmup)
+    e2e_on = not (args.no_e2e or args.profile)
+    context = prompt_len + 2 * (warm + steps) + 8
+    context = (context + 255) // 256 * 256
+    cpu_on = (rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile
+              and os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libneko_ref.so")))
+    h16 = [] if cpu_on else None
+    m = nmodel.Model(s, FMT, context=context, max_seqs=B, max_rows=64)
+    m.load_random_device(seed=0, host_copy=(lambda n, a: h16.append((n, a))) if cpu_on else None)
+
+    # prefill every sequence (different prompts per rank and sequence)
+    first = np.zeros(B, np.int32)
+    for i in range(B):
+        p = workload.prompt(s, prompt_len, seed=1 + rank * 100000 + i)
+        first[i] = int(np.argmax(m.prefill(p, slot=i)))
+    slots = np.arange(B, dtype=np.int32)
+    pos = np.full(B, prompt_len, np.int32)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream()
+    m.stage(slots, first, pos)
+    for k in range(warm):
+        m.step(B, prompt_len + k, stream.cuda_stream)
+    stream.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for k in range(steps):
+            m.step(B, prompt_len + warm + k, stream.cuda_stream)
+        e1.record(stream)
+        e1.synchronize()
+    barrier(world)
+    t = reduce_max(e0.elapsed_time(e1) / 1e3, world)
+    value = world * B * steps / t
+    launches = m.step_launches(B) * steps
+
+    # end to end through the host API (host token ids in, host logits out, every step)
+    e2e = None
+    if e2e_on:
+        toks, p0 = m.tokens(B)
+        h2d = B * 3 * 4
+        d2h = B * s["vocab"] * 4 + B * 4
+        tok = toks.copy()
+        for k in range(warm):
+            _, tok = m.decode(slots, tok, p0 + k)
+        barrier(world)
+        t0 = time.perf_counter()
+        for k in range(steps):
+            lg, tok = m.decode(slots, tok, p0 + warm + k)
+        t_e2e = reduce_max(time.perf_counter() - t0, world)
+        e2e = {"value": world * B * steps / t_e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h,
+               "path": "neko_model_decode: pinned-staged H2D of token/slot/position, CUDA graph step, D2H of the "
+                       "full logits and the greedy token, host synchronisation, every step"}
+
+    roof = None
+    if rank == 0:
+        per_launch, t_launch, n = gemv_roofline(m, s, stream)
+        peak, src = peaks()
+        ach = per_launch / t_launch / 1e9
+        roof = {"bound": "hbm", "kernel": "gemv_kernel<FP8> (M=1, all weight matrices of one step)",
+                "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src,
+                "traffic": None, "bytes_per_launch": per_launch, "launch_us": t_launch * 1e6}
+        bytes_step = workload.weight_stream_bytes(s, FMT) + B * workload.kv_bytes_per_position(s) * (
+            prompt_len + warm + steps / 2)
+        roof["step_bytes"] = bytes_step
+        roof["step_achieved_gbs"] = round(bytes_step / (t / steps) / 1e9, 1)
+        tf = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tf):
+            try:
+                roof["traffic"] = json.load(open(tf)).get("gemv_fp8_bytes_per_launch")
+            except Exception:
+                pass
+
+    cpu = None
+    if cpu_on:
+        with tempfile.TemporaryDirectory() as tmp:
+            try:
+                cpu = cpu_baseline(args, s, tmp, h16)
+            except Exception as e:  # the baseline is reported, never required
+                cpu = {"value": None, "unit": "tok/s", "error": str(e)[:200]}
+    m.close()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
+            "ms_per_step": t / steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"qwen3-0.6b fp8 (engine FP8 format), {prompt_len}-token random prompt, "
+                                   f"greedy decode, batch {B} per GPU", "batch": B, "prompt": prompt_len,
+                       "positions": [prompt_len + warm, prompt_len + warm + steps],
+                       "weights": "N(0,0.02) random init, quantized on the GPU by the engine's FP8 codec",
+                       "l2": "no flush needed: each step streams 633 MB of weights (> 126 MB L2)",
+                       "parallelism": f"dp{world} (independent replicas)"},
+            "gpu_launches": launches,
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

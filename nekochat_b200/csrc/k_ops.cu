@@ -1,0 +1,327 @@
+// Elementwise and reduction kernels around the matmuls: LayerNorm/RMSNorm, row softmax, argmax, embedding
+// gather, Qwen3 QK-norm + RoPE + KV-cache store, KV store, SwiGLU. All memory-bound; each reads its inputs
+// once where the row fits on chip and keeps fp32 (fp64 for the norm sums, like cpu_ops.cpp) arithmetic.
+#include <algorithm>
+#include <cfloat>
+
+#include "neko_common.cuh"
+#include "neko_internal.h"
+
+namespace neko {
+
+namespace {
+
+constexpr int kNormThreads = 256;
+constexpr int kRowCacheFloats = 24 * 1024;  // rows up to 96 KB are read once, into shared memory
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ double block_sum_d(double v, double* red) {
+    v = warp_sum_d(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    double t = l < int(blockDim.x >> 5) ? red[l] : 0.0;
+    return warp_sum_d(t);
+}
+
+// cpu::layerNorm / cpu::rmsNorm (cpu_ops.cpp:483-511), one block per row; layernorm.comp's rowOffset is
+// folded into x by the caller. Sums in double like the CPU; the row is cached in shared memory if it fits.
+__global__ void __launch_bounds__(kNormThreads) norm_kernel(const float* __restrict__ x, int64_t xs,
+                                                            float* __restrict__ y, int64_t ys,
+                                                            const float* __restrict__ g,
+                                                            const float* __restrict__ b, int C, float eps, int rms) {
+    extern __shared__ float row[];
+    __shared__ double red[kNormThreads / 32];
+    pdl_wait();
+    const float* xr = x + int64_t(blockIdx.x) * xs;
+    float* yr = y + int64_t(blockIdx.x) * ys;
+    const bool cached = C <= kRowCacheFloats;
+    double s1 = 0.0, s2 = 0.0;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const float v = xr[c];
+        if (cached) row[c] = v;
+        s1 += v;
+        s2 += double(v) * v;
+    }
+    float r, m = 0.0f;
+    if (rms) {
+        s2 = block_sum_d(s2, red);
+        r = float(1.0 / sqrt(s2 / C + double(eps)));
+    } else {
+        const double mean = block_sum_d(s1, red) / C;
+        double var = 0.0;
+        for (int c = threadIdx.x; c < C; c += blockDim.x) {
+            const double d = (cached ? row[c] : xr[c]) - mean;
+            var += d * d;
+        }
+        var = block_sum_d(var, red) / C;
+        r = float(1.0 / sqrt(var + double(eps)));
+        m = float(mean);
+    }
+    pdl_trigger();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const float v = cached ? row[c] : xr[c];
+        yr[c] = rms ? __fmul_rn(__fmul_rn(v, r), g[c]) : __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, m), r), g[c]), b[c]);
+    }
+}
+
+// Row softmax: max, exp(x - max), float sum, times 1 / sum (the softmax inside cpu::attention,
+// cpu_ops.cpp:556-572). Rows that fit are read once into shared memory.
+__global__ void __launch_bounds__(kNormThreads) softmax_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                                               int C) {
+    extern __shared__ float row[];
+    __shared__ float red[kNormThreads / 32];
+    const float* xr = x + int64_t(blockIdx.x) * C;
+    float* yr = y + int64_t(blockIdx.x) * C;
+    const bool cached = C <= kRowCacheFloats;
+    float mx = -INFINITY;
+    for (int c = threadIdx.x * 4; c < C; c += blockDim.x * 4) {
+        if (c + 3 < C && (C & 3) == 0) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + c);
+            if (cached) *reinterpret_cast<float4*>(row + c) = v;
+            mx = fmaxf(mx, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+        } else {
+            for (int k = c; k < min(C, c + 4); k++) {
+                const float v = xr[k];
+                if (cached) row[k] = v;
+                mx = fmaxf(mx, v);
+            }
+        }
+    }
+    mx = warp_max(mx);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) red[w] = mx;
+    __syncthreads();
+    mx = l < kNormThreads / 32 ? red[l] : -INFINITY;
+    mx = warp_max(mx);
+    float s = 0.0f;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const float e = expf((cached ? row[c] : xr[c]) - mx);
+        if (cached) row[c] = e;
+        s += e;
+    }
+    s = block_sum<kNormThreads>(s, red);
+    const float inv = 1.0f / s;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) yr[c] = (cached ? row[c] : expf(xr[c] - mx)) * inv;
+}
+
+// First index of the maximum of each row (std::max_element: strict '<' keeps the earliest).
+__global__ void __launch_bounds__(kNormThreads) argmax_kernel(const float* __restrict__ x, int64_t stride, int C,
+                                                              int* __restrict__ out) {
+    __shared__ float bv[kNormThreads / 32];
+    __shared__ int bi[kNormThreads / 32];
+    pdl_wait();
+    const float* xr = x + int64_t(blockIdx.x) * stride;
+    float v = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const float t = xr[c];
+        if (t > v) {  // strided scan visits increasing c, so '>' keeps this thread's first maximum
+            v = t;
+            idx = c;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > v || (ov == v && oi < idx)) {
+            v = ov;
+            idx = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) {
+        bv[w] = v;
+        bi[w] = idx;
+    }
+    __syncthreads();
+    if (w == 0) {
+        v = l < kNormThreads / 32 ? bv[l] : -INFINITY;
+        idx = l < kNormThreads / 32 ? bi[l] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+            if (ov > v || (ov == v && oi < idx)) {
+                v = ov;
+                idx = oi;
+            }
+        }
+        if (l == 0) out[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
+    }
+}
+
+// cpu::siluMul (cpu_ops.cpp:526-533) / silu_mul.comp.
+__global__ void silu_mul_kernel(const float* __restrict__ h, float* __restrict__ g, int T, int I) {
+    const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= int64_t(T) * I) return;
+    const int t = int(idx / I), i = int(idx % I);
+    const float a = h[int64_t(t) * 2 * I + i];
+    const float b = h[int64_t(t) * 2 * I + I + i];
+    g[idx] = a / (1.0f + expf(-a)) * b;
+}
+
+// embed.comp + QMatrix::dequantizeRow for the token rows (+ position row).
+__global__ void embed_kernel(const int* __restrict__ tokens, int T, int C, int fmt, const uint8_t* __restrict__ table,
+                             int64_t rb, int row_base, int nrows, const uint16_t* __restrict__ wpe16,
+                             const float* __restrict__ wpe32, int pos0, const int* __restrict__ pos_arr,
+                             float* __restrict__ x) {
+    pdl_wait();
+    const int t = blockIdx.y;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T || c >= C) return;
+    const int row = tokens[t] - row_base;
+    if (row < 0 || row >= nrows) return;
+    float v = dequant_one(fmt, table + int64_t(row) * rb, C, c);
+    const int pos = pos_arr ? pos_arr[t] : pos0 + t;
+    if (wpe16) v += half_bits_to_float(wpe16[int64_t(pos) * C + c]);
+    if (wpe32) v += wpe32[int64_t(pos) * C + c];
+    x[int64_t(t) * C + c] = v;
+}
+
+// kv_store.comp: K, V rows of qkv (f32) -> f16 caches [ctx][W] at pos0 + t (cpu::storeKv, cpu_ops.cpp:535-542).
+__global__ void kv_store_kernel(const float* __restrict__ qkv, int T, int W, int pos0, int stride, int k_off,
+                                int v_off, uint16_t* __restrict__ kc, uint16_t* __restrict__ vc) {
+    const int t = blockIdx.y;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T || c >= W) return;
+    const float* src = qkv + int64_t(t) * stride;
+    const int64_t dst = int64_t(pos0 + t) * W + c;
+    kc[dst] = __half_as_ushort(__float2half_rn(src[k_off + c]));
+    vc[dst] = __half_as_ushort(__float2half_rn(src[v_off + c]));
+}
+
+// Per-head QK RMSNorm (cpu::rmsNorm over hd, qwen3_model.cpp:249-252), NeoX rotation from the host table
+// (cpu::rope, cpu_ops.cpp:513-524) and the f16 KV store (cpu::storeKv), one warp per head. Heads
+// [0, H) are queries (rotated in place), [H, H + KV) keys and [H + KV, H + 2 KV) values (both stored).
+constexpr int kPostWarps = 4;
+__global__ void __launch_bounds__(kPostWarps * 32) qkv_post_kernel(const QkvPostArgs a) {
+    __shared__ float buf[kPostWarps][256];
+    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int head = blockIdx.x * kPostWarps + warp;
+    const int r = blockIdx.y;
+    const int heads_total = a.n_head + (a.store_kv ? 2 : 1) * a.n_kv;
+    if (head >= heads_total || r >= a.rows) return;
+    const int hd = a.hd;
+    const bool is_q = head < a.n_head, is_k = !is_q && head < a.n_head + a.n_kv;
+    float* row = a.qkv + int64_t(r) * a.qkv_stride;
+    const int col = is_q ? head * hd : is_k ? a.k_off + (head - a.n_head) * hd
+                                             : a.v_off + (head - a.n_head - a.n_kv) * hd;
+    const int pos = a.row_pos ? a.row_pos[r] : a.pos0 + r;
+    if (pos < 0 || pos >= a.pos_limit) {  // a cache row outside the context: report, never write it
+        if (lane == 0) set_device_error(kErrBadIndex);
+        return;
+    }
+    float* v = buf[warp];
+    double ss = 0.0;
+    for (int d = lane; d < hd; d += 32) {
+        const float t = row[col + d];
+        v[d] = t;
+        ss += double(t) * t;
+    }
+    __syncwarp();
+    if (!is_q && !is_k) {  // value head: store only
+        const int slot = a.row_slot ? a.row_slot[r] : a.slot0;
+        uint16_t* dst = a.vc + slot * a.slot_stride + int64_t(pos) * a.pos_stride +
+                        int64_t(head - a.n_head - a.n_kv) * a.head_stride;
+        for (int d = lane; d < hd; d += 32) dst[d] = __half_as_ushort(__float2half_rn(v[d]));
+        return;
+    }
+    if (a.do_norm) {
+        ss = warp_sum_d(ss);
+        const float s = float(1.0 / sqrt(ss / hd + double(a.eps)));
+        const float* w = a.wn + (is_q ? 0 : hd);
+        for (int d = lane; d < hd; d += 32) v[d] = __fmul_rn(__fmul_rn(v[d], s), w[d]);
+        __syncwarp();
+    }
+    const int half = hd / 2;
+    if (a.do_rope && (is_q || a.rope_kv_heads)) {
+        const float* cs = a.cs + int64_t(pos) * hd;
+        // Lane l owns the pairs (i, i + half) with i = l (mod 32): no element is shared between lanes.
+        for (int i = lane; i < half; i += 32) {
+            const float c = cs[2 * i], sn = cs[2 * i + 1];
+            const float x0 = v[i], x1 = v[i + half];
+            v[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+            v[i + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+        }
+        __syncwarp();
+    }
+    if (is_q || !a.store_kv) {
+        for (int d = lane; d < hd; d += 32) row[col + d] = v[d];
+    }
+    if (is_k && a.store_kv) {
+        const int slot = a.row_slot ? a.row_slot[r] : a.slot0;
+        uint16_t* dst = a.kc + slot * a.slot_stride + int64_t(pos) * a.pos_stride +
+                        int64_t(head - a.n_head) * a.head_stride;
+        for (int d = lane; d < hd; d += 32) dst[d] = __half_as_ushort(__float2half_rn(v[d]));
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_norm(const float* x, int64_t x_stride, float* y, int64_t y_stride, const float* gamma,
+                        const float* beta, int rows, int C, float eps, bool rms, cudaStream_t st, bool pdl) {
+    if (rows <= 0) return cudaSuccess;
+    const size_t smem = C <= kRowCacheFloats ? size_t(C) * 4 : 0;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowCacheFloats * 4);
+        cudaFuncSetAttribute(softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowCacheFloats * 4);
+        attr = true;
+    }
+    return launch_ex(norm_kernel, dim3(rows), dim3(kNormThreads), smem, st, pdl, x, x_stride, y, y_stride, gamma, beta,
+                     C, eps, rms ? 1 : 0);
+}
+
+cudaError_t launch_softmax(const float* x, float* y, int rows, int C, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    const size_t smem = C <= kRowCacheFloats ? size_t(C) * 4 : 0;
+    cudaFuncSetAttribute(softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowCacheFloats * 4);
+    softmax_kernel<<<rows, kNormThreads, smem, st>>>(x, y, C);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float* x, int64_t stride, int rows, int C, int* out, cudaStream_t st, bool pdl) {
+    if (rows <= 0) return cudaSuccess;
+    return launch_ex(argmax_kernel, dim3(rows), dim3(kNormThreads), 0, st, pdl, x, stride, C, out);
+}
+
+cudaError_t launch_silu_mul(const float* h, float* g, int T, int I, cudaStream_t st) {
+    const int64_t n = int64_t(T) * I;
+    if (n <= 0) return cudaSuccess;
+    silu_mul_kernel<<<unsigned((n + 255) / 256), 256, 0, st>>>(h, g, T, I);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_embed(const int* tokens, int T, int C, int fmt, const uint8_t* table, int64_t rb, int row_base,
+                         int nrows, const uint16_t* wpe16, const float* wpe32, int pos0, const int* pos_arr, float* x,
+                         cudaStream_t st, bool pdl) {
+    if (T <= 0 || C <= 0) return cudaSuccess;
+    return launch_ex(embed_kernel, dim3((C + 255) / 256, T), dim3(256), 0, st, pdl, tokens, T, C, fmt, table, rb,
+                     row_base, nrows, wpe16, wpe32, pos0, pos_arr, x);
+}
+
+cudaError_t launch_kv_store(const float* qkv, int T, int W, int pos0, int stride, int k_off, int v_off, uint16_t* kc,
+                            uint16_t* vc, cudaStream_t st) {
+    if (T <= 0 || W <= 0) return cudaSuccess;
+    kv_store_kernel<<<dim3((W + 127) / 128, T), 128, 0, st>>>(qkv, T, W, pos0, stride, k_off, v_off, kc, vc);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qkv_post(const QkvPostArgs& a, cudaStream_t st, bool pdl) {
+    if (a.rows <= 0) return cudaSuccess;
+    if (a.hd > 256 || (a.hd & 1)) return cudaErrorInvalidValue;
+    const int heads = a.n_head + (a.store_kv ? 2 : 1) * a.n_kv;
+    return launch_ex(qkv_post_kernel, dim3((heads + kPostWarps - 1) / kPostWarps, a.rows), dim3(kPostWarps * 32), 0,
+                     st, pdl, a);
+}
+
+}  // namespace neko

@@ -1,0 +1,822 @@
+// Native GPT-2 / Qwen3 runner on the sm_100a kernels (the neko_model_* ABI of include/neko_cuda.h).
+//
+// It computes what Gpt2Model::forwardCpu / Qwen3Model::forwardCpu compute (app/architecture/gpt2/cpp/
+// gpt2_model.cpp:179-218, qwen3/cpp/qwen3_model.cpp:232-276), with the fusions the reference's one-dispatch-
+// per-op sequence (forwardGpu, qwen3_model.cpp:278-341) leaves on the table:
+//   Qwen3 layer = [RMSNorm -> qkv GEMV] [QK-norm + RoPE + KV store] [attention] [o_proj GEMV + residual]
+//                 [RMSNorm -> gate|up GEMV -> SiLU*up] [down GEMV + residual]            6 launches (ref: 11)
+//   GPT-2 layer = [LayerNorm -> qkv GEMV + bias] [KV store] [attention] [proj GEMV + bias + residual]
+//                 [LayerNorm -> fc GEMV + bias + GELU] [fc2 GEMV + bias + residual]       6 launches (ref: 9)
+// Final norm + LM head (+ greedy argmax) close the step. All launches after the first use programmatic
+// dependent launch, so each GEMV streams its weights while its predecessor finishes, and a step is captured
+// once as a CUDA graph per (rows, outputs, context bucket) and replayed.
+//
+// Rows: a step processes R activation rows; row r belongs to KV slot slot[r] at position pos[r]. A prefill
+// chunk is R consecutive positions of one slot (Model::forward); a batched decode step is one row per
+// sequence. Logits are produced for `nout` rows given by out_rows.
+//
+// Device memory: one arena for the packed weights (engine row format, quantized on the GPU from f32 with the
+// byte-identical quantizer), one for the KV cache laid out [layer][slot][kv head][position][head dim] f16 (a
+// head's keys are contiguous), and a workspace sized for max_rows.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <new>
+#include <set>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/neko_cuda.h"
+#include "neko_common.cuh"
+#include "neko_internal.h"
+
+using namespace neko;
+
+namespace {
+
+thread_local std::string t_model_err;
+
+struct Mat {
+    uint8_t* w = nullptr;
+    int rows = 0, cols = 0, fmt = 0;
+    int64_t rb = 0;
+};
+
+struct Layer {
+    Mat wqkv, wo, wup, wdown;  // Qwen3: wup = gate|up (2F rows); GPT-2: wup = c_fc (4C rows)
+    float *ln1 = nullptr, *ln2 = nullptr, *ln1b = nullptr, *ln2b = nullptr;
+    float *qknorm = nullptr;  // Qwen3: q_norm | k_norm (2 hd)
+    float *bqkv = nullptr, *bo = nullptr, *bup = nullptr, *bdown = nullptr;  // GPT-2 biases
+};
+
+// advance kernel: next token = argmax, position + 1 (device-side greedy loop)
+// (a sequence that reaches the end of its context stays there and reports kErrBadIndex)
+__global__ void advance_kernel(const int* argmax, int* tokens, int* pos, int n, int context) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    pdl_wait();
+    if (i < n) {
+        tokens[i] = argmax[i];
+        if (pos[i] + 1 < context) pos[i] += 1;
+        else set_device_error(kErrBadIndex);
+    }
+}
+
+__global__ void gather_rows_kernel(const float* x, int C, const int* rows, int n, float* out) {
+    pdl_wait();
+    const int r = blockIdx.y;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < n && c < C) out[int64_t(r) * C + c] = x[int64_t(rows[r]) * C + c];
+}
+
+}  // namespace
+
+struct neko_model {
+    neko_model_config cfg{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    bool qwen = false;
+    int C = 0, H = 0, KV = 0, hd = 0, F = 0, V = 0, QW = 0, UPW = 0;
+    int fmt = 0;
+
+    // arenas
+    uint8_t* warena = nullptr;
+    size_t wbytes = 0, wused = 0;
+    uint16_t *kc = nullptr, *vc = nullptr;
+    size_t kv_bytes = 0;
+    int64_t kv_layer = 0, kv_slot = 0, kv_head = 0;  // element strides
+    // workspace
+    float *x = nullptr, *xn = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *hx = nullptr, *logits = nullptr;
+    int *d_tokens = nullptr, *d_slots = nullptr, *d_pos = nullptr, *d_argmax = nullptr, *d_outrows = nullptr;
+    float* part = nullptr;
+    unsigned* tickets = nullptr;
+    int64_t part_cap = 0, tick_cap = 0;
+    size_t work_bytes = 0;
+    // host pinned staging for the synchronous API
+    int* h_in = nullptr;     // tokens | slots | pos | outrows  (4 * max_rows)
+    float* h_logits = nullptr;
+    int* h_argmax = nullptr;
+    // weights
+    Mat embed;               // also the tied LM head
+    float* normf = nullptr;  // Qwen3 final RMSNorm / GPT-2 ln_f gamma
+    float* normfb = nullptr; // GPT-2 ln_f beta
+    float* rope = nullptr;   // Qwen3 [context][hd]
+    float* wpe = nullptr;    // GPT-2 [max_pos][C] f32 (the CPU path keeps positions in f32)
+    std::vector<Layer> layers;
+    std::set<std::string> have;
+    std::set<std::string> need;
+    float* staging = nullptr;  // f32 upload buffer for matrices
+    size_t staging_floats = 0;
+    bool final_ok = false;
+    // graphs keyed by (rows, nout, bucket, mode)
+    std::map<std::tuple<int, int, int, int>, cudaGraphExec_t> graphs;
+};
+
+namespace {
+
+int fail(neko_model* m, int code, const std::string& msg) {
+    if (m) m->err = msg;
+    t_model_err = msg;
+    return code;
+}
+
+#define CK(expr, what)                                                              \
+    do {                                                                            \
+        cudaError_t e_ = (expr);                                                    \
+        if (e_ != cudaSuccess) return fail(m, NEKO_ERR_CUDA, cuda_msg(e_, what)); \
+    } while (0)
+
+struct Guard {
+    int prev = -1;
+    explicit Guard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~Guard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+int fmt_for(int cols, int f) { return cols % kQuantBlock == 0 ? f : int(kF16); }  // Model::formatFor (model.h:164)
+
+// Carves the weight arena (two passes: size, then assign).
+struct Carver {
+    neko_model* m;
+    bool assign;
+    size_t off = 0;
+    uint8_t* take(size_t n) {
+        uint8_t* p = assign ? m->warena + off : nullptr;
+        off += align256(n);
+        return p;
+    }
+    float* vec(size_t n) { return reinterpret_cast<float*>(take(n * 4)); }
+    Mat mat(int rows, int cols) {
+        Mat t;
+        t.rows = rows;
+        t.cols = cols;
+        t.fmt = fmt_for(cols, m->fmt);
+        t.rb = row_bytes(t.fmt, cols);
+        t.w = take(size_t(rows) * t.rb);
+        return t;
+    }
+};
+
+void carve(neko_model* m, Carver& cv) {
+    const int C = m->C, V = m->V;
+    m->embed = cv.mat(V, C);
+    m->normf = cv.vec(C);
+    if (!m->qwen) {
+        m->normfb = cv.vec(C);
+        m->wpe = cv.vec(size_t(m->cfg.max_pos) * C);
+    } else {
+        m->rope = cv.vec(size_t(m->cfg.context) * m->hd);
+    }
+    for (auto& L : m->layers) {
+        L.wqkv = cv.mat(m->QW, C);
+        L.wo = cv.mat(C, m->H * m->hd);
+        L.wup = cv.mat(m->UPW, C);
+        L.wdown = cv.mat(C, m->F);
+        L.ln1 = cv.vec(C);
+        L.ln2 = cv.vec(C);
+        if (m->qwen) {
+            L.qknorm = cv.vec(2 * size_t(m->hd));
+        } else {
+            L.ln1b = cv.vec(C);
+            L.ln2b = cv.vec(C);
+            L.bqkv = cv.vec(m->QW);
+            L.bo = cv.vec(C);
+            L.bup = cv.vec(m->UPW);
+            L.bdown = cv.vec(C);
+        }
+    }
+}
+
+// Qwen3 rotary table [pos][hd/2](cos, sin), computed in double like Qwen3Model::ropeTable
+// (qwen3_model.cpp:102-114) so the device rotates with the same table the CPU does.
+std::vector<float> rope_table(int ctx, int hd, double theta) {
+    std::vector<float> t(size_t(ctx) * hd);
+    for (int i = 0; i < hd / 2; i++) {
+        const double inv = std::pow(theta, -2.0 * i / hd);
+        for (int p = 0; p < ctx; p++) {
+            const double a = p * inv;
+            t[size_t(p) * hd + 2 * i] = float(std::cos(a));
+            t[size_t(p) * hd + 2 * i + 1] = float(std::sin(a));
+        }
+    }
+    return t;
+}
+
+int bucket_for(neko_model* m, int max_pos) {
+    int b = 256;
+    while (b < max_pos + 1) b *= 2;
+    return std::min(b, m->cfg.context);
+}
+
+// Enqueues one step: R rows (tokens/slots/pos already in the device arrays), logits for nout rows listed in
+// d_outrows (or the last row when nout == 1 and rows are one prefill chunk), optional argmax and advance.
+int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_pos, bool do_argmax, bool advance,
+                 cudaStream_t st) {
+    const int C = m->C, H = m->H, KV = m->KV, hd = m->hd;
+    const float eps = m->cfg.eps;
+    bool first = true;
+    auto pdl = [&]() {
+        const bool p = !first;
+        first = false;
+        return p;
+    };
+    // embedding rows (+ f32 positions for GPT-2)
+    CK(launch_embed(m->d_tokens, R, C, m->embed.fmt, m->embed.w, m->embed.rb, 0, m->V, nullptr,
+                    m->qwen ? nullptr : m->wpe, 0, m->d_pos, m->x, st, pdl()),
+       "embed");
+
+    const bool x_fits = int64_t(R) * C * 4 <= kGemvXSmemMax;
+    auto gemv = [&](const Mat& W, int nrows, const float* x, int64_t xs, int M, int norm, const float* g,
+                    const float* b, const float* bias, int flags, float* y, int64_t ys, int64_t pair) -> cudaError_t {
+        GemvArgs a;
+        a.W = W.w;
+        a.row_bytes = W.rb;
+        a.rows = nrows;
+        a.K = W.cols;
+        a.fmt = W.fmt;
+        a.x = x;
+        a.x_stride = xs;
+        a.M = M;
+        a.norm = norm;
+        a.gamma = g;
+        a.beta = b;
+        a.eps = eps;
+        a.bias = bias;
+        a.flags = flags;
+        a.y = y;
+        a.y_stride = ys;
+        a.pair_off = pair;
+        return launch_gemv(a, st, pdl());
+    };
+    // norm (fused into the GEMV prologue when the activations fit in shared memory, else a separate kernel)
+    auto normed = [&](const float* g, const float* b, int& norm_kind, const float*& src) -> cudaError_t {
+        const int kind = m->qwen ? kNormRms : kNormLayer;
+        if (x_fits) {
+            norm_kind = kind;
+            src = m->x;
+            return cudaSuccess;
+        }
+        norm_kind = kNormNone;
+        src = m->xn;
+        return launch_norm(m->x, C, m->xn, C, g, b, R, C, eps, m->qwen, st, pdl());
+    };
+
+    for (size_t l = 0; l < m->layers.size(); l++) {
+        const Layer& L = m->layers[l];
+        uint16_t* kc = m->kc + int64_t(l) * m->kv_layer;
+        uint16_t* vc = m->vc + int64_t(l) * m->kv_layer;
+        int nk;
+        const float* src;
+        CK(normed(L.ln1, L.ln1b, nk, src), "norm1");
+        CK(gemv(L.wqkv, m->QW, src, C, R, nk, L.ln1, L.ln1b, L.bqkv, m->qwen ? 0 : kBias, m->qkv, m->QW, 0), "qkv");
+        QkvPostArgs q;
+        q.qkv = m->qkv;
+        q.qkv_stride = m->QW;
+        q.rows = R;
+        q.n_head = H;
+        q.n_kv = KV;
+        q.hd = hd;
+        q.do_norm = m->qwen;
+        q.wn = L.qknorm;
+        q.eps = eps;
+        q.do_rope = m->qwen;
+        q.cs = m->rope;
+        q.store_kv = 1;
+        q.kc = kc;
+        q.vc = vc;
+        q.slot_stride = m->kv_slot;
+        q.pos_stride = hd;
+        q.head_stride = m->kv_head;
+        q.row_slot = m->d_slots;
+        q.row_pos = m->d_pos;
+        q.k_off = H * hd;
+        q.v_off = (H + KV) * hd;
+        q.pos_limit = m->cfg.context;
+        CK(launch_qkv_post(q, st, pdl()), "qkv_post");
+        AttnArgs a;
+        a.q = m->qkv;
+        a.q_stride = m->QW;
+        a.kc = kc;
+        a.vc = vc;
+        a.slot_stride = m->kv_slot;
+        a.pos_stride = hd;
+        a.head_stride = m->kv_head;
+        a.row_slot = m->d_slots;
+        a.row_pos = m->d_pos;
+        a.rows = R;
+        a.n_head = H;
+        a.n_kv = KV;
+        a.hd = hd;
+        a.scale = 1.0f / std::sqrt(float(hd));
+        a.out = m->att;
+        a.out_stride = int64_t(H) * hd;
+        a.max_pos = max_pos;
+        a.pos_limit = m->cfg.context;
+        a.part = m->part;
+        a.tickets = m->tickets;
+        a.part_capacity = m->part_cap;
+        a.ticket_capacity = m->tick_cap;
+        CK(launch_attention(a, st, pdl()), "attention");
+        CK(gemv(L.wo, C, m->att, int64_t(H) * hd, R, kNormNone, nullptr, nullptr, L.bo,
+                kAccumulate | (m->qwen ? 0 : kBias), m->x, C, 0),
+           "o_proj");
+        CK(normed(L.ln2, L.ln2b, nk, src), "norm2");
+        if (m->qwen) {
+            CK(gemv(L.wup, m->F, src, C, R, nk, L.ln2, nullptr, nullptr, 0, m->h, m->F, m->F), "gate_up");
+        } else {
+            CK(gemv(L.wup, m->UPW, src, C, R, nk, L.ln2, L.ln2b, L.bup, kBias | kGelu, m->h, m->UPW, 0), "fc");
+        }
+        CK(gemv(L.wdown, C, m->h, m->F, R, kNormNone, nullptr, nullptr, L.bdown, kAccumulate | (m->qwen ? 0 : kBias),
+                m->x, C, 0),
+           "down");
+    }
+    // final norm + LM head on the output rows
+    const float* hx;
+    if (outrows_identity && nout == R) {
+        hx = m->x;
+    } else if (outrows_identity && nout == 1) {
+        hx = m->x + int64_t(R - 1) * C;
+    } else {
+        gather_rows_kernel<<<dim3((C + 255) / 256, nout), 256, 0, st>>>(m->x, C, m->d_outrows, nout, m->hx);
+        first = false;
+        CK(cudaGetLastError(), "gather");
+        hx = m->hx;
+    }
+    const bool head_fits = int64_t(nout) * C * 4 <= kGemvXSmemMax;
+    if (head_fits) {
+        CK(gemv(m->embed, m->V, hx, C, nout, m->qwen ? kNormRms : kNormLayer, m->normf, m->normfb, nullptr, 0,
+                m->logits, m->V, 0),
+           "lm_head");
+    } else {
+        CK(launch_norm(hx, C, m->xn, C, m->normf, m->normfb, nout, C, eps, m->qwen, st, pdl()), "final norm");
+        CK(gemv(m->embed, m->V, m->xn, C, nout, kNormNone, nullptr, nullptr, nullptr, 0, m->logits, m->V, 0),
+           "lm_head");
+    }
+    if (do_argmax) CK(launch_argmax(m->logits, m->V, nout, m->V, m->d_argmax, st, pdl()), "argmax");
+    if (advance) {
+        CK(launch_ex(advance_kernel, dim3((nout + 127) / 128), dim3(128), 0, st, pdl(), (const int*)m->d_argmax,
+                     m->d_tokens, m->d_pos, nout, m->cfg.context),
+           "advance");
+    }
+    return NEKO_OK;
+}
+
+int step_launches(neko_model* m, int R, int nout, bool gather, bool do_argmax, bool advance) {
+    const bool x_fits = int64_t(R) * m->C * 4 <= kGemvXSmemMax;
+    const int per_layer = 6 + (x_fits ? 0 : 2);
+    int n = 1 + int(m->layers.size()) * per_layer + (gather ? 1 : 0);
+    n += int64_t(nout) * m->C * 4 <= kGemvXSmemMax ? 1 : 2;
+    return n + (do_argmax ? 1 : 0) + (advance ? 1 : 0);
+}
+
+// Runs (capturing on first use) the graph of one step shape.
+int run_step(neko_model* m, int R, int nout, bool identity, int max_pos, bool do_argmax, bool advance, cudaStream_t st) {
+    const int bucket = bucket_for(m, max_pos);
+    const int mode = (identity ? 1 : 0) | (do_argmax ? 2 : 0) | (advance ? 4 : 0);
+    auto key = std::make_tuple(R, nout, bucket, mode);
+    auto it = m->graphs.find(key);
+    if (it == m->graphs.end()) {
+        cudaStream_t cap = nullptr;
+        CK(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking), "capture stream");
+        cudaGraph_t g = nullptr;
+        cudaError_t e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) {
+            cudaStreamDestroy(cap);
+            return fail(m, NEKO_ERR_CUDA, cuda_msg(e, "begin capture"));
+        }
+        int rc = enqueue_step(m, R, nout, identity, bucket - 1, do_argmax, advance, cap);
+        e = cudaStreamEndCapture(cap, &g);
+        cudaStreamDestroy(cap);
+        if (rc != NEKO_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (e != cudaSuccess) return fail(m, NEKO_ERR_CUDA, cuda_msg(e, "end capture"));
+        cudaGraphExec_t ex = nullptr;
+        e = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return fail(m, NEKO_ERR_CUDA, cuda_msg(e, "instantiate"));
+        it = m->graphs.emplace(key, ex).first;
+    }
+    CK(cudaGraphLaunch(it->second, st), "graph launch");
+    return NEKO_OK;
+}
+
+int wait_model(neko_model* m) {
+    cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return fail(m, NEKO_ERR_CUDA, cuda_msg(e, "step"));
+    if (unsigned d = read_device_error(true))
+        return fail(m, NEKO_ERR_DEVICE, "kernel reported device error " + std::to_string(d));
+    return NEKO_OK;
+}
+
+bool parse_layer(const std::string& n, const char* prefix, int& layer, std::string& leaf) {
+    const size_t pl = std::strlen(prefix);
+    if (n.compare(0, pl, prefix) != 0) return false;
+    size_t dot = n.find('.', pl);
+    if (dot == std::string::npos) return false;
+    try {
+        layer = std::stoi(n.substr(pl, dot - pl));
+    } catch (...) {
+        return false;
+    }
+    leaf = n.substr(dot + 1);
+    return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* neko_model_last_error(neko_model* m) { return m ? m->err.c_str() : t_model_err.c_str(); }
+
+neko_model* neko_model_create(int device, const neko_model_config* cfg, char* err, size_t err_len) {
+    auto bail = [&](neko_model* m, const std::string& msg) -> neko_model* {
+        t_model_err = msg;
+        if (err && err_len) std::snprintf(err, err_len, "%s", msg.c_str());
+        if (m) neko_model_destroy(m);
+        return nullptr;
+    };
+    if (!cfg) return bail(nullptr, "null config");
+    const neko_model_config& c = *cfg;
+    if (c.arch != NEKO_ARCH_GPT2 && c.arch != NEKO_ARCH_QWEN3) return bail(nullptr, "unknown architecture");
+    if (c.vocab <= 0 || c.embd <= 0 || c.layers <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads ||
+        c.head_dim <= 0 || c.head_dim > 256 || (c.head_dim & 7) || c.ff <= 0 || c.context <= 0 || c.max_seqs <= 0 ||
+        c.max_rows <= 0 || c.context > c.max_pos || c.weight_format < 0 || c.weight_format > 2)
+        return bail(nullptr, "invalid model config");
+    if (c.heads / c.kv_heads > 8) return bail(nullptr, "at most 8 query heads per KV head");
+    if (c.embd % 8 || c.ff % 8) return bail(nullptr, "embd and ff must be multiples of 8");
+    auto* m = new (std::nothrow) neko_model;
+    if (!m) return bail(nullptr, "out of host memory");
+    m->cfg = c;
+    m->device = device;
+    m->qwen = c.arch == NEKO_ARCH_QWEN3;
+    m->C = c.embd;
+    m->H = c.heads;
+    m->KV = m->qwen ? c.kv_heads : c.heads;
+    m->hd = m->qwen ? c.head_dim : c.embd / c.heads;
+    if (!m->qwen && m->hd * c.heads != c.embd) return bail(m, "GPT-2 embd must equal heads * head_dim");
+    m->F = c.ff;
+    m->V = c.vocab;
+    m->fmt = c.weight_format;
+    m->QW = (m->H + 2 * m->KV) * m->hd;
+    m->UPW = m->qwen ? 2 * c.ff : c.ff;
+    m->layers.resize(size_t(c.layers));
+    Guard g(device);
+    cudaError_t e;
+    if ((e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking)) != cudaSuccess)
+        return bail(m, cuda_msg(e, "stream"));
+    Carver size_pass{m, false};
+    carve(m, size_pass);
+    m->wbytes = size_pass.off;
+    if ((e = cudaMalloc(&m->warena, m->wbytes)) != cudaSuccess) return bail(m, cuda_msg(e, "weights"));
+    Carver assign{m, true};
+    carve(m, assign);
+    // KV cache [layer][slot][kv head][pos][hd]
+    m->kv_head = int64_t(c.context) * m->hd;
+    m->kv_slot = m->kv_head * m->KV;
+    m->kv_layer = m->kv_slot * c.max_seqs;
+    m->kv_bytes = size_t(m->kv_layer) * c.layers * 2;
+    if ((e = cudaMalloc(&m->kc, m->kv_bytes)) != cudaSuccess) return bail(m, cuda_msg(e, "k cache"));
+    if ((e = cudaMalloc(&m->vc, m->kv_bytes)) != cudaSuccess) return bail(m, cuda_msg(e, "v cache"));
+    cudaMemset(m->kc, 0, m->kv_bytes);
+    cudaMemset(m->vc, 0, m->kv_bytes);
+    // workspace
+    const size_t R = size_t(c.max_rows), nout = std::max<size_t>(R, size_t(c.max_seqs));
+    auto falloc = [&](float** p, size_t n) {
+        m->work_bytes += n * 4;
+        return cudaMalloc(p, std::max<size_t>(n, 1) * 4);
+    };
+    auto ialloc = [&](int** p, size_t n) {
+        m->work_bytes += n * 4;
+        return cudaMalloc(p, std::max<size_t>(n, 1) * 4);
+    };
+    if (falloc(&m->x, R * m->C) || falloc(&m->xn, nout * m->C) || falloc(&m->qkv, R * m->QW) ||
+        falloc(&m->att, R * m->H * m->hd) || falloc(&m->h, R * std::max(m->F, m->UPW)) || falloc(&m->hx, nout * m->C) ||
+        falloc(&m->logits, nout * size_t(m->V)) || ialloc(&m->d_tokens, nout) || ialloc(&m->d_slots, nout) ||
+        ialloc(&m->d_pos, nout) || ialloc(&m->d_argmax, nout) || ialloc(&m->d_outrows, nout))
+        return bail(m, "workspace allocation failed");
+    int64_t pf = 0, tk = 0;
+    attention_scratch(int(R), m->H, m->KV, m->hd, c.context - 1, &pf, &tk);
+    // smaller row counts split more: size for the worst case over 1..R rows
+    for (int r = 1; r <= int(R); r *= 2) {
+        int64_t p2 = 0, t2 = 0;
+        attention_scratch(r, m->H, m->KV, m->hd, c.context - 1, &p2, &t2);
+        pf = std::max(pf, p2);
+        tk = std::max(tk, t2);
+    }
+    m->part_cap = std::max<int64_t>(pf, 1);
+    m->tick_cap = std::max<int64_t>(tk, 1);
+    if (falloc(&m->part, size_t(m->part_cap)) || cudaMalloc(&m->tickets, size_t(m->tick_cap) * 4))
+        return bail(m, "attention scratch allocation failed");
+    cudaMemset(m->tickets, 0, size_t(m->tick_cap) * 4);
+    if (cudaMallocHost(&m->h_in, 4 * nout * sizeof(int)) || cudaMallocHost(&m->h_logits, nout * size_t(m->V) * 4) ||
+        cudaMallocHost(&m->h_argmax, nout * sizeof(int)))
+        return bail(m, "pinned host allocation failed");
+    if (m->qwen) {
+        std::vector<float> t = rope_table(c.context, m->hd, c.rope_theta);
+        if ((e = cudaMemcpy(m->rope, t.data(), t.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess)
+            return bail(m, cuda_msg(e, "rope table"));
+    }
+    // names every tensor must provide
+    if (m->qwen) {
+        m->need = {"embed_tokens.weight", "norm.weight"};
+        for (int l = 0; l < c.layers; l++)
+            for (const char* leaf : {"input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_norm.weight",
+                                     "self_attn.k_norm.weight", "self_attn.q_proj.weight", "self_attn.k_proj.weight",
+                                     "self_attn.v_proj.weight", "self_attn.o_proj.weight", "mlp.gate_proj.weight",
+                                     "mlp.up_proj.weight", "mlp.down_proj.weight"})
+                m->need.insert("layers." + std::to_string(l) + "." + leaf);
+    } else {
+        m->need = {"wte.weight", "wpe.weight", "ln_f.weight", "ln_f.bias"};
+        for (int l = 0; l < c.layers; l++)
+            for (const char* leaf : {"ln_1.weight", "ln_1.bias", "ln_2.weight", "ln_2.bias", "attn.c_attn.weight",
+                                     "attn.c_attn.bias", "attn.c_proj.weight", "attn.c_proj.bias", "mlp.c_fc.weight",
+                                     "mlp.c_fc.bias", "mlp.c_proj.weight", "mlp.c_proj.bias"})
+                m->need.insert("h." + std::to_string(l) + "." + leaf);
+    }
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess) return bail(m, cuda_msg(e, "init"));
+    return m;
+}
+
+void neko_model_destroy(neko_model* m) {
+    if (!m) return;
+    Guard g(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+    for (void* p : {(void*)m->warena, (void*)m->kc, (void*)m->vc, (void*)m->x, (void*)m->xn, (void*)m->qkv,
+                    (void*)m->att, (void*)m->h, (void*)m->hx, (void*)m->logits, (void*)m->d_tokens, (void*)m->d_slots,
+                    (void*)m->d_pos, (void*)m->d_argmax, (void*)m->d_outrows, (void*)m->part, (void*)m->tickets,
+                    (void*)m->staging})
+        if (p) cudaFree(p);
+    if (m->h_in) cudaFreeHost(m->h_in);
+    if (m->h_logits) cudaFreeHost(m->h_logits);
+    if (m->h_argmax) cudaFreeHost(m->h_argmax);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+static int set_tensor(neko_model* m, const char* cname, const float* data, int64_t rows, int64_t cols, bool on_device) {
+    if (!m || !cname || !data || rows <= 0 || cols <= 0) return fail(m, NEKO_ERR_ARG, "set_tensor: bad arguments");
+    Guard g(m->device);
+    std::string name(cname);
+    for (const char* pre : {"model.", "transformer."})
+        if (name.compare(0, std::strlen(pre), pre) == 0) name = name.substr(std::strlen(pre));
+    const int C = m->C, hd = m->hd;
+    // destination: a matrix row range (quantized) or an f32 vector
+    Mat* mat = nullptr;
+    int row0 = 0, exp_rows = 0, exp_cols = 0;
+    bool transpose = false;
+    float* vec = nullptr;
+    size_t vec_n = 0;
+    int layer = -1;
+    std::string leaf;
+    if (m->qwen) {
+        if (name == "embed_tokens.weight") {
+            mat = &m->embed, exp_rows = m->V, exp_cols = C;
+        } else if (name == "norm.weight") {
+            vec = m->normf, vec_n = C;
+        } else if (parse_layer(name, "layers.", layer, leaf) && layer < int(m->layers.size())) {
+            Layer& L = m->layers[size_t(layer)];
+            const int qh = m->H * hd, kvw = m->KV * hd;
+            if (leaf == "input_layernorm.weight") vec = L.ln1, vec_n = C;
+            else if (leaf == "post_attention_layernorm.weight") vec = L.ln2, vec_n = C;
+            else if (leaf == "self_attn.q_norm.weight") vec = L.qknorm, vec_n = hd;
+            else if (leaf == "self_attn.k_norm.weight") vec = L.qknorm + hd, vec_n = hd;
+            else if (leaf == "self_attn.q_proj.weight") mat = &L.wqkv, row0 = 0, exp_rows = qh, exp_cols = C;
+            else if (leaf == "self_attn.k_proj.weight") mat = &L.wqkv, row0 = qh, exp_rows = kvw, exp_cols = C;
+            else if (leaf == "self_attn.v_proj.weight") mat = &L.wqkv, row0 = qh + kvw, exp_rows = kvw, exp_cols = C;
+            else if (leaf == "self_attn.o_proj.weight") mat = &L.wo, exp_rows = C, exp_cols = qh;
+            else if (leaf == "mlp.gate_proj.weight") mat = &L.wup, row0 = 0, exp_rows = m->F, exp_cols = C;
+            else if (leaf == "mlp.up_proj.weight") mat = &L.wup, row0 = m->F, exp_rows = m->F, exp_cols = C;
+            else if (leaf == "mlp.down_proj.weight") mat = &L.wdown, exp_rows = C, exp_cols = m->F;
+        }
+    } else {
+        if (name == "wte.weight") {
+            mat = &m->embed, exp_rows = m->V, exp_cols = C;
+        } else if (name == "wpe.weight") {
+            vec = m->wpe, vec_n = size_t(m->cfg.max_pos) * C;
+        } else if (name == "ln_f.weight") {
+            vec = m->normf, vec_n = C;
+        } else if (name == "ln_f.bias") {
+            vec = m->normfb, vec_n = C;
+        } else if (parse_layer(name, "h.", layer, leaf) && layer < int(m->layers.size())) {
+            Layer& L = m->layers[size_t(layer)];
+            // Conv1D weights are stored [in][out]; the engine transposes them and rounds to f16 first.
+            if (leaf == "ln_1.weight") vec = L.ln1, vec_n = C;
+            else if (leaf == "ln_1.bias") vec = L.ln1b, vec_n = C;
+            else if (leaf == "ln_2.weight") vec = L.ln2, vec_n = C;
+            else if (leaf == "ln_2.bias") vec = L.ln2b, vec_n = C;
+            else if (leaf == "attn.c_attn.weight") mat = &L.wqkv, exp_rows = C, exp_cols = 3 * C, transpose = true;
+            else if (leaf == "attn.c_attn.bias") vec = L.bqkv, vec_n = 3 * size_t(C);
+            else if (leaf == "attn.c_proj.weight") mat = &L.wo, exp_rows = C, exp_cols = C, transpose = true;
+            else if (leaf == "attn.c_proj.bias") vec = L.bo, vec_n = C;
+            else if (leaf == "mlp.c_fc.weight") mat = &L.wup, exp_rows = C, exp_cols = m->UPW, transpose = true;
+            else if (leaf == "mlp.c_fc.bias") vec = L.bup, vec_n = size_t(m->UPW);
+            else if (leaf == "mlp.c_proj.weight") mat = &L.wdown, exp_rows = m->F, exp_cols = C, transpose = true;
+            else if (leaf == "mlp.c_proj.bias") vec = L.bdown, vec_n = C;
+            else if (leaf == "attn.bias" || leaf == "attn.masked_bias") return NEKO_OK;  // causal-mask buffers
+        }
+    }
+    if (!mat && !vec) return fail(m, NEKO_ERR_ARG, "set_tensor: unknown tensor " + name);
+    if (vec) {
+        if (size_t(rows * cols) != vec_n) return fail(m, NEKO_ERR_ARG, "set_tensor: wrong size for " + name);
+        CK(cudaMemcpy(vec, data, vec_n * 4, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice),
+           "upload vector");
+    } else {
+        if (rows != exp_rows || cols != exp_cols)
+            return fail(m, NEKO_ERR_ARG, "set_tensor: wrong shape for " + name + " (" + std::to_string(rows) + "x" +
+                                             std::to_string(cols) + ")");
+        const size_t n = size_t(rows) * size_t(cols);
+        const float* src = data;
+        if (!on_device) {
+            if (n > m->staging_floats) {
+                cudaFree(m->staging);
+                m->staging = nullptr;
+                CK(cudaMalloc(&m->staging, n * 4), "staging");
+                m->staging_floats = n;
+            }
+            CK(cudaMemcpy(m->staging, data, n * 4, cudaMemcpyHostToDevice), "upload matrix");
+            src = m->staging;
+        }
+        // out rows / in cols of the packed matrix
+        const int orows = transpose ? int(cols) : int(rows);
+        const int icols = transpose ? int(rows) : int(cols);
+        CK(launch_quantize(mat->fmt, src, orows, icols, cols, transpose ? 1 : 0,
+                           mat->w + int64_t(row0) * mat->rb, m->stream),
+           "quantize");
+        CK(cudaStreamSynchronize(m->stream), "quantize");
+    }
+    m->have.insert(name);
+    m->final_ok = false;
+    return NEKO_OK;
+}
+
+}  // extern "C"
+
+static int set_tensor_entry(neko_model* m, const char* name, const float* data, int64_t rows, int64_t cols,
+                            bool on_device) {
+    if (!m) return NEKO_ERR_ARG;
+    Guard g(m->device);
+    return set_tensor(m, name, data, rows, cols, on_device);
+}
+
+extern "C" {
+
+int neko_model_set_tensor(neko_model* m, const char* name, const float* data, int64_t rows, int64_t cols) {
+    return set_tensor_entry(m, name, data, rows, cols, false);
+}
+
+int neko_model_set_tensor_device(neko_model* m, const char* name, const float* d_data, int64_t rows, int64_t cols) {
+    return set_tensor_entry(m, name, d_data, rows, cols, true);
+}
+
+int neko_model_finalize(neko_model* m) {
+    if (!m) return NEKO_ERR_ARG;
+    for (const auto& n : m->need)
+        if (!m->have.count(n)) return fail(m, NEKO_ERR_ARG, "finalize: missing tensor " + n);
+    m->final_ok = true;
+    return NEKO_OK;
+}
+
+int neko_model_forward(neko_model* m, int slot, const int* tokens, int T, int pos0, float* logits) {
+    if (!m || !tokens || !logits) return fail(m, NEKO_ERR_ARG, "forward: null argument");
+    if (!m->final_ok) return fail(m, NEKO_ERR_ARG, "forward: call neko_model_finalize first");
+    // Model::checkBatch (model.cpp:127-132)
+    if (T <= 0 || T > m->cfg.max_rows) return fail(m, NEKO_ERR_ARG, "forward: bad batch size");
+    if (pos0 < 0 || pos0 + T > m->cfg.context) return fail(m, NEKO_ERR_ARG, "forward: context overflow");
+    if (slot < 0 || slot >= m->cfg.max_seqs) return fail(m, NEKO_ERR_ARG, "forward: bad slot");
+    for (int t = 0; t < T; t++)
+        if (tokens[t] < 0 || tokens[t] >= m->V) return fail(m, NEKO_ERR_ARG, "forward: token id out of range");
+    Guard g(m->device);
+    int* hi = m->h_in;
+    for (int t = 0; t < T; t++) {
+        hi[t] = tokens[t];
+        hi[T + t] = slot;
+        hi[2 * T + t] = pos0 + t;
+    }
+    CK(cudaMemcpyAsync(m->d_tokens, hi, size_t(T) * 4, cudaMemcpyHostToDevice, m->stream), "h2d");
+    CK(cudaMemcpyAsync(m->d_slots, hi + T, size_t(T) * 4, cudaMemcpyHostToDevice, m->stream), "h2d");
+    CK(cudaMemcpyAsync(m->d_pos, hi + 2 * T, size_t(T) * 4, cudaMemcpyHostToDevice, m->stream), "h2d");
+    if (int rc = run_step(m, T, 1, true, pos0 + T - 1, false, false, m->stream); rc != NEKO_OK) return rc;
+    CK(cudaMemcpyAsync(m->h_logits, m->logits, size_t(m->V) * 4, cudaMemcpyDeviceToHost, m->stream), "d2h");
+    if (int rc = wait_model(m); rc != NEKO_OK) return rc;
+    std::memcpy(logits, m->h_logits, size_t(m->V) * 4);
+    return NEKO_OK;
+}
+
+int neko_model_decode(neko_model* m, int n, const int* slots, const int* tokens, const int* pos, float* logits,
+                      int* argmax) {
+    if (!m || !slots || !tokens || !pos) return fail(m, NEKO_ERR_ARG, "decode: null argument");
+    if (!m->final_ok) return fail(m, NEKO_ERR_ARG, "decode: call neko_model_finalize first");
+    if (n <= 0 || n > m->cfg.max_rows || n > m->cfg.max_seqs) return fail(m, NEKO_ERR_ARG, "decode: bad count");
+    int max_pos = 0;
+    for (int i = 0; i < n; i++) {
+        if (slots[i] < 0 || slots[i] >= m->cfg.max_seqs) return fail(m, NEKO_ERR_ARG, "decode: bad slot");
+        if (pos[i] < 0 || pos[i] >= m->cfg.context) return fail(m, NEKO_ERR_ARG, "decode: context overflow");
+        if (tokens[i] < 0 || tokens[i] >= m->V) return fail(m, NEKO_ERR_ARG, "decode: token id out of range");
+        for (int j = 0; j < i; j++)
+            if (slots[j] == slots[i]) return fail(m, NEKO_ERR_ARG, "decode: a slot appears twice in one step");
+        max_pos = std::max(max_pos, pos[i]);
+    }
+    Guard g(m->device);
+    int* hi = m->h_in;
+    std::memcpy(hi, tokens, size_t(n) * 4);
+    std::memcpy(hi + n, slots, size_t(n) * 4);
+    std::memcpy(hi + 2 * n, pos, size_t(n) * 4);
+    CK(cudaMemcpyAsync(m->d_tokens, hi, size_t(n) * 4, cudaMemcpyHostToDevice, m->stream), "h2d");
+    CK(cudaMemcpyAsync(m->d_slots, hi + n, size_t(n) * 4, cudaMemcpyHostToDevice, m->stream), "h2d");
+    CK(cudaMemcpyAsync(m->d_pos, hi + 2 * n, size_t(n) * 4, cudaMemcpyHostToDevice, m->stream), "h2d");
+    if (int rc = run_step(m, n, n, true, max_pos, argmax != nullptr, false, m->stream); rc != NEKO_OK) return rc;
+    if (logits)
+        CK(cudaMemcpyAsync(m->h_logits, m->logits, size_t(n) * m->V * 4, cudaMemcpyDeviceToHost, m->stream), "d2h");
+    if (argmax) CK(cudaMemcpyAsync(m->h_argmax, m->d_argmax, size_t(n) * 4, cudaMemcpyDeviceToHost, m->stream), "d2h");
+    if (int rc = wait_model(m); rc != NEKO_OK) return rc;
+    if (logits) std::memcpy(logits, m->h_logits, size_t(n) * m->V * 4);
+    if (argmax) std::memcpy(argmax, m->h_argmax, size_t(n) * 4);
+    return NEKO_OK;
+}
+
+int neko_model_stage(neko_model* m, int n, const int* slots, const int* tokens, const int* pos) {
+    if (!m || !slots || !tokens || !pos) return fail(m, NEKO_ERR_ARG, "stage: null argument");
+    if (n <= 0 || n > m->cfg.max_rows || n > m->cfg.max_seqs) return fail(m, NEKO_ERR_ARG, "stage: bad count");
+    for (int i = 0; i < n; i++) {
+        if (slots[i] < 0 || slots[i] >= m->cfg.max_seqs) return fail(m, NEKO_ERR_ARG, "stage: bad slot");
+        if (pos[i] < 0 || pos[i] >= m->cfg.context) return fail(m, NEKO_ERR_ARG, "stage: context overflow");
+        if (tokens[i] < 0 || tokens[i] >= m->V) return fail(m, NEKO_ERR_ARG, "stage: token id out of range");
+        for (int j = 0; j < i; j++)
+            if (slots[j] == slots[i]) return fail(m, NEKO_ERR_ARG, "stage: a slot appears twice");
+    }
+    Guard g(m->device);
+    CK(cudaMemcpy(m->d_tokens, tokens, size_t(n) * 4, cudaMemcpyHostToDevice), "stage");
+    CK(cudaMemcpy(m->d_slots, slots, size_t(n) * 4, cudaMemcpyHostToDevice), "stage");
+    CK(cudaMemcpy(m->d_pos, pos, size_t(n) * 4, cudaMemcpyHostToDevice), "stage");
+    return NEKO_OK;
+}
+
+int neko_model_step(neko_model* m, int n, int max_pos, void* stream) {
+    if (!m) return NEKO_ERR_ARG;
+    if (!m->final_ok) return fail(m, NEKO_ERR_ARG, "step: call neko_model_finalize first");
+    if (n <= 0 || n > m->cfg.max_rows || n > m->cfg.max_seqs) return fail(m, NEKO_ERR_ARG, "step: bad count");
+    if (max_pos < 0 || max_pos >= m->cfg.context) return fail(m, NEKO_ERR_ARG, "step: context overflow");
+    Guard g(m->device);
+    return run_step(m, n, n, true, max_pos, true, true, static_cast<cudaStream_t>(stream));
+}
+
+int neko_model_tokens(neko_model* m, int n, int* tokens, int* pos) {
+    if (!m || n <= 0 || n > m->cfg.max_seqs) return NEKO_ERR_ARG;
+    Guard g(m->device);
+    CK(cudaDeviceSynchronize(), "tokens");
+    if (unsigned d = read_device_error(true))
+        return fail(m, NEKO_ERR_DEVICE, "kernel reported device error " + std::to_string(d));
+    if (tokens) CK(cudaMemcpy(tokens, m->d_tokens, size_t(n) * 4, cudaMemcpyDeviceToHost), "tokens");
+    if (pos) CK(cudaMemcpy(pos, m->d_pos, size_t(n) * 4, cudaMemcpyDeviceToHost), "tokens");
+    return NEKO_OK;
+}
+
+int neko_model_memory(neko_model* m, int64_t* weights, int64_t* kv, int64_t* workspace) {
+    if (!m) return NEKO_ERR_ARG;
+    if (weights) *weights = int64_t(m->wbytes);
+    if (kv) *kv = int64_t(m->kv_bytes) * 2;
+    if (workspace) *workspace = int64_t(m->work_bytes);
+    return NEKO_OK;
+}
+
+int neko_model_step_launches(neko_model* m, int n) {
+    if (!m) return NEKO_ERR_ARG;
+    return step_launches(m, n, n, false, true, true);
+}
+
+int neko_model_matrix(neko_model* m, const char* which, const uint8_t** ptr, int* rows, int* cols) {
+    if (!m || !which) return NEKO_ERR_ARG;
+    std::string w(which);
+    const Mat* t = nullptr;
+    int layer = -1;
+    std::string leaf;
+    if (w == "head" || w == "embed") t = &m->embed;
+    else if (parse_layer(w, "layers.", layer, leaf) && layer < int(m->layers.size())) {
+        const Layer& L = m->layers[size_t(layer)];
+        if (leaf == "wqkv") t = &L.wqkv;
+        else if (leaf == "wo") t = &L.wo;
+        else if (leaf == "wgu" || leaf == "wup") t = &L.wup;
+        else if (leaf == "wdown") t = &L.wdown;
+    }
+    if (!t) return fail(m, NEKO_ERR_ARG, "matrix: unknown name " + w);
+    if (ptr) *ptr = t->w;
+    if (rows) *rows = t->rows;
+    if (cols) *cols = t->cols;
+    return t->fmt;
+}
+
+}  // extern "C"

@@ -1,0 +1,145 @@
+// Internal host-side declarations shared by the CUDA translation units of libneko_cuda.so.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <utility>
+
+namespace neko {
+
+// Launch with optional programmatic dependent launch (the kernel may start while the previous kernel on the
+// stream finishes; it synchronises itself with griddepcontrol.wait).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                             Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+int num_sms();  // of the current device, cached per device
+
+// ------------------------------------------------------------------ weight codec (k_quant.cu)
+cudaError_t launch_quantize(int fmt, const float* w, int rows, int cols, int64_t ld, int transpose, uint8_t* out,
+                            cudaStream_t st);
+cudaError_t launch_dequantize(int fmt, const uint8_t* q, int rows, int cols, float* out, cudaStream_t st);
+
+// ------------------------------------------------------------------ dequant GEMV (k_gemv.cu)
+enum NormKind : int { kNormNone = 0, kNormRms = 1, kNormLayer = 2 };
+
+struct GemvArgs {
+    const uint8_t* W = nullptr;  // packed rows (engine layout)
+    int64_t row_bytes = 0;
+    int rows = 0;                // output rows (row pairs when pair_off != 0)
+    int K = 0;
+    int fmt = 0;
+    const float* x = nullptr;    // M activation rows, row m at x + m * x_stride
+    int64_t x_stride = 0;
+    int M = 1;
+    int norm = kNormNone;        // applied to x rows while staging them (needs x staged in shared memory)
+    const float* gamma = nullptr;
+    const float* beta = nullptr;
+    float eps = 0.0f;
+    const float* bias = nullptr;
+    int flags = 0;               // kGelu | kAccumulate | kBias
+    float* y = nullptr;          // out row m at y + m * y_stride + n_off
+    int64_t y_stride = 0;
+    int n_off = 0;
+    int64_t pair_off = 0;        // != 0: out n = silu(row n) * row(n + pair_off)  (SwiGLU epilogue)
+    // launch plan (filled by plan_gemv)
+    int x_smem = 0;
+    int rows_per_cta = 0;
+    int nstage = 0;
+    int64_t stage_stride = 0;
+    int xs_off = 0;
+    int ring_off = 0;
+};
+
+// Shared-memory budget of one GEMV CTA. Two fit on an SM, so the next kernel's CTAs (launched early by PDL)
+// can stream their weights while this one finishes.
+constexpr int kGemvSmemBudget = 110 * 1024;
+constexpr int kGemvXSmemMax = 40 * 1024;
+
+cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, bool pdl, int max_ctas = 0);
+int gemv_launch_count();  // number of launches launch_gemv issues per call (1)
+
+// ------------------------------------------------------------------ other ops (k_ops.cu)
+cudaError_t launch_norm(const float* x, int64_t x_stride, float* y, int64_t y_stride, const float* gamma,
+                        const float* beta, int rows, int C, float eps, bool rms, cudaStream_t st, bool pdl);
+cudaError_t launch_softmax(const float* x, float* y, int rows, int C, cudaStream_t st);
+cudaError_t launch_argmax(const float* x, int64_t stride, int rows, int C, int* out, cudaStream_t st, bool pdl);
+cudaError_t launch_silu_mul(const float* h, float* g, int T, int I, cudaStream_t st);
+// Embedding gather (embed.comp semantics + the native runner's f32 position table):
+// x[t][c] = deq(table[tok[t] - row_base])[c] (+ wpe[pos][c]); tokens outside [row_base, row_base + nrows) are
+// skipped. wpe16 is an f16 table (the reference GPU path), wpe32 an f32 one (the CPU path); pos per row from
+// pos_arr when not NULL, else pos0 + t.
+cudaError_t launch_embed(const int* tokens, int T, int C, int fmt, const uint8_t* table, int64_t rb, int row_base,
+                         int nrows, const uint16_t* wpe16, const float* wpe32, int pos0, const int* pos_arr, float* x,
+                         cudaStream_t st, bool pdl);
+
+// QK-norm + RoPE + KV-cache store for rows of a fused qkv buffer (rope.comp + kv_store.comp semantics).
+struct QkvPostArgs {
+    float* qkv = nullptr;
+    int64_t qkv_stride = 0;          // floats between rows
+    int rows = 0;
+    int n_head = 0, n_kv = 0, hd = 0;
+    int do_norm = 0;                 // per-head RMSNorm with wn (q: wn[0..hd), k: wn[hd..2hd))
+    const float* wn = nullptr;
+    float eps = 0.0f;
+    int do_rope = 0;                 // NeoX rotation from cs [pos][hd/2](cos, sin)
+    const float* cs = nullptr;
+    int rope_kv_heads = 1;           // 1: rotate the key heads too (always, in the models)
+    int store_kv = 0;                // write K, V (f16) to the caches
+    uint16_t* kc = nullptr;
+    uint16_t* vc = nullptr;
+    int64_t slot_stride = 0, pos_stride = 0, head_stride = 0;  // cache element strides
+    const int* row_slot = nullptr;   // per-row slot (NULL: slot0)
+    const int* row_pos = nullptr;    // per-row position (NULL: pos0 + row)
+    int slot0 = 0, pos0 = 0;
+    int k_off = 0, v_off = 0;        // column offsets of K and V inside a qkv row
+    int pos_limit = 0x7fffffff;      // positions >= limit are not stored (device error kErrBadIndex)
+};
+cudaError_t launch_qkv_post(const QkvPostArgs& a, cudaStream_t st, bool pdl);
+
+// ------------------------------------------------------------------ attention (k_attention.cu)
+struct AttnArgs {
+    const float* q = nullptr;        // row r, head h at q + r * q_stride + h * hd
+    int64_t q_stride = 0;
+    const uint16_t* kc = nullptr;    // element (slot, pos, kvh, d) at kc + slot*slot_stride + pos*pos_stride
+    const uint16_t* vc = nullptr;    //                                    + kvh*head_stride + d
+    int64_t slot_stride = 0, pos_stride = 0, head_stride = 0;
+    const int* row_slot = nullptr;
+    const int* row_pos = nullptr;
+    int slot0 = 0, pos0 = 0;
+    int rows = 0, n_head = 0, n_kv = 0, hd = 0;
+    float scale = 0.0f;
+    float* out = nullptr;            // row r, head h at out + r * out_stride + h * hd
+    int64_t out_stride = 0;
+    int max_pos = 0;                 // upper bound of any row's position (sizes the split-KV grid)
+    int pos_limit = 0x7fffffff;      // rows whose position is >= limit or > the planned max_pos are skipped
+    // split-KV scratch: partial (max, sum, acc[hd]) per (row, q head, split) and one ticket per (row, kv head)
+    float* part = nullptr;
+    unsigned* tickets = nullptr;
+    int64_t part_capacity = 0;       // floats available in part
+    int64_t ticket_capacity = 0;
+};
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl);
+// Scratch the split-KV attention needs for rows x n_head heads up to position max_pos.
+void attention_scratch(int rows, int n_head, int n_kv, int hd, int max_pos, int64_t* part_floats,
+                       int64_t* tickets);
+
+// ------------------------------------------------------------------ errors
+std::string cuda_msg(cudaError_t e, const char* what);
+unsigned read_device_error(bool clear);
+
+}  // namespace neko

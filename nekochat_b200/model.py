@@ -1,0 +1,162 @@
+"""The native GPT-2 / Qwen3 runner (``neko_model_*`` of include/neko_cuda.h).
+
+``Model.forward`` has the semantics of the engine's ``Model::forward(tokens, T, pos0, logits)``
+(app/architecture/shared/cpp/model.h:72) for one sequence slot; ``decode`` is the batched step the engine
+cannot express; ``stage`` + ``step`` run greedy decoding entirely on the device (the bench's inner loop).
+"""
+import ctypes as C
+
+import numpy as np
+
+from . import ARCH_GPT2, ARCH_QWEN3, ModelConfig, NekoError, lib
+from . import workload
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+class Model:
+    def __init__(self, shape, fmt, context, max_seqs=1, max_rows=64, device=0):
+        s = dict(shape)
+        self.shape = s
+        cfg = ModelConfig()
+        cfg.arch = ARCH_QWEN3 if s["arch"] == "qwen3" else ARCH_GPT2
+        cfg.vocab, cfg.embd, cfg.layers, cfg.heads = s["vocab"], s["embd"], s["layers"], s["heads"]
+        cfg.kv_heads, cfg.head_dim, cfg.ff, cfg.max_pos = s["kv_heads"], s["head_dim"], s["ff"], s["max_pos"]
+        cfg.eps, cfg.rope_theta, cfg.weight_format = s["eps"], s["rope_theta"], fmt
+        cfg.context, cfg.max_seqs, cfg.max_rows = context, max_seqs, max_rows
+        self.cfg = cfg
+        self.vocab = s["vocab"]
+        self.fmt = fmt
+        self.context = context
+        err = C.create_string_buffer(1024)
+        self.h = lib().neko_model_create(device, C.byref(cfg), err, 1024)
+        if not self.h:
+            raise NekoError("neko_model_create: " + err.value.decode())
+
+    def _check(self, rc, what):
+        if rc != 0:
+            raise NekoError(f"{what}: status {rc}: {lib().neko_model_last_error(self.h).decode()}")
+
+    def set_tensor(self, name, array):
+        a = np.ascontiguousarray(array, dtype=np.float32)
+        rows, cols = (a.shape[0], int(np.prod(a.shape[1:]))) if a.ndim > 1 else (1, a.shape[0])
+        self._check(lib().neko_model_set_tensor(self.h, name.encode(), _p(a), rows, cols), f"set_tensor {name}")
+
+    def set_tensor_device(self, name, t):
+        """t: a contiguous float32 CUDA tensor on the model's device."""
+        rows, cols = (t.shape[0], t.numel() // t.shape[0]) if t.dim() > 1 else (1, t.shape[0])
+        self._check(lib().neko_model_set_tensor_device(self.h, name.encode(), C.c_void_p(t.data_ptr()), rows, cols),
+                    f"set_tensor_device {name}")
+
+    def load_random_device(self, seed=0, host_copy=None):
+        """Random-init weights generated on the GPU (torch, seeded): N(0, 0.02) matrices, unit norm gains, zero
+        biases, in workload.tensor_specs order. host_copy(name, f16 numpy array) receives each tensor for a CPU
+        baseline checkpoint when given."""
+        import torch
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        for name, shp, kind in workload.tensor_specs(self.shape):
+            if kind == "w":
+                t = torch.randn(shp, generator=g, device="cuda", dtype=torch.float32).mul_(0.02)
+            elif kind == "g":
+                t = torch.ones(shp, device="cuda", dtype=torch.float32)
+            else:
+                t = torch.zeros(shp, device="cuda", dtype=torch.float32)
+            self.set_tensor_device(name, t)
+            if host_copy is not None:
+                host_copy(name, t.half().cpu().numpy())
+            del t
+        self._check(lib().neko_model_finalize(self.h), "finalize")
+        return self
+
+    def load(self, tensors):
+        """tensors: iterable of (name, float32 array), e.g. workload.weights(shape)."""
+        for name, a in tensors:
+            self.set_tensor(name, a)
+        self._check(lib().neko_model_finalize(self.h), "finalize")
+        return self
+
+    def forward(self, tokens, pos0, slot=0):
+        """Model::forward: last token's logits (vocab floats)."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty(self.vocab, np.float32)
+        self._check(lib().neko_model_forward(self.h, slot, _p(t), len(t), pos0, _p(out)), "forward")
+        return out
+
+    def prefill(self, tokens, slot=0, pos0=0, chunk=None):
+        """Runs a prompt in chunks of <= chunk tokens (Engine::generate's prefill loop, engine.cpp:98-112; at most
+        max_rows, 64 like Model::kMaxBatch by default) and returns the last token's logits."""
+        chunk = min(chunk or 64, self.cfg.max_rows)
+        tokens = np.asarray(tokens, np.int32)
+        logits = None
+        for i in range(0, len(tokens), chunk):
+            logits = self.forward(tokens[i:i + chunk], pos0 + i, slot)
+        return logits
+
+    def decode(self, slots, tokens, pos, want_logits=True):
+        """One decode step for n sequences. Returns (logits [n][vocab] or None, argmax [n])."""
+        slots = np.ascontiguousarray(slots, dtype=np.int32)
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        pos = np.ascontiguousarray(pos, dtype=np.int32)
+        n = len(slots)
+        logits = np.empty((n, self.vocab), np.float32) if want_logits else None
+        am = np.empty(n, np.int32)
+        self._check(lib().neko_model_decode(self.h, n, _p(slots), _p(tokens), _p(pos), _p(logits), _p(am)),
+                    "decode")
+        return logits, am
+
+    def stage(self, slots, tokens, pos):
+        slots = np.ascontiguousarray(slots, dtype=np.int32)
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        pos = np.ascontiguousarray(pos, dtype=np.int32)
+        self._check(lib().neko_model_stage(self.h, len(slots), _p(slots), _p(tokens), _p(pos)), "stage")
+
+    def step(self, n, max_pos, stream=None):
+        """Enqueues one greedy decode step of the n staged sequences on `stream` (a cudaStream_t handle)."""
+        self._check(lib().neko_model_step(self.h, n, max_pos, C.c_void_p(stream) if stream else None), "step")
+
+    def tokens(self, n):
+        t = np.empty(n, np.int32)
+        p = np.empty(n, np.int32)
+        self._check(lib().neko_model_tokens(self.h, n, _p(t), _p(p)), "tokens")
+        return t, p
+
+    def memory(self):
+        w, kv, ws = C.c_int64(), C.c_int64(), C.c_int64()
+        self._check(lib().neko_model_memory(self.h, C.byref(w), C.byref(kv), C.byref(ws)), "memory")
+        return dict(weights=w.value, kv=kv.value, workspace=ws.value)
+
+    def step_launches(self, n):
+        return int(lib().neko_model_step_launches(self.h, n))
+
+    def matrix(self, which):
+        """(device pointer, rows, cols, format) of one packed matrix: 'layers.L.wqkv|wo|wgu|wdown' or 'head'."""
+        p, r, c = C.c_void_p(), C.c_int(), C.c_int()
+        fmt = lib().neko_model_matrix(self.h, which.encode(), C.byref(p), C.byref(r), C.byref(c))
+        if fmt < 0:
+            raise NekoError(f"matrix {which}: {lib().neko_model_last_error(self.h).decode()}")
+        return p.value, r.value, c.value, fmt
+
+    def close(self):
+        if self.h:
+            lib().neko_model_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def build(shape_name, fmt, context, max_seqs=1, max_rows=64, seed=0, perturb=False, device=0):
+    s = workload.shape(shape_name)
+    m = Model(s, fmt, context, max_seqs, max_rows, device)
+    return m.load(workload.weights(s, seed, perturb))

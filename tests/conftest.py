@@ -1,0 +1,14 @@
+"""pytest configuration: the `gpu` marker and the repository root on sys.path.
+
+Tests marked `gpu` need a B200 (sm_100a) and the built libneko_cuda.so; everything else runs on the CPU
+(`pytest -m "not gpu"`)."""
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA B200 GPU and the built CUDA library")

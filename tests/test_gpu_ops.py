@@ -1,0 +1,136 @@
+"""Operator parity through the C ABI (neko_op_*) against the oracle: dequant matmul over the BASELINE shapes and
+odd shapes (tolerance |gpu - cpu| <= 2e-3 (1 + |cpu|), the engine's self-test bound for matmuls), norms,
+softmax, argmax and attention."""
+import numpy as np
+import pytest
+
+from oracle.oracle import ACCUMULATE, FP4, FP8, F16, GELU, Restatement
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as t
+    assert t.cuda.is_available()
+    return t
+
+
+@pytest.fixture(scope="module")
+def R():
+    return Restatement()
+
+
+def close(a, b, tol=TOL):
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    d = np.abs(a - b)
+    ok = d <= tol * (1 + np.abs(b))
+    assert ok.all(), f"max err {d.max()} at {np.unravel_index(np.argmax(~ok), a.shape)}"
+
+
+def run_matmul(torch, fmt, x, q, K, bias=None, y0=None, y_stride=None, n_off=0, flags=0):
+    from nekochat_b200 import ops
+    t = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    y = ops.matmul(fmt, t(x), t(q), K, t(bias), t(y0), y_stride, n_off, flags)
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+@pytest.mark.parametrize("fmt", [FP8, FP4, F16])
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 13])
+@pytest.mark.parametrize("K,N", [(96, 37), (1024, 300), (3072, 129), (2048, 1024)])
+def test_matmul_shapes(torch, R, fmt, M, K, N):
+    rng = np.random.default_rng(M * 1000 + K + N + fmt)
+    w = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    x = (rng.standard_normal((M, K))).astype(np.float32)
+    q = R.quantize(fmt, w) if fmt != F16 else w.astype(np.float16).view(np.uint8).reshape(N, 2 * K)
+    close(run_matmul(torch, fmt, x, q, K), R.matmul(fmt, x, q, K))
+
+
+@pytest.mark.parametrize("fmt", [FP8, FP4])
+@pytest.mark.parametrize("flags", [ACCUMULATE, GELU, GELU | ACCUMULATE])
+def test_matmul_epilogues(torch, R, fmt, flags):
+    rng = np.random.default_rng(flags)
+    K, N, M, NS, off = 1024, 200, 4, 211, 7
+    w = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    y0 = rng.standard_normal((M, NS)).astype(np.float32)
+    q = R.quantize(fmt, w)
+    close(run_matmul(torch, fmt, x, q, K, b, y0.copy(), NS, off, flags),
+          R.matmul(fmt, x, q, K, b, y0.copy(), NS, flags, off))
+
+
+@pytest.mark.parametrize("fmt", [FP8, FP4])
+@pytest.mark.parametrize("K,N", [(1024, 3072), (3072, 1024), (2048, 6144), (2560, 9728), (9728, 2560), (1024, 151936)])
+def test_matmul_baseline_sweep_m1(torch, R, fmt, K, N):
+    """The BASELINE operator sweep shapes at M = 1 (decode), weights quantized on the GPU, checked against an
+    fp64 product of the exactly dequantized weights (the oracle's sequential sum is too slow at 152K rows)."""
+    from nekochat_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(K * 7 + N)
+    w = torch.randn((N, K), generator=g, device="cuda") * 0.02
+    x = torch.randn((1, K), generator=g, device="cuda")
+    q = ops.quantize(fmt, w)
+    y = ops.matmul(fmt, x, q, K)
+    deq = ops.dequantize(fmt, q, K).double()
+    ref = (x.double() @ deq.T).float()
+    torch.cuda.synchronize()
+    close(y.cpu().numpy(), ref.cpu().numpy(), 1e-4)
+    # spot-check rows against the oracle's exact sequential sum
+    rows = np.linspace(0, N - 1, 16).astype(int)
+    qh = q[torch.as_tensor(rows, device="cuda")].cpu().numpy()
+    close(y.cpu().numpy()[:, rows], R.matmul(fmt, x.cpu().numpy(), qh, K))
+
+
+@pytest.mark.parametrize("M", [16, 64])
+def test_matmul_many_rows(torch, R, M):
+    """Prefill-sized activations (x read from global memory, several passes over each staged row block)."""
+    rng = np.random.default_rng(M)
+    K, N = 1024, 512
+    w = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    q = R.quantize(FP8, w)
+    close(run_matmul(torch, FP8, x, q, K), R.matmul(FP8, x, q, K))
+
+
+@pytest.mark.parametrize("C,rows", [(96, 3), (1024, 7), (2560, 2), (151936, 2)])
+def test_norms(torch, R, C, rows):
+    from nekochat_b200 import ops
+    rng = np.random.default_rng(C)
+    x = (rng.standard_normal((rows, C)) * 5).astype(np.float32)
+    g = rng.standard_normal(C).astype(np.float32)
+    b = rng.standard_normal(C).astype(np.float32)
+    tx, tg, tb = (torch.from_numpy(a).cuda() for a in (x, g, b))
+    close(ops.norm(tx, tg, None, 1e-6).cpu().numpy(), R.rms_norm(x, g, 1e-6), 1e-5)
+    close(ops.norm(tx, tg, tb, 1e-5).cpu().numpy(), R.layer_norm(x, g, b, 1e-5), 1e-5)
+
+
+@pytest.mark.parametrize("C,rows", [(1024, 5), (2048, 3), (2560, 1), (151936, 2), (1000, 4)])
+def test_softmax_argmax(torch, R, C, rows):
+    from nekochat_b200 import ops
+    rng = np.random.default_rng(C + 1)
+    x = (rng.standard_normal((rows, C)) * 4).astype(np.float32)
+    x[0, C // 3] = x[0].max() + 1  # a clear winner
+    if rows > 1:
+        x[1, 5] = x[1, 9] = x[1].max() + 1  # tie: the first index wins (std::max_element)
+    tx = torch.from_numpy(x).cuda()
+    close(ops.softmax(tx).cpu().numpy(), R.softmax_rows(x), 1e-5)
+    am = ops.argmax(tx).cpu().numpy()
+    assert [int(a) for a in am] == [R.argmax(r) for r in x]
+
+
+@pytest.mark.parametrize("H,KV,hd,T,pos0", [(16, 8, 128, 1, 700), (4, 2, 64, 3, 1030), (12, 12, 64, 5, 0),
+                                            (32, 8, 128, 1, 4000), (8, 8, 128, 64, 200)])
+def test_attention_op(torch, R, H, KV, hd, T, pos0):
+    from nekochat_b200 import ops
+    rng = np.random.default_rng(pos0 + T)
+    ctx = pos0 + T
+    stride = (H + 2 * KV) * hd
+    q = rng.uniform(-1, 1, (T, stride)).astype(np.float32)
+    kc = rng.uniform(-1, 1, (ctx, KV * hd)).astype(np.float16).view(np.uint16)
+    vc = rng.uniform(-1, 1, (ctx, KV * hd)).astype(np.float16).view(np.uint16)
+    ref = R.attention(q, stride, kc, vc, T, H, KV, hd, pos0)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16) if a.dtype == np.uint16 else a).cuda()
+    got = ops.attention(t(q), stride, t(kc), t(vc), T, H, KV, hd, pos0).cpu().numpy()
+    close(got, ref, 2e-3)
