@@ -117,6 +117,13 @@ int neko_op_dequantize(int format, const uint8_t* q, int rows, int cols, float* 
  * act(x[t] . W[n] + bias[n]) for n < rows, t < T. x rows have stride K; y rows have stride y_stride. */
 int neko_op_matmul(int format, const float* x, int T, int K, const uint8_t* W, int rows, const float* bias,
                    float* y, int y_stride, int n_off, int flags, void* stream);
+/* The fused forms the decode step uses, as one operator: norm (0 none, 1 RMSNorm, 2 LayerNorm with gamma/beta,
+ * eps) applied to the x rows before the product (the engine's LayerNorm dispatch + Matmul, qwen3_model.cpp:309-311),
+ * and swiglu != 0 for a [gate | up] weight of 2 * rows rows whose output is silu(x . gate[n]) * (x . up[n])
+ * (Matmul + SiluMul, qwen3_model.cpp:323-325). The norm needs T * K * 4 <= 40 KB. */
+int neko_op_matmul_fused(int format, const float* x, int T, int K, const uint8_t* W, int rows, int norm,
+                         const float* gamma, const float* beta, float eps, int swiglu, const float* bias, float* y,
+                         int y_stride, int n_off, int flags, void* stream);
 /* cpu::rmsNorm / cpu::layerNorm (cpu_ops.cpp:483-511). beta NULL selects RMSNorm. */
 int neko_op_norm(const float* x, float* y, const float* gamma, const float* beta, int rows, int C, float eps,
                  void* stream);
@@ -182,6 +189,12 @@ int neko_model_step(neko_model* m, int n, int max_pos, void* stream);
 int neko_model_tokens(neko_model* m, int n, int* tokens, int* pos);
 /* Bytes held on the device: weights, KV cache, workspace (Model::memory, model.h:91). */
 int neko_model_memory(neko_model* m, int64_t* weights, int64_t* kv, int64_t* workspace);
+/* Model::setDebugLayers(n, stage) (model.h:93-104): with n >= 0, neko_model_forward writes, instead of the last
+ * token's logits, the hidden states [T][embd] after n layers (stage 0) or the intermediate of layer n after
+ * `stage` ([T][width], the engine's debugStages numbering: Qwen3 2 qkv, 3 qk-norm+rope, 4 attn, 5 o_proj+res,
+ * 8 silu*up, 9 down+res; GPT-2 2 qkv, 3 attn, 4 proj+res, 6 fc+gelu, 7 fc2+res). Stages fused into a neighbour
+ * (the norms, gate|up) return NEKO_ERR_UNSUPPORTED. `logits` must hold T * width floats. n < 0 turns it off. */
+int neko_model_set_debug(neko_model* m, int layers, int stage);
 /* Kernel launches one decode step of n sequences issues (for the bench's launch count). */
 int neko_model_step_launches(neko_model* m, int n);
 /* Device pointer and byte size of one packed weight matrix ("layers.L.wqkv", "layers.L.wo", "layers.L.wgu",

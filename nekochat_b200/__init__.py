@@ -85,6 +85,8 @@ _SIGS = {
     "neko_op_dequantize": (C.c_int, [C.c_int, _vp, C.c_int, C.c_int, _vp, _vp]),
     "neko_op_matmul": (C.c_int, [C.c_int, _vp, C.c_int, C.c_int, _vp, C.c_int, _vp, _vp, C.c_int, C.c_int, C.c_int,
                                  _vp]),
+    "neko_op_matmul_fused": (C.c_int, [C.c_int, _vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, C.c_float,
+                                       C.c_int, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp]),
     "neko_op_norm": (C.c_int, [_vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_float, _vp]),
     "neko_op_softmax": (C.c_int, [_vp, _vp, C.c_int, C.c_int, _vp]),
     "neko_op_attention": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
@@ -102,6 +104,7 @@ _SIGS = {
     "neko_model_tokens": (C.c_int, [_vp, C.c_int, _vp, _vp]),
     "neko_model_memory": (C.c_int, [_vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "neko_model_step_launches": (C.c_int, [_vp, C.c_int]),
+    "neko_model_set_debug": (C.c_int, [_vp, C.c_int, C.c_int]),
     "neko_model_matrix": (C.c_int, [_vp, C.c_char_p, C.POINTER(C.c_void_p), C.POINTER(C.c_int),
                                     C.POINTER(C.c_int)]),
 }

@@ -442,6 +442,37 @@ int neko_op_matmul(int format, const float* x, int T, int K, const uint8_t* W, i
     NEKO_OP_RETURN(launch_gemv(a, static_cast<cudaStream_t>(stream), (flags & NEKO_PDL) != 0));
 }
 
+int neko_op_matmul_fused(int format, const float* x, int T, int K, const uint8_t* W, int rows, int norm,
+                         const float* gamma, const float* beta, float eps, int swiglu, const float* bias, float* y,
+                         int y_stride, int n_off, int flags, void* stream) {
+    if (!x || !W || !y || T <= 0 || K <= 0 || rows <= 0 || format < 0 || format > 2 || norm < 0 || norm > 2)
+        return set_err(nullptr, NEKO_ERR_ARG, "matmul_fused args");
+    if ((format == kF16 ? K % 8 : K % 32) != 0) return set_err(nullptr, NEKO_ERR_ARG, "matmul K alignment");
+    if (norm && (!gamma || (norm == kNormLayer && !beta))) return set_err(nullptr, NEKO_ERR_ARG, "norm weights");
+    if (norm && int64_t(T) * K * 4 > kGemvXSmemMax) return set_err(nullptr, NEKO_ERR_ARG, "norm prologue too large");
+    if ((flags & kBias) && !bias) return set_err(nullptr, NEKO_ERR_ARG, "matmul bias flag without bias");
+    GemvArgs a;
+    a.W = W;
+    a.row_bytes = row_bytes(format, K);
+    a.rows = rows;
+    a.K = K;
+    a.fmt = format;
+    a.x = x;
+    a.x_stride = K;
+    a.M = T;
+    a.norm = norm;
+    a.gamma = gamma;
+    a.beta = beta;
+    a.eps = eps;
+    a.bias = bias;
+    a.flags = swiglu ? 0 : flags & (kGelu | kAccumulate | kBias);
+    a.y = y;
+    a.y_stride = y_stride;
+    a.n_off = n_off;
+    a.pair_off = swiglu ? rows : 0;
+    NEKO_OP_RETURN(launch_gemv(a, static_cast<cudaStream_t>(stream), (flags & NEKO_PDL) != 0));
+}
+
 int neko_op_norm(const float* x, float* y, const float* gamma, const float* beta, int rows, int C, float eps,
                  void* stream) {
     if (!x || !y || !gamma || rows < 0 || C <= 0) return set_err(nullptr, NEKO_ERR_ARG, "norm args");

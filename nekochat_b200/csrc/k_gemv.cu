@@ -207,7 +207,6 @@ __device__ __forceinline__ void row_block(const uint8_t* rows0, int64_t rb, int 
 template <int FMT, int R, int MT>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    constexpr int RS = kConsumerWarps * R;
     constexpr float kFactor = FMT == kFP8 ? kFp8Factor : FMT == kFP4 ? kFp4Factor : 1.0f;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + a.nstage;
@@ -218,9 +217,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
 
     const int r0 = blockIdx.x * a.rows_per_cta;
     const int r1 = min(a.rows, r0 + a.rows_per_cta);
+    const int SR = a.stage_rows;
     pdl_trigger();
     if (r0 >= r1) return;
-    const int nst = (r1 - r0 + RS - 1) / RS;
+    const int nst = (r1 - r0 + SR - 1) / SR;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.nstage; s++) {
@@ -237,14 +237,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
             for (int st = 0; st < nst; st++) {
                 const int slot = st % a.nstage;
                 if (st >= a.nstage && !mbar_wait(&empty[slot], ((st / a.nstage) - 1) & 1)) break;
-                const int row = r0 + st * RS;
-                const int n = min(RS, r1 - row);
+                const int row = r0 + st * SR;
+                const int n = min(SR, r1 - row);
                 const uint32_t bytes = uint32_t(n * a.row_bytes);
                 uint8_t* dst = ring + slot * a.stage_stride;
                 mbar_arrive_expect_tx(&full[slot], paired ? 2 * bytes : bytes);
                 bulk_g2s(dst, a.W + int64_t(row) * a.row_bytes, bytes, &full[slot]);
                 if (paired)
-                    bulk_g2s(dst + RS * a.row_bytes, a.W + (int64_t(row) + a.pair_off) * a.row_bytes, bytes,
+                    bulk_g2s(dst + SR * a.row_bytes, a.W + (int64_t(row) + a.pair_off) * a.row_bytes, bytes,
                              &full[slot]);
             }
         }
@@ -265,8 +265,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     for (int st = 0; st < nst; st++) {
         const int slot = st % a.nstage;
         if (!mbar_wait(&full[slot], (st / a.nstage) & 1)) return;
-        const int row0 = r0 + st * RS;
-        const int nrows = min(RS, r1 - row0);
+        const int row0 = r0 + st * SR;
+        const int nrows = min(SR, r1 - row0);
         const int my0 = warp * R;
         const int nr = min(R, nrows - my0);
         if (nr > 0) {
@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
                 float acc[R][MT];
                 row_block<FMT, R, MT>(stage, a.row_bytes, nr, a.K, src, m0, a.M, lane, acc);
                 float accu[R][MT];
-                if (paired) row_block<FMT, R, MT>(stage + RS * a.row_bytes, a.row_bytes, nr, a.K, src, m0, a.M, lane,
+                if (paired) row_block<FMT, R, MT>(stage + SR * a.row_bytes, a.row_bytes, nr, a.K, src, m0, a.M, lane,
                                                   accu);
 #pragma unroll
                 for (int r = 0; r < R; r++) {
@@ -370,12 +370,18 @@ cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, bool pdl, int max_ctas) {
     // activation rows per pass over a stage (more rows loop; 4 x 4 accumulators keep the kernel spill-free)
     const int MT = a.M >= 4 ? 4 : a.M >= 2 ? 2 : 1;
 
-    a.stage_stride = (int64_t(kConsumerWarps) * R * rb + 127) / 128 * 128;
     a.xs_off = 128 * ((2 * 8 * 8 + 127) / 128);  // room for up to 8 stages of (full, empty) barriers
     const int x_alloc = a.x_smem ? int((x_bytes + 127) / 128 * 128) : 0;
     a.ring_off = a.xs_off + x_alloc;
     const int64_t room = kGemvSmemBudget - a.ring_off;
-    const int stages_needed = (a.rows_per_cta + kConsumerWarps * R - 1) / (kConsumerWarps * R);
+    // Rows per stage: one row block per warp, fewer when very wide rows would leave room for less than two stages.
+    int64_t sr = int64_t(kConsumerWarps) * R;
+    if (2 * sr * rb > room) sr = std::max<int64_t>(1, room / (2 * rb));
+    if (sr * rb > room) sr = room / rb;
+    if (sr < 1) return cudaErrorInvalidValue;  // a single row does not fit next to the staged activations
+    a.stage_rows = int(sr);
+    a.stage_stride = (sr * rb + 127) / 128 * 128;
+    const int stages_needed = int((a.rows_per_cta + sr - 1) / sr);
     a.nstage = int(std::min<int64_t>(std::min(8, stages_needed), room / a.stage_stride));
     if (a.nstage < 1) return cudaErrorInvalidValue;
     const size_t smem = size_t(a.ring_off + a.nstage * a.stage_stride);

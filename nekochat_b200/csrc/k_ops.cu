@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(kPostWarps * 32) qkv_post_kernel(const QkvPost
         }
         __syncwarp();
     }
-    if (is_q || !a.store_kv) {
+    if (is_q || !a.store_kv || a.write_back_k) {
         for (int d = lane; d < hd; d += 32) row[col + d] = v[d];
     }
     if (is_k && a.store_kv) {

@@ -21,6 +21,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <new>
@@ -111,6 +112,8 @@ struct neko_model {
     float* staging = nullptr;  // f32 upload buffer for matrices
     size_t staging_floats = 0;
     bool final_ok = false;
+    int debug_layers = -1;  // Model::setDebugLayers: stop after this many layers and output the hidden states
+    int debug_stage = 0;    // > 0: stop inside layer debug_layers after this stage (debugStages numbering)
     // graphs keyed by (rows, nout, bucket, mode)
     std::map<std::tuple<int, int, int, int>, cudaGraphExec_t> graphs;
 };
@@ -223,6 +226,7 @@ int bucket_for(neko_model* m, int max_pos) {
 // d_outrows (or the last row when nout == 1 and rows are one prefill chunk), optional argmax and advance.
 int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_pos, bool do_argmax, bool advance,
                  cudaStream_t st) {
+    cudaError_t dumped = cudaSuccess;
     const int C = m->C, H = m->H, KV = m->KV, hd = m->hd;
     const float eps = m->cfg.eps;
     bool first = true;
@@ -272,7 +276,17 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         return launch_norm(m->x, C, m->xn, C, g, b, R, C, eps, m->qwen, st, pdl());
     };
 
-    for (size_t l = 0; l < m->layers.size(); l++) {
+    const bool staged = m->debug_layers >= 0 && m->debug_stage > 0;
+    const size_t nlayers = m->debug_layers >= 0
+                               ? std::min(m->layers.size(), size_t(m->debug_layers) + (staged ? 1 : 0))
+                               : m->layers.size();
+    // Model::setDebugLayers(n, stage) (model.h:93-104): inside layer n, stop after `stage` and dump that buffer.
+    auto dump = [&](size_t l, int stage, const float* buf, int width) -> bool {
+        if (!staged || int(l) != m->debug_layers || m->debug_stage != stage) return false;
+        dumped = cudaMemcpyAsync(m->logits, buf, size_t(R) * width * 4, cudaMemcpyDeviceToDevice, st);
+        return true;
+    };
+    for (size_t l = 0; l < nlayers; l++) {
         const Layer& L = m->layers[l];
         uint16_t* kc = m->kc + int64_t(l) * m->kv_layer;
         uint16_t* vc = m->vc + int64_t(l) * m->kv_layer;
@@ -280,6 +294,7 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         const float* src;
         CK(normed(L.ln1, L.ln1b, nk, src), "norm1");
         CK(gemv(L.wqkv, m->QW, src, C, R, nk, L.ln1, L.ln1b, L.bqkv, m->qwen ? 0 : kBias, m->qkv, m->QW, 0), "qkv");
+        if (dump(l, 2, m->qkv, m->QW)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
         QkvPostArgs q;
         q.qkv = m->qkv;
         q.qkv_stride = m->QW;
@@ -303,7 +318,9 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         q.k_off = H * hd;
         q.v_off = (H + KV) * hd;
         q.pos_limit = m->cfg.context;
+        q.write_back_k = staged ? 1 : 0;
         CK(launch_qkv_post(q, st, pdl()), "qkv_post");
+        if (m->qwen && dump(l, 3, m->qkv, m->QW)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
         AttnArgs a;
         a.q = m->qkv;
         a.q_stride = m->QW;
@@ -328,18 +345,26 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         a.part_capacity = m->part_cap;
         a.ticket_capacity = m->tick_cap;
         CK(launch_attention(a, st, pdl()), "attention");
+        if (dump(l, m->qwen ? 4 : 3, m->att, H * hd)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
         CK(gemv(L.wo, C, m->att, int64_t(H) * hd, R, kNormNone, nullptr, nullptr, L.bo,
                 kAccumulate | (m->qwen ? 0 : kBias), m->x, C, 0),
            "o_proj");
+        if (dump(l, m->qwen ? 5 : 4, m->x, C)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
         CK(normed(L.ln2, L.ln2b, nk, src), "norm2");
         if (m->qwen) {
             CK(gemv(L.wup, m->F, src, C, R, nk, L.ln2, nullptr, nullptr, 0, m->h, m->F, m->F), "gate_up");
         } else {
             CK(gemv(L.wup, m->UPW, src, C, R, nk, L.ln2, L.ln2b, L.bup, kBias | kGelu, m->h, m->UPW, 0), "fc");
         }
+        if (dump(l, m->qwen ? 8 : 6, m->h, m->F)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
         CK(gemv(L.wdown, C, m->h, m->F, R, kNormNone, nullptr, nullptr, L.bdown, kAccumulate | (m->qwen ? 0 : kBias),
                 m->x, C, 0),
            "down");
+        if (dump(l, m->qwen ? 9 : 7, m->x, C)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
+    }
+    if (m->debug_layers >= 0) {  // hidden states of every row instead of logits
+        CK(cudaMemcpyAsync(m->logits, m->x, size_t(R) * C * 4, cudaMemcpyDeviceToDevice, st), "debug copy");
+        return NEKO_OK;
     }
     // final norm + LM head on the output rows
     const float* hx;
@@ -383,7 +408,8 @@ int step_launches(neko_model* m, int R, int nout, bool gather, bool do_argmax, b
 // Runs (capturing on first use) the graph of one step shape.
 int run_step(neko_model* m, int R, int nout, bool identity, int max_pos, bool do_argmax, bool advance, cudaStream_t st) {
     const int bucket = bucket_for(m, max_pos);
-    const int mode = (identity ? 1 : 0) | (do_argmax ? 2 : 0) | (advance ? 4 : 0);
+    const int mode = (identity ? 1 : 0) | (do_argmax ? 2 : 0) | (advance ? 4 : 0) |
+                     (m->debug_layers >= 0 ? (8 + (m->debug_layers << 4) + (m->debug_stage << 12)) : 0);
     auto key = std::make_tuple(R, nout, bucket, mode);
     auto it = m->graphs.find(key);
     if (it == m->graphs.end()) {
@@ -411,6 +437,17 @@ int run_step(neko_model* m, int R, int nout, bool identity, int max_pos, bool do
     }
     CK(cudaGraphLaunch(it->second, st), "graph launch");
     return NEKO_OK;
+}
+
+// floats per row that a debug dump holds (debugStages widths, qwen3_model.cpp:80-85, gpt2_model.cpp:61-64)
+int debug_width(const neko_model* m) {
+    switch (m->debug_stage) {
+        case 2: case 3: return m->qwen || m->debug_stage == 2 ? m->QW : m->H * m->hd;
+        case 4: return m->qwen ? m->H * m->hd : m->C;
+        case 6: return m->qwen ? m->C : m->F;
+        case 8: return m->F;
+        default: return m->C;
+    }
 }
 
 int wait_model(neko_model* m) {
@@ -509,8 +546,8 @@ neko_model* neko_model_create(int device, const neko_model_config* cfg, char* er
         return bail(m, "workspace allocation failed");
     int64_t pf = 0, tk = 0;
     attention_scratch(int(R), m->H, m->KV, m->hd, c.context - 1, &pf, &tk);
-    // smaller row counts split more: size for the worst case over 1..R rows
-    for (int r = 1; r <= int(R); r *= 2) {
+    // fewer rows split more: size for the worst case over every row count 1..R
+    for (int r = 1; r <= int(R); r++) {
         int64_t p2 = 0, t2 = 0;
         attention_scratch(r, m->H, m->KV, m->hd, c.context - 1, &p2, &t2);
         pf = std::max(pf, p2);
@@ -632,8 +669,12 @@ static int set_tensor(neko_model* m, const char* cname, const float* data, int64
     if (!mat && !vec) return fail(m, NEKO_ERR_ARG, "set_tensor: unknown tensor " + name);
     if (vec) {
         if (size_t(rows * cols) != vec_n) return fail(m, NEKO_ERR_ARG, "set_tensor: wrong size for " + name);
-        CK(cudaMemcpy(vec, data, vec_n * 4, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice),
+        // Stream-ordered copies only: a pageable cudaMemcpy may return before its DMA lands, and the model's
+        // stream does not order itself after the legacy default stream.
+        CK(cudaMemcpyAsync(vec, data, vec_n * 4, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                           m->stream),
            "upload vector");
+        CK(cudaStreamSynchronize(m->stream), "upload vector");
     } else {
         if (rows != exp_rows || cols != exp_cols)
             return fail(m, NEKO_ERR_ARG, "set_tensor: wrong shape for " + name + " (" + std::to_string(rows) + "x" +
@@ -647,7 +688,7 @@ static int set_tensor(neko_model* m, const char* cname, const float* data, int64
                 CK(cudaMalloc(&m->staging, n * 4), "staging");
                 m->staging_floats = n;
             }
-            CK(cudaMemcpy(m->staging, data, n * 4, cudaMemcpyHostToDevice), "upload matrix");
+            CK(cudaMemcpyAsync(m->staging, data, n * 4, cudaMemcpyHostToDevice, m->stream), "upload matrix");
             src = m->staging;
         }
         // out rows / in cols of the packed matrix
@@ -669,6 +710,8 @@ static int set_tensor_entry(neko_model* m, const char* name, const float* data, 
                             bool on_device) {
     if (!m) return NEKO_ERR_ARG;
     Guard g(m->device);
+    // device data may come from work on another stream (e.g. a framework's generator): let it finish first
+    if (on_device) CK(cudaDeviceSynchronize(), "set_tensor_device");
     return set_tensor(m, name, data, rows, cols, on_device);
 }
 
@@ -710,9 +753,10 @@ int neko_model_forward(neko_model* m, int slot, const int* tokens, int T, int po
     CK(cudaMemcpyAsync(m->d_slots, hi + T, size_t(T) * 4, cudaMemcpyHostToDevice, m->stream), "h2d");
     CK(cudaMemcpyAsync(m->d_pos, hi + 2 * T, size_t(T) * 4, cudaMemcpyHostToDevice, m->stream), "h2d");
     if (int rc = run_step(m, T, 1, true, pos0 + T - 1, false, false, m->stream); rc != NEKO_OK) return rc;
-    CK(cudaMemcpyAsync(m->h_logits, m->logits, size_t(m->V) * 4, cudaMemcpyDeviceToHost, m->stream), "d2h");
+    const size_t nout = m->debug_layers >= 0 ? size_t(T) * size_t(debug_width(m)) : size_t(m->V);
+    CK(cudaMemcpyAsync(m->h_logits, m->logits, nout * 4, cudaMemcpyDeviceToHost, m->stream), "d2h");
     if (int rc = wait_model(m); rc != NEKO_OK) return rc;
-    std::memcpy(logits, m->h_logits, size_t(m->V) * 4);
+    std::memcpy(logits, m->h_logits, nout * 4);
     return NEKO_OK;
 }
 
@@ -759,9 +803,14 @@ int neko_model_stage(neko_model* m, int n, const int* slots, const int* tokens, 
             if (slots[j] == slots[i]) return fail(m, NEKO_ERR_ARG, "stage: a slot appears twice");
     }
     Guard g(m->device);
-    CK(cudaMemcpy(m->d_tokens, tokens, size_t(n) * 4, cudaMemcpyHostToDevice), "stage");
-    CK(cudaMemcpy(m->d_slots, slots, size_t(n) * 4, cudaMemcpyHostToDevice), "stage");
-    CK(cudaMemcpy(m->d_pos, pos, size_t(n) * 4, cudaMemcpyHostToDevice), "stage");
+    CK(cudaDeviceSynchronize(), "stage");  // no step may still be reading the arrays
+    std::memcpy(m->h_in, tokens, size_t(n) * 4);
+    std::memcpy(m->h_in + n, slots, size_t(n) * 4);
+    std::memcpy(m->h_in + 2 * n, pos, size_t(n) * 4);
+    CK(cudaMemcpyAsync(m->d_tokens, m->h_in, size_t(n) * 4, cudaMemcpyHostToDevice, m->stream), "stage");
+    CK(cudaMemcpyAsync(m->d_slots, m->h_in + n, size_t(n) * 4, cudaMemcpyHostToDevice, m->stream), "stage");
+    CK(cudaMemcpyAsync(m->d_pos, m->h_in + 2 * n, size_t(n) * 4, cudaMemcpyHostToDevice, m->stream), "stage");
+    CK(cudaStreamSynchronize(m->stream), "stage");
     return NEKO_OK;
 }
 
@@ -780,8 +829,24 @@ int neko_model_tokens(neko_model* m, int n, int* tokens, int* pos) {
     CK(cudaDeviceSynchronize(), "tokens");
     if (unsigned d = read_device_error(true))
         return fail(m, NEKO_ERR_DEVICE, "kernel reported device error " + std::to_string(d));
-    if (tokens) CK(cudaMemcpy(tokens, m->d_tokens, size_t(n) * 4, cudaMemcpyDeviceToHost), "tokens");
-    if (pos) CK(cudaMemcpy(pos, m->d_pos, size_t(n) * 4, cudaMemcpyDeviceToHost), "tokens");
+    if (tokens) CK(cudaMemcpyAsync(tokens, m->d_tokens, size_t(n) * 4, cudaMemcpyDeviceToHost, m->stream), "tokens");
+    if (pos) CK(cudaMemcpyAsync(pos, m->d_pos, size_t(n) * 4, cudaMemcpyDeviceToHost, m->stream), "tokens");
+    CK(cudaStreamSynchronize(m->stream), "tokens");
+    return NEKO_OK;
+}
+
+int neko_model_set_debug(neko_model* m, int layers, int stage) {
+    if (!m) return NEKO_ERR_ARG;
+    // stages with a buffer of their own in the fused step (the others are fused into a neighbour)
+    static const int qwen_ok[] = {2, 3, 4, 5, 8, 9}, gpt2_ok[] = {2, 3, 4, 6, 7};
+    bool ok = stage == 0;
+    for (int s : m->qwen ? std::vector<int>(qwen_ok, qwen_ok + 6) : std::vector<int>(gpt2_ok, gpt2_ok + 5))
+        ok = ok || s == stage;
+    if (!ok) return fail(m, NEKO_ERR_UNSUPPORTED, "set_debug: stage " + std::to_string(stage) + " is fused away");
+    m->debug_layers = layers;
+    m->debug_stage = layers >= 0 ? stage : 0;
+    if (layers >= 0 && size_t(m->cfg.max_rows) * debug_width(m) > size_t(std::max(m->cfg.max_rows, m->cfg.max_seqs)) * m->V)
+        return fail(m, NEKO_ERR_UNSUPPORTED, "set_debug: the dump does not fit the logits workspace");
     return NEKO_OK;
 }
 

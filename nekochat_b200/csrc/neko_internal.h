@@ -59,6 +59,7 @@ struct GemvArgs {
     // launch plan (filled by plan_gemv)
     int x_smem = 0;
     int rows_per_cta = 0;
+    int stage_rows = 0;          // weight rows per ring stage (<= 8 warps x rows per warp)
     int nstage = 0;
     int64_t stage_stride = 0;
     int xs_off = 0;
@@ -108,6 +109,7 @@ struct QkvPostArgs {
     int slot0 = 0, pos0 = 0;
     int k_off = 0, v_off = 0;        // column offsets of K and V inside a qkv row
     int pos_limit = 0x7fffffff;      // positions >= limit are not stored (device error kErrBadIndex)
+    int write_back_k = 0;            // also write the rotated keys back into qkv (debug dumps)
 };
 cudaError_t launch_qkv_post(const QkvPostArgs& a, cudaStream_t st, bool pdl);
 

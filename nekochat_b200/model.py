@@ -122,6 +122,18 @@ class Model:
         self._check(lib().neko_model_tokens(self.h, n, _p(t), _p(p)), "tokens")
         return t, p
 
+    def set_debug(self, layers, stage=0):
+        """Model::setDebugLayers(n, stage) (model.h:101): forward() then returns the hidden states after n layers
+        (stage 0) or the intermediate after `stage` inside layer n; n < 0 restores logits."""
+        self._check(lib().neko_model_set_debug(self.h, layers, stage), "set_debug")
+
+    def hidden(self, tokens, pos0, slot=0, width=None):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        width = width or self.shape["embd"]
+        out = np.empty(max(self.vocab, len(t) * width), np.float32)
+        self._check(lib().neko_model_forward(self.h, slot, _p(t), len(t), pos0, _p(out)), "forward")
+        return out[:len(t) * width].reshape(len(t), width)
+
     def memory(self):
         w, kv, ws = C.c_int64(), C.c_int64(), C.c_int64()
         self._check(lib().neko_model_memory(self.h, C.byref(w), C.byref(kv), C.byref(ws)), "memory")

@@ -61,6 +61,22 @@ def matmul(fmt, x, q, K, bias=None, y=None, y_stride=None, n_off=0, flags=0):
     return y
 
 
+def matmul_fused(fmt, x, q, K, rows, norm=0, gamma=None, beta=None, eps=1e-6, swiglu=False, bias=None, y=None,
+                 y_stride=None, n_off=0, flags=0):
+    """Norm prologue (0 none, 1 RMSNorm, 2 LayerNorm) + matmul, or the SwiGLU pair (q holds 2 * rows rows)."""
+    import torch
+    T = x.numel() // K
+    y_stride = rows if y_stride is None else y_stride
+    if y is None:
+        y = torch.zeros((T, y_stride), dtype=torch.float32, device=x.device)
+    if bias is not None:
+        flags |= 4
+    check(lib().neko_op_matmul_fused(fmt, _ptr(x), T, K, _ptr(q), rows, norm, _ptr(gamma), _ptr(beta), eps,
+                                     1 if swiglu else 0, _ptr(bias), _ptr(y), y_stride, n_off, flags, _stream()),
+          "matmul_fused")
+    return y
+
+
 def norm(x, gamma, beta=None, eps=1e-6):
     """cpu::rmsNorm (beta None) / cpu::layerNorm over the last dimension."""
     import torch

@@ -60,7 +60,8 @@ class Qwen3(_Base):
                 wdown=self.q(p + "mlp.down_proj.weight"),
                 kc=np.zeros((context, KV * hd), np.uint16), vc=np.zeros((context, KV * hd), np.uint16)))
 
-    def forward(self, tokens, pos0, stop_layer=None):
+    def forward(self, tokens, pos0, stop_layer=None, stage=0):
+        """stop_layer / stage: Model::setDebugLayers semantics (qwen3_model.cpp:237-273)."""
         R, s = self.R, self.s
         C, H, KV, hd, F = s["embd"], s["heads"], s["kv_heads"], s["head_dim"], s["ff"]
         eps = s["eps"]
@@ -69,24 +70,43 @@ class Qwen3(_Base):
         f, q, _ = self.embed
         x = R.embed(f, q, C, tokens)
         for li, L in enumerate(self.layers):
-            if stop_layer is not None and li >= stop_layer:
+            if stop_layer is not None and li >= stop_layer and not (stage and li == stop_layer):
                 return x
+            at = (lambda st: stop_layer is not None and stage == st and li == stop_layer)
             xn = R.rms_norm(x, L["ln1"], eps)
+            if at(1):
+                return xn
             qkv = np.zeros((T, QW), np.float32)
             self.mm(L["wqkv"], xn, T, qkv, QW, 0)
+            if at(2):
+                return qkv
             for t in range(T):
                 r = qkv[t]
                 r[:kOff] = R.rms_norm(r[:kOff].reshape(H, hd), L["qn"], eps).reshape(-1)
                 r[kOff:vOff] = R.rms_norm(r[kOff:vOff].reshape(KV, hd), L["kn"], eps).reshape(-1)
                 R.rope(r, H + KV, hd, self.rope[pos0 + t])
+            if at(3):
+                return qkv
             R.store_kv(qkv[:, kOff:], qkv[:, vOff:], QW, L["kc"], L["vc"], KV * hd, T, pos0)
             att = R.attention(qkv, QW, L["kc"], L["vc"], T, H, KV, hd, pos0)
+            if at(4):
+                return att
             self.mm(L["wo"], att, T, x, C, ACCUMULATE)
+            if at(5):
+                return x
             xn = R.rms_norm(x, L["ln2"], eps)
+            if at(6):
+                return xn
             h = np.zeros((T, 2 * F), np.float32)
             self.mm(L["wgu"], xn, T, h, 2 * F, 0)
+            if at(7):
+                return h
             g = R.silu_mul(h, F)
+            if at(8):
+                return g
             self.mm(L["wdown"], g, T, x, C, ACCUMULATE)
+            if at(9):
+                return x
         if stop_layer is not None:
             return x
         xn = R.rms_norm(x[T - 1:T], self.normf, eps)
@@ -115,7 +135,8 @@ class Gpt2(_Base):
                 wfc2=self.q(p + "mlp.c_proj.weight", transpose_f16=True), bfc2=self.t[p + "mlp.c_proj.bias"],
                 kc=np.zeros((context, C), np.uint16), vc=np.zeros((context, C), np.uint16)))
 
-    def forward(self, tokens, pos0, stop_layer=None):
+    def forward(self, tokens, pos0, stop_layer=None, stage=0):
+        """stop_layer / stage: Model::setDebugLayers semantics (gpt2_model.cpp:188-215)."""
         R, s = self.R, self.s
         C, H = s["embd"], s["heads"]
         hd, F, eps = C // H, s["ff"], s["eps"]
@@ -123,18 +144,33 @@ class Gpt2(_Base):
         f, q, _ = self.wte
         x = R.embed(f, q, C, tokens, self.wpe, pos0)
         for li, L in enumerate(self.layers):
-            if stop_layer is not None and li >= stop_layer:
+            if stop_layer is not None and li >= stop_layer and not (stage and li == stop_layer):
                 return x
+            at = (lambda st: stop_layer is not None and stage == st and li == stop_layer)
             xn = R.layer_norm(x, *L["ln1"], eps)
+            if at(1):
+                return xn
             qkv = np.zeros((T, 3 * C), np.float32)
             self.mm(L["wqkv"], xn, T, qkv, 3 * C, 0, L["bqkv"])
+            if at(2):
+                return qkv
             R.store_kv(qkv[:, C:], qkv[:, 2 * C:], 3 * C, L["kc"], L["vc"], C, T, pos0)
             att = R.attention(qkv, 3 * C, L["kc"], L["vc"], T, H, H, hd, pos0)
+            if at(3):
+                return att
             self.mm(L["wproj"], att, T, x, C, ACCUMULATE, L["bproj"])
+            if at(4):
+                return x
             xn = R.layer_norm(x, *L["ln2"], eps)
+            if at(5):
+                return xn
             h = np.zeros((T, F), np.float32)
             self.mm(L["wfc"], xn, T, h, F, GELU, L["bfc"])
+            if at(6):
+                return h
             self.mm(L["wfc2"], h, T, x, C, ACCUMULATE, L["bfc2"])
+            if at(7):
+                return x
         if stop_layer is not None:
             return x
         xn = R.layer_norm(x[T - 1:T], *self.lnf, eps)
