@@ -132,6 +132,16 @@ int neko_op_softmax(const float* x, float* y, int rows, int C, void* stream);
 /* cpu::attention (cpu_ops.cpp:544-575) over caches in the engine layout [ctx][n_kv * hd] f16. */
 int neko_op_attention(const float* q, int q_stride, const uint16_t* k_cache, const uint16_t* v_cache, float* out,
                       int T, int n_head, int n_kv, int hd, int pos0, void* stream);
+/* neko_op_attention without any device allocation; it has no counterpart in the reference. For callers that
+ * cannot let a library allocate device memory behind their back: engines that budget and report every byte
+ * they hold (the engine's MemoryStats), callers that must not risk an out-of-memory failure in the middle of a
+ * reply, and hosts that forbid allocator calls once decoding has started. The split-KV scratch is a fixed array
+ * inside the library (4 MiB of partial state + 8192 tickets, held on every GPU that loads the library until
+ * the process exits); shapes that need more are rejected with NEKO_ERR_UNSUPPORTED. All calls share that
+ * array, so calls that can overlap on the GPU race: keep them on one stream. The first call on each device
+ * looks up the array's address with that device current; make it before any stream capture. */
+int neko_op_attention_noalloc(const float* q, int q_stride, const uint16_t* k_cache, const uint16_t* v_cache,
+                              float* out, int T, int n_head, int n_kv, int hd, int pos0, void* stream);
 /* Index of the first maximum of each row (std::max_element in Sampler::sample, sampler.cpp:24). */
 int neko_op_argmax(const float* x, int rows, int C, int* out, void* stream);
 

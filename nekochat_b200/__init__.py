@@ -91,6 +91,8 @@ _SIGS = {
     "neko_op_softmax": (C.c_int, [_vp, _vp, C.c_int, C.c_int, _vp]),
     "neko_op_attention": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
     "neko_op_argmax": (C.c_int, [_vp, C.c_int, C.c_int, _vp, _vp]),
+    "neko_op_attention_noalloc": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                            _vp]),
     "neko_model_create": (_vp, [C.c_int, C.POINTER(ModelConfig), C.c_char_p, C.c_size_t]),
     "neko_model_destroy": (None, [_vp]),
     "neko_model_last_error": (C.c_char_p, [_vp]),

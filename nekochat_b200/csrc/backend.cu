@@ -60,6 +60,12 @@ namespace {
 
 thread_local std::string t_err;
 
+}  // namespace
+
+void neko::set_last_error(const std::string& msg) { t_err = msg; }
+
+namespace {
+
 int set_err(std::string* dst, int code, const std::string& msg) {
     if (dst) *dst = msg;
     t_err = msg;

@@ -142,6 +142,7 @@ void attention_scratch(int rows, int n_head, int n_kv, int hd, int max_pos, int6
 
 // ------------------------------------------------------------------ errors
 std::string cuda_msg(cudaError_t e, const char* what);
+void set_last_error(const std::string& msg);  // the thread-local message behind neko_last_error()
 unsigned read_device_error(bool clear);
 
 }  // namespace neko
