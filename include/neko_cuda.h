@@ -120,7 +120,8 @@ int neko_op_matmul(int format, const float* x, int T, int K, const uint8_t* W, i
 /* The fused forms the decode step uses, as one operator: norm (0 none, 1 RMSNorm, 2 LayerNorm with gamma/beta,
  * eps) applied to the x rows before the product (the engine's LayerNorm dispatch + Matmul, qwen3_model.cpp:309-311),
  * and swiglu != 0 for a [gate | up] weight of 2 * rows rows whose output is silu(x . gate[n]) * (x . up[n])
- * (Matmul + SiluMul, qwen3_model.cpp:323-325). The norm needs T * K * 4 <= 40 KB. */
+ * (Matmul + SiluMul, qwen3_model.cpp:323-325). The norm needs T * K <= 4096, K % 128 == 0 and
+ * T * Kp * 4 <= 40 KB, Kp = K rounded up to 256 (F16), 512 (FP8) or 1024 (FP4) weights. */
 int neko_op_matmul_fused(int format, const float* x, int T, int K, const uint8_t* W, int rows, int norm,
                          const float* gamma, const float* beta, float eps, int swiglu, const float* bias, float* y,
                          int y_stride, int n_off, int flags, void* stream);

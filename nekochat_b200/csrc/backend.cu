@@ -455,7 +455,10 @@ int neko_op_matmul_fused(int format, const float* x, int T, int K, const uint8_t
         return set_err(nullptr, NEKO_ERR_ARG, "matmul_fused args");
     if ((format == kF16 ? K % 8 : K % 32) != 0) return set_err(nullptr, NEKO_ERR_ARG, "matmul K alignment");
     if (norm && (!gamma || (norm == kNormLayer && !beta))) return set_err(nullptr, NEKO_ERR_ARG, "norm weights");
-    if (norm && int64_t(T) * K * 4 > kGemvXSmemMax) return set_err(nullptr, NEKO_ERR_ARG, "norm prologue too large");
+    if (norm && !gemv_norm_fusable(format, T, K))
+        return set_err(nullptr, NEKO_ERR_ARG,
+                       "norm prologue needs T * K <= 4096, K % 128 == 0 and T * K padded to 512-byte code "
+                       "segments within 40 KB of activations");
     if ((flags & kBias) && !bias) return set_err(nullptr, NEKO_ERR_ARG, "matmul bias flag without bias");
     GemvArgs a;
     a.W = W;

@@ -3,21 +3,25 @@
 // cpu::matmul (cpu_ops.cpp:462-481), written for sm_100a.
 //
 // Shape of the work: y[m][n] = sum_k x[m][k] * deq(W[n])[k] for M <= a few rows (decode) and N up to 152K rows
-// of K <= 10K weights. Every weight byte is read once per step, so the kernel is bound by HBM bandwidth.
+// of K <= 10K weights. Every weight byte is read once per step, so the kernel is bound by HBM bandwidth and, for
+// the small per-layer matrices of a decode step, by latency.
 //
 // Design
 //  * Persistent CTAs, one contiguous range of weight rows each (rows are self-contained, quant.h:34-36).
-//  * A producer warp streams the range into a ring of shared-memory stages with cp.async.bulk (the TMA
-//    engine, no registers or LSU involved), each stage completing on an mbarrier; 8 consumer warps compute.
-//  * Programmatic dependent launch: the producer issues its first stages BEFORE griddepcontrol.wait, so the
-//    next kernel's weights stream in while the previous kernel (attention, another GEMV) is still running.
-//    Only activations depend on the predecessor; consumers wait for it before staging x.
-//  * Activations are staged once per CTA in shared memory, optionally normalised on the way (RMSNorm or
-//    LayerNorm prologue: the norm of the reference's preceding LayerNorm dispatch is fused here).
-//  * Consumers: warp w owns R consecutive rows of each stage; lane l reads 4 code bytes per 128-byte segment
-//    (conflict-free), decodes them in registers with the engine's own bit layout (exact), multiplies with
-//    fp32 activations and applies the f16 block scale per 32 weights; fp32 warp-shuffle reduction per row.
-//  * Fused epilogues: bias, GELU, residual accumulate, and the SwiGLU pair (gate row n with up row n + F).
+//  * A producer warp streams the range into a ring of shared-memory stages with cp.async.bulk (the TMA engine),
+//    in chunks of at most 4 KB issued by all its lanes, each stage completing on an mbarrier; 8 consumer warps
+//    compute. With programmatic dependent launch the producer issues its first stages BEFORE
+//    griddepcontrol.wait, so the weights stream in while the previous kernel is still running; only the
+//    activations depend on the predecessor.
+//  * Activations are staged once per CTA by all consumer threads into a permuted shared-memory layout in which
+//    each lane's 16-weight slice reads its activations as bank-conflict-free float4s; an RMSNorm / LayerNorm
+//    prologue (the engine's preceding LayerNorm dispatch) is applied on the way.
+//  * Consumers: a row is walked in 512-byte segments; lane l takes bytes [16 l, 16 l + 16) of each segment with
+//    one 128-bit shared load (16 FP8 codes, one 32-weight FP4 block, or 8 halves), decodes them in registers
+//    with the engine's own bit layout (exact), multiplies with fp32 activations in two independent chains,
+//    applies the f16 block scale and reduces each row with warp shuffles.
+//  * Fused epilogues: bias, GELU, residual accumulate, the SwiGLU pair (gate row n with up row n + F), and a
+//    greedy argmax (max of (value, ~index) keys) for the LM head.
 #include "neko_common.cuh"
 #include "neko_internal.h"
 
@@ -27,186 +31,259 @@ namespace {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMaxArgmaxRows = 64;
+constexpr int kMaxStageVec = 10;  // float4 activations staged per consumer thread (40 KB / 256 threads)
+constexpr int kStageRound = 6;    // float4 loads a thread keeps in flight while staging
+constexpr int kMaxNormVec = 4;    // float4 per thread when a norm prologue is fused (M * K <= 4096)
+constexpr int kSegBytes = 512;  // bytes of one row segment (16 per lane)
+constexpr int kChunkBytes = 4096;
 
-// Physical float index of logical activation k in the staged x row. FP4 reads x in two 4-float groups 16 apart
-// per lane; flipping bit 4 for odd 32-blocks keeps those reads bank-conflict free.
+// Weights per segment and float4s of activations per lane per segment, by format.
+template <int FMT> struct Seg;
+template <> struct Seg<kFP8> { static constexpr int W = 512, Q = 4; };
+template <> struct Seg<kFP4> { static constexpr int W = 1024, Q = 8; };
+template <> struct Seg<kF16> { static constexpr int W = 256, Q = 2; };
+
+__host__ __device__ inline int code_bytes(int fmt, int K) { return fmt == kFP8 ? K : fmt == kFP4 ? K / 2 : 2 * K; }
+__host__ __device__ inline int seg_count(int fmt, int K) { return (code_bytes(fmt, K) + kSegBytes - 1) / kSegBytes; }
+
+// Staged-activation index (in floats) of logical activation k: segment s, lane l, float4 q, element e.
 template <int FMT>
-__device__ __forceinline__ int xphys(int k) {
-    return FMT == kFP4 ? (k ^ (((k >> 5) & 1) << 4)) : k;
+__device__ __forceinline__ int xperm(int k) {
+    constexpr int W = Seg<FMT>::W, Q = Seg<FMT>::Q, WL = W / 32;
+    const int s = k / W, r = k % W, l = r / WL, t = r % WL;
+    return (((s * Q + t / 4) * 32 + l) << 2) + (t & 3);
 }
 
-struct XSrc {
-    const float* base;  // smem (staged) or global
-    int64_t stride;     // floats between rows
-    bool smem;
-};
-
-template <int FMT>
-__device__ __forceinline__ float4 load_x4(const XSrc& xs, int m, int k) {
-    const float* p = xs.base + int64_t(m) * xs.stride + (xs.smem ? xphys<FMT>(k) : k);
-    return *reinterpret_cast<const float4*>(p);
+// Greedy argmax key: the float's order-preserving bit pattern in the high word, the complement of the index in
+// the low word, so the largest key is the largest value with the smallest index (std::max_element).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
+    const unsigned b = __float_as_uint(v);
+    const unsigned ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return (static_cast<unsigned long long>(ord) << 32) | static_cast<unsigned>(0xFFFFFFFFu - unsigned(n));
 }
 
-// Stages activation rows [0, M) into shared memory, applying the norm prologue.
-// RMSNorm: y = x * rsqrt(mean(x^2) + eps) * gamma; LayerNorm: (x - mean) * rstd * gamma + beta
-// (cpu_ops.cpp:483-511: sums accumulated in double like the CPU reference).
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+}
+
+// Stages activation rows [0, M) into the permuted layout (zero-padded to whole segments), applying the norm
+// prologue: RMSNorm y = x * rsqrt(mean(x^2) + eps) * gamma, LayerNorm (x - mean) * rstd * gamma + beta
+// (cpu_ops.cpp:483-511; sums in double like the CPU reference, the LayerNorm variance as E[x^2] - mean^2 in
+// double). All activation (and gamma / beta) loads of a thread are issued before any is used, so staging costs
+// one L2 round trip; the row sums go through per-warp partials in shared memory in a fixed order.
 template <int FMT>
-__device__ void stage_x(const GemvArgs& a, float* xs, int warp, int lane) {
-    for (int m = warp; m < a.M; m += kConsumerWarps) {
-        const float* src = a.x + int64_t(m) * a.x_stride;
-        float* dst = xs + int64_t(m) * a.K;
-        double s1 = 0.0, s2 = 0.0;
-        for (int k = lane * 4; k < a.K; k += 128) {
-            float4 v = *reinterpret_cast<const float4*>(src + k);
-            *reinterpret_cast<float4*>(dst + xphys<FMT>(k)) = v;
-            s1 += double(v.x) + double(v.y) + double(v.z) + double(v.w);
-            s2 += double(v.x) * v.x + double(v.y) * v.y + double(v.z) * v.z + double(v.w) * v.w;
+__device__ void stage_x(const GemvArgs& a, float* xs, double* part, int tid, int warp, int lane) {
+    constexpr int NT = kConsumerWarps * 32;
+    const int K4 = a.K / 4, total = a.M * K4, padded = seg_count(FMT, a.K) * Seg<FMT>::W;
+    const bool norm = a.norm != kNormNone;
+    for (int m = 0; m < a.M; m++) {
+        float* row = xs + m * padded;
+        for (int k = a.K + tid; k < padded; k += NT) row[xperm<FMT>(k)] = 0.0f;
+    }
+    if (!norm) {
+        // rounds of kStageRound float4 per thread: all loads of a round are in flight together
+        for (int base = 0; base < total; base += kStageRound * NT) {
+            float4 v[kStageRound];
+#pragma unroll
+            for (int j = 0; j < kStageRound; j++) {
+                const int i = base + tid + j * NT;
+                if (i < total) v[j] = *reinterpret_cast<const float4*>(a.x + int64_t(i / K4) * a.x_stride + 4 * (i % K4));
+            }
+#pragma unroll
+            for (int j = 0; j < kStageRound; j++) {
+                const int i = base + tid + j * NT;
+                if (i < total) *reinterpret_cast<float4*>(xs + (i / K4) * padded + xperm<FMT>(4 * (i % K4))) = v[j];
+            }
         }
-        if (a.norm == kNormNone) continue;
+        consumer_sync();
+        return;
+    }
+    float4 v[kMaxNormVec], g[kMaxNormVec], b[kMaxNormVec];
+#pragma unroll
+    for (int j = 0; j < kMaxNormVec; j++) {
+        const int i = tid + j * NT;
+        if (i < total) v[j] = *reinterpret_cast<const float4*>(a.x + int64_t(i / K4) * a.x_stride + 4 * (i % K4));
+    }
+    // norm: at most kMaxNormVec float4 per thread and K % 128 == 0 (a warp's 32 float4 lie in one row)
+#pragma unroll
+    for (int j = 0; j < kMaxNormVec; j++) {
+        const int i = tid + j * NT;
+        if (i < total) {
+            g[j] = __ldg(reinterpret_cast<const float4*>(a.gamma + 4 * (i % K4)));
+            if (a.norm == kNormLayer) b[j] = __ldg(reinterpret_cast<const float4*>(a.beta + 4 * (i % K4)));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxNormVec; j++) {
+        const int i = tid + j * NT;
+        double s1 = 0.0, s2 = 0.0;
+        if (i < total) {
+            s1 = double(v[j].x) + double(v[j].y) + double(v[j].z) + double(v[j].w);
+            s2 = double(v[j].x) * v[j].x + double(v[j].y) * v[j].y + double(v[j].z) * v[j].z + double(v[j].w) * v[j].w;
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             s1 += __shfl_xor_sync(0xffffffffu, s1, o);
             s2 += __shfl_xor_sync(0xffffffffu, s2, o);
         }
+        if (lane == 0) {
+            part[2 * (j * kConsumerWarps + warp)] = s1;
+            part[2 * (j * kConsumerWarps + warp) + 1] = s2;
+        }
+    }
+    consumer_sync();
+#pragma unroll
+    for (int j = 0; j < kMaxNormVec; j++) {
+        const int i = tid + j * NT;
+        if (i >= total) continue;
+        const int m = i / K4;
+        double s1 = 0.0, s2 = 0.0;  // the row's partials, in a fixed order: slots (j', w') whose float4s are in row m
+        for (int jj = 0; jj < kMaxNormVec; jj++)
+            for (int w = 0; w < kConsumerWarps; w++) {
+                const int i0 = jj * NT + w * 32;
+                if (i0 < total && i0 / K4 == m) {
+                    s1 += part[2 * (jj * kConsumerWarps + w)];
+                    s2 += part[2 * (jj * kConsumerWarps + w) + 1];
+                }
+            }
         float r, mean = 0.0f;
         if (a.norm == kNormRms) {
             r = float(1.0 / sqrt(s2 / a.K + double(a.eps)));
         } else {
             const double mu = s1 / a.K;
-            double var = 0.0;
-            __syncwarp();
-            for (int k = lane * 4; k < a.K; k += 128) {
-                float4 v = *reinterpret_cast<const float4*>(dst + xphys<FMT>(k));
-                double d0 = v.x - mu, d1 = v.y - mu, d2 = v.z - mu, d3 = v.w - mu;
-                var += d0 * d0 + d1 * d1 + d2 * d2 + d3 * d3;
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
-            r = float(1.0 / sqrt(var / a.K + double(a.eps)));
+            r = float(1.0 / sqrt(s2 / a.K - mu * mu + double(a.eps)));
             mean = float(mu);
         }
-        __syncwarp();
-        for (int k = lane * 4; k < a.K; k += 128) {
-            float4* p = reinterpret_cast<float4*>(dst + xphys<FMT>(k));
-            float4 v = *p;
-            float4 g = *reinterpret_cast<const float4*>(a.gamma + k);
-            if (a.norm == kNormRms) {
-                v.x = __fmul_rn(__fmul_rn(v.x, r), g.x);
-                v.y = __fmul_rn(__fmul_rn(v.y, r), g.y);
-                v.z = __fmul_rn(__fmul_rn(v.z, r), g.z);
-                v.w = __fmul_rn(__fmul_rn(v.w, r), g.w);
-            } else {
-                float4 b = *reinterpret_cast<const float4*>(a.beta + k);
-                v.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, mean), r), g.x), b.x);
-                v.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, mean), r), g.y), b.y);
-                v.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, mean), r), g.z), b.z);
-                v.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, mean), r), g.w), b.w);
+        float4 y = v[j];
+        if (a.norm == kNormRms) {
+            y.x = __fmul_rn(__fmul_rn(y.x, r), g[j].x);
+            y.y = __fmul_rn(__fmul_rn(y.y, r), g[j].y);
+            y.z = __fmul_rn(__fmul_rn(y.z, r), g[j].z);
+            y.w = __fmul_rn(__fmul_rn(y.w, r), g[j].w);
+        } else {
+            y.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.x, mean), r), g[j].x), b[j].x);
+            y.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.y, mean), r), g[j].y), b[j].y);
+            y.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.z, mean), r), g[j].z), b[j].z);
+            y.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.w, mean), r), g[j].w), b[j].w);
+        }
+        *reinterpret_cast<float4*>(xs + m * padded + xperm<FMT>(4 * (i % K4))) = y;
+    }
+    consumer_sync();
+}
+
+// dot of 4 fp32 activations with 4 weights (even = weights 0, 2; odd = weights 1, 3)
+__device__ __forceinline__ float dot4(const float4 x, const float2 e, const float2 o, float p) {
+    p = fmaf(x.x, e.x, p);
+    p = fmaf(x.y, o.x, p);
+    p = fmaf(x.z, e.y, p);
+    return fmaf(x.w, o.y, p);
+}
+
+// One lane's 16 weight bytes of one row (segment s) against MT activation rows; accumulates into acc[m].
+template <int FMT, int MT>
+__device__ __forceinline__ void seg_dot(const uint8_t* row, int cbytes, int s, int lane,
+                                        const float4 (&xv)[MT][Seg<FMT>::Q], float (&acc)[MT]) {
+    const uint4 w = *reinterpret_cast<const uint4*>(row + s * kSegBytes + 16 * lane);
+    const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+    if (FMT == kFP8) {
+        const float sc =
+            half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + cbytes + 2 * (16 * s + (lane >> 1))));
+        float2 e[4], o[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            __half2 he, ho;
+            fp8x4_to_half2(wd[i], he, ho);
+            e[i] = __half22float2(he);
+            o[i] = __half22float2(ho);
+        }
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            float p0 = dot4(xv[m][0], e[0], o[0], 0.0f);
+            float p1 = dot4(xv[m][1], e[1], o[1], 0.0f);
+            p0 = dot4(xv[m][2], e[2], o[2], p0);
+            p1 = dot4(xv[m][3], e[3], o[3], p1);
+            acc[m] = fmaf(sc, p0 + p1, acc[m]);
+        }
+    } else if (FMT == kFP4) {
+        const float sc = half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + cbytes + 2 * (32 * s + lane)));
+        float2 le[4], lo[4], he[4], ho[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            le[i] = __half22float2(fp4x2_to_half2(wd[i] & 0x000F000Fu));
+            lo[i] = __half22float2(fp4x2_to_half2((wd[i] >> 8) & 0x000F000Fu));
+            he[i] = __half22float2(fp4x2_to_half2((wd[i] >> 4) & 0x000F000Fu));
+            ho[i] = __half22float2(fp4x2_to_half2((wd[i] >> 12) & 0x000F000Fu));
+        }
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            float p0 = 0.0f, p1 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                p0 = dot4(xv[m][i], le[i], lo[i], p0);      // weights 4i .. 4i+3 (low nibbles)
+                p1 = dot4(xv[m][4 + i], he[i], ho[i], p1);  // weights 16+4i .. (high nibbles)
             }
-            *p = v;
+            acc[m] = fmaf(sc, p0 + p1, acc[m]);
+        }
+    } else {
+        float2 h[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) h[i] = __half22float2(*reinterpret_cast<const __half2*>(&wd[i]));
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            float p0 = xv[m][0].x * h[0].x;
+            p0 = fmaf(xv[m][0].y, h[0].y, p0);
+            p0 = fmaf(xv[m][0].z, h[1].x, p0);
+            p0 = fmaf(xv[m][0].w, h[1].y, p0);
+            float p1 = xv[m][1].x * h[2].x;
+            p1 = fmaf(xv[m][1].y, h[2].y, p1);
+            p1 = fmaf(xv[m][1].z, h[3].x, p1);
+            p1 = fmaf(xv[m][1].w, h[3].y, p1);
+            acc[m] += p0 + p1;
         }
     }
 }
 
-// Partial dot product of one lane's slice of one row with MT activation rows.
-// FP8: 4 codes at byte k0 (weights k0..k0+3) of block k0/32.
-template <int MT>
-__device__ __forceinline__ void dot_fp8(const uint8_t* row, int K, int k0, const float4 (&xv)[MT], float (&acc)[MT]) {
-    const uint32_t q = *reinterpret_cast<const uint32_t*>(row + k0);
-    const float s = half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + K + 2 * (k0 >> 5)));
-    __half2 e, o;
-    fp8x4_to_half2(q, e, o);
-    const float2 fe = __half22float2(e), fo = __half22float2(o);
-#pragma unroll
-    for (int m = 0; m < MT; m++) {
-        float p = xv[m].x * fe.x;
-        p = fmaf(xv[m].y, fo.x, p);
-        p = fmaf(xv[m].z, fe.y, p);
-        p = fmaf(xv[m].w, fo.y, p);
-        acc[m] = fmaf(s, p, acc[m]);
-    }
-}
-
-// FP4: 4 code bytes at byte b0 of the row's code area; byte j of block blk holds weight j (low nibble) and
-// weight 16 + j (high nibble). xl/xh are activations 32*blk + j0 .. +3 and 32*blk + 16 + j0 .. +3.
-template <int MT>
-__device__ __forceinline__ void dot_fp4(const uint8_t* row, int K, int b0, const float4 (&xl)[MT],
-                                        const float4 (&xh)[MT], float (&acc)[MT]) {
-    const uint32_t q = *reinterpret_cast<const uint32_t*>(row + b0);
-    const float s = half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + (K >> 1) + 2 * (b0 >> 4)));
-    const float2 le = __half22float2(fp4x2_to_half2(q & 0x000F000Fu));
-    const float2 lo = __half22float2(fp4x2_to_half2((q >> 8) & 0x000F000Fu));
-    const float2 he = __half22float2(fp4x2_to_half2((q >> 4) & 0x000F000Fu));
-    const float2 ho = __half22float2(fp4x2_to_half2((q >> 12) & 0x000F000Fu));
-#pragma unroll
-    for (int m = 0; m < MT; m++) {
-        float p = xl[m].x * le.x;
-        p = fmaf(xl[m].y, lo.x, p);
-        p = fmaf(xl[m].z, le.y, p);
-        p = fmaf(xl[m].w, lo.y, p);
-        p = fmaf(xh[m].x, he.x, p);
-        p = fmaf(xh[m].y, ho.x, p);
-        p = fmaf(xh[m].z, he.y, p);
-        p = fmaf(xh[m].w, ho.y, p);
-        acc[m] = fmaf(s, p, acc[m]);
-    }
-}
-
-// F16: 4 halves at element k0.
-template <int MT>
-__device__ __forceinline__ void dot_f16(const uint8_t* row, int k0, const float4 (&xv)[MT], float (&acc)[MT]) {
-    const uint2 q = *reinterpret_cast<const uint2*>(row + 2 * k0);
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&q.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&q.y));
-#pragma unroll
-    for (int m = 0; m < MT; m++) {
-        acc[m] = fmaf(xv[m].x, a.x, acc[m]);
-        acc[m] = fmaf(xv[m].y, a.y, acc[m]);
-        acc[m] = fmaf(xv[m].z, b.x, acc[m]);
-        acc[m] = fmaf(xv[m].w, b.y, acc[m]);
-    }
-}
-
-// Accumulates R rows (row stride rb inside the stage) x MT activation rows over the full K of the rows.
+// Accumulates nr (<= R) rows (row stride rb inside the stage) x MT activation rows over the full K.
 template <int FMT, int R, int MT>
-__device__ __forceinline__ void row_block(const uint8_t* rows0, int64_t rb, int nr, int K, const XSrc& xs, int m0,
-                                          int M, int lane, float (&acc)[R][MT]) {
+__device__ __forceinline__ void row_block(const uint8_t* rows0, int64_t rb, int nr, const GemvArgs& a,
+                                          const float* xs, int m0, int lane, float (&acc)[R][MT]) {
+    constexpr int Q = Seg<FMT>::Q, W = Seg<FMT>::W;
+    const int cbytes = code_bytes(FMT, a.K), nseg = seg_count(FMT, a.K);
 #pragma unroll
     for (int r = 0; r < R; r++)
 #pragma unroll
         for (int m = 0; m < MT; m++) acc[r][m] = 0.0f;
-    if (FMT == kFP4) {
-        for (int b0 = lane * 4; b0 < (K >> 1); b0 += 128) {
-            const int blk = b0 >> 4, j0 = b0 & 15;
-            float4 xl[MT], xh[MT];
+    for (int s = 0; s < nseg; s++) {
+        if (s * kSegBytes + 16 * lane >= cbytes) continue;  // lanes past the end of a partial last segment
+        float4 xv[MT][Q];
 #pragma unroll
-            for (int m = 0; m < MT; m++) {
-                const bool ok = m0 + m < M;
-                xl[m] = ok ? load_x4<FMT>(xs, m0 + m, 32 * blk + j0) : make_float4(0, 0, 0, 0);
-                xh[m] = ok ? load_x4<FMT>(xs, m0 + m, 32 * blk + 16 + j0) : make_float4(0, 0, 0, 0);
-            }
+        for (int m = 0; m < MT; m++) {
 #pragma unroll
-            for (int r = 0; r < R; r++)
-                if (r < nr) dot_fp4<MT>(rows0 + r * rb, K, b0, xl, xh, acc[r]);
-        }
-    } else {
-        for (int k0 = lane * 4; k0 < K; k0 += 128) {
-            float4 xv[MT];
-#pragma unroll
-            for (int m = 0; m < MT; m++)
-                xv[m] = m0 + m < M ? load_x4<FMT>(xs, m0 + m, k0) : make_float4(0, 0, 0, 0);
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                if (r >= nr) continue;
-                if (FMT == kFP8) dot_fp8<MT>(rows0 + r * rb, K, k0, xv, acc[r]);
-                else dot_f16<MT>(rows0 + r * rb, k0, xv, acc[r]);
+            for (int q = 0; q < Q; q++) {
+                if (m0 + m >= a.M) {
+                    xv[m][q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                } else if (xs) {  // permuted staging: float4 index ((s * Q + q) * 32 + lane) of row m
+                    xv[m][q] =
+                        reinterpret_cast<const float4*>(xs)[(m0 + m) * (nseg * Q * 32) + (s * Q + q) * 32 + lane];
+                } else {  // activations read straight from global memory
+                    const int k = s * W + lane * (W / 32) + 4 * q;
+                    xv[m][q] = k < a.K ? __ldg(reinterpret_cast<const float4*>(a.x + int64_t(m0 + m) * a.x_stride + k))
+                                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
             }
         }
+#pragma unroll
+        for (int r = 0; r < R; r++)
+            if (r < nr) seg_dot<FMT, MT>(rows0 + r * rb, cbytes, s, lane, xv, acc[r]);
     }
 }
 
 template <int FMT, int R, int MT>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ unsigned long long skey[kMaxArgmaxRows];  // fused greedy argmax: this CTA's best key per row
+    __shared__ double part[2 * kMaxNormVec * kConsumerWarps];  // norm prologue: per-warp partial sums
     constexpr float kFactor = FMT == kFP8 ? kFp8Factor : FMT == kFP4 ? kFp4Factor : 1.0f;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + a.nstage;
@@ -229,38 +306,36 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
         }
         fence_barrier_init();
     }
+    if (threadIdx.x < kMaxArgmaxRows) skey[threadIdx.x] = 0;
     __syncthreads();
 
     if (warp == kConsumerWarps) {
-        // ---------------- producer: weights only, so it never waits for the previous kernel
-        if (lane == 0) {
-            for (int st = 0; st < nst; st++) {
-                const int slot = st % a.nstage;
-                if (st >= a.nstage && !mbar_wait(&empty[slot], ((st / a.nstage) - 1) & 1)) break;
-                const int row = r0 + st * SR;
-                const int n = min(SR, r1 - row);
-                const uint32_t bytes = uint32_t(n * a.row_bytes);
-                uint8_t* dst = ring + slot * a.stage_stride;
-                mbar_arrive_expect_tx(&full[slot], paired ? 2 * bytes : bytes);
-                bulk_g2s(dst, a.W + int64_t(row) * a.row_bytes, bytes, &full[slot]);
-                if (paired)
-                    bulk_g2s(dst + SR * a.row_bytes, a.W + (int64_t(row) + a.pair_off) * a.row_bytes, bytes,
-                             &full[slot]);
+        // ---------------- producer warp: weights only, so it never waits for the previous kernel
+        for (int st = 0; st < nst; st++) {
+            const int slot = st % a.nstage;
+            int ok = 1;
+            if (st >= a.nstage && lane == 0) ok = mbar_wait(&empty[slot], ((st / a.nstage) - 1) & 1);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            const int row = r0 + st * SR;
+            const int n = min(SR, r1 - row);
+            const uint32_t bytes = uint32_t(n * a.row_bytes);
+            uint8_t* dst = ring + slot * a.stage_stride;
+            if (lane == 0) mbar_arrive_expect_tx(&full[slot], paired ? 2 * bytes : bytes);
+            __syncwarp();
+            const int nchunk = int((bytes + kChunkBytes - 1) / kChunkBytes);
+            for (int c = lane; c < (paired ? 2 : 1) * nchunk; c += 32) {
+                const int half = c / nchunk, cc = c % nchunk;
+                const uint32_t off = uint32_t(cc) * kChunkBytes, sz = min(uint32_t(kChunkBytes), bytes - off);
+                const uint8_t* src = a.W + (int64_t(row) + (half ? a.pair_off : 0)) * a.row_bytes + off;
+                bulk_g2s(dst + (half ? SR * a.row_bytes : 0) + off, src, sz, &full[slot]);
             }
         }
         return;
     }
 
-    // ---------------- consumers
+    // ---------------- consumers: activations depend on the previous kernel
     pdl_wait();
-    XSrc src;
-    if (a.x_smem) {
-        stage_x<FMT>(a, xs, warp, lane);
-        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-        src = XSrc{xs, a.K, true};
-    } else {
-        src = XSrc{a.x, a.x_stride, false};
-    }
+    if (a.x_smem) stage_x<FMT>(a, xs, part, threadIdx.x, warp, lane);
 
     for (int st = 0; st < nst; st++) {
         const int slot = st % a.nstage;
@@ -273,10 +348,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
             const uint8_t* stage = ring + slot * a.stage_stride + my0 * a.row_bytes;
             for (int m0 = 0; m0 < a.M; m0 += MT) {
                 float acc[R][MT];
-                row_block<FMT, R, MT>(stage, a.row_bytes, nr, a.K, src, m0, a.M, lane, acc);
+                row_block<FMT, R, MT>(stage, a.row_bytes, nr, a, a.x_smem ? xs : nullptr, m0, lane, acc);
                 float accu[R][MT];
-                if (paired) row_block<FMT, R, MT>(stage + SR * a.row_bytes, a.row_bytes, nr, a.K, src, m0, a.M, lane,
-                                                  accu);
+                if (paired)
+                    row_block<FMT, R, MT>(stage + SR * a.row_bytes, a.row_bytes, nr, a, a.x_smem ? xs : nullptr, m0,
+                                          lane, accu);
 #pragma unroll
                 for (int r = 0; r < R; r++) {
 #pragma unroll
@@ -296,12 +372,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
                             if (a.flags & kAccumulate) v += *dst;
                         }
                         *dst = v;
+                        if (a.argmax) atomicMax(&skey[m0 + m], argmax_key(v, n));
                     }
                 }
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if (a.argmax) {  // one global atomic per CTA and activation row
+        consumer_sync();
+        if (threadIdx.x < a.M) atomicMax(a.argmax + threadIdx.x, skey[threadIdx.x]);
     }
 }
 
@@ -311,9 +392,10 @@ template <int FMT>
 KernelFn pick_mt(int R, int MT) {
 #define NEKO_PICK(RR, MM) \
     if (R == RR && MT == MM) return &gemv_kernel<FMT, RR, MM>;
-    NEKO_PICK(1, 1) NEKO_PICK(1, 2) NEKO_PICK(1, 4)
-    NEKO_PICK(2, 1) NEKO_PICK(2, 2) NEKO_PICK(2, 4)
-    NEKO_PICK(4, 1) NEKO_PICK(4, 2) NEKO_PICK(4, 4)
+    NEKO_PICK(1, 1) NEKO_PICK(1, 2) NEKO_PICK(2, 1) NEKO_PICK(2, 2) NEKO_PICK(4, 1)
+    if constexpr (FMT != kFP4) {  // FP4 tiles of 4 activation rows do not fit the register budget
+        NEKO_PICK(1, 4)
+    }
 #undef NEKO_PICK
     return nullptr;
 }
@@ -331,8 +413,9 @@ cudaError_t ensure_smem_attr() {
     for (int f : {kF16, kFP8, kFP4})
         for (int R : {1, 2, 4})
             for (int MT : {1, 2, 4}) {
-                cudaError_t e = cudaFuncSetAttribute(pick(f, R, MT), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                     kGemvSmemBudget);
+                KernelFn k = pick(f, R, MT);
+                if (!k) continue;
+                cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemBudget);
                 if (e != cudaSuccess) return e;
             }
     if (dev < 31) done_mask |= 1 << dev;
@@ -354,12 +437,18 @@ cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, bool pdl, int max_ctas) {
     a.rows_per_cta = (a.rows + ctas - 1) / ctas;
     ctas = (a.rows + a.rows_per_cta - 1) / a.rows_per_cta;
 
-    // Activations staged in shared memory when they fit (required for the norm prologue).
-    const int64_t x_bytes = int64_t(a.M) * a.K * 4;
-    a.x_smem = (x_bytes <= kGemvXSmemMax) ? 1 : 0;
-    if (!a.x_smem && a.norm != kNormNone) return cudaErrorInvalidValue;
-    if (!a.x_smem && (a.x_stride % 4 != 0 || (reinterpret_cast<uintptr_t>(a.x) & 15) != 0))
+    // Activations staged in shared memory (permuted, padded to whole segments) when they fit; the norm prologue
+    // needs them there.
+    static_assert(kGemvNormMaxElems == 4 * kConsumerWarps * 32 * kMaxNormVec, "norm prologue register budget");
+    const int64_t x_bytes = gemv_x_bytes(a.fmt, a.M, a.K);
+    a.x_smem = (x_bytes <= kGemvXSmemMax && int64_t(a.M) * a.K <= 4 * kConsumerWarps * 32 * kMaxStageVec) ? 1 : 0;
+    if (a.norm != kNormNone && !gemv_norm_fusable(a.fmt, a.M, a.K)) return cudaErrorInvalidValue;
+    if (a.x_stride % 4 != 0 || (reinterpret_cast<uintptr_t>(a.x) & 15) != 0 || a.K % 4 != 0)
+        return cudaErrorInvalidValue;  // float4 activation loads
+    if (a.norm != kNormNone && ((reinterpret_cast<uintptr_t>(a.gamma) & 15) ||
+                                (a.norm == kNormLayer && (reinterpret_cast<uintptr_t>(a.beta) & 15))))
         return cudaErrorInvalidValue;
+    if (a.argmax && (a.M > kMaxArgmaxRows || a.pair_off != 0)) return cudaErrorInvalidValue;
 
     // Rows per warp per stage: enough that one stage is ~16-32 KB, but not more than the CTA's share.
     const int64_t rb = a.row_bytes * (paired ? 2 : 1);
@@ -367,10 +456,13 @@ cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, bool pdl, int max_ctas) {
     const int per_warp = (a.rows_per_cta + kConsumerWarps - 1) / kConsumerWarps;
     R = std::min(R, per_warp);
     R = R >= 4 ? 4 : R >= 2 ? 2 : 1;
-    // activation rows per pass over a stage (more rows loop; 4 x 4 accumulators keep the kernel spill-free)
-    const int MT = a.M >= 4 ? 4 : a.M >= 2 ? 2 : 1;
+    // activation rows per pass over a stage (more rows loop); R x MT <= 4 (MT <= 2 for FP4) keeps the register
+    // tiles spill-free
+    int MT = a.M >= 4 ? 4 : a.M >= 2 ? 2 : 1;
+    MT = std::min(MT, 4 / R);
+    if (a.fmt == kFP4) MT = std::min(MT, 2);
 
-    a.xs_off = 128 * ((2 * 8 * 8 + 127) / 128);  // room for up to 8 stages of (full, empty) barriers
+    a.xs_off = 256;  // up to 8 stages of (full, empty) barriers
     const int x_alloc = a.x_smem ? int((x_bytes + 127) / 128 * 128) : 0;
     a.ring_off = a.xs_off + x_alloc;
     const int64_t room = kGemvSmemBudget - a.ring_off;

@@ -53,13 +53,19 @@ struct Layer {
     float *bqkv = nullptr, *bo = nullptr, *bup = nullptr, *bdown = nullptr;  // GPT-2 biases
 };
 
-// advance kernel: next token = argmax, position + 1 (device-side greedy loop)
-// (a sequence that reaches the end of its context stays there and reports kErrBadIndex)
-__global__ void advance_kernel(const int* argmax, int* tokens, int* pos, int n, int context) {
+// Greedy argmax finalize: the LM head's fused argmax left one (value, ~index) key per sequence; turn it into the
+// token id, clear the key for the next step and, for the device-side greedy loop, make it the next input token
+// with position + 1 (a sequence at the end of its context stays there and reports kErrBadIndex).
+__global__ void argmax_finalize_kernel(unsigned long long* keys, int* argmax, int* tokens, int* pos, int n,
+                                       int context, int advance) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     pdl_wait();
-    if (i < n) {
-        tokens[i] = argmax[i];
+    if (i >= n) return;
+    const int idx = int(0xFFFFFFFFu - unsigned(keys[i] & 0xFFFFFFFFull));
+    keys[i] = 0ull;
+    argmax[i] = idx;
+    if (advance) {
+        tokens[i] = idx;
         if (pos[i] + 1 < context) pos[i] += 1;
         else set_device_error(kErrBadIndex);
     }
@@ -92,6 +98,7 @@ struct neko_model {
     // workspace
     float *x = nullptr, *xn = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *hx = nullptr, *logits = nullptr;
     int *d_tokens = nullptr, *d_slots = nullptr, *d_pos = nullptr, *d_argmax = nullptr, *d_outrows = nullptr;
+    unsigned long long* d_keys = nullptr;  // fused greedy argmax keys, one per output row (zero between steps)
     float* part = nullptr;
     unsigned* tickets = nullptr;
     int64_t part_cap = 0, tick_cap = 0;
@@ -240,9 +247,10 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
                     m->qwen ? nullptr : m->wpe, 0, m->d_pos, m->x, st, pdl()),
        "embed");
 
-    const bool x_fits = int64_t(R) * C * 4 <= kGemvXSmemMax;
+    const bool x_fits = gemv_norm_fusable(fmt_for(C, m->fmt), R, C);
     auto gemv = [&](const Mat& W, int nrows, const float* x, int64_t xs, int M, int norm, const float* g,
-                    const float* b, const float* bias, int flags, float* y, int64_t ys, int64_t pair) -> cudaError_t {
+                    const float* b, const float* bias, int flags, float* y, int64_t ys, int64_t pair,
+                    unsigned long long* keys = nullptr) -> cudaError_t {
         GemvArgs a;
         a.W = W.w;
         a.row_bytes = W.rb;
@@ -261,6 +269,7 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         a.y = y;
         a.y_stride = ys;
         a.pair_off = pair;
+        a.argmax = keys;
         return launch_gemv(a, st, pdl());
     };
     // norm (fused into the GEMV prologue when the activations fit in shared memory, else a separate kernel)
@@ -378,31 +387,34 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         CK(cudaGetLastError(), "gather");
         hx = m->hx;
     }
-    const bool head_fits = int64_t(nout) * C * 4 <= kGemvXSmemMax;
+    const bool head_fits = gemv_norm_fusable(m->embed.fmt, nout, C);
+    const bool fused_argmax = do_argmax && nout <= 64;
+    unsigned long long* keys = fused_argmax ? m->d_keys : nullptr;
     if (head_fits) {
         CK(gemv(m->embed, m->V, hx, C, nout, m->qwen ? kNormRms : kNormLayer, m->normf, m->normfb, nullptr, 0,
-                m->logits, m->V, 0),
+                m->logits, m->V, 0, keys),
            "lm_head");
     } else {
         CK(launch_norm(hx, C, m->xn, C, m->normf, m->normfb, nout, C, eps, m->qwen, st, pdl()), "final norm");
-        CK(gemv(m->embed, m->V, m->xn, C, nout, kNormNone, nullptr, nullptr, nullptr, 0, m->logits, m->V, 0),
+        CK(gemv(m->embed, m->V, m->xn, C, nout, kNormNone, nullptr, nullptr, nullptr, 0, m->logits, m->V, 0, keys),
            "lm_head");
     }
-    if (do_argmax) CK(launch_argmax(m->logits, m->V, nout, m->V, m->d_argmax, st, pdl()), "argmax");
-    if (advance) {
-        CK(launch_ex(advance_kernel, dim3((nout + 127) / 128), dim3(128), 0, st, pdl(), (const int*)m->d_argmax,
-                     m->d_tokens, m->d_pos, nout, m->cfg.context),
-           "advance");
-    }
+    if (do_argmax && !fused_argmax) CK(launch_argmax(m->logits, m->V, nout, m->V, m->d_argmax, st, pdl()), "argmax");
+    if (fused_argmax)
+        CK(launch_ex(argmax_finalize_kernel, dim3((nout + 127) / 128), dim3(128), 0, st, pdl(), m->d_keys,
+                     m->d_argmax, m->d_tokens, m->d_pos, nout, m->cfg.context, advance ? 1 : 0),
+           "argmax finalize");
+    else if (advance)
+        return fail(m, NEKO_ERR_UNSUPPORTED, "device greedy loop supports at most 64 sequences per step");
     return NEKO_OK;
 }
 
 int step_launches(neko_model* m, int R, int nout, bool gather, bool do_argmax, bool advance) {
-    const bool x_fits = int64_t(R) * m->C * 4 <= kGemvXSmemMax;
+    const bool x_fits = gemv_norm_fusable(fmt_for(m->C, m->fmt), R, m->C);
     const int per_layer = 6 + (x_fits ? 0 : 2);
     int n = 1 + int(m->layers.size()) * per_layer + (gather ? 1 : 0);
-    n += int64_t(nout) * m->C * 4 <= kGemvXSmemMax ? 1 : 2;
-    return n + (do_argmax ? 1 : 0) + (advance ? 1 : 0);
+    n += gemv_norm_fusable(m->embed.fmt, nout, m->C) ? 1 : 2;
+    return n + (do_argmax ? 1 : 0) + (advance && nout > 64 ? 1 : 0);
 }
 
 // Runs (capturing on first use) the graph of one step shape.
@@ -542,8 +554,10 @@ neko_model* neko_model_create(int device, const neko_model_config* cfg, char* er
     if (falloc(&m->x, R * m->C) || falloc(&m->xn, nout * m->C) || falloc(&m->qkv, R * m->QW) ||
         falloc(&m->att, R * m->H * m->hd) || falloc(&m->h, R * std::max(m->F, m->UPW)) || falloc(&m->hx, nout * m->C) ||
         falloc(&m->logits, nout * size_t(m->V)) || ialloc(&m->d_tokens, nout) || ialloc(&m->d_slots, nout) ||
-        ialloc(&m->d_pos, nout) || ialloc(&m->d_argmax, nout) || ialloc(&m->d_outrows, nout))
+        ialloc(&m->d_pos, nout) || ialloc(&m->d_argmax, nout) || ialloc(&m->d_outrows, nout) ||
+        cudaMalloc(&m->d_keys, nout * sizeof(unsigned long long)) != cudaSuccess)
         return bail(m, "workspace allocation failed");
+    cudaMemset(m->d_keys, 0, nout * sizeof(unsigned long long));
     int64_t pf = 0, tk = 0;
     attention_scratch(int(R), m->H, m->KV, m->hd, c.context - 1, &pf, &tk);
     // fewer rows split more: size for the worst case over every row count 1..R
@@ -594,7 +608,8 @@ void neko_model_destroy(neko_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     for (void* p : {(void*)m->warena, (void*)m->kc, (void*)m->vc, (void*)m->x, (void*)m->xn, (void*)m->qkv,
                     (void*)m->att, (void*)m->h, (void*)m->hx, (void*)m->logits, (void*)m->d_tokens, (void*)m->d_slots,
-                    (void*)m->d_pos, (void*)m->d_argmax, (void*)m->d_outrows, (void*)m->part, (void*)m->tickets,
+                    (void*)m->d_pos, (void*)m->d_argmax, (void*)m->d_outrows, (void*)m->d_keys, (void*)m->part,
+                    (void*)m->tickets,
                     (void*)m->staging})
         if (p) cudaFree(p);
     if (m->h_in) cudaFreeHost(m->h_in);

@@ -56,6 +56,7 @@ struct GemvArgs {
     int64_t y_stride = 0;
     int n_off = 0;
     int64_t pair_off = 0;        // != 0: out n = silu(row n) * row(n + pair_off)  (SwiGLU epilogue)
+    unsigned long long* argmax = nullptr;  // M <= 64: per-row atomicMax of (value, ~index) keys (fused greedy argmax)
     // launch plan (filled by plan_gemv)
     int x_smem = 0;
     int rows_per_cta = 0;
@@ -70,6 +71,18 @@ struct GemvArgs {
 // can stream their weights while this one finishes.
 constexpr int kGemvSmemBudget = 110 * 1024;
 constexpr int kGemvXSmemMax = 40 * 1024;
+// Staged activations are zero-padded to whole 512-byte segments of weight codes: 256 f16, 512 FP8 or 1024 FP4
+// weights per segment.
+inline int64_t gemv_x_bytes(int fmt, int M, int K) {
+    const int w = fmt == 2 ? 1024 : fmt == 1 ? 512 : 256;
+    return int64_t(M) * ((K + w - 1) / w) * w * 4;
+}
+// A norm prologue can be fused into the GEMV when M * K <= kGemvNormMaxElems, K % 128 == 0 and the padded
+// activations fit the shared-memory budget.
+constexpr int kGemvNormMaxElems = 4096;
+inline bool gemv_norm_fusable(int fmt, int M, int K) {
+    return int64_t(M) * K <= kGemvNormMaxElems && K % 128 == 0 && gemv_x_bytes(fmt, M, K) <= kGemvXSmemMax;
+}
 
 cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, bool pdl, int max_ctas = 0);
 int gemv_launch_count();  // number of launches launch_gemv issues per call (1)

@@ -40,12 +40,12 @@ def cu(torch, a):
 
 
 @pytest.mark.parametrize("fmt", [FP8, FP4])
-@pytest.mark.parametrize("M", [1, 3, 8, 20])
+@pytest.mark.parametrize("M,K", [(1, 256), (3, 256), (8, 512), (10, 256)])  # up to M * K = 4096, 40 KB FP4
 @pytest.mark.parametrize("kind", ["rms", "ln"])
-def test_norm_prologue_matmul(torch, R, fmt, M, kind):
+def test_norm_prologue_matmul(torch, R, fmt, M, K, kind):
     from nekochat_b200 import ops
     rng = np.random.default_rng(M + 10 * fmt)
-    K, N = 256, 300
+    N = 300
     x = (rng.standard_normal((M, K)) * 3).astype(np.float32)
     g = (1 + 0.1 * rng.standard_normal(K)).astype(np.float32)
     b = (0.1 * rng.standard_normal(K)).astype(np.float32)
@@ -64,7 +64,7 @@ def test_norm_prologue_matmul(torch, R, fmt, M, kind):
 
 
 @pytest.mark.parametrize("fmt", [FP8, FP4, F16])
-@pytest.mark.parametrize("M", [1, 2, 8, 13])
+@pytest.mark.parametrize("M", [1, 2, 7, 10])
 @pytest.mark.parametrize("norm", [0, 1])
 def test_swiglu_pair(torch, R, fmt, M, norm):
     from nekochat_b200 import ops
