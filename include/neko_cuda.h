@@ -208,6 +208,12 @@ int neko_model_memory(neko_model* m, int64_t* weights, int64_t* kv, int64_t* wor
 int neko_model_set_debug(neko_model* m, int layers, int stage);
 /* Kernel launches one decode step of n sequences issues (for the bench's launch count). */
 int neko_model_step_launches(neko_model* m, int n);
+/* Decode steps of 1..4 sequences (decode, step, and forward of one token) run as ONE persistent kernel by
+ * default: enable = 0 makes them use the per-operator kernel chain instead (same results; for comparison).
+ * enable = 2 is a test of the kernel's bounded waits: the next steps wait for a CTA that does not exist, give
+ * up after 50 ms and report NEKO_ERR_DEVICE (the model stays usable; set 1 again afterwards).
+ * Returns 1 when the single-kernel path is available for this model, 0 when not, < 0 on error. */
+int neko_model_set_decode_kernel(neko_model* m, int enable);
 /* Device pointer and byte size of one packed weight matrix ("layers.L.wqkv", "layers.L.wo", "layers.L.wgu",
  * "layers.L.wdown", "head"), for the GEMV roofline measurement and the dequant bit-exactness tests. */
 int neko_model_matrix(neko_model* m, const char* which, const uint8_t** ptr, int* rows, int* cols);

@@ -24,6 +24,7 @@
 //    greedy argmax (max of (value, ~index) keys) for the LM head.
 #include "neko_common.cuh"
 #include "neko_internal.h"
+#include "gemv_core.cuh"
 
 namespace neko {
 
@@ -35,33 +36,7 @@ constexpr int kMaxArgmaxRows = 64;
 constexpr int kMaxStageVec = 10;  // float4 activations staged per consumer thread (40 KB / 256 threads)
 constexpr int kStageRound = 6;    // float4 loads a thread keeps in flight while staging
 constexpr int kMaxNormVec = 4;    // float4 per thread when a norm prologue is fused (M * K <= 4096)
-constexpr int kSegBytes = 512;  // bytes of one row segment (16 per lane)
 constexpr int kChunkBytes = 4096;
-
-// Weights per segment and float4s of activations per lane per segment, by format.
-template <int FMT> struct Seg;
-template <> struct Seg<kFP8> { static constexpr int W = 512, Q = 4; };
-template <> struct Seg<kFP4> { static constexpr int W = 1024, Q = 8; };
-template <> struct Seg<kF16> { static constexpr int W = 256, Q = 2; };
-
-__host__ __device__ inline int code_bytes(int fmt, int K) { return fmt == kFP8 ? K : fmt == kFP4 ? K / 2 : 2 * K; }
-__host__ __device__ inline int seg_count(int fmt, int K) { return (code_bytes(fmt, K) + kSegBytes - 1) / kSegBytes; }
-
-// Staged-activation index (in floats) of logical activation k: segment s, lane l, float4 q, element e.
-template <int FMT>
-__device__ __forceinline__ int xperm(int k) {
-    constexpr int W = Seg<FMT>::W, Q = Seg<FMT>::Q, WL = W / 32;
-    const int s = k / W, r = k % W, l = r / WL, t = r % WL;
-    return (((s * Q + t / 4) * 32 + l) << 2) + (t & 3);
-}
-
-// Greedy argmax key: the float's order-preserving bit pattern in the high word, the complement of the index in
-// the low word, so the largest key is the largest value with the smallest index (std::max_element).
-__device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
-    const unsigned b = __float_as_uint(v);
-    const unsigned ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-    return (static_cast<unsigned long long>(ord) << 32) | static_cast<unsigned>(0xFFFFFFFFu - unsigned(n));
-}
 
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
@@ -170,78 +145,6 @@ __device__ void stage_x(const GemvArgs& a, float* xs, double* part, int tid, int
         *reinterpret_cast<float4*>(xs + m * padded + xperm<FMT>(4 * (i % K4))) = y;
     }
     consumer_sync();
-}
-
-// dot of 4 fp32 activations with 4 weights (even = weights 0, 2; odd = weights 1, 3)
-__device__ __forceinline__ float dot4(const float4 x, const float2 e, const float2 o, float p) {
-    p = fmaf(x.x, e.x, p);
-    p = fmaf(x.y, o.x, p);
-    p = fmaf(x.z, e.y, p);
-    return fmaf(x.w, o.y, p);
-}
-
-// One lane's 16 weight bytes of one row (segment s) against MT activation rows; accumulates into acc[m].
-template <int FMT, int MT>
-__device__ __forceinline__ void seg_dot(const uint8_t* row, int cbytes, int s, int lane,
-                                        const float4 (&xv)[MT][Seg<FMT>::Q], float (&acc)[MT]) {
-    const uint4 w = *reinterpret_cast<const uint4*>(row + s * kSegBytes + 16 * lane);
-    const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
-    if (FMT == kFP8) {
-        const float sc =
-            half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + cbytes + 2 * (16 * s + (lane >> 1))));
-        float2 e[4], o[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            __half2 he, ho;
-            fp8x4_to_half2(wd[i], he, ho);
-            e[i] = __half22float2(he);
-            o[i] = __half22float2(ho);
-        }
-#pragma unroll
-        for (int m = 0; m < MT; m++) {
-            float p0 = dot4(xv[m][0], e[0], o[0], 0.0f);
-            float p1 = dot4(xv[m][1], e[1], o[1], 0.0f);
-            p0 = dot4(xv[m][2], e[2], o[2], p0);
-            p1 = dot4(xv[m][3], e[3], o[3], p1);
-            acc[m] = fmaf(sc, p0 + p1, acc[m]);
-        }
-    } else if (FMT == kFP4) {
-        const float sc = half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + cbytes + 2 * (32 * s + lane)));
-        float2 le[4], lo[4], he[4], ho[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            le[i] = __half22float2(fp4x2_to_half2(wd[i] & 0x000F000Fu));
-            lo[i] = __half22float2(fp4x2_to_half2((wd[i] >> 8) & 0x000F000Fu));
-            he[i] = __half22float2(fp4x2_to_half2((wd[i] >> 4) & 0x000F000Fu));
-            ho[i] = __half22float2(fp4x2_to_half2((wd[i] >> 12) & 0x000F000Fu));
-        }
-#pragma unroll
-        for (int m = 0; m < MT; m++) {
-            float p0 = 0.0f, p1 = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                p0 = dot4(xv[m][i], le[i], lo[i], p0);      // weights 4i .. 4i+3 (low nibbles)
-                p1 = dot4(xv[m][4 + i], he[i], ho[i], p1);  // weights 16+4i .. (high nibbles)
-            }
-            acc[m] = fmaf(sc, p0 + p1, acc[m]);
-        }
-    } else {
-        float2 h[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) h[i] = __half22float2(*reinterpret_cast<const __half2*>(&wd[i]));
-#pragma unroll
-        for (int m = 0; m < MT; m++) {
-            float p0 = xv[m][0].x * h[0].x;
-            p0 = fmaf(xv[m][0].y, h[0].y, p0);
-            p0 = fmaf(xv[m][0].z, h[1].x, p0);
-            p0 = fmaf(xv[m][0].w, h[1].y, p0);
-            float p1 = xv[m][1].x * h[2].x;
-            p1 = fmaf(xv[m][1].y, h[2].y, p1);
-            p1 = fmaf(xv[m][1].z, h[3].x, p1);
-            p1 = fmaf(xv[m][1].w, h[3].y, p1);
-            acc[m] += p0 + p1;
-        }
-    }
 }
 
 // Accumulates nr (<= R) rows (row stride rb inside the stage) x MT activation rows over the full K.

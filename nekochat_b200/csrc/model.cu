@@ -123,6 +123,16 @@ struct neko_model {
     int debug_stage = 0;    // > 0: stop inside layer debug_layers after this stage (debugStages numbering)
     // graphs keyed by (rows, nout, bucket, mode)
     std::map<std::tuple<int, int, int, int>, cudaGraphExec_t> graphs;
+    // single-kernel decode steps (k_decode.cu)
+    bool dec_enabled = true;
+    int dec_stall_test = 0;    // the next single-kernel step waits for a CTA that does not exist (50 ms limit)
+    int dec_seqs = 0;          // most sequences one launch serves
+    int dec_max_splits = 0;    // attention splits per (sequence, KV head) at the smallest span
+    float* dec_part = nullptr;
+    unsigned* dec_tickets = nullptr;
+    unsigned* dec_sync = nullptr;
+    int64_t dec_sync_n = 0, dec_tickets_n = 0;
+    int dec_ok[kDecodeMaxSeqs + 1] = {-1, -1, -1, -1, -1};  // per sequence count: -1 not planned yet
 };
 
 namespace {
@@ -409,7 +419,21 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
     return NEKO_OK;
 }
 
+bool fill_decode(neko_model* m, int R, int bucket, bool advance, DecodeParams& p, std::string* why);
+
+// Whether decode steps of R sequences can run as the single kernel (planned once per R).
+bool decode_ok(neko_model* m, int R) {
+    if (R < 1 || R > kDecodeMaxSeqs) return false;
+    if (m->dec_ok[R] < 0) {
+        DecodeParams dp;
+        m->dec_ok[R] = fill_decode(m, R, bucket_for(m, 0), false, dp, nullptr) ? 1 : 0;
+    }
+    return m->dec_ok[R] == 1;
+}
+
 int step_launches(neko_model* m, int R, int nout, bool gather, bool do_argmax, bool advance) {
+    if (!gather && nout == R && m->debug_layers < 0 && m->dec_enabled && R <= m->dec_seqs && decode_ok(m, R))
+        return 1;
     const bool x_fits = gemv_norm_fusable(fmt_for(m->C, m->fmt), R, m->C);
     const int per_layer = 6 + (x_fits ? 0 : 2);
     int n = 1 + int(m->layers.size()) * per_layer + (gather ? 1 : 0);
@@ -417,10 +441,96 @@ int step_launches(neko_model* m, int R, int nout, bool gather, bool do_argmax, b
     return n + (do_argmax ? 1 : 0) + (advance && nout > 64 ? 1 : 0);
 }
 
+// Parameters of the single-kernel decode step for R sequences (tokens / slots / positions in the device arrays);
+// false when the model or the step does not fit that kernel.
+bool fill_decode(neko_model* m, int R, int bucket, bool advance, DecodeParams& p, std::string* why) {
+    if (!m->dec_enabled || R < 1 || R > m->dec_seqs || size_t(m->layers.size()) > size_t(kDecodeMaxLayers)) {
+        if (why) *why = "disabled or too many sequences / layers";
+        return false;
+    }
+    const Layer& L0 = m->layers[0];
+    const int f = m->fmt;
+    if (m->embed.fmt != f || L0.wqkv.fmt != f || L0.wo.fmt != f || L0.wup.fmt != f || L0.wdown.fmt != f) {
+        if (why) *why = "f16 matrices";
+        return false;
+    }
+    p.M = R;
+    p.qwen = m->qwen ? 1 : 0;
+    p.fmt = f;
+    p.layers = int(m->layers.size());
+    p.C = m->C;
+    p.H = m->H;
+    p.KV = m->KV;
+    p.hd = m->hd;
+    p.F = m->F;
+    p.V = m->V;
+    p.QW = m->QW;
+    p.context = m->cfg.context;
+    p.rb_c = L0.wqkv.rb;
+    p.rb_att = L0.wo.rb;
+    p.rb_f = L0.wdown.rb;
+    p.eps = m->cfg.eps;
+    p.scale = 1.0f / std::sqrt(float(m->hd));
+    p.embed = m->embed.w;
+    p.normf = m->normf;
+    p.normfb = m->normfb;
+    p.rope = m->rope;
+    p.wpe = m->wpe;
+    p.kv_slot = m->kv_slot;
+    p.kv_head = m->kv_head;
+    p.x = m->x;
+    p.qkv = m->qkv;
+    p.att = m->att;
+    p.h = m->h;
+    p.logits = m->logits;
+    p.tokens = m->d_tokens;
+    p.slots = m->d_slots;
+    p.pos = m->d_pos;
+    p.argmax = m->d_argmax;
+    p.keys = m->d_keys;
+    p.advance = advance ? 1 : 0;
+    p.part = m->dec_part;
+    p.tickets = m->dec_tickets;
+    p.sync = m->dec_sync;
+    // keys per attention item: about one item per SM over the sequences' KV heads at this context bucket
+    const int per = std::max(1, num_sms() / std::max(1, R * m->KV));
+    int span = (bucket + per - 1) / per;
+    span = std::min(64, std::max(32, (span + 31) / 32 * 32));
+    p.span = span;
+    p.max_splits = m->dec_max_splits;
+    if (m->dec_stall_test) {
+        p.stall_test = 1;
+        p.wait_ns = 50000000ull;
+    }
+    for (size_t l = 0; l < m->layers.size(); l++) {
+        const Layer& L = m->layers[l];
+        DecodeLayer& d = p.layer[l];
+        d.wqkv = L.wqkv.w;
+        d.wo = L.wo.w;
+        d.wup = L.wup.w;
+        d.wdown = L.wdown.w;
+        d.ln1 = L.ln1;
+        d.ln2 = L.ln2;
+        d.ln1b = L.ln1b;
+        d.ln2b = L.ln2b;
+        d.qknorm = L.qknorm;
+        d.bqkv = L.bqkv;
+        d.bo = L.bo;
+        d.bup = L.bup;
+        d.bdown = L.bdown;
+        d.kc = m->kc + int64_t(l) * m->kv_layer;
+        d.vc = m->vc + int64_t(l) * m->kv_layer;
+    }
+    return plan_decode(p, why);
+}
+
 // Runs (capturing on first use) the graph of one step shape.
 int run_step(neko_model* m, int R, int nout, bool identity, int max_pos, bool do_argmax, bool advance, cudaStream_t st) {
     const int bucket = bucket_for(m, max_pos);
-    const int mode = (identity ? 1 : 0) | (do_argmax ? 2 : 0) | (advance ? 4 : 0) |
+    const bool single = m->dec_enabled && m->debug_layers < 0 && identity && nout == R && R <= m->dec_seqs &&
+                        decode_ok(m, R);
+    const int mode = (identity ? 1 : 0) | (do_argmax ? 2 : 0) | (advance ? 4 : 0) | (single ? 1 << 24 : 0) |
+                     (single && m->dec_stall_test ? 1 << 25 : 0) |
                      (m->debug_layers >= 0 ? (8 + (m->debug_layers << 4) + (m->debug_stage << 12)) : 0);
     auto key = std::make_tuple(R, nout, bucket, mode);
     auto it = m->graphs.find(key);
@@ -433,7 +543,16 @@ int run_step(neko_model* m, int R, int nout, bool identity, int max_pos, bool do
             cudaStreamDestroy(cap);
             return fail(m, NEKO_ERR_CUDA, cuda_msg(e, "begin capture"));
         }
-        int rc = enqueue_step(m, R, nout, identity, bucket - 1, do_argmax, advance, cap);
+        int rc = NEKO_OK;
+        DecodeParams dp;
+        if (single && !fill_decode(m, R, bucket, advance, dp, nullptr))
+            rc = fail(m, NEKO_ERR_CUDA, "decode kernel plan");
+        else if (single) {
+            const cudaError_t le = launch_decode(dp, cap);
+            if (le != cudaSuccess) rc = fail(m, NEKO_ERR_CUDA, cuda_msg(le, "decode kernel"));
+        } else {
+            rc = enqueue_step(m, R, nout, identity, bucket - 1, do_argmax, advance, cap);
+        }
         e = cudaStreamEndCapture(cap, &g);
         cudaStreamDestroy(cap);
         if (rc != NEKO_OK) {
@@ -462,11 +581,23 @@ int debug_width(const neko_model* m) {
     }
 }
 
+// After a device error the single-kernel step may have stopped between its phases: clear its counters,
+// tickets, argmax keys and abort flag so the next step starts clean.
+void decode_reset(neko_model* m) {
+    if (m->dec_sync) cudaMemset(m->dec_sync, 0, size_t(m->dec_sync_n) * 4);
+    if (m->dec_tickets) cudaMemset(m->dec_tickets, 0, size_t(m->dec_tickets_n) * 4);
+    cudaMemset(m->d_keys, 0, size_t(std::max(m->cfg.max_rows, m->cfg.max_seqs)) * sizeof(unsigned long long));
+    decode_clear_abort();
+    cudaDeviceSynchronize();
+}
+
 int wait_model(neko_model* m) {
     cudaError_t e = cudaStreamSynchronize(m->stream);
     if (e != cudaSuccess) return fail(m, NEKO_ERR_CUDA, cuda_msg(e, "step"));
-    if (unsigned d = read_device_error(true))
+    if (unsigned d = read_device_error(true)) {
+        decode_reset(m);
         return fail(m, NEKO_ERR_DEVICE, "kernel reported device error " + std::to_string(d));
+    }
     return NEKO_OK;
 }
 
@@ -572,6 +703,26 @@ neko_model* neko_model_create(int device, const neko_model_config* cfg, char* er
     if (falloc(&m->part, size_t(m->part_cap)) || cudaMalloc(&m->tickets, size_t(m->tick_cap) * 4))
         return bail(m, "attention scratch allocation failed");
     cudaMemset(m->tickets, 0, size_t(m->tick_cap) * 4);
+    // single-kernel decode steps: split-KV partials at the smallest span (32 keys), tickets, phase counters
+    m->dec_seqs = std::min({kDecodeMaxSeqs, c.max_rows, c.max_seqs});
+    m->dec_max_splits = (c.context + 31) / 32;
+    {
+        DecodeParams dp;
+        dp.M = m->dec_seqs;
+        dp.H = m->H;
+        dp.KV = m->KV;
+        dp.hd = m->hd;
+        dp.layers = c.layers;
+        dp.max_splits = m->dec_max_splits;
+        int64_t pf2 = 0;
+        decode_scratch(dp, &pf2, &m->dec_tickets_n, &m->dec_sync_n);
+        if (falloc(&m->dec_part, size_t(pf2)) || cudaMalloc(&m->dec_tickets, size_t(m->dec_tickets_n) * 4) ||
+            cudaMalloc(&m->dec_sync, size_t(m->dec_sync_n) * 4))
+            return bail(m, "decode scratch allocation failed");
+        m->work_bytes += size_t(m->dec_tickets_n + m->dec_sync_n) * 4;
+        cudaMemset(m->dec_tickets, 0, size_t(m->dec_tickets_n) * 4);
+        cudaMemset(m->dec_sync, 0, size_t(m->dec_sync_n) * 4);
+    }
     if (cudaMallocHost(&m->h_in, 4 * nout * sizeof(int)) || cudaMallocHost(&m->h_logits, nout * size_t(m->V) * 4) ||
         cudaMallocHost(&m->h_argmax, nout * sizeof(int)))
         return bail(m, "pinned host allocation failed");
@@ -609,7 +760,7 @@ void neko_model_destroy(neko_model* m) {
     for (void* p : {(void*)m->warena, (void*)m->kc, (void*)m->vc, (void*)m->x, (void*)m->xn, (void*)m->qkv,
                     (void*)m->att, (void*)m->h, (void*)m->hx, (void*)m->logits, (void*)m->d_tokens, (void*)m->d_slots,
                     (void*)m->d_pos, (void*)m->d_argmax, (void*)m->d_outrows, (void*)m->d_keys, (void*)m->part,
-                    (void*)m->tickets,
+                    (void*)m->tickets, (void*)m->dec_part, (void*)m->dec_tickets, (void*)m->dec_sync,
                     (void*)m->staging})
         if (p) cudaFree(p);
     if (m->h_in) cudaFreeHost(m->h_in);
@@ -842,8 +993,10 @@ int neko_model_tokens(neko_model* m, int n, int* tokens, int* pos) {
     if (!m || n <= 0 || n > m->cfg.max_seqs) return NEKO_ERR_ARG;
     Guard g(m->device);
     CK(cudaDeviceSynchronize(), "tokens");
-    if (unsigned d = read_device_error(true))
+    if (unsigned d = read_device_error(true)) {
+        decode_reset(m);
         return fail(m, NEKO_ERR_DEVICE, "kernel reported device error " + std::to_string(d));
+    }
     if (tokens) CK(cudaMemcpyAsync(tokens, m->d_tokens, size_t(n) * 4, cudaMemcpyDeviceToHost, m->stream), "tokens");
     if (pos) CK(cudaMemcpyAsync(pos, m->d_pos, size_t(n) * 4, cudaMemcpyDeviceToHost, m->stream), "tokens");
     CK(cudaStreamSynchronize(m->stream), "tokens");
@@ -871,6 +1024,15 @@ int neko_model_memory(neko_model* m, int64_t* weights, int64_t* kv, int64_t* wor
     if (kv) *kv = int64_t(m->kv_bytes) * 2;
     if (workspace) *workspace = int64_t(m->work_bytes);
     return NEKO_OK;
+}
+
+int neko_model_set_decode_kernel(neko_model* m, int enable) {
+    if (!m) return NEKO_ERR_ARG;
+    Guard g(m->device);
+    m->dec_enabled = enable != 0;
+    m->dec_stall_test = enable == 2 ? 1 : 0;
+    if (!m->dec_enabled) return 0;
+    return decode_ok(m, 1) ? 1 : 0;
 }
 
 int neko_model_step_launches(neko_model* m, int n) {

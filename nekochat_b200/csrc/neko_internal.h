@@ -153,6 +153,50 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl);
 void attention_scratch(int rows, int n_head, int n_kv, int hd, int max_pos, int64_t* part_floats,
                        int64_t* tickets);
 
+// ------------------------------------------------------------------ decode-step kernel (k_decode.cu)
+// One whole decode step (embedding, every layer, final norm, LM head, greedy argmax) of 1..4 sequences in a
+// single persistent launch. Weight pointers per layer; matrices use the packed rows of one format.
+constexpr int kDecodeMaxLayers = 64;
+constexpr int kDecodeMaxSeqs = 4;
+struct DecodeLayer {
+    const uint8_t *wqkv = nullptr, *wo = nullptr, *wup = nullptr, *wdown = nullptr;
+    const float *ln1 = nullptr, *ln2 = nullptr, *ln1b = nullptr, *ln2b = nullptr, *qknorm = nullptr;
+    const float *bqkv = nullptr, *bo = nullptr, *bup = nullptr, *bdown = nullptr;
+    uint16_t *kc = nullptr, *vc = nullptr;  // this layer's caches [slot][kv head][pos][hd]
+};
+struct DecodeParams {
+    int M = 0;          // sequences (activation rows), <= kDecodeMaxSeqs
+    int grid = 0;       // CTAs (one per SM, all co-resident)
+    int qwen = 0;       // 1: Qwen3 (RMSNorm, QK-norm, RoPE, SwiGLU); 0: GPT-2 (LayerNorm, biases, GELU, wpe)
+    int fmt = 0;        // weight format of every matrix
+    int layers = 0;
+    int C = 0, H = 0, KV = 0, hd = 0, F = 0, V = 0, QW = 0, context = 0;
+    int64_t rb_c = 0, rb_att = 0, rb_f = 0;  // row bytes of matrices with C, H * hd and F columns
+    float eps = 0.0f, scale = 0.0f;
+    const uint8_t* embed = nullptr;  // [V] rows, also the tied LM head
+    const float *normf = nullptr, *normfb = nullptr, *rope = nullptr, *wpe = nullptr;
+    int64_t kv_slot = 0, kv_head = 0;  // cache element strides (positions are hd apart)
+    float *x = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+    int *tokens = nullptr, *slots = nullptr, *pos = nullptr, *argmax = nullptr;
+    unsigned long long* keys = nullptr;  // greedy argmax keys (zero between steps)
+    int advance = 0;                     // device greedy loop: next token = argmax, position + 1
+    float* part = nullptr;               // split-KV partials [seq][kv head][split][group][hd + 2]
+    unsigned* tickets = nullptr;         // [seq][kv head], zero between steps
+    unsigned* sync = nullptr;            // phase counters [layers * 5 + 1], zero between steps
+    int span = 0, max_splits = 0;        // keys per attention split; splits per (seq, kv head) at most
+    uint64_t wait_ns = 2000000000ull;    // a wait of the kernel gives up after this long (device error)
+    int stall_test = 0;                  // 1: a wait that nothing satisfies (exercises the timeout path)
+    // shared-memory plan (filled by plan_decode)
+    int slot_bytes = 0, nslot = 0, xs_bytes = 0, kv_bytes = 0;
+    DecodeLayer layer[kDecodeMaxLayers];
+};
+// Checks that the step fits the kernel and plans its shared memory; false (with a reason) when it does not.
+bool plan_decode(DecodeParams& p, std::string* why);
+// Scratch the kernel needs: partial floats, tickets and phase counters.
+void decode_scratch(const DecodeParams& p, int64_t* part_floats, int64_t* tickets, int64_t* counters);
+cudaError_t launch_decode(const DecodeParams& p, cudaStream_t st);  // p planned by plan_decode
+cudaError_t decode_clear_abort();  // after a wait of the kernel gave up (device error reported)
+
 // ------------------------------------------------------------------ errors
 std::string cuda_msg(cudaError_t e, const char* what);
 void set_last_error(const std::string& msg);  // the thread-local message behind neko_last_error()

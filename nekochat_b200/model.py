@@ -142,6 +142,14 @@ class Model:
     def step_launches(self, n):
         return int(lib().neko_model_step_launches(self.h, n))
 
+    def set_decode_kernel(self, enable):
+        """Run decode steps of 1..4 sequences as one persistent kernel (True, the default) or as the per-operator
+        kernel chain (False); 2 makes the kernel's next steps hit a wait that runs out (timeout test). Returns
+        whether the single-kernel path is available for this model."""
+        rc = int(lib().neko_model_set_decode_kernel(self.h, int(enable)))
+        self._check(min(rc, 0), "set_decode_kernel")
+        return rc == 1
+
     def matrix(self, which):
         """(device pointer, rows, cols, format) of one packed matrix: 'layers.L.wqkv|wo|wgu|wdown' or 'head'."""
         p, r, c = C.c_void_p(), C.c_int(), C.c_int()
