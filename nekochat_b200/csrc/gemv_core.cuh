@@ -177,11 +177,11 @@ __device__ __forceinline__ void e4m3x4_to_half2(uint32_t q, __half2& lo, __half2
     hi = *reinterpret_cast<__half2*>(&b);
 }
 
-// RR rows' segment s at once: all weight and scale loads first, then the math, so the rows' latencies overlap.
-// Every rows[r] must point at a readable row (callers repeat a valid row for missing ones and drop those
-// results). Per row the operations and their order are those of seg_dot.
+// RR rows' segment s at once: all weight and scale loads first, then the math for the first nr rows, so the
+// rows' latencies overlap. Every rows[r] must point at a readable row (callers repeat a valid row for missing
+// ones). Per row the operations and their order are those of seg_dot.
 template <int FMT, int NM, int RR>
-__device__ __forceinline__ void seg_dot_rows(const uint8_t* const (&rows)[RR], int cbytes, int s, int lane,
+__device__ __forceinline__ void seg_dot_rows(const uint8_t* const (&rows)[RR], int nr, int cbytes, int s, int lane,
                                              const float4* xs4, int xrow4, int M, float (&acc)[RR][NM]) {
     constexpr int Q = Seg<FMT>::Q;
     uint4 w[RR];
@@ -202,6 +202,7 @@ __device__ __forceinline__ void seg_dot_rows(const uint8_t* const (&rows)[RR], i
         for (int q = 0; q < Q; q++) xv[q] = xm[32 * q];
 #pragma unroll
         for (int r = 0; r < RR; r++) {
+            if (r >= nr) break;  // rows past nr were only loaded (their loads keep the pass branch-free)
             const uint32_t wd[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
             if (FMT == kFP8) {  // hardware decode: sums are 256 x those of seg_dot (kFp8HwFactor)
                 float p0 = 0.0f, p1 = 0.0f;

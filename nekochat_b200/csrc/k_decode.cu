@@ -4,7 +4,7 @@
 //
 // Why: at batch 1 each matrix of Qwen3-0.6B is 1-6 MB, under a microsecond of HBM time, while a dependent kernel
 // launch plus its activation round trip costs several microseconds. Here the weights never wait for the math:
-//  * one CTA per SM (all co-resident), 8 consumer warps + 1 producer warp;
+//  * one CTA per SM (all co-resident), 12 consumer warps + 1 producer warp;
 //  * every CTA owns a fixed row range of every matrix; its producer warp streams those rows, phase after phase
 //    and layer after layer, through a ring of shared-memory slots with cp.async.bulk (TMA), gated only by free
 //    slots, so the next matrices are already on chip while the current phase waits for its inputs;
@@ -16,8 +16,8 @@
 // The dot products, activation staging, norm prologue and epilogues are the ones of the GEMV kernel (same
 // summation order), so both paths give the same logits.
 //
-// Every wait is bounded (DecodeParams::wait_ns on %globaltimer, 2 s by default): on expiry the kernel records kErrMbarTimeout, raises an abort
-// flag that makes every other wait return at once, and the producer waits (bounded) for its copies in flight
+// Every wait is bounded (DecodeParams::wait_ns on %globaltimer, 2 s by default): on expiry the kernel records
+// kErrMbarTimeout, raises an abort flag that makes every other wait return at once, and the producer waits (bounded) for its copies in flight
 // before leaving. The last CTA to finish resets the counters, so the launch can be replayed from a CUDA graph.
 #include <algorithm>
 
@@ -29,14 +29,14 @@ namespace neko {
 
 namespace {
 
-constexpr int kW = 8;                  // consumer warps
+constexpr int kW = 12;                 // consumer warps (12 + 1 warps: at most 128 registers a thread)
 constexpr int kNT = kW * 32;           // consumer threads
 constexpr int kThr = kNT + 32;         // + the producer warp
 constexpr int kMaxGroupRows = kW * 4;  // rows the CTA consumes per pass, at most (kRows<1> warps x 4)
 constexpr int kMaxSlots = 16;
-constexpr int kSlotBytes = 16384;
+constexpr int kSlotBytes = 32768;      // bigger stages stream faster (fewer producer / consumer hand-offs)
 constexpr int kMaxStatSlots = 256;     // 32-float4 groups with a norm partial (M * C / 128)
-constexpr int kChunk = 4096;           // bytes per bulk copy
+constexpr int kChunk = 8192;           // bytes per bulk copy
 constexpr int kPhases = 5;             // per layer: qkv, attention, o_proj, up, down
 constexpr int kMaxGq = 4;              // query heads per KV head
 constexpr int kMaxSpan = 64;           // keys per attention item (staged in shared memory)
@@ -376,10 +376,10 @@ __device__ void stage_x(const DecodeParams& p, const GemvPh& g, const NormPre& p
     csync();
 }
 
-// RR weight rows (stage pointers wr, all readable) against the M (<= NM) staged activation rows.
+// RR weight rows (stage pointers wr, all readable, the first nr real) against the M (<= NM) staged activations.
 template <int FMT, int NM, int RR>
-__device__ __forceinline__ void dot_rows(const uint8_t* const (&wr)[RR], int cbytes, int nseg, const float* xs,
-                                         int xrow, int M, int lane, float (&acc)[RR][NM]) {
+__device__ __forceinline__ void dot_rows(const uint8_t* const (&wr)[RR], int nr, int cbytes, int nseg,
+                                         const float* xs, int xrow, int M, int lane, float (&acc)[RR][NM]) {
 #pragma unroll
     for (int r = 0; r < RR; r++)
 #pragma unroll
@@ -387,23 +387,26 @@ __device__ __forceinline__ void dot_rows(const uint8_t* const (&wr)[RR], int cby
     const float4* xs4 = reinterpret_cast<const float4*>(xs);
     for (int s = 0; s < nseg; s++) {
         if (s * kSegBytes + 16 * lane >= cbytes) continue;  // lanes past the end of a partial last segment
-        seg_dot_rows<FMT, NM, RR>(wr, cbytes, s, lane, xs4, xrow / 4, M, acc);
+        seg_dot_rows<FMT, NM, RR>(wr, nr, cbytes, s, lane, xs4, xrow / 4, M, acc);
     }
 }
 
-struct Smem {
-    uint64_t* full;
-    uint64_t* empty;
-    float* xs;
-    uint8_t* ring;
-    double* spart;
-    float* snorm;
-    unsigned long long* skey;
-    int* flag;
-    int* ticket;
-    int* abort;  // a stage wait of this CTA gave up
-    uint16_t* kv;  // attention: an item's cached keys and values
-};
+// Shared-memory state of the kernel at file scope, so the phase functions address it directly (a struct of
+// pointers passed around ends up in local memory and puts a load on every access).
+extern __shared__ __align__(128) uint8_t dsm[];  // barriers | activations | attention keys/values | weight ring
+__shared__ double s_part[2 * kMaxStatSlots];      // norm prologue partial sums
+__shared__ float s_norm[2 * kDecodeMaxSeqs];
+__shared__ unsigned long long s_key[kDecodeMaxSeqs];  // LM head: the CTA's greedy argmax keys
+__shared__ int s_flag, s_ticket, s_last, s_abort;      // s_abort: a stage wait of this CTA gave up
+__shared__ __align__(8) uint64_t s_attn_bar;           // an attention item's keys / values have landed
+__device__ __forceinline__ uint64_t* full_bar() { return reinterpret_cast<uint64_t*>(dsm); }
+__device__ __forceinline__ uint64_t* empty_bar() { return reinterpret_cast<uint64_t*>(dsm) + kMaxSlots; }
+__device__ __forceinline__ float* xs_buf() { return reinterpret_cast<float*>(dsm + 256); }
+__device__ __forceinline__ uint16_t* kv_buf(const DecodeParams& p) {
+    return reinterpret_cast<uint16_t*>(dsm + 256 + p.xs_bytes);
+}
+__device__ __forceinline__ uint8_t* ring_buf(const DecodeParams& p) { return dsm + 256 + p.xs_bytes + p.kv_bytes; }
+
 
 // Where a warp's current row lies in the producer's stages, advanced without divisions: stage s of the
 // phase (ring slot, mbarrier parity) and row o inside it.
@@ -422,21 +425,22 @@ struct RowWalk {
     }
 };
 
-// One GEMV phase on this CTA's rows: wait for the inputs, stage them, consume the producer's stages.
+// One GEMV phase on this CTA's rows: wait for the inputs, stage them, consume the producer's stages. A pass of a
+// warp takes RR rows (RR / 2 gate / up pairs for SwiGLU) spaced kW apart, so the CTA's warps walk the stages
+// together and free them in order.
 template <int FMT, int NM>
-__device__ bool gemv_run(const DecodeParams& p, const GemvPh& g, const unsigned* dep, unsigned target,
-                         uint32_t& st_base, const Smem& S, int warp, int lane) {
-    constexpr int RR = kRows<NM>, GR = kW * RR;
+__device__ __forceinline__ bool gemv_run(const DecodeParams& p, const GemvPh& g, const unsigned* dep,
+                                         unsigned target, uint32_t& st_base, int warp, int lane) {
+    constexpr int RR = kRows<NM>;
     int r0, r1;
     cta_rows(g.rows, p.grid, r0, r1);
     if (r0 >= r1) return true;
     NormPre pre;
     norm_prefetch(p, g, pre);
-    if (dep && !wait_count(dep, target, S.flag, S.abort, p.wait_ns)) return false;
-    stage_x<FMT>(p, g, pre, S.xs, S.spart, S.snorm, warp, lane);
     constexpr float kF = FMT == kFP8 ? kFp8HwFactor : kFp4Factor;
     const int n = r1 - r0, rps = stage_rows(p, g), nst = (n + rps - 1) / rps;
     const int cbytes = code_bytes(FMT, g.K), nseg = seg_count(FMT, g.K), xrow = nseg * Seg<FMT>::W;
+    const int rpp = g.pair ? RR / 2 : RR;  // output rows per pass
     RowWalk w{0, 0, int(st_base % uint32_t(p.nslot)), int((st_base / uint32_t(p.nslot)) & 1u)};
     w.advance(warp, rps, p.nslot);  // this warp's first row
     int released = 0;               // stages [0, released) of this phase that this warp has let go
@@ -444,50 +448,74 @@ __device__ bool gemv_run(const DecodeParams& p, const GemvPh& g, const unsigned*
     unsigned long long best[NM];    // LM head: this warp's greedy argmax key per sequence
 #pragma unroll
     for (int m = 0; m < NM; m++) best[m] = 0ull;
-    for (int i0 = warp; i0 < n; i0 += GR) {
-        const uint8_t* wr[RR];
-        const uint8_t* ur[RR];
-        int nr = 0;
-        RowWalk v = w;
+    const uint8_t* wr[RR];
+    int nr = 0;
+    RowWalk v = w;
+    // Rows of the pass starting at i0: their stages waited for (one lane waits), their pointers in wr. False if
+    // a wait gave up.
+    auto setup = [&](int i0) -> bool {
+        nr = 0;
+        v = w;
 #pragma unroll
         for (int r = 0; r < RR; r++) {
+            if (r >= rpp) break;
             if (i0 + r * kW < n) {
                 if (v.s != waited) {
-                    if (!__all_sync(0xffffffffu, mbar_try_wait(&S.full[v.slot], v.par) ||
-                                                     dwait(&S.full[v.slot], v.par, p.wait_ns))) {
-                        // Gave up: stop consuming but keep the CTA's barriers in step; the next wait_count (or
-                        // the end of the step) sees the flag and every consumer warp leaves together.
-                        if (lane == 0) *S.abort = 1;
-                        return true;
-                    }
+                    int ok = 1;
+                    if (lane == 0)
+                        ok = mbar_try_wait(&full_bar()[v.slot], v.par) || dwait(&full_bar()[v.slot], v.par, p.wait_ns);
+                    if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
                     waited = v.s;
                 }
-                const uint8_t* b = S.ring + size_t(v.slot) * p.slot_bytes;
-                const int in_stage = min(rps, n - v.s * rps);
+                const uint8_t* b = ring_buf(p) + size_t(v.slot) * p.slot_bytes;
                 wr[r] = b + int64_t(v.o) * g.rb;
-                ur[r] = b + int64_t(in_stage + v.o) * g.rb;
+                if (g.pair) wr[rpp + r] = b + int64_t(min(rps, n - v.s * rps) + v.o) * g.rb;
                 nr = r + 1;
-            } else {  // no row: repeat row 0 (result dropped) so every load of the pass is unconditional
+            } else {  // no row: repeat row 0 (never used) so every load of the pass is unconditional
                 wr[r] = wr[0];
-                ur[r] = ur[0];
+                if (g.pair) wr[rpp + r] = wr[rpp];
             }
             v.advance(kW, rps, p.nslot);
         }
-        float acc[RR][NM], accu[RR][NM];
-        dot_rows<FMT, NM, RR>(wr, cbytes, nseg, S.xs, xrow, p.M, lane, acc);
-        if (g.pair) dot_rows<FMT, NM, RR>(ur, cbytes, nseg, S.xs, xrow, p.M, lane, accu);
+        return true;
+    };
+    // The first pass's weights were streamed in during earlier phases: take them before the activations' wait.
+    // A wait that gives up stops the consumption but keeps the CTA's barriers in step; the next wait_count (or
+    // the end of the step) sees the flag and every consumer warp leaves together.
+    if (warp < n && !setup(warp)) {
+        if (lane == 0) s_abort = 1;
+        return true;
+    }
+    if (dep && !wait_count(dep, target, &s_flag, &s_abort, p.wait_ns)) return false;
+    stage_x<FMT>(p, g, pre, xs_buf(), s_part, s_norm, warp, lane);
+    for (int i0 = warp; i0 < n; i0 += kW * rpp) {
+        if (i0 != warp && !setup(i0)) {
+            if (lane == 0) s_abort = 1;
+            return true;
+        }
+        // SwiGLU: up row r sits at rpp + r (gate rows nr .. rpp - 1 are computed but unused)
+        const int nrows = g.pair ? rpp + nr : nr;
+        float acc[RR][NM];
+        dot_rows<FMT, NM, RR>(wr, nrows, cbytes, nseg, xs_buf(), xrow, p.M, lane, acc);
+        // reductions of every row first (independent shuffle chains), then the lanes that own a row store it
+        float red_[RR][NM];
+#pragma unroll
+        for (int r = 0; r < RR; r++)
+#pragma unroll
+            for (int m = 0; m < NM; m++) red_[r][m] = (r < nrows && m < p.M) ? warp_sum(acc[r][m]) * kF : 0.0f;
 #pragma unroll
         for (int r = 0; r < RR; r++) {
+            if (r >= rpp) break;
 #pragma unroll
             for (int m = 0; m < NM; m++) {
                 if (m >= p.M) break;
-                const float gs = warp_sum(acc[r][m]) * kF;
-                const float us = g.pair ? warp_sum(accu[r][m]) * kF : 0.0f;
                 if (r >= nr || lane != ((r * NM + m) & 31)) continue;
                 const int row = r0 + i0 + r * kW;
                 float* dst = g.y + int64_t(m) * g.ys + row;
+                const float gs = red_[r][m];
                 float val;
                 if (g.pair) {
+                    const float us = red_[rpp + r < RR ? rpp + r : 0][m];
                     val = gs / (1.0f + expf(-gs)) * us;  // cpu::siluMul (cpu_ops.cpp:526-533)
                 } else {
                     val = gs;
@@ -501,13 +529,13 @@ __device__ bool gemv_run(const DecodeParams& p, const GemvPh& g, const unsigned*
         }
         __syncwarp();
         w = v;  // the first row of this warp's next pass
-        const int s_next = i0 + GR < n ? w.s : nst;
+        const int s_next = i0 + kW * rpp < n ? w.s : nst;
         for (; released < s_next; released++)
-            if (lane == 0) mbar_arrive(&S.empty[(st_base + uint32_t(released)) % uint32_t(p.nslot)]);
+            if (lane == 0) mbar_arrive(&empty_bar()[(st_base + uint32_t(released)) % uint32_t(p.nslot)]);
     }
     __syncwarp();
     for (; released < nst; released++)
-        if (lane == 0) mbar_arrive(&S.empty[(st_base + uint32_t(released)) % uint32_t(p.nslot)]);
+        if (lane == 0) mbar_arrive(&empty_bar()[(st_base + uint32_t(released)) % uint32_t(p.nslot)]);
     if (g.head) {  // one shared atomic per warp and sequence
 #pragma unroll
         for (int m = 0; m < NM; m++) {
@@ -515,7 +543,7 @@ __device__ bool gemv_run(const DecodeParams& p, const GemvPh& g, const unsigned*
             unsigned long long k = best[m];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) k = max(k, __shfl_xor_sync(0xffffffffu, k, o));
-            if (lane == 0 && k) atomicMax(&S.skey[m], k);
+            if (lane == 0 && k) atomicMax(&s_key[m], k);
         }
     }
     st_base += uint32_t(nst);
@@ -566,20 +594,34 @@ __device__ __forceinline__ AttnItem attn_item(const DecodeParams& p, const int (
     return a;
 }
 
-// Copies the item's cached keys and values (positions below pos; the newest comes from this step) into
-// shared memory with cp.async. Issued before the item's inputs are ready: the cache rows are from earlier
-// steps.
-__device__ __forceinline__ void attn_prefetch(const DecodeParams& p, const DecodeLayer& Ly, const AttnItem& a,
-                                              uint16_t* kbuf, uint16_t* vbuf) {
-    const int hd = p.hd, chunks = hd / 8;  // 16-byte pieces per row
+// Attention items of the step: Sm[m] splits of sequence m, Pm[m] its (clamped) position; returns the count.
+__device__ __forceinline__ int attn_items(const DecodeParams& p, int (&Sm)[kDecodeMaxSeqs], int (&Pm)[kDecodeMaxSeqs]) {
+    int total = 0;
+#pragma unroll
+    for (int m = 0; m < kDecodeMaxSeqs; m++) {
+        Sm[m] = 1;
+        Pm[m] = 0;
+        if (m >= p.M) continue;
+        const int pos = max(0, min(p.pos[m], p.context - 1));  // out of range: reported at kernel start
+        Pm[m] = pos;
+        Sm[m] = (pos + 1 + p.span - 1) / p.span;
+        total += p.KV * Sm[m];
+    }
+    return total;
+}
+
+// One thread: copies the item's cached keys and values (positions below pos; the newest comes from this step)
+// into shared memory with two bulk copies (a head's positions are contiguous in the cache), completing on
+// s_attn_bar. The cache rows are from earlier steps, so this is issued long before the item runs.
+__device__ __forceinline__ void attn_issue(const DecodeParams& p, int l, const AttnItem& a) {
+    const DecodeLayer& Ly = p.layer[l];
     const int nold = min(a.n, a.pos - a.k0);  // rows that are in the cache already
-    const int64_t base = int64_t(a.slot) * p.kv_slot + int64_t(a.g) * p.kv_head + int64_t(a.k0) * hd;
-    for (int c = threadIdx.x; c < 2 * nold * chunks; c += kNT) {
-        const int v = c >= nold * chunks ? 1 : 0, cc = c - v * nold * chunks;
-        const int t = cc / chunks, q = cc - t * chunks;
-        const uint16_t* src = (v ? Ly.vc : Ly.kc) + base + int64_t(t) * hd + 8 * q;
-        uint16_t* dst = (v ? vbuf : kbuf) + t * hd + 8 * q;
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+    const uint32_t bytes = uint32_t(nold) * uint32_t(p.hd) * 2u;
+    const int64_t base = int64_t(a.slot) * p.kv_slot + int64_t(a.g) * p.kv_head + int64_t(a.k0) * p.hd;
+    mbar_arrive_expect_tx(&s_attn_bar, 2u * bytes);
+    if (bytes) {
+        bulk_g2s(kv_buf(p), Ly.kc + base, bytes, &s_attn_bar);
+        bulk_g2s(kv_buf(p) + p.span * p.hd, Ly.vc + base, bytes, &s_attn_bar);
     }
 }
 
@@ -589,34 +631,25 @@ __device__ __forceinline__ void attn_prefetch(const DecodeParams& p, const Decod
 // are copied to shared memory before the wait for this step's qkv. Lane l owns dims [l * DL, l * DL + DL) of a
 // key / value row for scores (cpu_ops.cpp:558) and P.V.
 template <int DL>
-__device__ __noinline__ bool attn_run(const DecodeParams& p, int l, const Smem& S, int warp, int lane) {
+__device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued, int warp, int lane) {
     const int Gq = p.H / p.KV, hd = p.hd, span = p.span;
     int Sm[kDecodeMaxSeqs], Pm[kDecodeMaxSeqs];
-    int total = 0;
-    for (int m = 0; m < kDecodeMaxSeqs; m++) {
-        Sm[m] = 1;
-        Pm[m] = 0;
-        if (m >= p.M) continue;
-        const int pos = max(0, min(p.pos[m], p.context - 1));  // out of range: reported at kernel start
-        Pm[m] = pos;
-        Sm[m] = (pos + 1 + span - 1) / span;
-        total += p.KV * Sm[m];
-    }
+    const int total = attn_items(p, Sm, Pm);
     if (int(blockIdx.x) >= total) return true;
     unsigned* sy = p.sync + l * kPhases;
     const DecodeLayer& Ly = p.layer[l];
-    float* sq = S.xs;                 // [Gq][hd]
+    float* sq = xs_buf();             // [Gq][hd]
     float* snk = sq + Gq * hd;        // [hd]
     float* snv = snk + hd;            // [hd]
     float* sc = snv + hd;             // [Gq][span]
     float* red = sc + Gq * span;      // [kW][Gq][hd]
     float* sst = red + kW * Gq * hd;  // [Gq](max, sum)
-    uint16_t* kbuf = S.kv;            // [span][hd]
-    uint16_t* vbuf = S.kv + span * hd;
+    const uint16_t* kbuf = kv_buf(p);  // [span][hd]
+    const uint16_t* vbuf = kv_buf(p) + span * hd;
 
-    // Before the wait: the first item's cached keys / values, and the rotation and norm weights it needs.
+    // The first item's keys / values were requested at the start of the layer (attn_issue); before the wait,
+    // the rotation and norm weights it needs.
     AttnItem a = attn_item(p, Sm, Pm, blockIdx.x);
-    attn_prefetch(p, Ly, a, kbuf, vbuf);
     float cs_c[DL / 2], cs_s[DL / 2], wn[DL];
     auto load_rot = [&](const AttnItem& it) {
         if (p.qwen && warp <= Gq) {
@@ -631,12 +664,13 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, const Smem& 
         }
     };
     load_rot(a);
-    if (!wait_count(sy + kQkv, unsigned(p.grid + (p.stall_test ? 1 : 0)), S.flag, S.abort, p.wait_ns)) return false;
+    // stall_test: wait for one CTA more than there are, so the wait runs out (timeout path test)
+    if (!wait_count(sy + kQkv, unsigned(p.grid + (p.stall_test ? 1 : 0)), &s_flag, &s_abort, p.wait_ns))
+        return false;
 
     for (int it = blockIdx.x; it < total; it += p.grid) {
-        if (it != int(blockIdx.x)) {  // later items of this CTA (long contexts): fetch now
+        if (it != int(blockIdx.x)) {  // later items of this CTA (long contexts): requested after the previous
             a = attn_item(p, Sm, Pm, it);
-            attn_prefetch(p, Ly, a, kbuf, vbuf);
             load_rot(a);
         }
         const int L = a.pos + 1, n = a.n, g = a.g, m = a.m;
@@ -679,7 +713,12 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, const Smem& 
                 }
             }
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
+        if (!dwait(&s_attn_bar, uint32_t(issued - 1) & 1u, p.wait_ns)) {
+            // the keys never landed: leave (the consumers' barriers stay in step: every thread is here)
+            if (threadIdx.x == 0) s_abort = 1;
+            csync();
+            return false;
+        }
         csync();
         // 2. scores
         for (int t = warp; t < n; t += kW) {
@@ -748,6 +787,10 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, const Smem& 
             for (int i = 0; i < DL; i++) red[(warp * Gq + gq) * hd + lane * DL + i] = acc[gq][i];
         }
         csync();
+        if (it + p.grid < total) {  // the staged keys / values are consumed: request the next item's
+            if (threadIdx.x == 0) attn_issue(p, l, attn_item(p, Sm, Pm, it + p.grid));
+            issued++;
+        }
         // 5. merge the warps; one split: the output, else a partial for the ticket merge
         const int outs = Gq * hd;
         float* att = p.att + int64_t(m) * p.H * hd + int64_t(g) * Gq * hd;
@@ -777,11 +820,11 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, const Smem& 
         if (threadIdx.x == 0) {
             unsigned* tk = p.tickets + m * p.KV + g;
             const unsigned t = atomicAdd(tk, 1u);
-            *S.ticket = t == unsigned(a.ns - 1) ? 1 : 0;
+            s_ticket = t == unsigned(a.ns - 1) ? 1 : 0;
             if (t == unsigned(a.ns - 1)) *tk = 0u;  // every item of (m, g) has its ticket: ready for the next layer
         }
         csync();
-        if (*reinterpret_cast<volatile int*>(S.ticket)) {
+        if (*reinterpret_cast<volatile int*>(&s_ticket)) {
             __threadfence();
             for (int o = threadIdx.x; o < outs; o += kNT) {
                 const int gq = o / hd, d = o - gq * hd;
@@ -807,36 +850,20 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, const Smem& 
 // ---------------------------------------------------------------------------------------------- the kernel
 template <int FMT, int NM>
 __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ double spart[2 * kMaxStatSlots];
-    __shared__ float snorm[2 * kDecodeMaxSeqs];
-    __shared__ unsigned long long skey[kDecodeMaxSeqs];
-    __shared__ int flag, ticket, last, abort;
-    Smem S;
-    S.full = reinterpret_cast<uint64_t*>(smem);
-    S.empty = S.full + kMaxSlots;
-    S.xs = reinterpret_cast<float*>(smem + 256);
-    S.kv = reinterpret_cast<uint16_t*>(smem + 256 + p.xs_bytes);
-    S.ring = smem + 256 + p.xs_bytes + p.kv_bytes;
-    S.spart = spart;
-    S.snorm = snorm;
-    S.skey = skey;
-    S.flag = &flag;
-    S.ticket = &ticket;
-    S.abort = &abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.nslot; s++) {
-            mbar_init(&S.full[s], 1);
-            mbar_init(&S.empty[s], kW);
+            mbar_init(&full_bar()[s], 1);
+            mbar_init(&empty_bar()[s], kW);
         }
+        mbar_init(&s_attn_bar, 1);
         fence_barrier_init();
     }
-    if (threadIdx.x < kDecodeMaxSeqs) skey[threadIdx.x] = 0ull;
-    if (threadIdx.x == 0) abort = 0;
+    if (threadIdx.x < kDecodeMaxSeqs) s_key[threadIdx.x] = 0ull;
+    if (threadIdx.x == 0) s_abort = 0;
     __syncthreads();
     if (warp == kW) {
-        producer(p, S.full, S.empty, S.ring, lane);
+        producer(p, full_bar(), empty_bar(), ring_buf(p), lane);
         return;
     }
 
@@ -855,33 +882,56 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
             p.x[int64_t(m) * p.C + c] = v;
         }
     }
+    // Phases in order: per layer qkv, attention, o_proj, up, down; then the LM head. Each GEMV phase waits for the
+    // counter of the phase that produced its activations (the attention counter counts (sequence, KV head)
+    // merges, the others CTAs) and bumps its own.
     uint32_t st = 0;
-    for (int l = 0; l < p.layers; l++) {
+    int issued = 0;  // attention copies requested so far (the parity of s_attn_bar)
+    int Sm[kDecodeMaxSeqs], Pm[kDecodeMaxSeqs];
+    const bool attn_cta = int(blockIdx.x) < attn_items(p, Sm, Pm);
+    for (int l = 0; l <= p.layers; l++) {
         unsigned* sy = p.sync + l * kPhases;
-        if (!gemv_run<FMT, NM>(p, gemv_ph(p, l, kQkv), l ? sy - kPhases + kDown : nullptr, unsigned(p.grid), st, S,
-                               warp, lane))
-            return;
-        signal(sy + kQkv);
-        const bool ok = p.hd == 128 ? attn_run<4>(p, l, S, warp, lane) : attn_run<2>(p, l, S, warp, lane);
-        if (!ok) return;
-        if (!gemv_run<FMT, NM>(p, gemv_ph(p, l, kO), sy + kAttn, unsigned(p.M * p.KV), st, S, warp, lane)) return;
-        signal(sy + kO);
-        if (!gemv_run<FMT, NM>(p, gemv_ph(p, l, kUp), sy + kO, unsigned(p.grid), st, S, warp, lane)) return;
-        signal(sy + kUp);
-        if (!gemv_run<FMT, NM>(p, gemv_ph(p, l, kDown), sy + kUp, unsigned(p.grid), st, S, warp, lane)) return;
-        signal(sy + kDown);
+        for (int k = 0; k < (l == p.layers ? 1 : kPhases); k++) {
+            if (k == kQkv && l < p.layers && attn_cta) {  // this layer's first attention item: keys / values now
+                if (threadIdx.x == 0) attn_issue(p, l, attn_item(p, Sm, Pm, blockIdx.x));
+                issued++;
+            }
+            // Leaving early (a wait gave up): no attention copy of ours may still be landing in shared memory.
+            auto drain = [&]() {
+                if (threadIdx.x == 0 && issued > 0) {
+                    const uint64_t t0 = gtimer();
+                    while (!mbar_try_wait(&s_attn_bar, uint32_t(issued - 1) & 1u) && gtimer() - t0 < p.wait_ns) {
+                    }
+                }
+            };
+            if (k == kAttn) {
+                const bool ok = p.hd == 128 ? attn_run<4>(p, l, issued, warp, lane)
+                                            : attn_run<2>(p, l, issued, warp, lane);
+                if (!ok) {
+                    drain();
+                    return;
+                }
+                continue;
+            }
+            const int kind = l == p.layers ? int(kHead) : k;
+            const unsigned* dep = kind == kQkv ? (l ? sy - kPhases + kDown : nullptr)
+                                : kind == kHead ? sy - kPhases + kDown : sy + k - 1;
+            const unsigned target = kind == kO ? unsigned(p.M * p.KV) : unsigned(p.grid);
+            if (!gemv_run<FMT, NM>(p, gemv_ph(p, l, kind), dep, target, st, warp, lane)) {
+                drain();
+                return;
+            }
+            if (kind != kHead) signal(sy + k);
+        }
     }
-    if (!gemv_run<FMT, NM>(p, gemv_ph(p, p.layers, kHead), p.sync + (p.layers - 1) * kPhases + kDown,
-                           unsigned(p.grid), st, S, warp, lane))
-        return;
     csync();
-    if (*reinterpret_cast<volatile int*>(&abort)) return;
-    if (threadIdx.x < p.M && skey[threadIdx.x]) atomicMax(p.keys + threadIdx.x, skey[threadIdx.x]);
+    if (*reinterpret_cast<volatile int*>(&s_abort)) return;
+    if (threadIdx.x < p.M && s_key[threadIdx.x]) atomicMax(p.keys + threadIdx.x, s_key[threadIdx.x]);
     __threadfence();
     csync();
-    if (threadIdx.x == 0) last = atomicAdd(p.sync + p.layers * kPhases, 1u) == unsigned(p.grid - 1) ? 1 : 0;
+    if (threadIdx.x == 0) s_last = atomicAdd(p.sync + p.layers * kPhases, 1u) == unsigned(p.grid - 1) ? 1 : 0;
     csync();
-    if (!last) return;
+    if (!s_last) return;
     // Last CTA: every other CTA has passed its last wait. Greedy token per sequence (argmax_finalize_kernel
     // semantics), then reset the counters for the next launch.
     __threadfence();
@@ -939,8 +989,17 @@ bool plan_decode(DecodeParams& p, std::string* why) {
     xs = (xs + 127) / 128 * 128;
     const int64_t rb_max = std::max({p.rb_c * (p.qwen ? 2 : 1), p.rb_att, p.rb_f});
     int64_t slot = std::max<int64_t>(kSlotBytes, (rb_max + 1023) / 1024 * 1024);
-    const int64_t rps = slot / rb_max;
-    const int need = int((kMaxGroupRows + rps - 1) / rps) + 2;
+    // A warp's pass touches rows up to kMaxGroupRows - 1 apart; while it waits for the last of their stages it
+    // holds the first, so the ring must hold every stage a pass can span plus one being refilled (fewer when the
+    // CTA's share of the matrix has fewer stages).
+    auto need_for = [&](int64_t rows, int64_t rbe) {
+        const int64_t rps = slot / rbe, share = (rows + p.grid - 1) / p.grid;
+        const int64_t nst = (share + rps - 1) / rps, span = (kMaxGroupRows - 1) / rps + 2;
+        return int(std::min(nst, span) + 1);
+    };
+    const int need = std::max({need_for(p.QW, p.rb_c), need_for(p.C, p.rb_att),
+                               need_for(p.F, p.rb_c * (p.qwen ? 2 : 1)), need_for(p.C, p.rb_f),
+                               need_for(p.V, p.rb_c), 2});
     const int64_t kvb = int64_t(2) * kMaxSpan * p.hd * 2;
     const int64_t budget = 227 * 1024 - kStaticSmem - 256 - xs - kvb;
     const int nslot = int(std::min<int64_t>(kMaxSlots, budget / slot));
