@@ -38,7 +38,7 @@ def parse():
     p.add_argument("--steps", type=int, default=256)
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--batch", type=int, default=1)
-    p.add_argument("--prompt", type=int, default=512)
+    p.add_argument("--prompt", type=int, default=None, help="prompt tokens (default 512; 32 with --profile)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -284,7 +284,7 @@ def run_ours(args):
     world, rank, local = dist_setup(args)
     s = workload.shape(SHAPE)
     B = args.batch
-    prompt_len = 32 if args.profile else args.prompt
+    prompt_len = args.prompt or (32 if args.profile else 512)
     steps, warm = (4, 3) if args.profile else (args.steps, args.warmup)
     e2e_on = not (args.no_e2e or args.profile)
     context = prompt_len + 2 * (warm + steps) + 8
@@ -343,23 +343,39 @@ def run_ours(args):
 
     roof = None
     if rank == 0 and not args.profile:
-        per_launch, t_launch, n = gemv_roofline(m, s, stream)
         peak, src = peaks()
-        ach = per_launch / t_launch / 1e9
-        roof = {"bound": "hbm", "kernel": "gemv_kernel<FP8> (M=1, all weight matrices of one step)",
+        psrc = f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else \
+            "fallback (MEASURED_PEAKS.json absent: the profiling recipe's 6650 GB/s)"
+        # algorithmic bytes of one step: every weight byte once, each sequence's KV cache up to its position
+        # (mean over the timed steps), the activations are a few KB
+        mean_pos = prompt_len + warm + (steps - 1) / 2
+        bytes_step = workload.weight_stream_bytes(s, FMT) + B * workload.kv_bytes_per_position(s) * (mean_pos + 1)
+        single = m.step_launches(B) == 1
+        ach = bytes_step / (t / steps) / 1e9
+        roof = {"bound": "hbm",
+                "kernel": f"decode_kernel<FP8,{1 if B == 1 else 4}> (a whole decode step, one launch)" if single
+                else "decode step as a kernel chain (gemv_kernel dominant)",
                 "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
-                "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src,
-                "traffic": None, "bytes_per_launch": per_launch, "launch_us": t_launch * 1e6}
-        bytes_step = workload.weight_stream_bytes(s, FMT) + B * workload.kv_bytes_per_position(s) * (
-            prompt_len + warm + steps / 2)
-        roof["step_bytes"] = bytes_step
-        roof["step_achieved_gbs"] = round(bytes_step / (t / steps) / 1e9, 1)
+                "peak_source": psrc, "traffic": None, "bytes_per_launch": bytes_step if single else None,
+                "launch_us": t / steps * 1e6 if single else None,
+                "timing": "CUDA events on the launch stream around the timed steps (graph replays back to back)"}
         tf = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tf):
+        key = f"decode_fp8_b{B}"
+        if single and os.path.exists(tf):
             try:
-                roof["traffic"] = json.load(open(tf)).get("gemv_fp8_bytes_per_launch")
+                rec = json.load(open(tf)).get(key)
+                if rec:  # ncu DRAM bytes of one launch, scaled from the captured position to this run's mean
+                    roof["traffic"] = round(rec["dram_bytes"] * bytes_step / rec["algorithmic_bytes"])
+                    roof["traffic_note"] = (f"ncu dram__bytes_read+write of one launch at position {rec['position']} "
+                                            f"({rec['dram_bytes']} B vs {rec['algorithmic_bytes']} B algorithmic), "
+                                            "scaled by the algorithmic bytes to the mean timed position")
             except Exception:
                 pass
+        # the same weight matrices as single GEMV launches (the operator the step is built from), for reference
+        per_launch, t_launch, n = gemv_roofline(m, s, stream)
+        roof["gemv_op"] = {"kernel": "gemv_kernel<FP8> (M=1, every weight matrix of a step, one launch each)",
+                           "achieved": round(per_launch / t_launch / 1e9, 1), "bytes_per_launch": per_launch,
+                           "launch_us": t_launch * 1e6}
 
     cpu = None
     if cpu_on:
