@@ -235,4 +235,36 @@ __device__ __forceinline__ void seg_dot_rows(const uint8_t* const (&rows)[RR], i
     }
 }
 
+// RR weight rows (stage pointers wr, all readable, the first nr real) against the M (<= NM) staged activations.
+template <int FMT, int NM, int RR>
+__device__ __forceinline__ void dot_rows(const uint8_t* const (&wr)[RR], int nr, int cbytes, int nseg,
+                                         const float* xs, int xrow, int M, int lane, float (&acc)[RR][NM]) {
+#pragma unroll
+    for (int r = 0; r < RR; r++)
+#pragma unroll
+        for (int m = 0; m < NM; m++) acc[r][m] = 0.0f;
+    const float4* xs4 = reinterpret_cast<const float4*>(xs);
+    for (int s = 0; s < nseg; s++) {
+        if (s * kSegBytes + 16 * lane >= cbytes) continue;  // lanes past the end of a partial last segment
+        seg_dot_rows<FMT, NM, RR>(wr, nr, cbytes, s, lane, xs4, xrow / 4, M, acc);
+    }
+}
+
+// Where a warp's current row lies in the producer's stages, advanced without divisions: stage s of the
+// phase (ring slot, mbarrier parity) and row o inside it.
+struct RowWalk {
+    int s, o, slot, par;
+    __device__ __forceinline__ void advance(int k, int rps, int nslot) {
+        o += k;
+        while (o >= rps) {
+            o -= rps;
+            s++;
+            if (++slot == nslot) {
+                slot = 0;
+                par ^= 1;
+            }
+        }
+    }
+};
+
 }  // namespace neko

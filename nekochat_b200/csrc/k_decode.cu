@@ -376,21 +376,6 @@ __device__ void stage_x(const DecodeParams& p, const GemvPh& g, const NormPre& p
     csync();
 }
 
-// RR weight rows (stage pointers wr, all readable, the first nr real) against the M (<= NM) staged activations.
-template <int FMT, int NM, int RR>
-__device__ __forceinline__ void dot_rows(const uint8_t* const (&wr)[RR], int nr, int cbytes, int nseg,
-                                         const float* xs, int xrow, int M, int lane, float (&acc)[RR][NM]) {
-#pragma unroll
-    for (int r = 0; r < RR; r++)
-#pragma unroll
-        for (int m = 0; m < NM; m++) acc[r][m] = 0.0f;
-    const float4* xs4 = reinterpret_cast<const float4*>(xs);
-    for (int s = 0; s < nseg; s++) {
-        if (s * kSegBytes + 16 * lane >= cbytes) continue;  // lanes past the end of a partial last segment
-        seg_dot_rows<FMT, NM, RR>(wr, nr, cbytes, s, lane, xs4, xrow / 4, M, acc);
-    }
-}
-
 // Shared-memory state of the kernel at file scope, so the phase functions address it directly (a struct of
 // pointers passed around ends up in local memory and puts a load on every access).
 extern __shared__ __align__(128) uint8_t dsm[];  // barriers | activations | attention keys/values | weight ring
@@ -408,22 +393,6 @@ __device__ __forceinline__ uint16_t* kv_buf(const DecodeParams& p) {
 __device__ __forceinline__ uint8_t* ring_buf(const DecodeParams& p) { return dsm + 256 + p.xs_bytes + p.kv_bytes; }
 
 
-// Where a warp's current row lies in the producer's stages, advanced without divisions: stage s of the
-// phase (ring slot, mbarrier parity) and row o inside it.
-struct RowWalk {
-    int s, o, slot, par;
-    __device__ __forceinline__ void advance(int k, int rps, int nslot) {
-        o += k;
-        while (o >= rps) {
-            o -= rps;
-            s++;
-            if (++slot == nslot) {
-                slot = 0;
-                par ^= 1;
-            }
-        }
-    }
-};
 
 // One GEMV phase on this CTA's rows: wait for the inputs, stage them, consume the producer's stages. A pass of a
 // warp takes RR rows (RR / 2 gate / up pairs for SwiGLU) spaced kW apart, so the CTA's warps walk the stages

@@ -1,0 +1,339 @@
+// Streaming dequant GEMV for 1..4 activation rows: the MatmulQ8 / MatmulQ4 dispatch (matmul_q8.comp,
+// matmul_q4.comp; cpu::matmul, cpu_ops.cpp:462-481) when the weights are the whole cost.
+//
+// At M <= 4 every weight byte is used for at most 4 multiply-adds, so the kernel's job is to move the packed
+// rows from HBM at full bandwidth and keep the decode arithmetic off the critical path:
+//  * one CTA per SM, a contiguous range of rows each; a producer warp streams the range through a ring of
+//    stages of up to 52 KB with cp.async.bulk (TMA), 8 KB per copy (large stages: fewer producer / consumer
+//    hand-offs, which is what limits a TMA ring's rate);
+//  * 12 consumer warps work stage by stage: a stage holds 12 x rpw rows (rpw <= 4, the rows per warp), warp w
+//    takes rows w, w + 12, ... of it with all their 128-bit weight loads issued before the math (SwiGLU: gate
+//    and up rows together); one lane waits for the stage and releases it; FP8 codes are decoded by the
+//    hardware e4m3 -> f16 conversion (the engine's FP8 code is e4m3, see gemv_core.cuh), FP4 by bit arithmetic;
+//  * four rows are reduced across the warp together (6 shuffles instead of 20) before the stores;
+//  * activations (with the optional RMSNorm / LayerNorm prologue) are staged once per CTA with cp.async.
+// The per-row arithmetic is seg_dot_rows, the same as the single-kernel decode step's, so the two agree.
+#include <algorithm>
+
+#include "gemv_core.cuh"
+#include "neko_common.cuh"
+#include "neko_internal.h"
+
+namespace neko {
+
+namespace {
+
+constexpr int kSW = 12;              // consumer warps
+constexpr int kSNT = kSW * 32;       // consumer threads
+constexpr int kSThr = kSNT + 32;     // + the producer warp
+constexpr int kSMaxSlots = 16;
+constexpr int kSChunk = 8192;        // bytes per bulk copy
+constexpr int kSMaxStat = 64;        // norm partial slots (M * K / 128 <= 4096 / 128)
+constexpr int kSStatic = 8192;       // margin for the static shared memory and the per-block reservation
+
+extern __shared__ __align__(128) uint8_t gsm[];  // full[8] | empty[8] | activations | ring
+__shared__ double t_part[2 * kSMaxStat];
+__shared__ unsigned long long t_key[kDecodeMaxSeqs];
+
+template <int NM>
+constexpr int kSRows = NM == 1 ? 4 : 2;  // rows per warp pass
+
+__device__ __forceinline__ void ssync() { asm volatile("bar.sync 1, %0;" ::"n"(kSNT) : "memory"); }
+__device__ __forceinline__ double wsum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// The M activation rows into the permuted layout of seg_dot_rows, with the norm prologue (sums in double,
+// cpu_ops.cpp:483-511).
+template <int FMT>
+__device__ void stage_act(const GemvArgs& a, float* xs, int warp, int lane) {
+    const int tid = threadIdx.x, K4 = a.K / 4, total = a.M * K4, xrow = seg_count(FMT, a.K) * Seg<FMT>::W;
+    for (int i = tid; i < total; i += kSNT) {
+        const int m = i / K4, k = 4 * (i - m * K4);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(xs + m * xrow + xperm<FMT>(k))),
+                     "l"(a.x + int64_t(m) * a.x_stride + k)
+                     : "memory");
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (a.norm == kNormNone) {
+        ssync();
+        return;
+    }
+    for (int base = 0; base < total; base += kSNT) {  // K % 128 == 0: a warp's 32 float4 share a row
+        const int i = base + tid;
+        double s1 = 0.0, s2 = 0.0;
+        if (i < total) {
+            const int m = i / K4;
+            const float4 v = *reinterpret_cast<const float4*>(xs + m * xrow + xperm<FMT>(4 * (i - m * K4)));
+            s1 = double(v.x) + double(v.y) + double(v.z) + double(v.w);
+            s2 = double(v.x) * v.x + double(v.y) * v.y + double(v.z) * v.z + double(v.w) * v.w;
+        }
+        if (base + warp * 32 < total) {
+            s1 = wsum_d(s1);
+            s2 = wsum_d(s2);
+            if (lane == 0) {
+                t_part[2 * (base / 32 + warp)] = s1;
+                t_part[2 * (base / 32 + warp) + 1] = s2;
+            }
+        }
+    }
+    ssync();
+    const int gpr = K4 / 32;  // partial slots per row
+    for (int i = tid; i < total; i += kSNT) {
+        const int m = i / K4, k = 4 * (i - m * K4);
+        double a1 = 0.0, a2 = 0.0;
+        for (int q = m * gpr; q < (m + 1) * gpr; q++) {
+            a1 += t_part[2 * q];
+            a2 += t_part[2 * q + 1];
+        }
+        float mean = 0.0f, r;
+        if (a.norm == kNormRms) {
+            r = float(1.0 / sqrt(a2 / a.K + double(a.eps)));
+        } else {
+            const double mu = a1 / a.K;
+            mean = float(mu);
+            r = float(1.0 / sqrt(a2 / a.K - mu * mu + double(a.eps)));
+        }
+        float4* px = reinterpret_cast<float4*>(xs + m * xrow + xperm<FMT>(k));
+        float4 y = *px;
+        const float4 ga = __ldg(reinterpret_cast<const float4*>(a.gamma + k));
+        if (a.norm == kNormRms) {
+            y.x = __fmul_rn(__fmul_rn(y.x, r), ga.x);
+            y.y = __fmul_rn(__fmul_rn(y.y, r), ga.y);
+            y.z = __fmul_rn(__fmul_rn(y.z, r), ga.z);
+            y.w = __fmul_rn(__fmul_rn(y.w, r), ga.w);
+        } else {
+            const float4 be = __ldg(reinterpret_cast<const float4*>(a.beta + k));
+            y.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.x, mean), r), ga.x), be.x);
+            y.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.y, mean), r), ga.y), be.y);
+            y.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.z, mean), r), ga.z), be.z);
+            y.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.w, mean), r), ga.w), be.w);
+        }
+        *px = y;
+    }
+    ssync();
+}
+
+struct StreamPlan {
+    int rows_per_cta;
+    int rpw;         // rows per warp per stage (output rows; pairs for SwiGLU)
+    int rps;         // rows per stage = kSW * rpw
+    int nslot, slot_bytes, xs_bytes;
+};
+
+template <int FMT, int NM>
+__global__ void __launch_bounds__(kSThr, 1) gemv_stream_kernel(const GemvArgs a, const StreamPlan sp) {
+    constexpr int RR = kSRows<NM>;
+    uint64_t* full = reinterpret_cast<uint64_t*>(gsm);
+    uint64_t* empty = full + kSMaxSlots;
+    float* xs = reinterpret_cast<float*>(gsm + 256);
+    uint8_t* ring = gsm + 256 + sp.xs_bytes;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool pair = a.pair_off != 0;
+    const int r0 = blockIdx.x * sp.rows_per_cta, r1 = min(a.rows, r0 + sp.rows_per_cta);
+    pdl_trigger();
+    if (r0 >= r1) return;
+    const int n = r1 - r0, rps = sp.rps, nst = (n + rps - 1) / rps;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < sp.nslot; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kSW);
+        }
+        fence_barrier_init();
+    }
+    if (threadIdx.x < kDecodeMaxSeqs) t_key[threadIdx.x] = 0ull;
+    __syncthreads();
+
+    if (warp == kSW) {  // producer: weights only, so it never waits for the previous kernel
+        int st = 0;
+        for (; st < nst; st++) {
+            const int slot = st % sp.nslot;
+            if (st >= sp.nslot) {
+                int ok = 1;
+                if (lane == 0) ok = mbar_wait(&empty[slot], ((st / sp.nslot) - 1) & 1);
+                if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            }
+            const int row = r0 + st * rps, cnt = min(rps, r1 - row);
+            const uint32_t bytes = uint32_t(cnt) * uint32_t(a.row_bytes);
+            uint8_t* dst = ring + size_t(slot) * sp.slot_bytes;
+            if (lane == 0) mbar_arrive_expect_tx(&full[slot], pair ? 2 * bytes : bytes);
+            __syncwarp();
+            const int nch = int((bytes + kSChunk - 1) / kSChunk);
+            for (int c = lane; c < (pair ? 2 : 1) * nch; c += 32) {
+                const int half = c >= nch ? 1 : 0, cc = c - half * nch;
+                const uint32_t off = uint32_t(cc) * kSChunk, sz = min(uint32_t(kSChunk), bytes - off);
+                bulk_g2s(dst + (half ? bytes : 0) + off, a.W + (int64_t(row) + (half ? a.pair_off : 0)) * a.row_bytes + off,
+                         sz, &full[slot]);
+            }
+        }
+        if (lane == 0)  // leave only when no copy of ours is still landing (a consumer may have given up)
+            for (int s = st > sp.nslot ? st - sp.nslot : 0; s < st; s++) mbar_wait(&full[s % sp.nslot], (s / sp.nslot) & 1);
+        return;
+    }
+
+    // ---------------- consumers
+    pdl_wait();  // the activations come from the previous kernel
+    stage_act<FMT>(a, xs, warp, lane);
+    constexpr float kF = FMT == kFP8 ? kFp8HwFactor : kFp4Factor;
+    const int cbytes = code_bytes(FMT, a.K), nseg = seg_count(FMT, a.K), xrow = nseg * Seg<FMT>::W;
+    const int rpp = pair ? RR / 2 : RR;  // output rows a pass can take
+    unsigned long long best[NM];
+#pragma unroll
+    for (int m = 0; m < NM; m++) best[m] = 0ull;
+    int slot = 0, par = 0;
+    for (int st = 0; st < nst; st++) {
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(&full[slot], par);
+        ok = __shfl_sync(0xffffffffu, ok, 0);  // a wait that gave up is a device error; the stage is skipped
+        const int srow = st * rps, in_stage = min(rps, n - srow);
+        const uint8_t* base = ring + size_t(slot) * sp.slot_bytes;
+        for (int q0 = warp; ok && q0 < in_stage; q0 += kSW * rpp) {  // one pass unless rpw > rpp
+            const uint8_t* wr[RR];
+            int nr = 0;
+#pragma unroll
+            for (int r = 0; r < RR; r++) {
+                if (r >= rpp) break;
+                const int q = q0 + r * kSW;
+                if (q < in_stage && r < sp.rpw) {
+                    wr[r] = base + int64_t(q) * a.row_bytes;
+                    if (pair) wr[rpp + r] = base + int64_t(in_stage + q) * a.row_bytes;
+                    nr = r + 1;
+                } else {  // no row: repeat row 0 (never used) so every load of the pass is unconditional
+                    wr[r] = wr[0];
+                    if (pair) wr[rpp + r] = wr[rpp];
+                }
+            }
+            const int nrows = pair ? rpp + nr : nr;
+            float acc[RR][NM];
+            dot_rows<FMT, NM, RR>(wr, nrows, cbytes, nseg, xs, xrow, a.M, lane, acc);
+            float red_[RR][NM];
+            if constexpr (RR == 4 && NM == 1) {
+                // four rows at once: halves exchange rows (0,1) / (2,3), then quarters, then three xor steps;
+                // lane 8 q ends up with row q
+                const bool h16 = lane & 16, h8 = lane & 8;
+                float v0 = h16 ? acc[2][0] : acc[0][0], v1 = h16 ? acc[3][0] : acc[1][0];
+                v0 += __shfl_xor_sync(0xffffffffu, h16 ? acc[0][0] : acc[2][0], 16);
+                v1 += __shfl_xor_sync(0xffffffffu, h16 ? acc[1][0] : acc[3][0], 16);
+                float t = h8 ? v1 : v0;
+                t += __shfl_xor_sync(0xffffffffu, h8 ? v0 : v1, 8);
+                t += __shfl_xor_sync(0xffffffffu, t, 4);
+                t += __shfl_xor_sync(0xffffffffu, t, 2);
+                t += __shfl_xor_sync(0xffffffffu, t, 1);
+#pragma unroll
+                for (int r = 0; r < 4; r++) red_[r][0] = __shfl_sync(0xffffffffu, t, 8 * r) * kF;
+            } else {
+#pragma unroll
+                for (int r = 0; r < RR; r++)
+#pragma unroll
+                    for (int m = 0; m < NM; m++)
+                        red_[r][m] = (r < nrows && m < a.M) ? warp_sum(acc[r][m]) * kF : 0.0f;
+            }
+#pragma unroll
+            for (int r = 0; r < RR; r++) {
+                if (r >= rpp) break;
+#pragma unroll
+                for (int m = 0; m < NM; m++) {
+                    if (m >= a.M) break;
+                    if (r >= nr || lane != ((r * NM + m) & 31)) continue;
+                    const int row = r0 + srow + q0 + r * kSW;
+                    float* dst = a.y + int64_t(m) * a.y_stride + a.n_off + row;
+                    const float gs = red_[r][m];
+                    float val;
+                    if (pair) {
+                        const float us = red_[rpp + r < RR ? rpp + r : 0][m];
+                        val = gs / (1.0f + expf(-gs)) * us;  // cpu::siluMul (cpu_ops.cpp:526-533)
+                    } else {
+                        val = gs;
+                        if (a.flags & kBias) val += a.bias[row];
+                        if (a.flags & kGelu) val = gelu(val);
+                        if (a.flags & kAccumulate) val += *dst;
+                    }
+                    *dst = val;
+                    if (a.argmax) best[m] = max(best[m], argmax_key(val, row));
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++slot == sp.nslot) {
+            slot = 0;
+            par ^= 1;
+        }
+    }
+    if (a.argmax) {  // per warp, then one global atomic per CTA and activation row
+#pragma unroll
+        for (int m = 0; m < NM; m++) {
+            if (m >= a.M) break;
+            unsigned long long k = best[m];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) k = max(k, __shfl_xor_sync(0xffffffffu, k, o));
+            if (lane == 0 && k) atomicMax(&t_key[m], k);
+        }
+        ssync();
+        if (threadIdx.x < a.M && t_key[threadIdx.x]) atomicMax(a.argmax + threadIdx.x, t_key[threadIdx.x]);
+    }
+}
+
+using StreamFn = void (*)(const GemvArgs, const StreamPlan);
+
+StreamFn pick(int fmt, int M) {
+    if (fmt == kFP8) return M == 1 ? gemv_stream_kernel<kFP8, 1> : gemv_stream_kernel<kFP8, kDecodeMaxSeqs>;
+    return M == 1 ? gemv_stream_kernel<kFP4, 1> : gemv_stream_kernel<kFP4, kDecodeMaxSeqs>;
+}
+
+}  // namespace
+
+// The streaming kernel takes the call when it fits: 1..4 FP8 / FP4 activation rows, activations (padded) in
+// 64 KB of shared memory, a ring of at least the stages a pass can span. Returns cudaErrorNotSupported (and
+// launches nothing) otherwise, so the caller falls back to the general kernel.
+cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl) {
+    if (a.M < 1 || a.M > kDecodeMaxSeqs || (a.fmt != kFP8 && a.fmt != kFP4)) return cudaErrorNotSupported;
+    if (a.x_stride % 4 || (reinterpret_cast<uintptr_t>(a.x) & 15) || a.K % 4) return cudaErrorNotSupported;
+    if (a.argmax && a.pair_off) return cudaErrorNotSupported;
+    const int64_t xs = (gemv_x_bytes(a.fmt, a.M, a.K) + 127) / 128 * 128;
+    if (xs > 64 * 1024) return cudaErrorNotSupported;
+    if (a.norm != kNormNone && !gemv_norm_fusable(a.fmt, a.M, a.K)) return cudaErrorNotSupported;
+    const int64_t rbe = a.row_bytes * (a.pair_off ? 2 : 1);
+    if (a.row_bytes % 16) return cudaErrorNotSupported;
+    StreamPlan sp;
+    const int sms = num_sms();
+    int ctas = std::max(1, std::min(sms, (a.rows + 3) / 4));
+    sp.rows_per_cta = (a.rows + ctas - 1) / ctas;
+    ctas = (a.rows + sp.rows_per_cta - 1) / sp.rows_per_cta;
+    sp.xs_bytes = int(xs);
+    const int64_t budget = 227 * 1024 - kSStatic - 256 - xs;
+    // Stage = kSW x rpw rows: the most rows per warp (up to what a pass takes) that still leaves a ring of
+    // at least four stages (three, then two, for very wide rows).
+    const int rpp = (a.M == 1 ? 4 : 2) / (a.pair_off ? 2 : 1);
+    sp.rpw = 0;
+    for (int want : {4, 3, 2}) {
+        for (int rpw = rpp; rpw >= 1 && !sp.rpw; rpw--) {
+            const int64_t sb = (int64_t(kSW) * rpw * rbe + 127) / 128 * 128;
+            if (budget / sb >= want) {
+                sp.rpw = rpw;
+                sp.slot_bytes = int(sb);
+            }
+        }
+        if (sp.rpw) break;
+    }
+    if (!sp.rpw) return cudaErrorNotSupported;
+    sp.rps = kSW * sp.rpw;
+    sp.nslot = int(std::min<int64_t>(kSMaxSlots, budget / sp.slot_bytes));
+    StreamFn k = pick(a.fmt, a.M);
+    const size_t smem = 256 + size_t(xs) + size_t(sp.nslot) * sp.slot_bytes;
+    // the dynamic shared-memory limit of the instantiation, raised to this call's size when needed (per device)
+    static int attr_set[4][32] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int* set = dev < 32 ? &attr_set[(a.fmt == kFP8 ? 0 : 2) + (a.M == 1 ? 0 : 1)][dev] : nullptr;
+    if (!set || *set < int(smem)) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        if (set) *set = int(smem);
+    }
+    return launch_ex(k, dim3(ctas), dim3(kSThr), smem, st, pdl, a, sp);
+}
+
+}  // namespace neko
