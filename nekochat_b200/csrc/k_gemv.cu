@@ -331,8 +331,10 @@ int gemv_launch_count() { return 1; }
 
 cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, bool pdl, int max_ctas) {
     if (a.rows <= 0 || a.M <= 0) return cudaSuccess;
-    if (max_ctas <= 0) {  // 1..4 activation rows: the streaming kernel when the call fits it
-        const cudaError_t e = launch_gemv_stream(a, st, pdl);
+    if (max_ctas <= 0) {  // 1..4 activation rows: the streaming kernel; 5+: tensor cores (when the call fits)
+        cudaError_t e = launch_gemv_stream(a, st, pdl);
+        if (e != cudaErrorNotSupported) return e;
+        e = launch_gemm_tc(a, st, pdl);
         if (e != cudaErrorNotSupported) return e;
     }
     if (cudaError_t e = ensure_smem_attr(); e != cudaSuccess) return e;

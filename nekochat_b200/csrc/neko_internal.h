@@ -88,6 +88,8 @@ cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, bool pdl, int max_ctas = 0)
 // The streaming kernel for 1..4 FP8 / FP4 activation rows (k_gemv_stream.cu); cudaErrorNotSupported when the
 // call does not fit it (launch_gemv then uses the general kernel).
 cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl);
+// The tensor-core kernel for 5+ activation rows (k_mma.cu); cudaErrorNotSupported when the call does not fit.
+cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl);
 int gemv_launch_count();  // number of launches launch_gemv issues per call (1)
 
 // ------------------------------------------------------------------ other ops (k_ops.cu)

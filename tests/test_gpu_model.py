@@ -74,7 +74,9 @@ def test_greedy_32_steps_teacher_forced(name, fmt):
 
 
 def test_batched_decode_matches_single_sequence():
-    """b sequences in one step == each sequence decoded alone (slots are independent)."""
+    """b sequences in one step == each sequence decoded alone (slots are independent). Six sequences run on the
+    tensor-core matmul and one on the single-kernel step: different summation orders, so they agree to the
+    fp32 rounding level, not bit for bit."""
     s = workload.shape("qwen3-tiny")
     tensors = list(workload.weights(s, seed=5, perturb=True))
     m = nmodel.Model(s, FP8, context=96, max_seqs=6, max_rows=32).load(tensors)
@@ -91,8 +93,10 @@ def test_batched_decode_matches_single_sequence():
     for slot, p in enumerate(prompts):
         m2.prefill(p, slot)
         lg, am = m2.decode([slot], [first[slot]], [pos[slot]])
-        np.testing.assert_allclose(lg_b[slot], lg[0], rtol=1e-5, atol=1e-5)
-        assert am_b[slot] == am[0]
+        np.testing.assert_allclose(lg_b[slot], lg[0], rtol=1e-4, atol=1e-4)
+        if am_b[slot] != am[0]:
+            srt = np.sort(lg[0])
+            assert srt[-1] - srt[-2] <= 2e-4, "greedy token differs beyond a near-tie"
     m.close()
     m2.close()
 
