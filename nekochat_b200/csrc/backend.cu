@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstring>
 #include <new>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -102,6 +103,57 @@ struct DeviceGuard {
         if (prev >= 0 && cur != prev) cudaSetDevice(prev);
     }
 };
+
+// Stream-ordered scratch for operators called outside a model comes from the library's own memory pool on the
+// current device: it keeps what it has grown to (release threshold at its maximum), so after the first calls an
+// allocation maps no memory, and the default pool's settings stay the caller's.
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t st) {
+    static std::mutex mu;
+    static cudaMemPool_t pools[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaMallocAsync(p, bytes, st);
+    cudaMemPool_t pool;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!pools[dev]) {
+            cudaMemPoolProps props = {};
+            props.allocType = cudaMemAllocationTypePinned;
+            props.handleTypes = cudaMemHandleTypeNone;
+            props.location.type = cudaMemLocationTypeDevice;
+            props.location.id = dev;
+            if ((e = cudaMemPoolCreate(&pools[dev], &props)) != cudaSuccess) return e;
+            uint64_t keep = UINT64_MAX;
+            cudaMemPoolSetAttribute(pools[dev], cudaMemPoolAttrReleaseThreshold, &keep);
+        }
+        pool = pools[dev];
+    }
+    return cudaMallocFromPoolAsync(p, bytes, pool, st);
+}
+
+// A matmul outside a model: a stream-ordered workspace for the tensor-core path's K splits and activation split,
+// allocated and freed around the call (both stream-ordered, so the call can be captured in a graph). Without the
+// memory the call still runs, on fewer CTAs.
+cudaError_t launch_gemv_op(GemvArgs a, cudaStream_t st, bool pdl) {
+    int64_t wf = 0, wt = 0;
+    if (a.M >= 5 && a.norm == kNormNone) gemm_tc_scratch(a.fmt, a.rows, a.K, a.M, a.pair_off != 0, &wf, &wt);
+    if (wf == 0) return launch_gemv(a, st, pdl);
+    const size_t fb = (size_t(wf) * 4 + 255) / 256 * 256, tb = size_t(wt) * 4;
+    void* mem = nullptr;
+    if (scratch_alloc(&mem, fb + tb, st) != cudaSuccess) {
+        cudaGetLastError();
+        return launch_gemv(a, st, pdl);
+    }
+    if (tb) cudaMemsetAsync(static_cast<char*>(mem) + fb, 0, tb, st);
+    a.ws = static_cast<float*>(mem);
+    a.ws_floats = wf;
+    a.ws_tickets = tb ? reinterpret_cast<unsigned*>(static_cast<char*>(mem) + fb) : nullptr;
+    a.ws_ntickets = int(wt);
+    const cudaError_t e = launch_gemv(a, st, pdl);
+    cudaFreeAsync(mem, st);
+    return e;
+}
 
 }  // namespace
 
@@ -304,7 +356,7 @@ int neko_cuda_dispatch(neko_ctx* c, int kernel, neko_buf* const bind[4], const i
             a.y = static_cast<float*>(ptr(3));
             a.y_stride = N;
             a.n_off = noff;
-            e = launch_gemv(a, c->stream, false);
+            e = launch_gemv_op(a, c->stream, false);
             break;
         }
         case NEKO_K_KVSTORE: {  // kv_store.comp
@@ -445,7 +497,7 @@ int neko_op_matmul(int format, const float* x, int T, int K, const uint8_t* W, i
     a.y = y;
     a.y_stride = y_stride;
     a.n_off = n_off;
-    NEKO_OP_RETURN(launch_gemv(a, static_cast<cudaStream_t>(stream), (flags & NEKO_PDL) != 0));
+    NEKO_OP_RETURN(launch_gemv_op(a, static_cast<cudaStream_t>(stream), (flags & NEKO_PDL) != 0));
 }
 
 int neko_op_matmul_fused(int format, const float* x, int T, int K, const uint8_t* W, int rows, int norm,
@@ -479,7 +531,7 @@ int neko_op_matmul_fused(int format, const float* x, int T, int K, const uint8_t
     a.y_stride = y_stride;
     a.n_off = n_off;
     a.pair_off = swiglu ? rows : 0;
-    NEKO_OP_RETURN(launch_gemv(a, static_cast<cudaStream_t>(stream), (flags & NEKO_PDL) != 0));
+    NEKO_OP_RETURN(launch_gemv_op(a, static_cast<cudaStream_t>(stream), (flags & NEKO_PDL) != 0));
 }
 
 int neko_op_norm(const float* x, float* y, const float* gamma, const float* beta, int rows, int C, float eps,
@@ -522,13 +574,15 @@ int neko_op_attention(const float* q, int q_stride, const uint16_t* k_cache, con
     int64_t need_p = 0, need_t = 0;
     attention_scratch(T, n_head, n_kv, hd, a.max_pos, &need_p, &need_t);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // Scratch for the split-KV merge, allocated per call on the stream's pool.
+    // Scratch for the split-KV merge, allocated per call (stream-ordered, from the library's pool).
     cudaError_t e = cudaSuccess;
     if (need_p) {
-        if ((e = cudaMallocAsync(reinterpret_cast<void**>(&a.part), size_t(need_p) * 4, st)) != cudaSuccess)
+        if ((e = scratch_alloc(reinterpret_cast<void**>(&a.part), size_t(need_p) * 4, st)) != cudaSuccess)
             return set_err(nullptr, NEKO_ERR_NOMEM, cuda_msg(e, "attention scratch"));
-        if ((e = cudaMallocAsync(reinterpret_cast<void**>(&a.tickets), size_t(need_t) * 4, st)) != cudaSuccess)
+        if ((e = scratch_alloc(reinterpret_cast<void**>(&a.tickets), size_t(need_t) * 4, st)) != cudaSuccess) {
+            cudaFreeAsync(a.part, st);
             return set_err(nullptr, NEKO_ERR_NOMEM, cuda_msg(e, "attention scratch"));
+        }
         cudaMemsetAsync(a.tickets, 0, size_t(need_t) * 4, st);
         a.part_capacity = need_p;
         a.ticket_capacity = need_t;

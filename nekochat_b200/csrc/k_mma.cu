@@ -9,15 +9,22 @@
 //    that block's partial sums (two k16 steps), as dequantizeRow multiplies code by scale in fp32;
 //  * activations are split x = hi + lo into two f16 (round to nearest, then the rounding error rounded again):
 //    two MMAs per step, about 22 bits of each activation kept (fp32 has 24), products exact in fp32;
-//  * CTA tile: 64 activation rows x BN output rows (16 / 32 / 64 by N so that there are enough CTAs; SwiGLU:
-//    BN gate + BN up rows, BN <= 32); K walked in stages of 64 through a 4-deep cp.async pipeline; per stage
-//    the CTA converts codes and activations once into padded shared memory; 4 warps, warp w owns activation
-//    rows 16w..16w+15 of the tile, ldmatrix.x4 fragments, all BN columns.
+//  * CTA tile: 64 activation rows x 64 weight rows (SwiGLU: 32 gate + 32 up rows); K walked in stages of 64
+//    through a 4-deep cp.async pipeline; per stage the CTA converts the codes once into padded shared memory;
+//    4 warps, warp w owns activation rows 16w..16w+15 of the tile (warps without rows skip the math),
+//    ldmatrix.x4 fragments, all 64 columns;
+//  * when the tiles alone leave SMs idle, K is split over up to ~2 CTAs per SM: partial tiles go to a workspace
+//    and the tile's last CTA (atomic ticket) sums them in split order 0, 1, ... (deterministic) before the
+//    epilogue;
+//  * when 8+ tiles share the activations, one small kernel splits them into hi / lo f16 first, and the stages
+//    copy those straight into the padded tiles (otherwise every CTA splits its own fp32 copy).
 // Activations must stay within the f16 range (|x| < 65504), which the matmul inputs of the models are
 // (normalised activations, attention outputs, SwiGLU products).
 #include <algorithm>
+#include <type_traits>
 
 #include "gemv_core.cuh"
+#include "mma_frag.cuh"
 #include "neko_common.cuh"
 #include "neko_internal.h"
 
@@ -31,58 +38,68 @@ constexpr int kTP = kTK + 8;   // padded row pitch of the converted tiles (halve
 constexpr int kTThreads = 128;
 constexpr int kTStages = 4;   // cp.async pipeline depth
 
-__device__ __forceinline__ void cp16(void* dst, const void* src, int src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void cp4(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-
-// Raw stage: W codes [BNW][kTK] (FP8 bytes / FP4 kTK / 2 bytes), scales [BNW][2] f16, activations [kTM][kTK] f32.
-template <int FMT, int BNW>
+// Raw stage: W codes [BNW][kTK] (FP8 bytes / FP4 kTK / 2 bytes), scales [BNW][2] f16, and the activations:
+// fp32 [kTM][kTK], or (split once per matmul beforehand) f16 hi and lo [2][kTM][kTP] read by ldmatrix in place.
+struct XsF32 {
+    float v[kTM][kTK];
+};
+struct XsHiLo {
+    __half v[2][kTM][kTP];
+};
+template <int FMT, int BNW, bool PRE>
 struct Stage {
     static constexpr int kCode = FMT == kFP8 ? kTK : kTK / 2;
     uint8_t w[BNW][kCode];
     uint16_t sc[BNW][2];
-    float x[kTM][kTK];
+    typename std::conditional<PRE, XsHiLo, XsF32>::type x;
 };
 
-template <int FMT, int BN, bool PAIR>
-__global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a) {
+// How a launch divides K and where its activations come from.
+struct TcSplit {
+    int ksplit;              // CTAs along K; > 1: partial tiles summed by the last CTA of the tile
+    int sper;                // K stages per split
+    const __half* xh;        // activations split into f16 hi / lo ([M][K] each), or null: split per stage
+    const __half* xl;
+    float* part;             // [ksplit][tiles][kTM][BNW] partial tiles
+    unsigned* tickets;       // [tiles], zero between launches
+};
+
+// x = hi + lo, both f16 (round to nearest): once per matmul when many CTAs read the same activations.
+__global__ void split_act_kernel(const float* __restrict__ x, int64_t x_stride, int M, int K, __half* __restrict__ xh,
+                                 __half* __restrict__ xl) {
+    pdl_wait();
+    const int64_t n = int64_t(M) * (K / 4);
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const int m = int(i / (K / 4)), k = 4 * int(i - int64_t(m) * (K / 4));
+        const float4 v = *reinterpret_cast<const float4*>(x + int64_t(m) * x_stride + k);
+        const __half2 h01 = __floats2half2_rn(v.x, v.y), h23 = __floats2half2_rn(v.z, v.w);
+        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+        const int64_t o = int64_t(m) * K + k;
+        *reinterpret_cast<uint2*>(xh + o) = make_uint2(h2u(h01), h2u(h23));
+        *reinterpret_cast<uint2*>(xl + o) = make_uint2(h2u(__floats2half2_rn(v.x - f01.x, v.y - f01.y)),
+                                                       h2u(__floats2half2_rn(v.z - f23.x, v.w - f23.y)));
+    }
+    pdl_trigger();
+}
+
+template <int FMT, int BN, bool PAIR, bool PRE>
+__global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a, const TcSplit sp) {
     constexpr int BNW = PAIR ? 2 * BN : BN;  // weight rows per CTA
     constexpr int NT = BNW / 8;              // n8 tiles per warp
-    using St = Stage<FMT, BNW>;
+    using St = Stage<FMT, BNW, PRE>;
     extern __shared__ __align__(128) uint8_t tsm[];
     St* raw = reinterpret_cast<St*>(tsm);                                        // [kTStages]
     __half* wh = reinterpret_cast<__half*>(tsm + kTStages * sizeof(St));         // [BNW][kTP] codes
-    __half* xhi = wh + BNW * kTP;                                                // [kTM][kTP]
-    __half* xlo = xhi + kTM * kTP;                                               // [kTM][kTP]
-    float* scs = reinterpret_cast<float*>(xlo + kTM * kTP);                      // [2][BNW] block scales
+    __half* xhi = wh + BNW * kTP;                                                // [kTM][kTP] (!PRE)
+    __half* xlo = xhi + kTM * kTP;                                               // [kTM][kTP] (!PRE)
+    float* scs = reinterpret_cast<float*>(PRE ? xhi : xlo + kTM * kTP);         // [2][BNW] block scales
     __shared__ unsigned long long keys[kTM];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kTM;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kTM, z = blockIdx.z;
+    const int mv = min(kTM, a.M - m0);  // activation rows of this tile
     const int cbytes = FMT == kFP8 ? a.K : a.K / 2;
-    const int nst = a.K / kTK;
+    const int s_begin = z * sp.sper, s_end = min(a.K / kTK, s_begin + sp.sper), nst = s_end - s_begin;
     constexpr float kCodeFactor = FMT == kFP8 ? kFp8HwFactor : kFp4Factor;  // code value -> engine decode
     pdl_wait();
     if (a.argmax && tid < kTM) keys[tid] = 0ull;
@@ -93,18 +110,26 @@ __global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a) {
         const int nc = min(n, a.rows - 1);
         return a.W + (int64_t(nc) + (PAIR && r >= BN ? a.pair_off : 0)) * a.row_bytes;
     };
-    auto issue = [&](int s) {
-        St& S = raw[s % kTStages];
+    auto issue = [&](int i_s) {  // i_s: stage index within this CTA's range
+        St& S = raw[i_s % kTStages];
+        const int s = s_begin + i_s;
         constexpr int kPieces = St::kCode / 16;  // 16-byte pieces of codes per row
         for (int i = tid; i < BNW * kPieces; i += kTThreads) {
             const int r = i / kPieces, q = i - r * kPieces;
             cp16(&S.w[r][16 * q], wrow(r) + s * St::kCode + 16 * q, 16);
         }
         for (int r = tid; r < BNW; r += kTThreads) cp4(&S.sc[r][0], wrow(r) + cbytes + 4 * s);
-        for (int i = tid; i < kTM * (kTK / 4); i += kTThreads) {
-            const int m = i / (kTK / 4), q = i - m * (kTK / 4);
-            const bool in = m0 + m < a.M;
-            cp16(&S.x[m][4 * q], in ? a.x + int64_t(m0 + m) * a.x_stride + s * kTK + 4 * q : a.x, in ? 16 : 0);
+        if constexpr (PRE) {  // hi / lo halves straight into their padded tiles
+            for (int i = tid; i < 2 * mv * (kTK / 8); i += kTThreads) {
+                const int h = i >= mv * (kTK / 8) ? 1 : 0, j = i - h * mv * (kTK / 8);
+                const int m = j / (kTK / 8), q = j - m * (kTK / 8);
+                cp16(&S.x.v[h][m][8 * q], (h ? sp.xl : sp.xh) + int64_t(m0 + m) * a.K + s * kTK + 8 * q, 16);
+            }
+        } else {
+            for (int i = tid; i < mv * (kTK / 4); i += kTThreads) {
+                const int m = i / (kTK / 4), q = i - m * (kTK / 4);
+                cp16(&S.x.v[m][4 * q], a.x + int64_t(m0 + m) * a.x_stride + s * kTK + 4 * q, 16);
+            }
         }
     };
 
@@ -118,10 +143,11 @@ __global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a) {
         cp_commit();
     }
     for (int s = 0; s < nst; s++) {
-        if (s + kTStages - 1 < nst) issue(s + kTStages - 1);
+        cp_wait<kTStages - 2>();  // stage s landed (this thread's copies)
+        __syncthreads();          // ... every thread's; and every warp is done with stage s - 1 (its buffer,
+                                  // which pre-split activations feed to the mma directly, and wh / xhi / xlo)
+        if (s + kTStages - 1 < nst) issue(s + kTStages - 1);  // into the buffer of stage s - 1
         cp_commit();
-        cp_wait<kTStages - 1>();  // stage s landed (this thread's copies)
-        __syncthreads();          // ... every thread's; and the previous stage's mma is done with wh / xhi / xlo
         const St& S = raw[s % kTStages];
         // codes -> f16 (exact)
         if (FMT == kFP8) {
@@ -156,10 +182,10 @@ __global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a) {
             scs[r] = __half2float(__ushort_as_half(S.sc[r][0])) * kCodeFactor;
             scs[BNW + r] = __half2float(__ushort_as_half(S.sc[r][1])) * kCodeFactor;
         }
-        // activations -> hi + lo f16
-        for (int i = tid; i < kTM * (kTK / 4); i += kTThreads) {
+        // activations -> hi + lo f16 (rows of the tile only; rows past mv only feed discarded outputs)
+        for (int i = tid; !PRE && i < mv * (kTK / 4); i += kTThreads) {
             const int m = i / (kTK / 4), q = i - m * (kTK / 4);
-            const float4 v = *reinterpret_cast<const float4*>(&S.x[m][4 * q]);
+            const float4 v = *reinterpret_cast<const float4*>(&reinterpret_cast<const XsF32&>(S.x).v[m][4 * q]);
             const __half2 h01 = __floats2half2_rn(v.x, v.y), h23 = __floats2half2_rn(v.z, v.w);
             const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
             *reinterpret_cast<uint2*>(xhi + m * kTP + 4 * q) = make_uint2(h2u(h01), h2u(h23));
@@ -170,8 +196,11 @@ __global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a) {
         __syncthreads();
         // tensor cores: per 32-block, exact partial sums of codes x (hi + lo), then the block scale in fp32
         const int c2 = 2 * (lane & 3);
+        const __half* ahi = PRE ? &reinterpret_cast<const XsHiLo&>(S.x).v[0][0][0] : xhi;
+        const __half* alo = PRE ? &reinterpret_cast<const XsHiLo&>(S.x).v[1][0][0] : xlo;
 #pragma unroll
         for (int blk = 0; blk < 2; blk++) {
+            if (16 * warp >= mv) break;  // no activation row of this warp
             float part[NT][4];
 #pragma unroll
             for (int t = 0; t < NT; t++) part[t][0] = part[t][1] = part[t][2] = part[t][3] = 0.0f;
@@ -179,8 +208,8 @@ __global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a) {
             for (int kk = 2 * blk; kk < 2 * blk + 2; kk++) {
                 uint32_t ah[4], al[4];
                 const int ao = (16 * warp + (lane & 15)) * kTP + 16 * kk + 8 * (lane >> 4);
-                ldsm_x4(ah, xhi + ao);
-                ldsm_x4(al, xlo + ao);
+                ldsm_x4(ah, ahi + ao);
+                ldsm_x4(al, alo + ao);
 #pragma unroll
                 for (int t = 0; t < NT; t += 2) {
                     uint32_t bf[4];
@@ -204,6 +233,48 @@ __global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a) {
 
     // epilogue: acc[t] holds rows (g, g + 8) x columns (2c, 2c + 1) of n8 tile t
     const int g = lane >> 2, c = lane & 3;
+    if (sp.ksplit > 1) {
+        // partial tile to the workspace; the last CTA of the tile (ticket) sums the splits in order 0..ksplit-1
+        const int tile = blockIdx.y * gridDim.x + blockIdx.x, ntiles = gridDim.x * gridDim.y;
+        auto at = [&](int zz, int t, int h) {  // columns 2c, 2c + 1 of row g + 8h of n8 tile t
+            return reinterpret_cast<float2*>(sp.part + ((int64_t(zz) * ntiles + tile) * kTM + 16 * warp + g + 8 * h) *
+                                                           BNW + 8 * t + 2 * c);
+        };
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            *at(z, t, 0) = make_float2(acc[t][0], acc[t][1]);
+            *at(z, t, 1) = make_float2(acc[t][2], acc[t][3]);
+        }
+        __threadfence();
+        __syncthreads();
+        __shared__ int last;
+        if (tid == 0) {
+            const unsigned tk = atomicAdd(sp.tickets + tile, 1u);
+            last = tk == unsigned(sp.ksplit - 1) ? 1 : 0;
+            if (last) sp.tickets[tile] = 0u;  // every split has its ticket: ready for the next launch
+        }
+        __syncthreads();
+        if (!last) {
+            pdl_trigger();
+            return;
+        }
+        __threadfence();
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int zz = 0; zz < sp.ksplit; zz++) {
+                const float2 p0 = __ldcg(at(zz, t, 0)), p1 = __ldcg(at(zz, t, 1));
+                v.x += p0.x;
+                v.y += p0.y;
+                v.z += p1.x;
+                v.w += p1.y;
+            }
+            acc[t][0] = v.x;
+            acc[t][1] = v.y;
+            acc[t][2] = v.z;
+            acc[t][3] = v.w;
+        }
+    }
     unsigned long long best[2] = {0ull, 0ull};
 #pragma unroll
     for (int t = 0; t < (PAIR ? NT / 2 : NT); t++) {
@@ -241,57 +312,132 @@ __global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a) {
     pdl_trigger();
 }
 
-using TcFn = void (*)(const GemvArgs);
+using TcFn = void (*)(const GemvArgs, const TcSplit);
 
-template <int FMT, int BN>
-TcFn pick_pair(bool pair) {
-    if constexpr (BN > 32) return tc_gemm_kernel<FMT, BN, false>;  // SwiGLU tiles take BN <= 32
-    else return pair ? tc_gemm_kernel<FMT, BN, true> : tc_gemm_kernel<FMT, BN, false>;
-}
-template <int FMT>
-TcFn pick_bn(int bn, bool pair) {
-    return bn == 16 ? pick_pair<FMT, 16>(pair) : bn == 32 ? pick_pair<FMT, 32>(pair) : pick_pair<FMT, 64>(pair);
+// CTA tiles: 64 weight rows, or 32 gate + 32 up rows for SwiGLU
+template <int FMT, bool PRE>
+TcFn pick(bool pair) {
+    return pair ? tc_gemm_kernel<FMT, 32, true, PRE> : tc_gemm_kernel<FMT, 64, false, PRE>;
 }
 
-template <int FMT, int BNW>
+template <int FMT, bool PRE>
 constexpr size_t tc_smem() {
-    return kTStages * sizeof(Stage<FMT, BNW>) + size_t(BNW + 2 * kTM) * kTP * 2 + 2 * BNW * 4;
+    return kTStages * sizeof(Stage<FMT, 64, PRE>) + size_t(PRE ? 64 : 64 + 2 * kTM) * kTP * 2 + 2 * 64 * 4;
 }
 
-size_t tc_smem_for(int fmt, int bn, bool pair) {
-    const int bnw = pair ? 2 * bn : bn;
-    if (fmt == kFP8)
-        return bnw == 16 ? tc_smem<kFP8, 16>() : bnw == 32 ? tc_smem<kFP8, 32>() : bnw == 64 ? tc_smem<kFP8, 64>()
-                                                                                           : tc_smem<kFP8, 128>();
-    return bnw == 16 ? tc_smem<kFP4, 16>() : bnw == 32 ? tc_smem<kFP4, 32>() : bnw == 64 ? tc_smem<kFP4, 64>()
-                                                                                     : tc_smem<kFP4, 128>();
+// Tile plan of a call: weight rows per CTA, row blocks, tiles, K splits (the workspace decides how many).
+struct TcPlan {
+    int bn, mblk, ntile, ksplit, sper;
+    bool presplit;
+    int64_t part_floats, x_floats;  // workspace: partial tiles, and hi / lo activations (as floats)
+};
+
+TcPlan tc_plan(const GemvArgs& a, int64_t ws_floats, int ntickets) {
+    TcPlan p;
+    const bool pair = a.pair_off != 0;
+    const int sms = num_sms(), nst = a.K / kTK;
+    p.mblk = (a.M + kTM - 1) / kTM;
+    p.bn = pair ? 32 : 64;  // at most 64 weight rows per CTA (the registers of the partial sums)
+    p.ntile = (a.rows + p.bn - 1) / p.bn;
+    const int64_t tiles = int64_t(p.ntile) * p.mblk;
+    // activations split once when at least 8 tiles share them
+    p.x_floats = int64_t(a.M) * a.K;  // hi + lo halves
+    p.presplit = p.ntile >= 8 && ws_floats >= p.x_floats;
+    const int64_t room = ws_floats - (p.presplit ? p.x_floats : 0);
+    // K splits: about two CTAs per SM, each with at least 4 stages
+    p.ksplit = 1;
+    if (tiles < 2 * sms && tiles <= ntickets) {
+        int ks = int(std::min<int64_t>((2 * sms + tiles - 1) / tiles, std::max(1, nst / 4)));
+        const int64_t per = tiles * kTM * (pair ? 2 * p.bn : p.bn);
+        while (ks > 1 && ks * per > room) ks--;
+        p.ksplit = std::max(1, ks);
+    }
+    p.sper = (nst + p.ksplit - 1) / p.ksplit;
+    p.ksplit = (nst + p.sper - 1) / p.sper;
+    p.part_floats = p.ksplit > 1 ? int64_t(p.ksplit) * tiles * kTM * (pair ? 2 * p.bn : p.bn) : 0;
+    return p;
+}
+
+size_t tc_smem_for(int fmt, bool pre) {
+    if (fmt == kFP8) return pre ? tc_smem<kFP8, true>() : tc_smem<kFP8, false>();
+    return pre ? tc_smem<kFP4, true>() : tc_smem<kFP4, false>();
 }
 
 }  // namespace
 
+bool gemm_tc_fits(const GemvArgs& a) {
+    return a.M >= 5 && (a.fmt == kFP8 || a.fmt == kFP4) && a.norm == kNormNone && a.K % kTK == 0 &&
+           a.x_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && a.row_bytes % 16 == 0 &&
+           !(a.pair_off && a.argmax);
+}
+
+namespace {
+GemvArgs shape_args(int fmt, int rows, int K, int M, bool pair) {
+    GemvArgs a;
+    a.fmt = fmt;
+    a.rows = rows;
+    a.K = K;
+    a.M = M;
+    a.x_stride = K;
+    a.row_bytes = 16;
+    a.pair_off = pair ? rows : 0;
+    return a;
+}
+}  // namespace
+
+int gemm_tc_launches(int fmt, int rows, int K, int M, bool pair) {
+    const GemvArgs a = shape_args(fmt, rows, K, M, pair);
+    if (!gemm_tc_fits(a)) return 0;
+    return tc_plan(a, int64_t(1) << 40, 1 << 30).presplit ? 2 : 1;
+}
+
+void gemm_tc_scratch(int fmt, int rows, int K, int M, bool pair, int64_t* floats, int64_t* tickets) {
+    *floats = 0;
+    *tickets = 0;
+    const GemvArgs a = shape_args(fmt, rows, K, M, pair);
+    if (!gemm_tc_fits(a)) return;
+    const TcPlan p = tc_plan(a, int64_t(1) << 40, 1 << 30);
+    *floats = (p.presplit ? p.x_floats : 0) + p.part_floats;
+    *tickets = p.ksplit > 1 ? int64_t(p.ntile) * p.mblk : 0;
+}
+
 // The tensor-core kernel takes 5+ activation rows of FP8 / FP4 weights without a norm prologue, K a multiple of
-// 64; cudaErrorNotSupported otherwise.
+// 64; cudaErrorNotSupported otherwise. a.ws (a.ws_floats floats, a.ws_tickets zeroed tickets) lets it split
+// K over more CTAs and split the activations once; without it the call still runs, with fewer CTAs.
 cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl) {
-    if (a.M < 5 || (a.fmt != kFP8 && a.fmt != kFP4) || a.norm != kNormNone || a.K % kTK) return cudaErrorNotSupported;
-    if (a.x_stride % 4 || (reinterpret_cast<uintptr_t>(a.x) & 15) || a.row_bytes % 16) return cudaErrorNotSupported;
+    if (!gemm_tc_fits(a)) return cudaErrorNotSupported;
     const bool pair = a.pair_off != 0;
-    if (pair && a.argmax) return cudaErrorNotSupported;
-    const int sms = num_sms();
-    const int mblk = (a.M + kTM - 1) / kTM;
-    int bn = pair ? 32 : 64;  // at most 64 weight rows per CTA (the registers of the partial sums)
-    while (bn > 16 && int64_t((a.rows + bn - 1) / bn) * mblk < sms) bn /= 2;
-    TcFn k = a.fmt == kFP8 ? pick_bn<kFP8>(bn, pair) : pick_bn<kFP4>(bn, pair);
-    const size_t smem = tc_smem_for(a.fmt, bn, pair);
-    static int attr_set[2 * 6 * 8] = {};  // per (format, BN, pair, device), device < 8
+    const TcPlan pl = tc_plan(a, a.ws ? a.ws_floats : 0, a.ws_tickets ? a.ws_ntickets : 0);
+    TcSplit sp{};
+    sp.ksplit = pl.ksplit;
+    sp.sper = pl.sper;
+    if (pl.presplit) {
+        sp.xh = reinterpret_cast<const __half*>(a.ws);
+        sp.xl = sp.xh + int64_t(a.M) * a.K;
+        const int64_t n4 = int64_t(a.M) * (a.K / 4);
+        const int blocks = int(std::min<int64_t>((n4 + 255) / 256, 4 * num_sms()));
+        const cudaError_t e = launch_ex(split_act_kernel, dim3(blocks), dim3(256), 0, st, pdl, a.x, a.x_stride, a.M,
+                                        a.K, const_cast<__half*>(sp.xh), const_cast<__half*>(sp.xl));
+        if (e != cudaSuccess) return e;
+    }
+    if (pl.ksplit > 1) {
+        sp.part = a.ws + (pl.presplit ? pl.x_floats : 0);
+        sp.tickets = a.ws_tickets;
+    }
+    const bool pre = pl.presplit;
+    TcFn k = a.fmt == kFP8 ? (pre ? pick<kFP8, true>(pair) : pick<kFP8, false>(pair))
+                           : (pre ? pick<kFP4, true>(pair) : pick<kFP4, false>(pair));
+    const size_t smem = tc_smem_for(a.fmt, pre);
+    static int attr_set[8 * 8] = {};  // per (format, pair, pre-split, device), device < 8
     int dev = 0;
     cudaGetDevice(&dev);
-    const int slot = ((a.fmt == kFP8 ? 0 : 1) * 6 + (bn == 16 ? 0 : bn == 32 ? 1 : 2) * 2 + (pair ? 1 : 0)) * 8 + dev;
+    const int slot = ((a.fmt == kFP8 ? 0 : 4) + (pair ? 2 : 0) + (pre ? 1 : 0)) * 8 + dev;
     if (dev >= 8 || attr_set[slot] < int(smem)) {
         const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         if (e != cudaSuccess) return e;
         if (dev < 8) attr_set[slot] = int(smem);
     }
-    return launch_ex(k, dim3((a.rows + bn - 1) / bn, mblk), dim3(kTThreads), smem, st, pdl, a);
+    return launch_ex(k, dim3(pl.ntile, pl.mblk, pl.ksplit), dim3(kTThreads), smem, st, pdl || pl.presplit, a, sp);
 }
 
 }  // namespace neko

@@ -102,6 +102,9 @@ struct neko_model {
     float* part = nullptr;
     unsigned* tickets = nullptr;
     int64_t part_cap = 0, tick_cap = 0;
+    float* mm_ws = nullptr;          // tensor-core matmul workspace (K splits, split activations)
+    unsigned* mm_tickets = nullptr;
+    int64_t mm_ws_floats = 0, mm_tickets_n = 0;
     size_t work_bytes = 0;
     // host pinned staging for the synchronous API
     int* h_in = nullptr;     // tokens | slots | pos | outrows  (4 * max_rows)
@@ -280,6 +283,10 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         a.y_stride = ys;
         a.pair_off = pair;
         a.argmax = keys;
+        a.ws = m->mm_ws;
+        a.ws_floats = m->mm_ws_floats;
+        a.ws_tickets = m->mm_tickets;
+        a.ws_ntickets = int(m->mm_tickets_n);
         return launch_gemv(a, st, pdl());
     };
     // norm (fused into the GEMV prologue when the activations fit in shared memory, else a separate kernel)
@@ -431,12 +438,31 @@ bool decode_ok(neko_model* m, int R) {
     return m->dec_ok[R] == 1;
 }
 
+// The matmuls of a step (format, output rows, K, SwiGLU pair), the LM head last.
+struct MatShape {
+    int fmt, rows, K;
+    bool pair, lm_head;
+};
+std::vector<MatShape> mat_shapes(const neko_model* m) {
+    const int K_att = m->H * m->hd;
+    std::vector<MatShape> v = {{fmt_for(m->C, m->fmt), m->QW, m->C, false, false},
+                               {fmt_for(K_att, m->fmt), m->C, K_att, false, false},
+                               {fmt_for(m->C, m->fmt), m->qwen ? m->F : m->UPW, m->C, m->qwen, false},
+                               {fmt_for(m->F, m->fmt), m->C, m->F, false, false},
+                               {m->embed.fmt, m->V, m->C, false, true}};
+    return v;
+}
+
 int step_launches(neko_model* m, int R, int nout, bool gather, bool do_argmax, bool advance) {
     if (!gather && nout == R && m->debug_layers < 0 && m->dec_enabled && R <= m->dec_seqs && decode_ok(m, R))
         return 1;
     const bool x_fits = gemv_norm_fusable(fmt_for(m->C, m->fmt), R, m->C);
-    const int per_layer = 6 + (x_fits ? 0 : 2);
+    int per_layer = 6 + (x_fits ? 0 : 2);
+    for (const MatShape& ms : mat_shapes(m))  // activation splits of tensor-core matmuls
+        if (!ms.lm_head) per_layer += std::max(0, gemm_tc_launches(ms.fmt, ms.rows, ms.K, R, ms.pair) - 1);
     int n = 1 + int(m->layers.size()) * per_layer + (gather ? 1 : 0);
+    for (const MatShape& ms : mat_shapes(m))
+        if (ms.lm_head) n += std::max(0, gemm_tc_launches(ms.fmt, ms.rows, ms.K, nout, ms.pair) - 1);
     n += gemv_norm_fusable(m->embed.fmt, nout, m->C) ? 1 : 2;
     return n + (do_argmax ? 1 : 0) + (advance && nout > 64 ? 1 : 0);
 }
@@ -703,6 +729,24 @@ neko_model* neko_model_create(int device, const neko_model_config* cfg, char* er
     if (falloc(&m->part, size_t(m->part_cap)) || cudaMalloc(&m->tickets, size_t(m->tick_cap) * 4))
         return bail(m, "attention scratch allocation failed");
     cudaMemset(m->tickets, 0, size_t(m->tick_cap) * 4);
+    // tensor-core matmul workspace: the largest any matmul asks for at any row count 5..max(R, seqs)
+    {
+        int64_t wf = 0, wt = 0;
+        for (int r = 5; r <= int(nout); r++)
+            for (const MatShape& ms : mat_shapes(m)) {
+                if (!ms.lm_head && r > int(R)) continue;
+                int64_t f = 0, t = 0;
+                gemm_tc_scratch(ms.fmt, ms.rows, ms.K, r, ms.pair, &f, &t);
+                wf = std::max(wf, f);
+                wt = std::max(wt, t);
+            }
+        m->mm_ws_floats = wf;
+        m->mm_tickets_n = wt;
+        if (wf > 0 && (falloc(&m->mm_ws, size_t(wf)) || cudaMalloc(&m->mm_tickets, size_t(std::max<int64_t>(wt, 1)) * 4)))
+            return bail(m, "matmul workspace allocation failed");
+        if (m->mm_tickets) cudaMemset(m->mm_tickets, 0, size_t(std::max<int64_t>(wt, 1)) * 4);
+        m->work_bytes += size_t(wt) * 4;
+    }
     // single-kernel decode steps: split-KV partials at the smallest span (32 keys), tickets, phase counters
     m->dec_seqs = std::min({kDecodeMaxSeqs, c.max_rows, c.max_seqs});
     m->dec_max_splits = (c.context + 31) / 32;
@@ -760,7 +804,7 @@ void neko_model_destroy(neko_model* m) {
     for (void* p : {(void*)m->warena, (void*)m->kc, (void*)m->vc, (void*)m->x, (void*)m->xn, (void*)m->qkv,
                     (void*)m->att, (void*)m->h, (void*)m->hx, (void*)m->logits, (void*)m->d_tokens, (void*)m->d_slots,
                     (void*)m->d_pos, (void*)m->d_argmax, (void*)m->d_outrows, (void*)m->d_keys, (void*)m->part,
-                    (void*)m->tickets, (void*)m->dec_part, (void*)m->dec_tickets, (void*)m->dec_sync,
+                    (void*)m->tickets, (void*)m->mm_ws, (void*)m->mm_tickets, (void*)m->dec_part, (void*)m->dec_tickets, (void*)m->dec_sync,
                     (void*)m->staging})
         if (p) cudaFree(p);
     if (m->h_in) cudaFreeHost(m->h_in);

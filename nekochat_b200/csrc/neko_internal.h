@@ -57,6 +57,11 @@ struct GemvArgs {
     int n_off = 0;
     int64_t pair_off = 0;        // != 0: out n = silu(row n) * row(n + pair_off)  (SwiGLU epilogue)
     unsigned long long* argmax = nullptr;  // M <= 64: per-row atomicMax of (value, ~index) keys (fused greedy argmax)
+    // tensor-core path (5+ rows): workspace for K splits and split activations, tickets zero between launches
+    float* ws = nullptr;
+    int64_t ws_floats = 0;
+    unsigned* ws_tickets = nullptr;
+    int ws_ntickets = 0;
     // launch plan (filled by plan_gemv)
     int x_smem = 0;
     int rows_per_cta = 0;
@@ -90,6 +95,12 @@ cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, bool pdl, int max_ctas = 0)
 cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl);
 // The tensor-core kernel for 5+ activation rows (k_mma.cu); cudaErrorNotSupported when the call does not fit.
 cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl);
+// Workspace (floats, tickets) with which launch_gemm_tc splits this matmul fully; 0, 0 when it takes no workspace
+// or the tensor-core path does not apply.
+void gemm_tc_scratch(int fmt, int rows, int K, int M, bool pair, int64_t* floats, int64_t* tickets);
+// Kernel launches of such a matmul with that workspace (the activation split and the GEMM), 0 when the
+// tensor-core path does not apply.
+int gemm_tc_launches(int fmt, int rows, int K, int M, bool pair);
 int gemv_launch_count();  // number of launches launch_gemv issues per call (1)
 
 // ------------------------------------------------------------------ other ops (k_ops.cu)

@@ -85,3 +85,33 @@ def test_tc_swiglu_pair(torch, R, fmt, M):
     h = R.matmul(fmt, x, q, K)
     want = R.silu_mul(h, F)
     close(y.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("fmt", [FP8, FP4])
+@pytest.mark.parametrize("M,K,N", [(7, 1344, 300), (64, 1344, 520), (130, 4096, 96), (9, 64, 2000)])
+def test_tc_matmul_uneven_k_splits(torch, R, fmt, M, K, N):
+    """K stage counts that the splits do not divide evenly (a short last split), a single K stage, row blocks
+    past 64 and split activations (8+ column tiles)."""
+    from nekochat_b200 import ops
+    rng = np.random.default_rng(M + K + N + fmt)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    q = R.quantize(fmt, w)
+    y = ops.matmul(fmt, cu(torch, x), cu(torch, q), K)
+    torch.cuda.synchronize()
+    close(y.cpu().numpy(), R.matmul(fmt, x, q, K))
+
+
+@pytest.mark.parametrize("fmt", [FP8, FP4])
+def test_tc_matmul_deterministic(torch, R, fmt):
+    """Split-K partial tiles are summed in split order by whichever CTA finishes last: repeated calls give
+    bit-identical results."""
+    from nekochat_b200 import ops
+    rng = np.random.default_rng(5 + fmt)
+    M, K, N = 48, 3072, 1024
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    xt = cu(torch, rng.standard_normal((M, K)).astype(np.float32))
+    qt = cu(torch, R.quantize(fmt, w))
+    first = ops.matmul(fmt, xt, qt, K).cpu().numpy()
+    for _ in range(4):
+        assert np.array_equal(ops.matmul(fmt, xt, qt, K).cpu().numpy(), first)
