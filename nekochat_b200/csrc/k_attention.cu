@@ -12,6 +12,7 @@
 // elected by a ticket counter that it resets (so the kernel can be replayed from a CUDA graph).
 #include <algorithm>
 
+#include "mma_frag.cuh"
 #include "neko_common.cuh"
 #include "neko_internal.h"
 
@@ -318,13 +319,232 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
     }
 }
 
+// ------------------------------------------------------------------------------------------------ tensor cores
+// The same work units and split-KV merge with the arithmetic on mma.sync m16n8k16 (f16 operands, fp32
+// accumulation), for head_dim 64 / 128 and up to 8 query heads per KV head:
+//  * the cache rows are f16 already, so keys and values enter the MMA exactly; the query and the probabilities
+//    are split into hi + lo f16 (about 22 bits, as in the matmul), so scores and P.V keep fp32-level accuracy;
+//  * MMA rows = the group's query heads (rows past G are zero), columns = 8 keys (scores) or 8 dims (P.V);
+//  * warp w owns keys 16w..16w+15 of each 64-key chunk with its own running max / sum (online softmax per
+//    warp, no block barrier inside a chunk); the score fragments of its two key tiles are exactly the A fragment
+//    of the P.V step. The four warps' (max, sum, acc) are merged once at the end of the split;
+//  * all threads stage the chunks with 16-byte cp.async into padded shared-memory rows (pitch hd + 8 halves,
+//    conflict-free ldmatrix; rows past the last key are zero-filled), three buffers, one barrier per chunk.
+constexpr int kTcChunk = 64;
+constexpr int kTcBufs = 3;
+
+template <int HD>
+constexpr int tc_attn_smem() {
+    return kTcBufs * 2 * kTcChunk * (HD + 8) * 2;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads, 2) attention_tc_kernel(const AttnArgs a, const Geometry geo) {
+    constexpr int P = HD + 8;  // padded row pitch (halves)
+    constexpr int CH = kTcChunk, KS = HD / 16, NTO = HD / 8;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint16_t* kvb = reinterpret_cast<uint16_t*>(smem);  // [kTcBufs][2][CH][P]: keys, then values
+    __shared__ int last;
+
+    const int split = blockIdx.x, kvh = blockIdx.y, r = blockIdx.z;
+    const int G = a.n_head / a.n_kv;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gr = lane >> 2, c = lane & 3;
+    pdl_wait();  // q and the newest cache rows come from the previous kernels
+    pdl_trigger();
+    const int pos = a.row_pos ? a.row_pos[r] : a.pos0 + r;
+    const int slot = a.row_slot ? a.row_slot[r] : a.slot0;
+    const int L = pos + 1;
+    if (pos < 0 || pos >= a.pos_limit || L > geo.splits * geo.span) {  // outside the planned key range
+        if (tid == 0 && split == 0) set_device_error(kErrBadIndex);
+        return;
+    }
+    const int active = (L + geo.span - 1) / geo.span;
+    if (split >= active) return;
+    const int j_begin = split * geo.span, j_end = min(L, j_begin + geo.span);
+    const int nchunks = (j_end - j_begin + CH - 1) / CH;
+    const uint16_t* kbase = a.kc + int64_t(slot) * a.slot_stride + int64_t(kvh) * a.head_stride;
+    const uint16_t* vbase = a.vc + int64_t(slot) * a.slot_stride + int64_t(kvh) * a.head_stride;
+    // every thread: its 16-byte pieces of chunk cc's key and value rows into buffer cc % kTcBufs (one commit group
+    // per chunk); rows past the chunk's last key are zero-filled without reading memory
+    auto issue = [&](int cc) {
+        const int j0 = j_begin + cc * CH, n = min(CH, j_end - j0);
+        uint16_t* dk = kvb + (cc % kTcBufs) * 2 * CH * P;
+        constexpr int PR = HD / 8;  // pieces per row
+#pragma unroll 4
+        for (int i = tid; i < 2 * CH * PR; i += kAttnThreads) {
+            const int v = i >= CH * PR ? 1 : 0, j = (i - v * CH * PR) / PR, q = i - v * CH * PR - j * PR;
+            const uint16_t* src = (v ? vbase : kbase) + int64_t(j0 + min(j, n - 1)) * a.pos_stride + 8 * q;
+            cp16(dk + (v * CH + j) * P + 8 * q, src, j < n ? 16 : 0);
+        }
+    };
+#pragma unroll
+    for (int cc = 0; cc < kTcBufs - 1; cc++) {
+        if (cc < nchunks) issue(cc);
+        cp_commit();
+    }
+
+    // query fragments (row gr = query head gr of the group; rows 8..15 and heads past G are zero)
+    uint32_t qh[KS][2], ql[KS][2];
+    {
+        const float* qrow = a.q + int64_t(r) * a.q_stride + int64_t(kvh * G + gr) * HD;
+#pragma unroll
+        for (int ks = 0; ks < KS; ks++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int d = 16 * ks + 8 * h + 2 * c;
+                const float x0 = gr < G ? qrow[d] : 0.0f, x1 = gr < G ? qrow[d + 1] : 0.0f;
+                split_hilo(x0, x1, qh[ks][h], ql[ks][h]);
+            }
+    }
+    float o[NTO][4];
+#pragma unroll
+    for (int t = 0; t < NTO; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+    float m_run = -INFINITY, l_part = 0.0f;  // row gr: running max; this lane's share of the running sum
+    const int k0 = 16 * warp;
+
+    for (int cc = 0; cc < nchunks; cc++) {
+        const int b = cc % kTcBufs, n = min(CH, j_end - (j_begin + cc * CH));
+        cp_wait<kTcBufs - 2>();  // chunk cc landed (this thread's pieces)
+        __syncthreads();         // ... every thread's; and every warp is done with chunk cc - 1's buffer
+        if (cc + kTcBufs - 1 < nchunks) issue(cc + kTcBufs - 1);
+        cp_commit();
+        if (k0 < n) {
+            const uint16_t* kb = kvb + b * 2 * CH * P;
+            const uint16_t* vb = kb + CH * P;
+            // scores of keys k0..k0+15: two n8 tiles
+            float s[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+#pragma unroll
+            for (int ks = 0; ks < KS; ks++) {
+                uint32_t bf[4];
+                ldsm_x4(bf, kb + (k0 + 8 * (lane >> 4) + (lane & 7)) * P + 16 * ks + 8 * ((lane >> 3) & 1));
+                const uint32_t ah[4] = {qh[ks][0], 0u, qh[ks][1], 0u}, al[4] = {ql[ks][0], 0u, ql[ks][1], 0u};
+                mma16816(s[0], ah, bf[0], bf[1]);
+                mma16816(s[0], al, bf[0], bf[1]);
+                mma16816(s[1], ah, bf[2], bf[3]);
+                mma16816(s[1], al, bf[2], bf[3]);
+            }
+            // online softmax for row gr over this warp's keys (4 lanes share a row)
+            float mx = -INFINITY;
+#pragma unroll
+            for (int t = 0; t < 2; t++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int key = k0 + 8 * t + 2 * c + e;
+                    s[t][e] = key < n ? s[t][e] * a.scale : -INFINITY;
+                    mx = fmaxf(mx, s[t][e]);
+                }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float m_new = fmaxf(m_run, mx);  // finite: key k0 < n is in every row's range
+            const float corr = expf(m_run - m_new);  // 0 on this warp's first keys (m_run = -inf)
+            l_part *= corr;
+#pragma unroll
+            for (int t = 0; t < NTO; t++) {
+                o[t][0] *= corr;
+                o[t][1] *= corr;
+            }
+            float p[2][2];
+#pragma unroll
+            for (int t = 0; t < 2; t++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    p[t][e] = expf(s[t][e] - m_new);
+                    l_part += p[t][e];
+                }
+            m_run = m_new;
+            // P.V: A = probabilities of keys k0..k0+15 (hi + lo), B = value rows (transposed fragments)
+            uint32_t ph[4], pl[4];
+            split_hilo(p[0][0], p[0][1], ph[0], pl[0]);
+            split_hilo(p[1][0], p[1][1], ph[2], pl[2]);
+            ph[1] = ph[3] = pl[1] = pl[3] = 0u;
+#pragma unroll
+            for (int t2 = 0; t2 < NTO / 2; t2++) {
+                uint32_t vf[4];
+                ldsm_x4_trans(vf, vb + (k0 + (lane & 7) + 8 * ((lane >> 3) & 1)) * P + 16 * t2 + 8 * (lane >> 4));
+                mma16816(o[2 * t2], ph, vf[0], vf[1]);
+                mma16816(o[2 * t2], pl, vf[0], vf[1]);
+                mma16816(o[2 * t2 + 1], ph, vf[2], vf[3]);
+                mma16816(o[2 * t2 + 1], pl, vf[2], vf[3]);
+            }
+        }
+    }
+
+    // merge the four warps (the buffers are free once every warp is past its last chunk)
+    __syncthreads();
+    l_part += __shfl_xor_sync(0xffffffffu, l_part, 1);
+    l_part += __shfl_xor_sync(0xffffffffu, l_part, 2);
+    float* wm = reinterpret_cast<float*>(smem);  // [4][8] max
+    float* wl = wm + 32;                         // [4][8] sum
+    float* wo = wl + 32;                         // [4][8][HD] acc
+    if (gr < G) {
+        if (c == 0) {
+            wm[warp * 8 + gr] = m_run;
+            wl[warp * 8 + gr] = l_part;
+        }
+#pragma unroll
+        for (int t = 0; t < NTO; t++)
+            *reinterpret_cast<float2*>(wo + (warp * 8 + gr) * HD + 8 * t + 2 * c) = make_float2(o[t][0], o[t][1]);
+    }
+    __syncthreads();
+    const bool split_mode = active > 1;
+    const int64_t rec = HD + 2;
+    for (int i = tid; i < G * HD; i += kAttnThreads) {
+        const int g = i / HD, d = i - g * HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; w++) M = fmaxf(M, wm[w * 8 + g]);
+        float num = 0.0f, den = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            const float f = expf(wm[w * 8 + g] - M);  // 0 for a warp that saw no keys (max -inf)
+            num += f * wo[(w * 8 + g) * HD + d];
+            den += f * wl[w * 8 + g];
+        }
+        if (!split_mode) {
+            a.out[int64_t(r) * a.out_stride + int64_t(kvh * G + g) * HD + d] = num / den;
+        } else {
+            float* pr = a.part + ((int64_t(r) * a.n_head + kvh * G + g) * geo.splits + split) * rec;
+            if (d == 0) {
+                pr[0] = M;
+                pr[1] = den;
+            }
+            pr[2 + d] = num;
+        }
+    }
+    if (!split_mode) return;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        unsigned* t = a.tickets + int64_t(r) * a.n_kv + kvh;
+        const unsigned ticket = atomicAdd(t, 1u);
+        last = ticket == unsigned(active - 1);
+        if (last) *t = 0u;  // every CTA of this (row, KV head) has taken its ticket: reset for the next launch
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int i = tid; i < G * HD; i += kAttnThreads) {
+        const int g = i / HD, d = i - g * HD;
+        const float* base = a.part + (int64_t(r) * a.n_head + kvh * G + g) * geo.splits * rec;
+        float M = -INFINITY;
+        for (int sp = 0; sp < active; sp++) M = fmaxf(M, __ldcg(base + sp * rec));
+        float num = 0.0f, den = 0.0f;
+        for (int sp = 0; sp < active; sp++) {
+            const float w = expf(__ldcg(base + sp * rec) - M);
+            den += __ldcg(base + sp * rec + 1) * w;
+            num += __ldcg(base + sp * rec + 2 + d) * w;
+        }
+        a.out[int64_t(r) * a.out_stride + int64_t(kvh * G + g) * HD + d] = num / den;
+    }
+}
+
 Geometry plan(int rows, int n_kv, int max_pos, int G, int hd) {
     const int L = max_pos + 1;
     const int sms = num_sms();
     Geometry g;
     g.chunk = chunk_for(hd);
-    // enough CTAs for two waves over the SMs, at least one chunk of keys per split
-    const int want = std::max(1, (2 * sms + rows * n_kv - 1) / (rows * n_kv));
+    // about eight CTAs per SM (several waves, so the last one is short), at least two chunks of keys per split
+    const int want = std::max(1, std::min((8 * sms + rows * n_kv - 1) / (rows * n_kv), L / (2 * g.chunk)));
     int span = (L + want - 1) / want;
     span = std::max(g.chunk, (span + g.chunk - 1) / g.chunk * g.chunk);
     g.span = span;
@@ -354,6 +574,21 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl) {
         const int64_t need = int64_t(a.rows) * a.n_head * g.splits * (a.hd + 2);
         if (!a.part || !a.tickets || need > a.part_capacity || int64_t(a.rows) * a.n_kv > a.ticket_capacity)
             return cudaErrorInvalidValue;
+    }
+    const int G = a.n_head / a.n_kv;
+    if ((a.hd == 64 || a.hd == 128) && G <= 8 && kTcChunk == g.chunk) {  // tensor-core kernel
+        auto k = a.hd == 128 ? attention_tc_kernel<128> : attention_tc_kernel<64>;
+        const int smem = a.hd == 128 ? tc_attn_smem<128>() : tc_attn_smem<64>();
+        static int attr_tc[2][8] = {};  // per head_dim, device < 8
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev >= 8 || !attr_tc[a.hd == 128][dev]) {
+            if (cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                e != cudaSuccess)
+                return e;
+            if (dev < 8) attr_tc[a.hd == 128][dev] = 1;
+        }
+        return launch_ex(k, dim3(g.splits, a.n_kv, a.rows), dim3(kAttnThreads), size_t(smem), st, pdl, a, g);
     }
     static bool attr = false;
     if (!attr) {

@@ -13,13 +13,16 @@
 //    through a 4-deep cp.async pipeline; per stage the CTA converts the codes once into padded shared memory;
 //    4 warps, warp w owns activation rows 16w..16w+15 of the tile (warps without rows skip the math),
 //    ldmatrix.x4 fragments, all 64 columns;
-//  * when the tiles alone leave SMs idle, K is split over up to ~2 CTAs per SM: partial tiles go to a workspace
-//    and the tile's last CTA (atomic ticket) sums them in split order 0, 1, ... (deterministic) before the
-//    epilogue;
+//  * when the tiles alone leave SMs idle, K is split over a thread-block cluster of up to 8 CTAs: each leaves
+//    its fp32 partial tile in its own shared memory, and after a cluster barrier CTA z sums rows z, z + ks, ...
+//    of the tile over the cluster's shared memory (distributed shared memory) in split order 0, 1, ...
+//    (deterministic) and runs the epilogue for them;
 //  * when 8+ tiles share the activations, one small kernel splits them into hi / lo f16 first, and the stages
 //    copy those straight into the padded tiles (otherwise every CTA splits its own fp32 copy).
 // Activations must stay within the f16 range (|x| < 65504), which the matmul inputs of the models are
 // (normalised activations, attention outputs, SwiGLU products).
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <type_traits>
 
@@ -54,14 +57,14 @@ struct Stage {
     typename std::conditional<PRE, XsHiLo, XsF32>::type x;
 };
 
+constexpr int kTMaxSplit = 8;  // CTAs of a cluster (portable limit)
+
 // How a launch divides K and where its activations come from.
 struct TcSplit {
-    int ksplit;              // CTAs along K; > 1: partial tiles summed by the last CTA of the tile
+    int ksplit;              // CTAs along K = the cluster's size; partial tiles summed over distributed smem
     int sper;                // K stages per split
     const __half* xh;        // activations split into f16 hi / lo ([M][K] each), or null: split per stage
     const __half* xl;
-    float* part;             // [ksplit][tiles][kTM][BNW] partial tiles
-    unsigned* tickets;       // [tiles], zero between launches
 };
 
 // x = hi + lo, both f16 (round to nearest): once per matmul when many CTAs read the same activations.
@@ -231,62 +234,48 @@ __global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a, co
         }
     }
 
-    // epilogue: acc[t] holds rows (g, g + 8) x columns (2c, 2c + 1) of n8 tile t
+    // epilogue. acc[t] holds rows (g, g + 8) x columns (2c, 2c + 1) of n8 tile t: to a row-major fp32 tile in
+    // this CTA's shared memory (the stage buffers are free once every warp is past its last stage)
     const int g = lane >> 2, c = lane & 3;
-    if (sp.ksplit > 1) {
-        // partial tile to the workspace; the last CTA of the tile (ticket) sums the splits in order 0..ksplit-1
-        const int tile = blockIdx.y * gridDim.x + blockIdx.x, ntiles = gridDim.x * gridDim.y;
-        auto at = [&](int zz, int t, int h) {  // columns 2c, 2c + 1 of row g + 8h of n8 tile t
-            return reinterpret_cast<float2*>(sp.part + ((int64_t(zz) * ntiles + tile) * kTM + 16 * warp + g + 8 * h) *
-                                                           BNW + 8 * t + 2 * c);
-        };
+    constexpr int TPF = BNW + 4;  // padded row pitch (floats)
+    static_assert(kTM * TPF * 4 <= kTStages * sizeof(St), "partial tile fits the stage buffers");
+    __syncthreads();
+    float* tile = reinterpret_cast<float*>(tsm);
+    if (16 * warp < mv) {
 #pragma unroll
         for (int t = 0; t < NT; t++) {
-            *at(z, t, 0) = make_float2(acc[t][0], acc[t][1]);
-            *at(z, t, 1) = make_float2(acc[t][2], acc[t][3]);
-        }
-        __threadfence();
-        __syncthreads();
-        __shared__ int last;
-        if (tid == 0) {
-            const unsigned tk = atomicAdd(sp.tickets + tile, 1u);
-            last = tk == unsigned(sp.ksplit - 1) ? 1 : 0;
-            if (last) sp.tickets[tile] = 0u;  // every split has its ticket: ready for the next launch
-        }
-        __syncthreads();
-        if (!last) {
-            pdl_trigger();
-            return;
-        }
-        __threadfence();
-#pragma unroll
-        for (int t = 0; t < NT; t++) {
-            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            for (int zz = 0; zz < sp.ksplit; zz++) {
-                const float2 p0 = __ldcg(at(zz, t, 0)), p1 = __ldcg(at(zz, t, 1));
-                v.x += p0.x;
-                v.y += p0.y;
-                v.z += p1.x;
-                v.w += p1.y;
-            }
-            acc[t][0] = v.x;
-            acc[t][1] = v.y;
-            acc[t][2] = v.z;
-            acc[t][3] = v.w;
+            *reinterpret_cast<float2*>(tile + (16 * warp + g) * TPF + 8 * t + 2 * c) = make_float2(acc[t][0], acc[t][1]);
+            *reinterpret_cast<float2*>(tile + (16 * warp + g + 8) * TPF + 8 * t + 2 * c) =
+                make_float2(acc[t][2], acc[t][3]);
         }
     }
-    unsigned long long best[2] = {0ull, 0ull};
+    namespace cg = cooperative_groups;
+    const int ks = sp.ksplit;
+    if (ks > 1) cg::this_cluster().sync();  // every split's partial tile is in place
+    else __syncthreads();
+    // rows z, z + ks, ... of the tile: sums over the splits in order, then bias / GELU / accumulate or SiLU * up
+    constexpr int OC = PAIR ? BN : BNW;  // output columns of the tile
+    const float* peer[kTMaxSplit];
 #pragma unroll
-    for (int t = 0; t < (PAIR ? NT / 2 : NT); t++) {
+    for (int zz = 0; zz < kTMaxSplit; zz++)
+        peer[zz] = zz < ks ? (ks > 1 ? cg::this_cluster().map_shared_rank(tile, zz) : tile) : tile;
+    const int nrow = (mv - z + ks - 1) / ks;  // rows of this CTA
+    static_assert(OC % 32 == 0, "a warp's 32 elements share a row");
+    for (int i = tid; i < nrow * OC; i += kTThreads) {
+        const int row = z + ks * (i / OC), col = i - (i / OC) * OC;
+        const int m = m0 + row, n = n0 + col;
+        float v = 0.0f, u = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const int mr = 16 * warp + g + (e >= 2 ? 8 : 0), m = m0 + mr;
-            const int n = n0 + 8 * t + 2 * c + (e & 1);
-            if (m >= a.M || n >= a.rows) continue;
+        for (int zz = 0; zz < kTMaxSplit; zz++) {
+            if (zz >= ks) break;
+            v += peer[zz][row * TPF + col];
+            if (PAIR) u += peer[zz][row * TPF + BN + col];
+        }
+        unsigned long long key = 0ull;
+        if (n < a.rows) {
             float* dst = a.y + int64_t(m) * a.y_stride + a.n_off + n;
-            float val = acc[t][e];
+            float val = v;
             if (PAIR) {
-                const float u = acc[t + NT / 2][e];
                 val = val / (1.0f + expf(-val)) * u;  // cpu::siluMul (cpu_ops.cpp:526-533)
             } else {
                 if (a.flags & kBias) val += a.bias[n];
@@ -294,21 +283,19 @@ __global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a, co
                 if (a.flags & kAccumulate) val += *dst;
             }
             *dst = val;
-            if (a.argmax) best[e >> 1] = max(best[e >> 1], argmax_key(val, n));
+            key = argmax_key(val, n);
         }
-    }
-    if (a.argmax) {  // rows g and g + 8: the 4 lanes of a row, then one shared and one global atomic per row
-        __syncthreads();
+        if (a.argmax) {  // the warp's 32 columns of the row, then one shared atomic
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            unsigned long long k = best[h];
-            k = max(k, __shfl_xor_sync(0xffffffffu, k, 1));
-            k = max(k, __shfl_xor_sync(0xffffffffu, k, 2));
-            if (c == 0 && k) atomicMax(&keys[16 * warp + g + 8 * h], k);
+            for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+            if (lane == 0 && key) atomicMax(&keys[row], key);
         }
-        __syncthreads();
-        if (tid < kTM && m0 + tid < a.M && keys[tid]) atomicMax(a.argmax + m0 + tid, keys[tid]);
     }
+    if (a.argmax) {  // one global atomic per row of this CTA
+        __syncthreads();
+        if (tid < nrow && keys[z + ks * tid]) atomicMax(a.argmax + m0 + z + ks * tid, keys[z + ks * tid]);
+    }
+    if (ks > 1) cg::this_cluster().sync();  // no CTA leaves while a peer may still read its tile
     pdl_trigger();
 }
 
@@ -329,10 +316,10 @@ constexpr size_t tc_smem() {
 struct TcPlan {
     int bn, mblk, ntile, ksplit, sper;
     bool presplit;
-    int64_t part_floats, x_floats;  // workspace: partial tiles, and hi / lo activations (as floats)
+    int64_t x_floats;  // workspace: hi / lo activations (as floats)
 };
 
-TcPlan tc_plan(const GemvArgs& a, int64_t ws_floats, int ntickets) {
+TcPlan tc_plan(const GemvArgs& a, int64_t ws_floats) {
     TcPlan p;
     const bool pair = a.pair_off != 0;
     const int sms = num_sms(), nst = a.K / kTK;
@@ -343,18 +330,12 @@ TcPlan tc_plan(const GemvArgs& a, int64_t ws_floats, int ntickets) {
     // activations split once when at least 8 tiles share them
     p.x_floats = int64_t(a.M) * a.K;  // hi + lo halves
     p.presplit = p.ntile >= 8 && ws_floats >= p.x_floats;
-    const int64_t room = ws_floats - (p.presplit ? p.x_floats : 0);
-    // K splits: about two CTAs per SM, each with at least 4 stages
+    // K splits (one cluster per tile): about two CTAs per SM, each with at least 2 stages
     p.ksplit = 1;
-    if (tiles < 2 * sms && tiles <= ntickets) {
-        int ks = int(std::min<int64_t>((2 * sms + tiles - 1) / tiles, std::max(1, nst / 4)));
-        const int64_t per = tiles * kTM * (pair ? 2 * p.bn : p.bn);
-        while (ks > 1 && ks * per > room) ks--;
-        p.ksplit = std::max(1, ks);
-    }
+    if (tiles < 2 * sms)
+        p.ksplit = int(std::min<int64_t>({(2 * sms + tiles - 1) / tiles, int64_t(kTMaxSplit), std::max(1, nst / 2)}));
     p.sper = (nst + p.ksplit - 1) / p.ksplit;
-    p.ksplit = (nst + p.sper - 1) / p.sper;
-    p.part_floats = p.ksplit > 1 ? int64_t(p.ksplit) * tiles * kTM * (pair ? 2 * p.bn : p.bn) : 0;
+    p.ksplit = (nst + p.sper - 1) / p.sper;  // no empty split
     return p;
 }
 
@@ -388,7 +369,7 @@ GemvArgs shape_args(int fmt, int rows, int K, int M, bool pair) {
 int gemm_tc_launches(int fmt, int rows, int K, int M, bool pair) {
     const GemvArgs a = shape_args(fmt, rows, K, M, pair);
     if (!gemm_tc_fits(a)) return 0;
-    return tc_plan(a, int64_t(1) << 40, 1 << 30).presplit ? 2 : 1;
+    return tc_plan(a, int64_t(1) << 40).presplit ? 2 : 1;
 }
 
 void gemm_tc_scratch(int fmt, int rows, int K, int M, bool pair, int64_t* floats, int64_t* tickets) {
@@ -396,18 +377,17 @@ void gemm_tc_scratch(int fmt, int rows, int K, int M, bool pair, int64_t* floats
     *tickets = 0;
     const GemvArgs a = shape_args(fmt, rows, K, M, pair);
     if (!gemm_tc_fits(a)) return;
-    const TcPlan p = tc_plan(a, int64_t(1) << 40, 1 << 30);
-    *floats = (p.presplit ? p.x_floats : 0) + p.part_floats;
-    *tickets = p.ksplit > 1 ? int64_t(p.ntile) * p.mblk : 0;
+    const TcPlan p = tc_plan(a, int64_t(1) << 40);
+    *floats = p.presplit ? p.x_floats : 0;
 }
 
 // The tensor-core kernel takes 5+ activation rows of FP8 / FP4 weights without a norm prologue, K a multiple of
-// 64; cudaErrorNotSupported otherwise. a.ws (a.ws_floats floats, a.ws_tickets zeroed tickets) lets it split
-// K over more CTAs and split the activations once; without it the call still runs, with fewer CTAs.
+// 64; cudaErrorNotSupported otherwise. a.ws (a.ws_floats floats) lets it split the activations once; without it
+// every CTA splits its own copy.
 cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl) {
     if (!gemm_tc_fits(a)) return cudaErrorNotSupported;
     const bool pair = a.pair_off != 0;
-    const TcPlan pl = tc_plan(a, a.ws ? a.ws_floats : 0, a.ws_tickets ? a.ws_ntickets : 0);
+    const TcPlan pl = tc_plan(a, a.ws ? a.ws_floats : 0);
     TcSplit sp{};
     sp.ksplit = pl.ksplit;
     sp.sper = pl.sper;
@@ -419,10 +399,6 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl) {
         const cudaError_t e = launch_ex(split_act_kernel, dim3(blocks), dim3(256), 0, st, pdl, a.x, a.x_stride, a.M,
                                         a.K, const_cast<__half*>(sp.xh), const_cast<__half*>(sp.xl));
         if (e != cudaSuccess) return e;
-    }
-    if (pl.ksplit > 1) {
-        sp.part = a.ws + (pl.presplit ? pl.x_floats : 0);
-        sp.tickets = a.ws_tickets;
     }
     const bool pre = pl.presplit;
     TcFn k = a.fmt == kFP8 ? (pre ? pick<kFP8, true>(pair) : pick<kFP8, false>(pair))
@@ -437,7 +413,28 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl) {
         if (e != cudaSuccess) return e;
         if (dev < 8) attr_set[slot] = int(smem);
     }
-    return launch_ex(k, dim3(pl.ntile, pl.mblk, pl.ksplit), dim3(kTThreads), smem, st, pdl || pl.presplit, a, sp);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(pl.ntile, pl.mblk, pl.ksplit);
+    cfg.blockDim = dim3(kTThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl || pl.presplit) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (pl.ksplit > 1) {  // the K splits of a tile form one cluster
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = pl.ksplit;
+        na++;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, k, a, sp);
 }
 
 }  // namespace neko

@@ -127,7 +127,8 @@ def test_softmax_argmax(torch, R, C, rows):
 
 
 @pytest.mark.parametrize("H,KV,hd,T,pos0", [(16, 8, 128, 1, 700), (4, 2, 64, 3, 1030), (12, 12, 64, 5, 0),
-                                            (32, 8, 128, 1, 4000), (8, 8, 128, 64, 200)])
+                                            (32, 8, 128, 1, 4000), (8, 8, 128, 64, 200), (32, 4, 128, 3, 63),
+                                            (8, 1, 64, 2, 127), (4, 4, 32, 4, 90)])
 def test_attention_op(torch, R, H, KV, hd, T, pos0):
     from nekochat_b200 import ops
     rng = np.random.default_rng(pos0 + T)
