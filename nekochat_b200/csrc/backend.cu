@@ -137,7 +137,7 @@ cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t st) {
 // memory the call still runs, on fewer CTAs.
 cudaError_t launch_gemv_op(GemvArgs a, cudaStream_t st, bool pdl) {
     int64_t wf = 0, wt = 0;
-    if (a.M >= 5 && a.norm == kNormNone) gemm_tc_scratch(a.fmt, a.rows, a.K, a.M, a.pair_off != 0, &wf, &wt);
+    if (a.M >= 5) gemm_tc_scratch(a.fmt, a.rows, a.K, a.M, a.pair_off != 0, a.norm != kNormNone, &wf, &wt);
     if (wf == 0) return launch_gemv(a, st, pdl);
     const size_t fb = (size_t(wf) * 4 + 255) / 256 * 256, tb = size_t(wt) * 4;
     void* mem = nullptr;

@@ -412,17 +412,29 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_tc_kernel(const Att
             const uint16_t* kb = kvb + b * 2 * CH * P;
             const uint16_t* vb = kb + CH * P;
             // scores of keys k0..k0+15: two n8 tiles
-            float s[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+            // four independent accumulators (tile x hi/lo) so consecutive MMAs do not wait on each other
+            float s[2][4], sl[2][4];
 #pragma unroll
             for (int ks = 0; ks < KS; ks++) {
                 uint32_t bf[4];
                 ldsm_x4(bf, kb + (k0 + 8 * (lane >> 4) + (lane & 7)) * P + 16 * ks + 8 * ((lane >> 3) & 1));
                 const uint32_t ah[4] = {qh[ks][0], 0u, qh[ks][1], 0u}, al[4] = {ql[ks][0], 0u, ql[ks][1], 0u};
-                mma16816(s[0], ah, bf[0], bf[1]);
-                mma16816(s[0], al, bf[0], bf[1]);
-                mma16816(s[1], ah, bf[2], bf[3]);
-                mma16816(s[1], al, bf[2], bf[3]);
+                if (ks == 0) {
+                    mma16816_z(s[0], ah, bf[0], bf[1]);
+                    mma16816_z(s[1], ah, bf[2], bf[3]);
+                    mma16816_z(sl[0], al, bf[0], bf[1]);
+                    mma16816_z(sl[1], al, bf[2], bf[3]);
+                } else {
+                    mma16816(s[0], ah, bf[0], bf[1]);
+                    mma16816(s[1], ah, bf[2], bf[3]);
+                    mma16816(sl[0], al, bf[0], bf[1]);
+                    mma16816(sl[1], al, bf[2], bf[3]);
+                }
             }
+#pragma unroll
+            for (int t = 0; t < 2; t++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) s[t][e] += sl[t][e];
             // online softmax for row gr over this warp's keys (4 lanes share a row)
             float mx = -INFINITY;
 #pragma unroll
@@ -462,8 +474,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_tc_kernel(const Att
                 uint32_t vf[4];
                 ldsm_x4_trans(vf, vb + (k0 + (lane & 7) + 8 * ((lane >> 3) & 1)) * P + 16 * t2 + 8 * (lane >> 4));
                 mma16816(o[2 * t2], ph, vf[0], vf[1]);
-                mma16816(o[2 * t2], pl, vf[0], vf[1]);
                 mma16816(o[2 * t2 + 1], ph, vf[2], vf[3]);
+                mma16816(o[2 * t2], pl, vf[0], vf[1]);
                 mma16816(o[2 * t2 + 1], pl, vf[2], vf[3]);
             }
         }

@@ -11,8 +11,9 @@
 //    two MMAs per step, about 22 bits of each activation kept (fp32 has 24), products exact in fp32;
 //  * CTA tile: 64 activation rows x 64 weight rows (SwiGLU: 32 gate + 32 up rows); K walked in stages of 64
 //    through a 4-deep cp.async pipeline; per stage the CTA converts the codes once into padded shared memory;
-//    4 warps, warp w owns activation rows 16w..16w+15 of the tile (warps without rows skip the math),
-//    ldmatrix.x4 fragments, all 64 columns;
+//    8 warps: warp w owns activation rows 16(w % 4)..+15 and weight rows 32(w / 4)..+31 of the tile (warps
+//    without activation rows skip the math), ldmatrix.x4 fragments; two warps per scheduler per CTA and two
+//    CTAs per SM hide the MMA and shared-memory latencies;
 //  * when the tiles alone leave SMs idle, K is split over a thread-block cluster of up to 8 CTAs: each leaves
 //    its fp32 partial tile in its own shared memory, and after a cluster barrier CTA z sums rows z, z + ks, ...
 //    of the tile over the cluster's shared memory (distributed shared memory) in split order 0, 1, ...
@@ -38,7 +39,7 @@ namespace {
 constexpr int kTM = 64;        // activation rows per CTA
 constexpr int kTK = 64;        // K per stage
 constexpr int kTP = kTK + 8;   // padded row pitch of the converted tiles (halves): ldmatrix without conflicts
-constexpr int kTThreads = 128;
+constexpr int kTThreads = 256;
 constexpr int kTStages = 4;   // cp.async pipeline depth
 
 // Raw stage: W codes [BNW][kTK] (FP8 bytes / FP4 kTK / 2 bytes), scales [BNW][2] f16, and the activations:
@@ -85,10 +86,71 @@ __global__ void split_act_kernel(const float* __restrict__ x, int64_t x_stride, 
     pdl_trigger();
 }
 
+// RMSNorm / LayerNorm of each activation row (norm_kernel's arithmetic: sums in double, cpu_ops.cpp:483-511),
+// written as hi / lo f16 for the matmul: one CTA per row, the row read once into shared memory.
+constexpr int kNsThreads = 256;
+constexpr int kNsMaxK = 10240;  // row cached in static shared memory (40 KB)
+__global__ void __launch_bounds__(kNsThreads) norm_split_kernel(const GemvArgs a, __half* __restrict__ xh,
+                                                                __half* __restrict__ xl) {
+    __shared__ float row[kNsMaxK];
+    __shared__ double red[kNsThreads / 32];
+    pdl_wait();
+    const float* xr = a.x + int64_t(blockIdx.x) * a.x_stride;
+    const int K = a.K;
+    auto block_sum = [&](double v) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+        __syncthreads();
+        if (l == 0) red[w] = v;
+        __syncthreads();
+        double t = l < kNsThreads / 32 ? red[l] : 0.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        return t;
+    };
+    double s1 = 0.0, s2 = 0.0;
+    for (int c = threadIdx.x; c < K; c += kNsThreads) {
+        const float v = xr[c];
+        row[c] = v;
+        s1 += v;
+        s2 += double(v) * v;
+    }
+    const bool rms = a.norm == kNormRms;
+    float r, mean = 0.0f;
+    if (rms) {
+        r = float(1.0 / sqrt(block_sum(s2) / K + double(a.eps)));
+    } else {
+        const double mu = block_sum(s1) / K;
+        double var = 0.0;
+        for (int c = threadIdx.x; c < K; c += kNsThreads) {
+            const double d = row[c] - mu;
+            var += d * d;
+        }
+        r = float(1.0 / sqrt(block_sum(var) / K + double(a.eps)));
+        mean = float(mu);
+    }
+    pdl_trigger();
+    for (int c = 2 * threadIdx.x; c < K; c += 2 * kNsThreads) {
+        float y[2];
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const float v = row[c + e];
+            y[e] = rms ? __fmul_rn(__fmul_rn(v, r), a.gamma[c + e])
+                       : __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, mean), r), a.gamma[c + e]), a.beta[c + e]);
+        }
+        uint32_t hi, lo;
+        split_hilo(y[0], y[1], hi, lo);
+        const int64_t o = int64_t(blockIdx.x) * K + c;
+        *reinterpret_cast<uint32_t*>(xh + o) = hi;
+        *reinterpret_cast<uint32_t*>(xl + o) = lo;
+    }
+}
+
 template <int FMT, int BN, bool PAIR, bool PRE>
-__global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a, const TcSplit sp) {
+__global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a, const TcSplit sp) {
     constexpr int BNW = PAIR ? 2 * BN : BN;  // weight rows per CTA
-    constexpr int NT = BNW / 8;              // n8 tiles per warp
+    constexpr int NT = BNW / 16;             // n8 tiles per warp (half of the tile's columns)
     using St = Stage<FMT, BNW, PRE>;
     extern __shared__ __align__(128) uint8_t tsm[];
     St* raw = reinterpret_cast<St*>(tsm);                                        // [kTStages]
@@ -99,6 +161,7 @@ __global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a, co
     __shared__ unsigned long long keys[kTM];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wm = warp & 3, wn = warp >> 2;  // activation rows 16 wm.., weight rows (columns) 8 NT wn..
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kTM, z = blockIdx.z;
     const int mv = min(kTM, a.M - m0);  // activation rows of this tile
     const int cbytes = FMT == kFP8 ? a.K : a.K / 2;
@@ -203,29 +266,30 @@ __global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a, co
         const __half* alo = PRE ? &reinterpret_cast<const XsHiLo&>(S.x).v[1][0][0] : xlo;
 #pragma unroll
         for (int blk = 0; blk < 2; blk++) {
-            if (16 * warp >= mv) break;  // no activation row of this warp
+            if (16 * wm >= mv) break;  // no activation row of this warp
             float part[NT][4];
 #pragma unroll
-            for (int t = 0; t < NT; t++) part[t][0] = part[t][1] = part[t][2] = part[t][3] = 0.0f;
-#pragma unroll
             for (int kk = 2 * blk; kk < 2 * blk + 2; kk++) {
-                uint32_t ah[4], al[4];
-                const int ao = (16 * warp + (lane & 15)) * kTP + 16 * kk + 8 * (lane >> 4);
+                uint32_t ah[4], al[4], bf[NT / 2][4];
+                const int ao = (16 * wm + (lane & 15)) * kTP + 16 * kk + 8 * (lane >> 4);
                 ldsm_x4(ah, ahi + ao);
                 ldsm_x4(al, alo + ao);
 #pragma unroll
-                for (int t = 0; t < NT; t += 2) {
-                    uint32_t bf[4];
-                    ldsm_x4(bf, wh + (8 * t + 8 * (lane >> 4) + (lane & 7)) * kTP + 16 * kk + 8 * ((lane >> 3) & 1));
-                    mma16816(part[t], ah, bf[0], bf[1]);
-                    mma16816(part[t], al, bf[0], bf[1]);
-                    mma16816(part[t + 1], ah, bf[2], bf[3]);
-                    mma16816(part[t + 1], al, bf[2], bf[3]);
+                for (int t = 0; t < NT; t += 2)
+                    ldsm_x4(bf[t / 2],
+                            wh + (8 * (NT * wn + t) + 8 * (lane >> 4) + (lane & 7)) * kTP + 16 * kk + 8 * ((lane >> 3) & 1));
+                // every tile's hi product, then every tile's lo product: NT independent MMAs between dependent ones
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    if (kk == 2 * blk) mma16816_z(part[t], ah, bf[t / 2][2 * (t & 1)], bf[t / 2][2 * (t & 1) + 1]);
+                    else mma16816(part[t], ah, bf[t / 2][2 * (t & 1)], bf[t / 2][2 * (t & 1) + 1]);
                 }
+#pragma unroll
+                for (int t = 0; t < NT; t++) mma16816(part[t], al, bf[t / 2][2 * (t & 1)], bf[t / 2][2 * (t & 1) + 1]);
             }
 #pragma unroll
             for (int t = 0; t < NT; t++) {
-                const float2 sc = *reinterpret_cast<const float2*>(scs + blk * BNW + 8 * t + c2);
+                const float2 sc = *reinterpret_cast<const float2*>(scs + blk * BNW + 8 * (NT * wn + t) + c2);
                 acc[t][0] = fmaf(sc.x, part[t][0], acc[t][0]);
                 acc[t][1] = fmaf(sc.y, part[t][1], acc[t][1]);
                 acc[t][2] = fmaf(sc.x, part[t][2], acc[t][2]);
@@ -234,19 +298,19 @@ __global__ void __launch_bounds__(kTThreads) tc_gemm_kernel(const GemvArgs a, co
         }
     }
 
-    // epilogue. acc[t] holds rows (g, g + 8) x columns (2c, 2c + 1) of n8 tile t: to a row-major fp32 tile in
+    // epilogue. acc[t] holds rows (g, g + 8) x columns (2c, 2c + 1) of n8 tile NT wn + t: to a row-major fp32 tile in
     // this CTA's shared memory (the stage buffers are free once every warp is past its last stage)
     const int g = lane >> 2, c = lane & 3;
     constexpr int TPF = BNW + 4;  // padded row pitch (floats)
     static_assert(kTM * TPF * 4 <= kTStages * sizeof(St), "partial tile fits the stage buffers");
     __syncthreads();
     float* tile = reinterpret_cast<float*>(tsm);
-    if (16 * warp < mv) {
+    if (16 * wm < mv) {
 #pragma unroll
         for (int t = 0; t < NT; t++) {
-            *reinterpret_cast<float2*>(tile + (16 * warp + g) * TPF + 8 * t + 2 * c) = make_float2(acc[t][0], acc[t][1]);
-            *reinterpret_cast<float2*>(tile + (16 * warp + g + 8) * TPF + 8 * t + 2 * c) =
-                make_float2(acc[t][2], acc[t][3]);
+            const int col = 8 * (NT * wn + t) + 2 * c;
+            *reinterpret_cast<float2*>(tile + (16 * wm + g) * TPF + col) = make_float2(acc[t][0], acc[t][1]);
+            *reinterpret_cast<float2*>(tile + (16 * wm + g + 8) * TPF + col) = make_float2(acc[t][2], acc[t][3]);
         }
     }
     namespace cg = cooperative_groups;
@@ -329,7 +393,7 @@ TcPlan tc_plan(const GemvArgs& a, int64_t ws_floats) {
     const int64_t tiles = int64_t(p.ntile) * p.mblk;
     // activations split once when at least 8 tiles share them
     p.x_floats = int64_t(a.M) * a.K;  // hi + lo halves
-    p.presplit = p.ntile >= 8 && ws_floats >= p.x_floats;
+    p.presplit = (p.ntile >= 8 || a.norm != kNormNone) && ws_floats >= p.x_floats;
     // K splits (one cluster per tile): about two CTAs per SM, each with at least 2 stages
     p.ksplit = 1;
     if (tiles < 2 * sms)
@@ -347,14 +411,16 @@ size_t tc_smem_for(int fmt, bool pre) {
 }  // namespace
 
 bool gemm_tc_fits(const GemvArgs& a) {
-    return a.M >= 5 && (a.fmt == kFP8 || a.fmt == kFP4) && a.norm == kNormNone && a.K % kTK == 0 &&
+    return a.M >= 5 && (a.fmt == kFP8 || a.fmt == kFP4) && a.K % kTK == 0 &&
+           (a.norm == kNormNone || a.K <= kNsMaxK) &&
            a.x_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && a.row_bytes % 16 == 0 &&
            !(a.pair_off && a.argmax);
 }
 
 namespace {
-GemvArgs shape_args(int fmt, int rows, int K, int M, bool pair) {
+GemvArgs shape_args(int fmt, int rows, int K, int M, bool pair, bool norm) {
     GemvArgs a;
+    a.norm = norm ? kNormRms : kNormNone;
     a.fmt = fmt;
     a.rows = rows;
     a.K = K;
@@ -366,38 +432,45 @@ GemvArgs shape_args(int fmt, int rows, int K, int M, bool pair) {
 }
 }  // namespace
 
-int gemm_tc_launches(int fmt, int rows, int K, int M, bool pair) {
-    const GemvArgs a = shape_args(fmt, rows, K, M, pair);
+int gemm_tc_launches(int fmt, int rows, int K, int M, bool pair, bool norm) {
+    const GemvArgs a = shape_args(fmt, rows, K, M, pair, norm);
     if (!gemm_tc_fits(a)) return 0;
     return tc_plan(a, int64_t(1) << 40).presplit ? 2 : 1;
 }
 
-void gemm_tc_scratch(int fmt, int rows, int K, int M, bool pair, int64_t* floats, int64_t* tickets) {
+void gemm_tc_scratch(int fmt, int rows, int K, int M, bool pair, bool norm, int64_t* floats, int64_t* tickets) {
     *floats = 0;
     *tickets = 0;
-    const GemvArgs a = shape_args(fmt, rows, K, M, pair);
+    const GemvArgs a = shape_args(fmt, rows, K, M, pair, norm);
     if (!gemm_tc_fits(a)) return;
     const TcPlan p = tc_plan(a, int64_t(1) << 40);
     *floats = p.presplit ? p.x_floats : 0;
 }
 
-// The tensor-core kernel takes 5+ activation rows of FP8 / FP4 weights without a norm prologue, K a multiple of
-// 64; cudaErrorNotSupported otherwise. a.ws (a.ws_floats floats) lets it split the activations once; without it
-// every CTA splits its own copy.
+// The tensor-core kernel takes 5+ activation rows of FP8 / FP4 weights, K a multiple of 64; cudaErrorNotSupported
+// otherwise. a.ws (a.ws_floats floats) lets it split the activations once (without it every CTA splits its own
+// copy); a norm prologue is applied by that split, so it needs the workspace.
 cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl) {
     if (!gemm_tc_fits(a)) return cudaErrorNotSupported;
     const bool pair = a.pair_off != 0;
     const TcPlan pl = tc_plan(a, a.ws ? a.ws_floats : 0);
+    if (a.norm != kNormNone && !pl.presplit) return cudaErrorNotSupported;
     TcSplit sp{};
     sp.ksplit = pl.ksplit;
     sp.sper = pl.sper;
     if (pl.presplit) {
         sp.xh = reinterpret_cast<const __half*>(a.ws);
         sp.xl = sp.xh + int64_t(a.M) * a.K;
-        const int64_t n4 = int64_t(a.M) * (a.K / 4);
-        const int blocks = int(std::min<int64_t>((n4 + 255) / 256, 4 * num_sms()));
-        const cudaError_t e = launch_ex(split_act_kernel, dim3(blocks), dim3(256), 0, st, pdl, a.x, a.x_stride, a.M,
-                                        a.K, const_cast<__half*>(sp.xh), const_cast<__half*>(sp.xl));
+        cudaError_t e;
+        if (a.norm != kNormNone) {
+            e = launch_ex(norm_split_kernel, dim3(a.M), dim3(kNsThreads), 0, st, pdl, a, const_cast<__half*>(sp.xh),
+                          const_cast<__half*>(sp.xl));
+        } else {
+            const int64_t n4 = int64_t(a.M) * (a.K / 4);
+            const int blocks = int(std::min<int64_t>((n4 + 255) / 256, 4 * num_sms()));
+            e = launch_ex(split_act_kernel, dim3(blocks), dim3(256), 0, st, pdl, a.x, a.x_stride, a.M, a.K,
+                          const_cast<__half*>(sp.xh), const_cast<__half*>(sp.xl));
+        }
         if (e != cudaSuccess) return e;
     }
     const bool pre = pl.presplit;

@@ -289,10 +289,13 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         a.ws_ntickets = int(m->mm_tickets_n);
         return launch_gemv(a, st, pdl());
     };
-    // norm (fused into the GEMV prologue when the activations fit in shared memory, else a separate kernel)
-    auto normed = [&](const float* g, const float* b, int& norm_kind, const float*& src) -> cudaError_t {
+    const bool staged = m->debug_layers >= 0 && m->debug_stage > 0;
+    // norm: applied by the matmul call (the GEMV prologue when the activations fit in shared memory, or the
+    // tensor-core path's activation split) or by a separate kernel
+    auto normed = [&](const Mat& W, int rows, bool pair, const float* g, const float* b, int& norm_kind,
+                      const float*& src) -> cudaError_t {
         const int kind = m->qwen ? kNormRms : kNormLayer;
-        if (x_fits) {
+        if (x_fits || (!staged && gemm_tc_launches(W.fmt, rows, W.cols, R, pair, true) > 0)) {
             norm_kind = kind;
             src = m->x;
             return cudaSuccess;
@@ -302,7 +305,6 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         return launch_norm(m->x, C, m->xn, C, g, b, R, C, eps, m->qwen, st, pdl());
     };
 
-    const bool staged = m->debug_layers >= 0 && m->debug_stage > 0;
     const size_t nlayers = m->debug_layers >= 0
                                ? std::min(m->layers.size(), size_t(m->debug_layers) + (staged ? 1 : 0))
                                : m->layers.size();
@@ -318,7 +320,7 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         uint16_t* vc = m->vc + int64_t(l) * m->kv_layer;
         int nk;
         const float* src;
-        CK(normed(L.ln1, L.ln1b, nk, src), "norm1");
+        CK(normed(L.wqkv, m->QW, false, L.ln1, L.ln1b, nk, src), "norm1");
         CK(gemv(L.wqkv, m->QW, src, C, R, nk, L.ln1, L.ln1b, L.bqkv, m->qwen ? 0 : kBias, m->qkv, m->QW, 0), "qkv");
         if (dump(l, 2, m->qkv, m->QW)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
         QkvPostArgs q;
@@ -376,7 +378,7 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
                 kAccumulate | (m->qwen ? 0 : kBias), m->x, C, 0),
            "o_proj");
         if (dump(l, m->qwen ? 5 : 4, m->x, C)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
-        CK(normed(L.ln2, L.ln2b, nk, src), "norm2");
+        CK(normed(L.wup, m->qwen ? m->F : m->UPW, m->qwen, L.ln2, L.ln2b, nk, src), "norm2");
         if (m->qwen) {
             CK(gemv(L.wup, m->F, src, C, R, nk, L.ln2, nullptr, nullptr, 0, m->h, m->F, m->F), "gate_up");
         } else {
@@ -404,7 +406,8 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         CK(cudaGetLastError(), "gather");
         hx = m->hx;
     }
-    const bool head_fits = gemv_norm_fusable(m->embed.fmt, nout, C);
+    const bool head_fits = gemv_norm_fusable(m->embed.fmt, nout, C) ||
+                           gemm_tc_launches(m->embed.fmt, m->V, C, nout, false, true) > 0;
     const bool fused_argmax = do_argmax && nout <= 64;
     unsigned long long* keys = fused_argmax ? m->d_keys : nullptr;
     if (head_fits) {
@@ -441,29 +444,42 @@ bool decode_ok(neko_model* m, int R) {
 // The matmuls of a step (format, output rows, K, SwiGLU pair), the LM head last.
 struct MatShape {
     int fmt, rows, K;
-    bool pair, lm_head;
+    bool pair, norm, lm_head;
 };
 std::vector<MatShape> mat_shapes(const neko_model* m) {
     const int K_att = m->H * m->hd;
-    std::vector<MatShape> v = {{fmt_for(m->C, m->fmt), m->QW, m->C, false, false},
-                               {fmt_for(K_att, m->fmt), m->C, K_att, false, false},
-                               {fmt_for(m->C, m->fmt), m->qwen ? m->F : m->UPW, m->C, m->qwen, false},
-                               {fmt_for(m->F, m->fmt), m->C, m->F, false, false},
-                               {m->embed.fmt, m->V, m->C, false, true}};
+    std::vector<MatShape> v = {{fmt_for(m->C, m->fmt), m->QW, m->C, false, true, false},
+                               {fmt_for(K_att, m->fmt), m->C, K_att, false, false, false},
+                               {fmt_for(m->C, m->fmt), m->qwen ? m->F : m->UPW, m->C, m->qwen, true, false},
+                               {fmt_for(m->F, m->fmt), m->C, m->F, false, false, false},
+                               {m->embed.fmt, m->V, m->C, false, true, true}};
     return v;
+}
+
+// Launches of one matmul of the step and of its norm: into the matmul call (GEMV prologue or the tensor-core
+// path's split) when x_fits or the tensor-core path takes it, else a norm kernel first.
+int matmul_launches(const MatShape& ms, int M, bool x_fits) {
+    if (ms.norm) {
+        const int tcn = gemm_tc_launches(ms.fmt, ms.rows, ms.K, M, ms.pair, true);
+        if (tcn > 0) return tcn;
+        if (x_fits) return 1;
+        const int tc = gemm_tc_launches(ms.fmt, ms.rows, ms.K, M, ms.pair, false);
+        return 1 + (tc > 0 ? tc : 1);
+    }
+    const int tc = gemm_tc_launches(ms.fmt, ms.rows, ms.K, M, ms.pair, false);
+    return tc > 0 ? tc : 1;
 }
 
 int step_launches(neko_model* m, int R, int nout, bool gather, bool do_argmax, bool advance) {
     if (!gather && nout == R && m->debug_layers < 0 && m->dec_enabled && R <= m->dec_seqs && decode_ok(m, R))
         return 1;
     const bool x_fits = gemv_norm_fusable(fmt_for(m->C, m->fmt), R, m->C);
-    int per_layer = 6 + (x_fits ? 0 : 2);
-    for (const MatShape& ms : mat_shapes(m))  // activation splits of tensor-core matmuls
-        if (!ms.lm_head) per_layer += std::max(0, gemm_tc_launches(ms.fmt, ms.rows, ms.K, R, ms.pair) - 1);
+    int per_layer = 2;  // qkv_post, attention
+    for (const MatShape& ms : mat_shapes(m))
+        if (!ms.lm_head) per_layer += matmul_launches(ms, R, x_fits);
     int n = 1 + int(m->layers.size()) * per_layer + (gather ? 1 : 0);
     for (const MatShape& ms : mat_shapes(m))
-        if (ms.lm_head) n += std::max(0, gemm_tc_launches(ms.fmt, ms.rows, ms.K, nout, ms.pair) - 1);
-    n += gemv_norm_fusable(m->embed.fmt, nout, m->C) ? 1 : 2;
+        if (ms.lm_head) n += matmul_launches(ms, nout, gemv_norm_fusable(m->embed.fmt, nout, m->C));
     return n + (do_argmax ? 1 : 0) + (advance && nout > 64 ? 1 : 0);
 }
 
@@ -736,7 +752,7 @@ neko_model* neko_model_create(int device, const neko_model_config* cfg, char* er
             for (const MatShape& ms : mat_shapes(m)) {
                 if (!ms.lm_head && r > int(R)) continue;
                 int64_t f = 0, t = 0;
-                gemm_tc_scratch(ms.fmt, ms.rows, ms.K, r, ms.pair, &f, &t);
+                gemm_tc_scratch(ms.fmt, ms.rows, ms.K, r, ms.pair, ms.norm, &f, &t);
                 wf = std::max(wf, f);
                 wt = std::max(wt, t);
             }

@@ -95,12 +95,12 @@ cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, bool pdl, int max_ctas = 0)
 cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl);
 // The tensor-core kernel for 5+ activation rows (k_mma.cu); cudaErrorNotSupported when the call does not fit.
 cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl);
-// Workspace (floats, tickets) with which launch_gemm_tc splits this matmul fully; 0, 0 when it takes no workspace
-// or the tensor-core path does not apply.
-void gemm_tc_scratch(int fmt, int rows, int K, int M, bool pair, int64_t* floats, int64_t* tickets);
-// Kernel launches of such a matmul with that workspace (the activation split and the GEMM), 0 when the
+// Workspace (floats, tickets) with which launch_gemm_tc splits this matmul's activations once (norm: with the
+// norm prologue applied); 0, 0 when it needs none or the tensor-core path does not apply.
+void gemm_tc_scratch(int fmt, int rows, int K, int M, bool pair, bool norm, int64_t* floats, int64_t* tickets);
+// Kernel launches of such a matmul with that workspace (the activation split or norm, and the GEMM), 0 when the
 // tensor-core path does not apply.
-int gemm_tc_launches(int fmt, int rows, int K, int M, bool pair);
+int gemm_tc_launches(int fmt, int rows, int K, int M, bool pair, bool norm);
 int gemv_launch_count();  // number of launches launch_gemv issues per call (1)
 
 // ------------------------------------------------------------------ other ops (k_ops.cu)
