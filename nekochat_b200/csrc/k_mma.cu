@@ -167,7 +167,6 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
     const int cbytes = FMT == kFP8 ? a.K : a.K / 2;
     const int s_begin = z * sp.sper, s_end = min(a.K / kTK, s_begin + sp.sper), nst = s_end - s_begin;
     constexpr float kCodeFactor = FMT == kFP8 ? kFp8HwFactor : kFp4Factor;  // code value -> engine decode
-    pdl_wait();
     if (a.argmax && tid < kTM) keys[tid] = 0ull;
 
     // weight row r of the tile -> packed row in W (rows past the end repeat the last row; never stored)
@@ -176,7 +175,7 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
         const int nc = min(n, a.rows - 1);
         return a.W + (int64_t(nc) + (PAIR && r >= BN ? a.pair_off : 0)) * a.row_bytes;
     };
-    auto issue = [&](int i_s) {  // i_s: stage index within this CTA's range
+    auto issue_w = [&](int i_s) {  // weights and scales of stage i_s (an index within this CTA's range)
         St& S = raw[i_s % kTStages];
         const int s = s_begin + i_s;
         constexpr int kPieces = St::kCode / 16;  // 16-byte pieces of codes per row
@@ -185,6 +184,10 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
             cp16(&S.w[r][16 * q], wrow(r) + s * St::kCode + 16 * q, 16);
         }
         for (int r = tid; r < BNW; r += kTThreads) cp4(&S.sc[r][0], wrow(r) + cbytes + 4 * s);
+    };
+    auto issue_x = [&](int i_s) {  // activations of stage i_s
+        St& S = raw[i_s % kTStages];
+        const int s = s_begin + i_s;
         if constexpr (PRE) {  // hi / lo halves straight into their padded tiles
             for (int i = tid; i < 2 * mv * (kTK / 8); i += kTThreads) {
                 const int h = i >= mv * (kTK / 8) ? 1 : 0, j = i - h * mv * (kTK / 8);
@@ -203,16 +206,28 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
 #pragma unroll
     for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
 
+    // Prologue: the weights of the first stages (one group each) stream before the wait for the previous kernel
+    // (weights never depend on it), then their activations (one group).
 #pragma unroll
-    for (int s = 0; s < kTStages - 1; s++) {  // prologue: the first stages in flight (one group each)
-        if (s < nst) issue(s);
+    for (int s = 0; s < kTStages - 1; s++) {
+        if (s < nst) issue_w(s);
         cp_commit();
     }
+    pdl_wait();
+#pragma unroll
+    for (int s = 0; s < kTStages - 1; s++)
+        if (s < nst) issue_x(s);
+    cp_commit();
     for (int s = 0; s < nst; s++) {
-        cp_wait<kTStages - 2>();  // stage s landed (this thread's copies)
-        __syncthreads();          // ... every thread's; and every warp is done with stage s - 1 (its buffer,
-                                  // which pre-split activations feed to the mma directly, and wh / xhi / xlo)
-        if (s + kTStages - 1 < nst) issue(s + kTStages - 1);  // into the buffer of stage s - 1
+        // stage s landed (this thread's copies): everything of the prologue for s = 0; then one group per stage
+        if (s == 0) cp_wait<0>();
+        else cp_wait<kTStages - 2>();
+        __syncthreads();  // ... every thread's; and every warp is done with stage s - 1 (its buffer, which
+                          // pre-split activations feed to the mma directly, and wh / xhi / xlo)
+        if (s + kTStages - 1 < nst) {  // into the buffer of stage s - 1
+            issue_w(s + kTStages - 1);
+            issue_x(s + kTStages - 1);
+        }
         cp_commit();
         const St& S = raw[s % kTStages];
         // codes -> f16 (exact)
@@ -298,6 +313,7 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
         }
     }
 
+    pdl_trigger();  // the next kernel may start streaming its weights while this one finishes
     // epilogue. acc[t] holds rows (g, g + 8) x columns (2c, 2c + 1) of n8 tile NT wn + t: to a row-major fp32 tile in
     // this CTA's shared memory (the stage buffers are free once every warp is past its last stage)
     const int g = lane >> 2, c = lane & 3;
@@ -360,7 +376,6 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
         if (tid < nrow && keys[z + ks * tid]) atomicMax(a.argmax + m0 + z + ks * tid, keys[z + ks * tid]);
     }
     if (ks > 1) cg::this_cluster().sync();  // no CTA leaves while a peer may still read its tile
-    pdl_trigger();
 }
 
 using TcFn = void (*)(const GemvArgs, const TcSplit);
