@@ -602,10 +602,15 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl) {
         }
         return launch_ex(k, dim3(g.splits, a.n_kv, a.rows), dim3(kAttnThreads), size_t(smem), st, pdl, a, g);
     }
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-        attr = true;
+    static unsigned attr_done = 0u;  // bit d: device d (< 32); function attributes are per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 32 || !((attr_done >> dev) & 1u)) {
+        if (cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 160 * 1024);
+            e != cudaSuccess)
+            return e;
+        if (dev < 32) attr_done |= 1u << dev;
     }
     return launch_ex(attention_kernel, dim3(g.splits, a.n_kv, a.rows), dim3(kAttnThreads), size_t(g.smem), st, pdl, a,
                      g);

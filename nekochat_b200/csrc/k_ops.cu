@@ -267,16 +267,25 @@ __global__ void __launch_bounds__(kPostWarps * 32) qkv_post_kernel(const QkvPost
 
 }  // namespace
 
+// The row-cache shared-memory limit of a norm / softmax kernel on the current device (function attributes are
+// per device), set once per (kernel, device).
+template <typename K>
+cudaError_t row_cache_attr(K kernel) {
+    static unsigned done[2] = {0u, 0u};  // bit d: device d (< 32) done; [0] norm, [1] softmax
+    const int which = reinterpret_cast<const void*>(kernel) == reinterpret_cast<const void*>(norm_kernel) ? 0 : 1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 32 && ((done[which] >> dev) & 1u)) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowCacheFloats * 4);
+    if (e == cudaSuccess && dev < 32) done[which] |= 1u << dev;
+    return e;
+}
+
 cudaError_t launch_norm(const float* x, int64_t x_stride, float* y, int64_t y_stride, const float* gamma,
                         const float* beta, int rows, int C, float eps, bool rms, cudaStream_t st, bool pdl) {
     if (rows <= 0) return cudaSuccess;
     const size_t smem = C <= kRowCacheFloats ? size_t(C) * 4 : 0;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowCacheFloats * 4);
-        cudaFuncSetAttribute(softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowCacheFloats * 4);
-        attr = true;
-    }
+    if (cudaError_t e = row_cache_attr(norm_kernel); e != cudaSuccess) return e;
     return launch_ex(norm_kernel, dim3(rows), dim3(kNormThreads), smem, st, pdl, x, x_stride, y, y_stride, gamma, beta,
                      C, eps, rms ? 1 : 0);
 }
@@ -284,7 +293,7 @@ cudaError_t launch_norm(const float* x, int64_t x_stride, float* y, int64_t y_st
 cudaError_t launch_softmax(const float* x, float* y, int rows, int C, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
     const size_t smem = C <= kRowCacheFloats ? size_t(C) * 4 : 0;
-    cudaFuncSetAttribute(softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowCacheFloats * 4);
+    if (cudaError_t e = row_cache_attr(softmax_kernel); e != cudaSuccess) return e;
     softmax_kernel<<<rows, kNormThreads, smem, st>>>(x, y, C);
     return cudaGetLastError();
 }
