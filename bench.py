@@ -11,7 +11,10 @@ ids in, host logits out every step, like Model::forward); roofline = the dequant
 one step, timed with CUDA events; cpu_baseline = the reference engine's CPU backend (compiled from its sources in
 oracle/_ref) on this host's cores.
 
-    python bench.py [--gpus N --steps K --warmup W --batch B --impl ours|reference]
+    python bench.py [--gpus N --steps K --warmup W --batch B --impl ours|reference --model M]
+
+--model qwen3-1.7b-fp4 runs BASELINE configs[2] instead (Qwen3-1.7B shape, the engine's FP4 weights, a
+1024-token prompt); the default is the headline configuration above.
 """
 import argparse
 import json
@@ -27,9 +30,11 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-SHAPE = "qwen3-0.6b"
-FMT = 1  # FP8
-METRIC = "Qwen3-0.6B FP8 decode tok/s"
+# --model: the headline configuration or the FP4 one
+MODELS = {"qwen3-0.6b-fp8": ("qwen3-0.6b", 1, 512, "Qwen3-0.6B FP8 decode tok/s"),
+          "qwen3-1.7b-fp4": ("qwen3-1.7b", 2, 1024, "Qwen3-1.7B FP4 decode tok/s")}
+SHAPE, FMT, PROMPT, METRIC = MODELS["qwen3-0.6b-fp8"]
+FMT_NAME = {1: "FP8", 2: "FP4"}
 
 
 def parse():
@@ -38,7 +43,10 @@ def parse():
     p.add_argument("--steps", type=int, default=256)
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--batch", type=int, default=1)
-    p.add_argument("--prompt", type=int, default=None, help="prompt tokens (default 512; 32 with --profile)")
+    p.add_argument("--model", choices=sorted(MODELS), default="qwen3-0.6b-fp8",
+                   help="qwen3-0.6b-fp8 (512-token prompt, the headline) or qwen3-1.7b-fp4 (1024-token prompt)")
+    p.add_argument("--prompt", type=int, default=None,
+                   help="prompt tokens (default: the model's, 512 / 1024; 32 with --profile)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -271,7 +279,8 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world, "steps": k,
         "warmup": w, "ms_per_step": dt / k * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "qwen3-0.6b fp8 greedy decode, batch 1", "batch": 1, "prompt": n_prompt},
+        "config": {"workload": f"{SHAPE} {FMT_NAME[FMT].lower()} greedy decode, batch 1", "batch": 1,
+                   "prompt": n_prompt},
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -284,7 +293,7 @@ def run_ours(args):
     world, rank, local = dist_setup(args)
     s = workload.shape(SHAPE)
     B = args.batch
-    prompt_len = args.prompt or (32 if args.profile else 512)
+    prompt_len = args.prompt or (32 if args.profile else PROMPT)
     steps, warm = (4, 3) if args.profile else (args.steps, args.warmup)
     e2e_on = not (args.no_e2e or args.profile)
     context = prompt_len + 2 * (warm + steps) + 8
@@ -353,14 +362,14 @@ def run_ours(args):
         single = m.step_launches(B) == 1
         ach = bytes_step / (t / steps) / 1e9
         roof = {"bound": "hbm",
-                "kernel": f"decode_kernel<FP8,{1 if B == 1 else 4}> (a whole decode step, one launch)" if single
-                else "decode step as a kernel chain (gemv_kernel dominant)",
+                "kernel": f"decode_kernel<{FMT_NAME[FMT]},{1 if B == 1 else 4}> (a whole decode step, one launch)"
+                if single else "decode step as a kernel chain (tc_gemm_kernel and attention_tc_kernel dominant)",
                 "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
                 "peak_source": psrc, "traffic": None, "bytes_per_launch": bytes_step if single else None,
                 "launch_us": t / steps * 1e6 if single else None,
                 "timing": "CUDA events on the launch stream around the timed steps (graph replays back to back)"}
         tf = os.path.join(ROOT, "profiles", "traffic.json")
-        key = f"decode_fp8_b{B}"
+        key = f"decode_{FMT_NAME[FMT].lower()}_b{B}" + ("" if SHAPE == "qwen3-0.6b" else "_" + SHAPE)
         if single and os.path.exists(tf):
             try:
                 rec = json.load(open(tf)).get(key)
@@ -373,7 +382,8 @@ def run_ours(args):
                 pass
         # the same weight matrices as single GEMV launches (the operator the step is built from), for reference
         per_launch, t_launch, n = gemv_roofline(m, s, stream)
-        roof["gemv_op"] = {"kernel": "gemv_kernel<FP8> (M=1, every weight matrix of a step, one launch each)",
+        roof["gemv_op"] = {"kernel": f"gemv_stream_kernel<{FMT_NAME[FMT]},1> (M=1, every weight matrix of a step, "
+                                     "one launch each)",
                            "achieved": round(per_launch / t_launch / 1e9, 1), "bytes_per_launch": per_launch,
                            "launch_us": t_launch * 1e6}
 
@@ -390,11 +400,12 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
             "ms_per_step": t / steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"qwen3-0.6b fp8 (engine FP8 format), {prompt_len}-token random prompt, "
-                                   f"greedy decode, batch {B} per GPU", "batch": B, "prompt": prompt_len,
+            "config": {"workload": f"{SHAPE} {FMT_NAME[FMT].lower()} (engine {FMT_NAME[FMT]} format), {prompt_len}-token "
+                                   f"random prompt, greedy decode, batch {B} per GPU", "batch": B, "prompt": prompt_len,
                        "positions": [prompt_len + warm, prompt_len + warm + steps],
-                       "weights": "N(0,0.02) random init, quantized on the GPU by the engine's FP8 codec",
-                       "l2": "no flush needed: each step streams 633 MB of weights (> 126 MB L2)",
+                       "weights": f"N(0,0.02) random init, quantized on the GPU by the engine's {FMT_NAME[FMT]} codec",
+                       "l2": f"no flush needed: each step streams "
+                             f"{workload.weight_stream_bytes(s, FMT) / 1e6:.0f} MB of weights (> 126 MB L2)",
                        "parallelism": f"dp{world} (independent replicas)"},
             "gpu_launches": launches,
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
@@ -406,7 +417,9 @@ def run_ours(args):
 
 
 def main():
+    global SHAPE, FMT, PROMPT, METRIC
     args = parse()
+    SHAPE, FMT, PROMPT, METRIC = MODELS[args.model]
     if args.impl == "reference":
         run_reference(args)
     else:
