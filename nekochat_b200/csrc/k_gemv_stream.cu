@@ -6,8 +6,8 @@
 //  * one CTA per SM, a contiguous range of rows each; a producer warp streams the range through a ring of
 //    stages of up to 52 KB with cp.async.bulk (TMA), 8 KB per copy (large stages: fewer producer / consumer
 //    hand-offs, which is what limits a TMA ring's rate);
-//  * 12 consumer warps work stage by stage: a stage holds 12 x rpw rows (rpw <= 4, the rows per warp), warp w
-//    takes rows w, w + 12, ... of it with all their 128-bit weight loads issued before the math (SwiGLU: gate
+//  * 16 consumer warps work stage by stage: a stage holds 16 x rpw rows (rpw <= 4, the rows per warp), warp w
+//    takes rows w, w + 16, ... of it with all their 128-bit weight loads issued before the math (SwiGLU: gate
 //    and up rows together); one lane waits for the stage and releases it; FP8 codes are decoded by the
 //    hardware e4m3 -> f16 conversion (the engine's FP8 code is e4m3, see gemv_core.cuh), FP4 by bit arithmetic;
 //  * four rows are reduced across the warp together (6 shuffles instead of 20) before the stores;
@@ -16,6 +16,7 @@
 #include <algorithm>
 
 #include "gemv_core.cuh"
+#include "mma_frag.cuh"
 #include "neko_common.cuh"
 #include "neko_internal.h"
 
@@ -23,7 +24,7 @@ namespace neko {
 
 namespace {
 
-constexpr int kSW = 12;              // consumer warps
+constexpr int kSW = 16;              // consumer warps
 constexpr int kSNT = kSW * 32;       // consumer threads
 constexpr int kSThr = kSNT + 32;     // + the producer warp
 constexpr int kSMaxSlots = 16;
@@ -116,6 +117,37 @@ __device__ void stage_act(const GemvArgs& a, float* xs, int warp, int lane) {
     ssync();
 }
 
+// The producer warp: every stage of this CTA's rows (rps rows per stage; SwiGLU: the gate rows, then the up
+// rows) into the ring with cp.async.bulk, 8 KB per copy, waiting for a slot to be released before reusing it.
+__device__ void stream_producer(const GemvArgs& a, int r0, int r1, int rps, int nslot, int slot_bytes, uint64_t* full,
+                                uint64_t* empty, uint8_t* ring, int lane) {
+    const bool pair = a.pair_off != 0;
+    const int nst = (r1 - r0 + rps - 1) / rps;
+    int st = 0;
+    for (; st < nst; st++) {
+        const int slot = st % nslot;
+        if (st >= nslot) {
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&empty[slot], ((st / nslot) - 1) & 1);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        }
+        const int row = r0 + st * rps, cnt = min(rps, r1 - row);
+        const uint32_t bytes = uint32_t(cnt) * uint32_t(a.row_bytes);
+        uint8_t* dst = ring + size_t(slot) * slot_bytes;
+        if (lane == 0) mbar_arrive_expect_tx(&full[slot], pair ? 2 * bytes : bytes);
+        __syncwarp();
+        const int nch = int((bytes + kSChunk - 1) / kSChunk);
+        for (int c = lane; c < (pair ? 2 : 1) * nch; c += 32) {
+            const int half = c >= nch ? 1 : 0, cc = c - half * nch;
+            const uint32_t off = uint32_t(cc) * kSChunk, sz = min(uint32_t(kSChunk), bytes - off);
+            bulk_g2s(dst + (half ? bytes : 0) + off, a.W + (int64_t(row) + (half ? a.pair_off : 0)) * a.row_bytes + off,
+                     sz, &full[slot]);
+        }
+    }
+    if (lane == 0)  // leave only when no copy of ours is still landing (a consumer may have given up)
+        for (int s = st > nslot ? st - nslot : 0; s < st; s++) mbar_wait(&full[s % nslot], (s / nslot) & 1);
+}
+
 struct StreamPlan {
     int rows_per_cta;
     int rpw;         // rows per warp per stage (output rows; pairs for SwiGLU)
@@ -147,29 +179,7 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_stream_kernel(const GemvArgs a,
     __syncthreads();
 
     if (warp == kSW) {  // producer: weights only, so it never waits for the previous kernel
-        int st = 0;
-        for (; st < nst; st++) {
-            const int slot = st % sp.nslot;
-            if (st >= sp.nslot) {
-                int ok = 1;
-                if (lane == 0) ok = mbar_wait(&empty[slot], ((st / sp.nslot) - 1) & 1);
-                if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-            }
-            const int row = r0 + st * rps, cnt = min(rps, r1 - row);
-            const uint32_t bytes = uint32_t(cnt) * uint32_t(a.row_bytes);
-            uint8_t* dst = ring + size_t(slot) * sp.slot_bytes;
-            if (lane == 0) mbar_arrive_expect_tx(&full[slot], pair ? 2 * bytes : bytes);
-            __syncwarp();
-            const int nch = int((bytes + kSChunk - 1) / kSChunk);
-            for (int c = lane; c < (pair ? 2 : 1) * nch; c += 32) {
-                const int half = c >= nch ? 1 : 0, cc = c - half * nch;
-                const uint32_t off = uint32_t(cc) * kSChunk, sz = min(uint32_t(kSChunk), bytes - off);
-                bulk_g2s(dst + (half ? bytes : 0) + off, a.W + (int64_t(row) + (half ? a.pair_off : 0)) * a.row_bytes + off,
-                         sz, &full[slot]);
-            }
-        }
-        if (lane == 0)  // leave only when no copy of ours is still landing (a consumer may have given up)
-            for (int s = st > sp.nslot ? st - sp.nslot : 0; s < st; s++) mbar_wait(&full[s % sp.nslot], (s / sp.nslot) & 1);
+        stream_producer(a, r0, r1, sp.rps, sp.nslot, sp.slot_bytes, full, empty, ring, lane);
         return;
     }
 
@@ -276,6 +286,252 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_stream_kernel(const GemvArgs a,
     }
 }
 
+// ------------------------------------------------------------------------------------------------ tensor cores
+// The same stream of weight rows with the dot products on mma.sync m16n8k16 (f16 operands, fp32 accumulation):
+// D[m][n] = sum_k x[m][k] w[n][k] with the 1..4 activation rows as M (rows 4..15 zero) and 8 weight rows as N.
+// K is permuted inside each 16-step so that lane (g, c) reads 4 contiguous code bytes of weight row g (bytes 4c..
+// 4c+3 of the step, MMA k = 2c, 2c+1, 2c+8, 2c+9) and the same 4 activations: one 32-bit load and two hardware
+// conversions feed two MMAs (the activations as hi + lo f16, about 22 bits). Codes are exact in f16; each 32-weight
+// block's partial sums are scaled in fp32, as in the CUDA-core kernel. A stage holds 8 T rows (T tiles of 8,
+// T dividing the consumer warp count); warp w takes tile w % T over part w / T of K (kSW / T parts of whole
+// 32-weight blocks), and the parts are added in order through shared memory. Its cost hardly depends on M, so
+// it takes the calls of 2..4 activation rows; one row runs the CUDA-core kernel, which needs no row padding.
+constexpr int kMmaRedBytes = 2 * kSW * 32 * 4 * 4;  // partial sums of the K parts, double-buffered by stage
+
+struct MmaPlan {
+    int rows_per_cta;
+    int tiles;       // 8-row tiles per stage; kSW / tiles K parts
+    int rps;         // rows per stage = 8 tiles
+    int nslot, slot_bytes, xs_bytes;
+};
+
+// The M activation rows as f16 hi / lo ([M][K] each), with the norm prologue (sums in double, cpu_ops.cpp:
+// 483-511), read straight from global memory (a few KB, L2-resident).
+__device__ void stage_act_hilo(const GemvArgs& a, __half* xh, __half* xl, int warp, int lane) {
+    const int tid = threadIdx.x, K4 = a.K / 4, total = a.M * K4;
+    float r[kDecodeMaxSeqs], mean[kDecodeMaxSeqs];
+    if (a.norm != kNormNone) {
+        double s1[kDecodeMaxSeqs] = {0.0, 0.0, 0.0, 0.0}, s2[kDecodeMaxSeqs] = {0.0, 0.0, 0.0, 0.0};
+        for (int i = tid; i < total; i += kSNT) {
+            const int m = i / K4, k = 4 * (i - m * K4);
+            const float4 v = *reinterpret_cast<const float4*>(a.x + int64_t(m) * a.x_stride + k);
+#pragma unroll
+            for (int mm = 0; mm < kDecodeMaxSeqs; mm++)
+                if (mm == m) {
+                    s1[mm] += double(v.x) + double(v.y) + double(v.z) + double(v.w);
+                    s2[mm] += double(v.x) * v.x + double(v.y) * v.y + double(v.z) * v.z + double(v.w) * v.w;
+                }
+        }
+#pragma unroll
+        for (int m = 0; m < kDecodeMaxSeqs; m++) {
+            const double t1 = wsum_d(s1[m]), t2 = wsum_d(s2[m]);
+            if (lane == 0) {
+                t_part[2 * (m * kSW + warp)] = t1;
+                t_part[2 * (m * kSW + warp) + 1] = t2;
+            }
+        }
+        ssync();
+#pragma unroll
+        for (int m = 0; m < kDecodeMaxSeqs; m++) {
+            double a1 = 0.0, a2 = 0.0;
+            for (int w = 0; w < kSW; w++) {
+                a1 += t_part[2 * (m * kSW + w)];
+                a2 += t_part[2 * (m * kSW + w) + 1];
+            }
+            mean[m] = 0.0f;
+            if (a.norm == kNormRms) {
+                r[m] = float(1.0 / sqrt(a2 / a.K + double(a.eps)));
+            } else {
+                const double mu = a1 / a.K;
+                mean[m] = float(mu);
+                r[m] = float(1.0 / sqrt(a2 / a.K - mu * mu + double(a.eps)));
+            }
+        }
+    }
+    for (int i = tid; i < total; i += kSNT) {
+        const int m = i / K4, k = 4 * (i - m * K4);
+        float4 y = *reinterpret_cast<const float4*>(a.x + int64_t(m) * a.x_stride + k);
+        if (a.norm != kNormNone) {
+            float rm = r[0], mm = mean[0];
+#pragma unroll
+            for (int q = 1; q < kDecodeMaxSeqs; q++)
+                if (q == m) {
+                    rm = r[q];
+                    mm = mean[q];
+                }
+            const float4 ga = __ldg(reinterpret_cast<const float4*>(a.gamma + k));
+            if (a.norm == kNormRms) {
+                y.x = __fmul_rn(__fmul_rn(y.x, rm), ga.x);
+                y.y = __fmul_rn(__fmul_rn(y.y, rm), ga.y);
+                y.z = __fmul_rn(__fmul_rn(y.z, rm), ga.z);
+                y.w = __fmul_rn(__fmul_rn(y.w, rm), ga.w);
+            } else {
+                const float4 be = __ldg(reinterpret_cast<const float4*>(a.beta + k));
+                y.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.x, mm), rm), ga.x), be.x);
+                y.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.y, mm), rm), ga.y), be.y);
+                y.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.z, mm), rm), ga.z), be.z);
+                y.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.w, mm), rm), ga.w), be.w);
+            }
+        }
+        uint32_t h0, l0, h1, l1;
+        split_hilo(y.x, y.y, h0, l0);
+        split_hilo(y.z, y.w, h1, l1);
+        *reinterpret_cast<uint2*>(xh + m * a.K + k) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2*>(xl + m * a.K + k) = make_uint2(l0, l1);
+    }
+    ssync();
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kSThr, 1) gemv_mma_kernel(const GemvArgs a, const MmaPlan sp) {
+    uint64_t* full = reinterpret_cast<uint64_t*>(gsm);
+    uint64_t* empty = full + kSMaxSlots;
+    __half* xh = reinterpret_cast<__half*>(gsm + 256);
+    __half* xl = xh + a.M * a.K;
+    float* red = reinterpret_cast<float*>(gsm + 256 + sp.xs_bytes);  // [2][kSW][32][4] K-part partial sums
+    uint8_t* ring = gsm + 256 + sp.xs_bytes + kMmaRedBytes;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const bool pair = a.pair_off != 0;
+    const int r0 = blockIdx.x * sp.rows_per_cta, r1 = min(a.rows, r0 + sp.rows_per_cta);
+    pdl_trigger();
+    if (r0 >= r1) return;
+    const int n = r1 - r0, rps = sp.rps, nst = (n + rps - 1) / rps;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < sp.nslot; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kSW);
+        }
+        fence_barrier_init();
+    }
+    if (threadIdx.x < kDecodeMaxSeqs) t_key[threadIdx.x] = 0ull;
+    __syncthreads();
+    if (warp == kSW) {  // producer: weights only, so it never waits for the previous kernel
+        stream_producer(a, r0, r1, rps, sp.nslot, sp.slot_bytes, full, empty, ring, lane);
+        return;
+    }
+
+    // ---------------- consumers
+    pdl_wait();  // the activations come from the previous kernel
+    stage_act_hilo(a, xh, xl, warp, lane);
+    constexpr float kF = FMT == kFP8 ? kFp8HwFactor : kFp4Factor;
+    const int cbytes = code_bytes(FMT, a.K), nblk = a.K / kQuantBlock;
+    const int tiles = sp.tiles, parts = kSW / tiles, tile = warp % tiles, part = warp / tiles;
+    const int b_begin = part * nblk / parts, b_end = (part + 1) * nblk / parts;
+    const bool xrow = g < a.M;  // this lane's activation row exists (MMA rows past M stay zero)
+    const __half* xhr = xh + (xrow ? g : 0) * a.K + 4 * c;
+    const __half* xlr = xl + (xrow ? g : 0) * a.K + 4 * c;
+    unsigned long long best = 0ull;  // this lane's activation row g
+    int slot = 0, par = 0;
+    for (int st = 0; st < nst; st++) {
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(&full[slot], par);
+        ok = __shfl_sync(0xffffffffu, ok, 0);  // a wait that gave up is a device error; the stage is skipped
+        const int srow = st * rps, in_stage = min(rps, n - srow);
+        const uint8_t* base = ring + size_t(slot) * sp.slot_bytes;
+        // this lane's weight row (B operand) and the two rows whose outputs it holds (D columns 2c, 2c + 1)
+        const int qb = min(8 * tile + g, in_stage - 1);
+        const uint8_t* wb = base + int64_t(qb) * a.row_bytes;
+        const uint8_t* wu = base + int64_t(in_stage + qb) * a.row_bytes;  // up row (SwiGLU)
+        const int qd0 = min(8 * tile + 2 * c, in_stage - 1), qd1 = min(8 * tile + 2 * c + 1, in_stage - 1);
+        const uint16_t* sc0 = reinterpret_cast<const uint16_t*>(base + int64_t(qd0) * a.row_bytes + cbytes);
+        const uint16_t* sc1 = reinterpret_cast<const uint16_t*>(base + int64_t(qd1) * a.row_bytes + cbytes);
+        const uint16_t* su0 = reinterpret_cast<const uint16_t*>(base + int64_t(in_stage + qd0) * a.row_bytes + cbytes);
+        const uint16_t* su1 = reinterpret_cast<const uint16_t*>(base + int64_t(in_stage + qd1) * a.row_bytes + cbytes);
+        float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};  // [gate | up][column 2c + e]
+        if (ok && 8 * tile < in_stage) {
+            for (int b = b_begin; b < b_end; b++) {
+                uint32_t ah0[4] = {0u, 0u, 0u, 0u}, al0[4] = {0u, 0u, 0u, 0u}, ah1[4] = {0u, 0u, 0u, 0u},
+                         al1[4] = {0u, 0u, 0u, 0u};
+                if (xrow) {  // steps 2b (weights 32b + 4c ..) and 2b + 1 (32b + 16 + 4c ..)
+                    const uint2 h0 = *reinterpret_cast<const uint2*>(xhr + 32 * b);
+                    const uint2 l0 = *reinterpret_cast<const uint2*>(xlr + 32 * b);
+                    const uint2 h1 = *reinterpret_cast<const uint2*>(xhr + 32 * b + 16);
+                    const uint2 l1 = *reinterpret_cast<const uint2*>(xlr + 32 * b + 16);
+                    ah0[0] = h0.x, ah0[2] = h0.y, al0[0] = l0.x, al0[2] = l0.y;
+                    ah1[0] = h1.x, ah1[2] = h1.y, al1[0] = l1.x, al1[2] = l1.y;
+                }
+#pragma unroll
+                for (int u = 0; u < 2; u++) {  // gate (or the only) row, then the up row
+                    if (u == 1 && !pair) break;
+                    const uint8_t* w = u ? wu : wb;
+                    uint32_t b00, b01, b10, b11;  // step 0: (b00, b01), step 1: (b10, b11)
+                    if (FMT == kFP8) {
+                        __half2 p0, p1, p2, p3;
+                        e4m3x4_to_half2(*reinterpret_cast<const uint32_t*>(w + 32 * b + 4 * c), p0, p1);
+                        e4m3x4_to_half2(*reinterpret_cast<const uint32_t*>(w + 32 * b + 16 + 4 * c), p2, p3);
+                        b00 = h2u(p0), b01 = h2u(p1), b10 = h2u(p2), b11 = h2u(p3);
+                    } else {  // bytes 4c..4c+3 of the block: low nibbles = weights 4c.., high = 16 + 4c..
+                        const uint32_t wd = *reinterpret_cast<const uint32_t*>(w + 16 * b + 4 * c);
+                        b00 = h2u(__halves2half2(__low2half(fp4x2_to_half2(wd & 0x000F000Fu)),
+                                                 __low2half(fp4x2_to_half2((wd >> 8) & 0x000F000Fu))));
+                        b01 = h2u(__halves2half2(__high2half(fp4x2_to_half2(wd & 0x000F000Fu)),
+                                                 __high2half(fp4x2_to_half2((wd >> 8) & 0x000F000Fu))));
+                        b10 = h2u(__halves2half2(__low2half(fp4x2_to_half2((wd >> 4) & 0x000F000Fu)),
+                                                 __low2half(fp4x2_to_half2((wd >> 12) & 0x000F000Fu))));
+                        b11 = h2u(__halves2half2(__high2half(fp4x2_to_half2((wd >> 4) & 0x000F000Fu)),
+                                                 __high2half(fp4x2_to_half2((wd >> 12) & 0x000F000Fu))));
+                    }
+                    float d[4], dl[4];
+                    mma16816_z(d, ah0, b00, b01);
+                    mma16816_z(dl, al0, b00, b01);
+                    mma16816(d, ah1, b10, b11);
+                    mma16816(dl, al1, b10, b11);
+                    const uint16_t* s0 = u ? su0 : sc0;
+                    const uint16_t* s1 = u ? su1 : sc1;
+                    acc[u][0] = fmaf(half_bits_to_float(s0[b]) * kF, d[0] + dl[0], acc[u][0]);
+                    acc[u][1] = fmaf(half_bits_to_float(s1[b]) * kF, d[1] + dl[1], acc[u][1]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);  // the stage's weights are no longer read
+        // the K parts of each tile, added in order by the part-0 warp
+        float* rb = red + (st & 1) * kSW * 128;
+        if (parts > 1) {
+            *reinterpret_cast<float4*>(rb + (warp * 32 + lane) * 4) = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
+            ssync();
+        }
+        if (part == 0 && ok) {
+            float v[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+            for (int p = 0; p < parts; p++) {
+                const float4 t = parts > 1 ? *reinterpret_cast<const float4*>(rb + ((tile + p * tiles) * 32 + lane) * 4)
+                                           : make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
+                v[0][0] += t.x, v[0][1] += t.y, v[1][0] += t.z, v[1][1] += t.w;
+            }
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int q = 8 * tile + 2 * c + e;
+                if (!xrow || q >= in_stage) continue;
+                const int row = r0 + srow + q, m = g;
+                float* dst = a.y + int64_t(m) * a.y_stride + a.n_off + row;
+                float val;
+                if (pair) {
+                    const float gs = v[0][e], us = v[1][e];
+                    val = gs / (1.0f + expf(-gs)) * us;  // cpu::siluMul (cpu_ops.cpp:526-533)
+                } else {
+                    val = v[0][e];
+                    if (a.flags & kBias) val += a.bias[row];
+                    if (a.flags & kGelu) val = gelu(val);
+                    if (a.flags & kAccumulate) val += *dst;
+                }
+                *dst = val;
+                if (a.argmax) best = max(best, argmax_key(val, row));
+            }
+        }
+        if (++slot == sp.nslot) {
+            slot = 0;
+            par ^= 1;
+        }
+    }
+    if (a.argmax) {  // the 4 lanes of each activation row, then per CTA, then one global atomic per row
+        best = max(best, __shfl_xor_sync(0xffffffffu, best, 1));
+        best = max(best, __shfl_xor_sync(0xffffffffu, best, 2));
+        if (c == 0 && xrow && best) atomicMax(&t_key[g], best);
+        ssync();
+        if (threadIdx.x < a.M && t_key[threadIdx.x]) atomicMax(a.argmax + threadIdx.x, t_key[threadIdx.x]);
+    }
+}
+
 using StreamFn = void (*)(const GemvArgs, const StreamPlan);
 
 StreamFn pick(int fmt, int M) {
@@ -285,9 +541,61 @@ StreamFn pick(int fmt, int M) {
 
 }  // namespace
 
+// The tensor-core streaming kernel: activations as hi / lo f16 in shared memory (<= 64 KB), stages of 8 T rows
+// with T the largest divisor of the consumer warp count that does not exceed the CTA's rows (rounded up to a
+// tile) and leaves a ring of four stages (three, then two, for wide rows).
+cudaError_t launch_gemv_mma(const GemvArgs& a, cudaStream_t st, bool pdl) {
+    const int64_t xs = (int64_t(a.M) * a.K * 4 + 127) / 128 * 128;
+    if (xs > 64 * 1024 || a.K % kQuantBlock) return cudaErrorNotSupported;
+    const int64_t rbe = a.row_bytes * (a.pair_off ? 2 : 1);
+    MmaPlan sp;
+    const int sms = num_sms();
+    int ctas = std::max(1, std::min(sms, (a.rows + 3) / 4));
+    sp.rows_per_cta = (a.rows + ctas - 1) / ctas;
+    ctas = (a.rows + sp.rows_per_cta - 1) / sp.rows_per_cta;
+    sp.xs_bytes = int(xs);
+    const int64_t budget = 227 * 1024 - kSStatic - 256 - xs - kMmaRedBytes;
+    const int tneed = (sp.rows_per_cta + 7) / 8;
+    int cap = kSW;
+    for (int t = 1; t <= kSW; t++)
+        if (kSW % t == 0 && t >= tneed) {
+            cap = t;
+            break;
+        }
+    sp.tiles = 0;
+    for (int want : {4, 3, 2}) {
+        for (int t = kSW; t >= 1; t--) {
+            if (kSW % t) continue;
+            const int64_t sb = (8 * t * rbe + 127) / 128 * 128;
+            if (t <= cap && budget / sb >= want) {
+                sp.tiles = t;
+                sp.slot_bytes = int(sb);
+                break;
+            }
+        }
+        if (sp.tiles) break;
+    }
+    if (!sp.tiles) return cudaErrorNotSupported;
+    sp.rps = 8 * sp.tiles;
+    sp.nslot = int(std::min<int64_t>(kSMaxSlots, budget / sp.slot_bytes));
+    auto k = a.fmt == kFP8 ? gemv_mma_kernel<kFP8> : gemv_mma_kernel<kFP4>;
+    const size_t smem = 256 + size_t(xs) + kMmaRedBytes + size_t(sp.nslot) * sp.slot_bytes;
+    static int attr_set[2][32] = {};  // per (format, device < 32): the limit only grows
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int* set = dev < 32 ? &attr_set[a.fmt == kFP8 ? 0 : 1][dev] : nullptr;
+    if (!set || *set < int(smem)) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        if (set) *set = int(smem);
+    }
+    return launch_ex(k, dim3(ctas), dim3(kSThr), smem, st, pdl, a, sp);
+}
+
 // The streaming kernel takes the call when it fits: 1..4 FP8 / FP4 activation rows, activations (padded) in
 // 64 KB of shared memory, a ring of at least the stages a pass can span. Returns cudaErrorNotSupported (and
-// launches nothing) otherwise, so the caller falls back to the general kernel.
+// launches nothing) otherwise, so the caller falls back to the general kernel. The tensor-core variant runs
+// when it fits; the CUDA-core one otherwise.
 cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl) {
     if (a.M < 1 || a.M > kDecodeMaxSeqs || (a.fmt != kFP8 && a.fmt != kFP4)) return cudaErrorNotSupported;
     if (a.x_stride % 4 || (reinterpret_cast<uintptr_t>(a.x) & 15) || a.K % 4) return cudaErrorNotSupported;
@@ -297,6 +605,8 @@ cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl) {
     if (a.norm != kNormNone && !gemv_norm_fusable(a.fmt, a.M, a.K)) return cudaErrorNotSupported;
     const int64_t rbe = a.row_bytes * (a.pair_off ? 2 : 1);
     if (a.row_bytes % 16) return cudaErrorNotSupported;
+    if (a.M >= 2)
+        if (const cudaError_t e = launch_gemv_mma(a, st, pdl); e != cudaErrorNotSupported) return e;
     StreamPlan sp;
     const int sms = num_sms();
     int ctas = std::max(1, std::min(sms, (a.rows + 3) / 4));
