@@ -301,7 +301,7 @@ def run_ours(args):
     cpu_on = (rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile
               and os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libneko_ref.so")))
     h16 = [] if cpu_on else None
-    m = nmodel.Model(s, FMT, context=context, max_seqs=B, max_rows=64)
+    m = nmodel.Model(s, FMT, context=context, max_seqs=B, max_rows=64, device=local)
     m.load_random_device(seed=0, host_copy=(lambda n, a: h16.append((n, a))) if cpu_on else None)
 
     # prefill every sequence (different prompts per rank and sequence)

@@ -936,8 +936,19 @@ static int set_tensor_entry(neko_model* m, const char* name, const float* data, 
                             bool on_device) {
     if (!m) return NEKO_ERR_ARG;
     Guard g(m->device);
-    // device data may come from work on another stream (e.g. a framework's generator): let it finish first
-    if (on_device) CK(cudaDeviceSynchronize(), "set_tensor_device");
+    if (on_device) {
+        // the runner's kernels read the tensor on its own device: memory of another device is refused here
+        // (a kernel would fault on it without peer access)
+        cudaPointerAttributes pa{};
+        if (cudaPointerGetAttributes(&pa, data) != cudaSuccess || pa.type != cudaMemoryTypeDevice ||
+            pa.device != m->device) {
+            cudaGetLastError();
+            return fail(m, NEKO_ERR_ARG, "set_tensor_device: the data is not device memory of the model's device " +
+                                             std::to_string(m->device));
+        }
+        // device data may come from work on another stream (e.g. a framework's generator): let it finish first
+        CK(cudaDeviceSynchronize(), "set_tensor_device");
+    }
     return set_tensor(m, name, data, rows, cols, on_device);
 }
 

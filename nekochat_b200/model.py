@@ -16,8 +16,20 @@ def _p(a):
     return None if a is None else a.ctypes.data_as(C.c_void_p)
 
 
+def _current_device():
+    try:
+        import torch
+        return torch.cuda.current_device() if torch.cuda.is_available() else 0
+    except ImportError:
+        return 0
+
+
 class Model:
-    def __init__(self, shape, fmt, context, max_seqs=1, max_rows=64, device=0):
+    def __init__(self, shape, fmt, context, max_seqs=1, max_rows=64, device=None):
+        """device: CUDA device index of the runner (default: torch's current device, else 0)."""
+        if device is None:
+            device = _current_device()
+        self.device = device
         s = dict(shape)
         self.shape = s
         cfg = ModelConfig()
@@ -46,6 +58,8 @@ class Model:
 
     def set_tensor_device(self, name, t):
         """t: a contiguous float32 CUDA tensor on the model's device."""
+        if t.device.type != "cuda" or t.device.index != self.device:
+            raise NekoError(f"set_tensor_device {name}: tensor on {t.device}, model on cuda:{self.device}")
         rows, cols = (t.shape[0], t.numel() // t.shape[0]) if t.dim() > 1 else (1, t.shape[0])
         self._check(lib().neko_model_set_tensor_device(self.h, name.encode(), C.c_void_p(t.data_ptr()), rows, cols),
                     f"set_tensor_device {name}")
@@ -55,14 +69,15 @@ class Model:
         biases, in workload.tensor_specs order. host_copy(name, f16 numpy array) receives each tensor for a CPU
         baseline checkpoint when given."""
         import torch
-        g = torch.Generator(device="cuda").manual_seed(seed)
+        dev = torch.device("cuda", self.device)
+        g = torch.Generator(device=dev).manual_seed(seed)
         for name, shp, kind in workload.tensor_specs(self.shape):
             if kind == "w":
-                t = torch.randn(shp, generator=g, device="cuda", dtype=torch.float32).mul_(0.02)
+                t = torch.randn(shp, generator=g, device=dev, dtype=torch.float32).mul_(0.02)
             elif kind == "g":
-                t = torch.ones(shp, device="cuda", dtype=torch.float32)
+                t = torch.ones(shp, device=dev, dtype=torch.float32)
             else:
-                t = torch.zeros(shp, device="cuda", dtype=torch.float32)
+                t = torch.zeros(shp, device=dev, dtype=torch.float32)
             self.set_tensor_device(name, t)
             if host_copy is not None:
                 host_copy(name, t.half().cpu().numpy())
@@ -176,7 +191,7 @@ class Model:
             pass
 
 
-def build(shape_name, fmt, context, max_seqs=1, max_rows=64, seed=0, perturb=False, device=0):
+def build(shape_name, fmt, context, max_seqs=1, max_rows=64, seed=0, perturb=False, device=None):
     s = workload.shape(shape_name)
     m = Model(s, fmt, context, max_seqs, max_rows, device)
     return m.load(workload.weights(s, seed, perturb))

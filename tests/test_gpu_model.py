@@ -10,6 +10,7 @@ import os
 import numpy as np
 import pytest
 
+import nekochat_b200 as nb
 from nekochat_b200 import workload
 from nekochat_b200 import model as nmodel
 from oracle import models as omodels
@@ -139,4 +140,19 @@ def test_forward_rejects_bad_input():
         m.forward([1] * 9, 0)               # batch above max_rows
     with pytest.raises(nb.NekoError):
         m.forward([1, 2], 31)               # context overflow
+    m.close()
+
+
+def test_device_tensor_on_another_device_is_refused():
+    """Weights in another GPU's memory are refused by the host with an error (a kernel would fault on them)."""
+    import ctypes as C
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    m = nmodel.build("qwen3-tiny", FP8, context=32, max_seqs=1, max_rows=8, device=0)
+    t = torch.zeros((4, 4), device="cuda:1")
+    rc = nb.lib().neko_model_set_tensor_device(m.h, b"embed_tokens.weight", C.c_void_p(t.data_ptr()), 4, 4)
+    assert rc != 0 and "device" in nb.lib().neko_model_last_error(m.h).decode()
+    with pytest.raises(nb.NekoError, match="cuda:1"):
+        m.set_tensor_device("embed_tokens.weight", t)
     m.close()
