@@ -408,7 +408,7 @@ TcPlan tc_plan(const GemvArgs& a, int64_t ws_floats) {
     const int64_t tiles = int64_t(p.ntile) * p.mblk;
     // activations split once when at least 8 tiles share them
     p.x_floats = int64_t(a.M) * a.K;  // hi + lo halves
-    p.presplit = (p.ntile >= 8 || a.norm != kNormNone) && ws_floats >= p.x_floats;
+    p.presplit = (p.ntile >= 8 || a.norm != kNormNone || a.M >= 64) && ws_floats >= p.x_floats;
     // K splits (one cluster per tile): about two CTAs per SM, each with at least 2 stages
     p.ksplit = 1;
     if (tiles < 2 * sms)
@@ -487,6 +487,9 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl) {
                           const_cast<__half*>(sp.xh), const_cast<__half*>(sp.xl));
         }
         if (e != cudaSuccess) return e;
+        // 128+ rows: the tcgen05 kernel (TMEM accumulators) on the split activations
+        e = launch_gemm_umma(a, sp.xh, sp.xl, st, true);
+        if (e != cudaErrorNotSupported) return e;
     }
     const bool pre = pl.presplit;
     TcFn k = a.fmt == kFP8 ? (pre ? pick<kFP8, true>(pair) : pick<kFP8, false>(pair))

@@ -1,0 +1,413 @@
+// Dequant matmul on the 5th-generation tensor cores (tcgen05 / UMMA, TMEM accumulators) for 128+ activation rows
+// (prefill chunks): the MatmulQ8 / MatmulQ4 dispatch (matmul_q8.comp, matmul_q4.comp;
+// cpu::matmul, cpu_ops.cpp:462-481) where the multiply-adds are the cost.
+//
+// y[m][n] (+)= act(x[m] . deq(W[n]) + b[n]) with the precision of the fp32 kernels:
+//  * each weight enters as its dequantised value w = code x scale (QMatrix::dequantizeRow's product, exact in fp32
+//    with at most 15 significant bits) split into two f16, w = w_hi + w_lo: w_hi = f16(code x scale) (hmul),
+//    w_lo = fma(code, scale, -w_hi) (the exact residual, rounded only when it falls below f16's subnormal step,
+//    an absolute error under 3e-8 per weight). Folding the block scale into the operand lets TMEM accumulate over
+//    all of K, with no per-block rescaling;
+//  * the activations arrive split into hi + lo f16 (split_act_kernel / norm_split_kernel, about 22 bits);
+//  * D = x_hi w_hi + x_lo w_hi + x_hi w_lo (three UMMAs per 16-wide K step; x_lo w_lo is below 2^-22 relative),
+//    fp32 in TMEM.
+// CTA tile: 128 activation rows (UMMA M = 128; rows past M are zero) x BN = 64 / 128 weight rows (SwiGLU: BN / 2
+// gate + BN / 2 up rows), K in stages of 64 (one 128-byte swizzle atom of f16). Eight warps: every thread stages
+// the activations (cp.async into the 128B-swizzled K-major layout) and converts the weight codes of a stage into
+// the same layout; thread 0 issues the UMMAs and commits them to the stage's mbarrier, which frees the stage's
+// buffers for the stage three ahead. K is split over a thread-block cluster (<= 8 CTAs) when the tiles leave SMs
+// idle: each CTA moves its fp32 tile from TMEM to shared memory and CTA z sums rows z, z + ks, ... over the
+// cluster in split order (deterministic), then runs the epilogue. All waits are bounded; TMEM is always freed.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+
+#include "gemv_core.cuh"
+#include "mma_frag.cuh"
+#include "neko_common.cuh"
+#include "neko_internal.h"
+
+namespace neko {
+
+namespace {
+
+constexpr int kUM = 128;       // activation rows per CTA (UMMA M)
+constexpr int kUK = 64;        // K per stage: 64 f16 = one 128-byte swizzle atom
+constexpr int kUBufs = 3;      // f16 operand buffers
+constexpr int kUThreads = 256;
+constexpr int kUMaxSplit = 8;  // CTAs of a cluster (portable limit)
+// Below 128 rows the mma.sync kernel is faster (measured: M = 64 decode-layer shapes 27-31 us there vs 33 us
+// here, where two stages of prefetch leave the pipeline latency-bound); from 128 rows on, this one (M = 512:
+// 1.3-1.5x).
+constexpr int kUMinRows = 128;
+
+// ------------------------------------------------------------------------------------------------ tcgen05 PTX
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart (SBO), version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
+           (uint64_t(2) << 61);
+}
+// Instruction descriptor of kind::f16: f32 accumulator, f16 A and B, both K-major, N >> 3, M >> 4.
+__host__ __device__ constexpr uint32_t f16_idesc(int M, int N) {
+    return (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// 32 lanes x 16 columns of fp32 from TMEM (this warp's lane quarter)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Byte offset of f16 element (row r, k) in a K-major tile of 64-wide rows with the 128-byte swizzle (the
+// tile starts on a 1024-byte boundary): 16-byte chunk k / 8 of row r is stored at chunk (k / 8) ^ (r % 8).
+__device__ __forceinline__ uint32_t sw128_off(int r, int chunk) {
+    return uint32_t((r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4));
+}
+
+struct UmmaSplit {
+    int ksplit, sper;
+    const __half* xh;  // activations as f16 hi / lo, [M][K] each
+    const __half* xl;
+};
+
+template <int FMT, int BN, bool PAIR>
+struct UmmaSmem {
+    static constexpr int kCode = FMT == kFP8 ? kUK : kUK / 2;            // code bytes per row per stage
+    static constexpr int kATile = kUM * kUK * 2;                         // bytes of one f16 A tile
+    static constexpr int kBTile = BN * kUK * 2;                          // bytes of one f16 B tile
+    static constexpr int kBuf = 2 * kATile + 2 * kBTile;                 // A hi, A lo, B hi, B lo
+    static constexpr int kRaw = BN * kCode + BN * 4;                     // codes + 2 scales per row
+    static constexpr int kRawOff = kUBufs * kBuf;
+    static constexpr int kBytes = kRawOff + 2 * kRaw;                    // + two raw code buffers
+    static constexpr int kTilePitch = BN + 4;                            // epilogue fp32 tile pitch
+    static_assert(kUM * kTilePitch * 4 <= kUBufs * kBuf, "epilogue tile fits the operand buffers");
+};
+
+template <int FMT, int BN, bool PAIR>
+__global__ void __launch_bounds__(kUThreads, 1) umma_gemm_kernel(const GemvArgs a, const UmmaSplit sp) {
+    using L = UmmaSmem<FMT, BN, PAIR>;
+    extern __shared__ uint8_t usm_raw[];
+    __shared__ uint64_t mma_bar[kUBufs];
+    __shared__ uint32_t tmem_base;
+    __shared__ int s_fail;
+    // operand tiles need 1024-byte alignment (the swizzle pattern is anchored on address bits 7..9)
+    uint8_t* usm = usm_raw + ((1024 - (smem_u32(usm_raw) & 1023)) & 1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * (PAIR ? BN / 2 : BN), m0 = blockIdx.y * kUM, z = blockIdx.z;
+    const int mv = min(kUM, a.M - m0);
+    const int cbytes = FMT == kFP8 ? a.K : a.K / 2;
+    const int s_begin = z * sp.sper, nst = min(a.K / kUK, s_begin + sp.sper) - s_begin;
+    constexpr uint32_t kIdesc = f16_idesc(kUM, BN);
+
+    if (warp == 0) {  // TMEM: BN fp32 columns x 128 lanes
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                     "r"(BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int b = 0; b < kUBufs; b++) mbar_init(&mma_bar[b], 1);
+        fence_barrier_init();
+        s_fail = 0;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+
+    // weight row r of the tile (SwiGLU: gate rows, then up rows) -> packed row (rows past the end repeat the last)
+    auto wrow = [&](int r) -> const uint8_t* {
+        const int n = PAIR ? (r < BN / 2 ? n0 + r : n0 + (r - BN / 2)) : n0 + r;
+        const int nc = min(n, a.rows - 1);
+        return a.W + (int64_t(nc) + (PAIR && r >= BN / 2 ? a.pair_off : 0)) * a.row_bytes;
+    };
+    auto buf = [&](int i) { return usm + (i % kUBufs) * L::kBuf; };
+    auto raw = [&](int i) { return usm + L::kRawOff + (i & 1) * L::kRaw; };
+    // weight codes + scales of stage i (index within this CTA's range) -> raw buffer i & 1
+    auto issue_w = [&](int i) {
+        const int s = s_begin + i;
+        uint8_t* rb = raw(i);
+        constexpr int kPieces = L::kCode / 16;
+        for (int j = tid; j < BN * kPieces; j += kUThreads) {
+            const int r = j / kPieces, q = j - r * kPieces;
+            cp16(rb + r * L::kCode + 16 * q, wrow(r) + s * L::kCode + 16 * q, 16);
+        }
+        for (int r = tid; r < BN; r += kUThreads) cp4(rb + BN * L::kCode + 4 * r, wrow(r) + cbytes + 4 * s);
+    };
+    // activations (hi, lo) of stage i -> the A tiles of buffer i, swizzled (rows past M stay zero: cleared once)
+    auto issue_x = [&](int i) {
+        const int s = s_begin + i;
+        uint8_t* bb = buf(i);
+        for (int j = tid; j < 2 * mv * 8; j += kUThreads) {
+            const int h = j >= mv * 8 ? 1 : 0, jj = j - h * mv * 8, r = jj >> 3, q = jj & 7;
+            cp16(bb + h * L::kATile + sw128_off(r, q), (h ? sp.xl : sp.xh) + int64_t(m0 + r) * a.K + s * kUK + 8 * q,
+                 16);
+        }
+    };
+    if (mv < kUM) {  // A rows past M: zero in every buffer, never written again
+        for (int j = tid; j < kUBufs * 2 * (kUM - mv) * 8; j += kUThreads) {
+            const int b = j / (2 * (kUM - mv) * 8), jj = j - b * 2 * (kUM - mv) * 8;
+            const int h = jj >= (kUM - mv) * 8 ? 1 : 0, k2 = jj - h * (kUM - mv) * 8, r = mv + (k2 >> 3), q = k2 & 7;
+            *reinterpret_cast<uint4*>(usm + b * L::kBuf + h * L::kATile + sw128_off(r, q)) = make_uint4(0, 0, 0, 0);
+        }
+    }
+    // raw buffer i & 1 -> B hi / lo tiles of buffer i: w = code x scale split into two f16
+    auto convert = [&](int i) {
+        const uint8_t* rb = raw(i);
+        uint8_t* bb = buf(i) + 2 * L::kATile;
+        for (int j = tid; j < BN * 8; j += kUThreads) {
+            const int r = j >> 3, q = j & 7;  // row r, weights 8q .. 8q + 7 of the stage
+            const uint16_t sbits = *reinterpret_cast<const uint16_t*>(rb + BN * L::kCode + 4 * r + 2 * (q >> 2));
+            __half2 sc = __halves2half2(__ushort_as_half(sbits), __ushort_as_half(sbits));
+            __half2 c[4];
+            if (FMT == kFP8) {
+                const uint2 w = *reinterpret_cast<const uint2*>(rb + r * L::kCode + 8 * q);
+                e4m3x4_to_half2(w.x, c[0], c[1]);
+                e4m3x4_to_half2(w.y, c[2], c[3]);
+            } else {  // weights 8q.. of a 32-block: low nibbles of bytes 8(q%4).. (q%4 < 2) or high nibbles
+                const int blk = q >> 2, j0 = 8 * (q & 3);
+                const uint2 w = *reinterpret_cast<const uint2*>(rb + r * L::kCode + 16 * blk + (j0 & 15));
+                const int sh = j0 >= 16 ? 4 : 0;
+                const __half2 k16 = __float2half2_rn(kFp4Factor);  // engine FP4 decode (value / 16384) x 16384
+                const uint32_t wd[2] = {w.x >> sh, w.y >> sh};
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    const __half2 e = fp4x2_to_half2(wd[u] & 0x000F000Fu);         // weights 4u, 4u + 2
+                    const __half2 o = fp4x2_to_half2((wd[u] >> 8) & 0x000F000Fu);  // weights 4u + 1, 4u + 3
+                    c[2 * u] = __hmul2(__halves2half2(__low2half(e), __low2half(o)), k16);
+                    c[2 * u + 1] = __hmul2(__halves2half2(__high2half(e), __high2half(o)), k16);
+                }
+            }
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const __half2 h = __hmul2(c[u], sc);
+                hi[u] = h2u(h);
+                lo[u] = h2u(__hfma2(c[u], sc, __hneg2(h)));
+            }
+            *reinterpret_cast<uint4*>(bb + sw128_off(r, q)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(bb + L::kBTile + sw128_off(r, q)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+    };
+    // bounded wait for the UMMAs of stage i (their commit): their buffer is free / their results are in TMEM
+    auto mma_wait = [&](int i) {
+        if (!mbar_wait(&mma_bar[i % kUBufs], uint32_t(i / kUBufs) & 1u)) s_fail = 1;
+    };
+
+    // prologue: stages 0 and 1 (weights before the dependency wait: they never depend on the previous kernel)
+    if (nst > 0) issue_w(0);
+    if (nst > 1) issue_w(1);
+    pdl_wait();
+    if (nst > 0) issue_x(0);
+    cp_commit();
+    if (nst > 1) issue_x(1);
+    cp_commit();
+    for (int i = 0; i < nst; i++) {
+        cp_wait<1>();  // stage i landed (this thread's copies)
+        __syncthreads();
+        if (i >= kUBufs) mma_wait(i - kUBufs);  // buffer i % 3 was last read by the UMMAs of stage i - 3
+        convert(i);
+        fence_proxy_async();  // generic-proxy writes (conversions, cp.async) -> visible to the tensor cores
+        __syncthreads();
+        if (tid == 0 && !s_fail) {
+            tc_fence_after();
+            const uint8_t* bb = buf(i);
+            const uint32_t ah = smem_u32(bb), al = ah + L::kATile, bh = al + L::kATile, bl = bh + L::kBTile;
+#pragma unroll
+            for (int k = 0; k < kUK / 16; k++) {  // 16-wide K steps: 32 bytes into each swizzled row
+                const uint32_t o = 32 * k;
+                umma_f16(tmem, sw128_desc(ah + o), sw128_desc(bh + o), kIdesc, (i > 0 || k > 0) ? 1u : 0u);
+                umma_f16(tmem, sw128_desc(al + o), sw128_desc(bh + o), kIdesc, 1u);
+                umma_f16(tmem, sw128_desc(ah + o), sw128_desc(bl + o), kIdesc, 1u);
+            }
+            umma_commit(&mma_bar[i % kUBufs]);
+        }
+        // stage i + 2: its weights into the raw buffer just converted, its activations into buffer (i + 2) % 3,
+        // last read by the UMMAs of stage i - 1
+        if (i + 2 < nst) {
+            if (i >= 1) mma_wait(i - 1);
+            issue_w(i + 2);
+            issue_x(i + 2);
+        }
+        cp_commit();
+    }
+    // every UMMA of this CTA has completed (the last commit tracks all earlier ones)
+    if (nst > 0) mma_wait(nst - 1);
+    pdl_trigger();
+    tc_fence_after();
+    __syncthreads();
+
+    // TMEM -> this CTA's fp32 tile in shared memory (row = lane of the warp's quarter, BN columns)
+    constexpr int TP = L::kTilePitch;
+    float* tile = reinterpret_cast<float*>(usm);
+    const bool ok = !s_fail && nst > 0;
+    {
+        const int quarter = warp & 3, row = 32 * quarter + lane;
+        constexpr int kHalf = BN / (kUThreads / 128);  // columns per warp of a lane quarter
+#pragma unroll 1
+        for (int c0 = (warp >> 2) * kHalf; c0 < (warp >> 2) * kHalf + kHalf; c0 += 16) {
+            float v[16];
+            if (ok) tmem_ld16(tmem + (uint32_t(32 * quarter) << 16) + uint32_t(c0), v);
+            else
+#pragma unroll
+                for (int u = 0; u < 16; u++) v[u] = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 16; u += 4)
+                *reinterpret_cast<float4*>(tile + row * TP + c0 + u) = make_float4(v[u], v[u + 1], v[u + 2], v[u + 3]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+    namespace cg = cooperative_groups;
+    const int ks = sp.ksplit;
+    if (ks > 1) cg::this_cluster().sync();  // every split's tile is in place
+    if (s_fail) set_device_error(kErrMbarTimeout);
+
+    // rows z, z + ks, ...: the splits summed in order, then bias / GELU / accumulate or SiLU * up
+    constexpr int OC = PAIR ? BN / 2 : BN;
+    const float* peer[kUMaxSplit];
+#pragma unroll
+    for (int zz = 0; zz < kUMaxSplit; zz++)
+        peer[zz] = zz < ks ? (ks > 1 ? cg::this_cluster().map_shared_rank(tile, zz) : tile) : tile;
+    __shared__ unsigned long long keys[kUM];
+    if (a.argmax && tid < kUM) keys[tid] = 0ull;
+    __syncthreads();
+    const int nrow = (mv - z + ks - 1) / ks;
+    static_assert(OC % 32 == 0, "a warp's 32 elements share a row");
+    for (int i = tid; i < nrow * OC; i += kUThreads) {
+        const int row = z + ks * (i / OC), col = i - (i / OC) * OC;
+        const int m = m0 + row, n = n0 + col;
+        float v = 0.0f, u = 0.0f;
+#pragma unroll
+        for (int zz = 0; zz < kUMaxSplit; zz++) {
+            if (zz >= ks) break;
+            v += peer[zz][row * TP + col];
+            if (PAIR) u += peer[zz][row * TP + BN / 2 + col];
+        }
+        unsigned long long key = 0ull;
+        if (n < a.rows) {
+            float* dst = a.y + int64_t(m) * a.y_stride + a.n_off + n;
+            float val = v;
+            if (PAIR) {
+                val = val / (1.0f + expf(-val)) * u;  // cpu::siluMul (cpu_ops.cpp:526-533)
+            } else {
+                if (a.flags & kBias) val += a.bias[n];
+                if (a.flags & kGelu) val = gelu(val);
+                if (a.flags & kAccumulate) val += *dst;
+            }
+            *dst = val;
+            key = argmax_key(val, n);
+        }
+        if (a.argmax) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+            if (lane == 0 && key) atomicMax(&keys[row], key);
+        }
+    }
+    if (a.argmax) {
+        __syncthreads();
+        if (tid < nrow && keys[z + ks * tid]) atomicMax(a.argmax + m0 + z + ks * tid, keys[z + ks * tid]);
+    }
+    if (ks > 1) cg::this_cluster().sync();  // no CTA leaves while a peer may still read its tile
+}
+
+using UmmaFn = void (*)(const GemvArgs, const UmmaSplit);
+
+template <int FMT>
+UmmaFn pick_umma(int bn, bool pair) {
+    if (pair) return bn == 128 ? umma_gemm_kernel<FMT, 128, true> : umma_gemm_kernel<FMT, 64, true>;
+    return bn == 128 ? umma_gemm_kernel<FMT, 128, false> : umma_gemm_kernel<FMT, 64, false>;
+}
+template <int FMT>
+size_t umma_smem(int bn, bool pair) {
+    const int b = pair ? (bn == 128 ? UmmaSmem<FMT, 128, true>::kBytes : UmmaSmem<FMT, 64, true>::kBytes)
+                       : (bn == 128 ? UmmaSmem<FMT, 128, false>::kBytes : UmmaSmem<FMT, 64, false>::kBytes);
+    return size_t(b) + 1024;  // + alignment slack
+}
+
+}  // namespace
+
+// The tcgen05 kernel takes 128+ activation rows of FP8 / FP4 weights whose activations were split into hi / lo
+// f16 (xh, xl: [M][K]); K a multiple of 64. cudaErrorNotSupported otherwise.
+cudaError_t launch_gemm_umma(const GemvArgs& a, const __half* xh, const __half* xl, cudaStream_t st, bool pdl) {
+    if (a.M < kUMinRows || (a.fmt != kFP8 && a.fmt != kFP4) || a.K % kUK || !xh || !xl || a.row_bytes % 16 ||
+        (a.pair_off && a.argmax))
+        return cudaErrorNotSupported;
+    const bool pair = a.pair_off != 0;
+    const int sms = num_sms(), nst = a.K / kUK;
+    const int mblk = (a.M + kUM - 1) / kUM;
+    // 128 weight rows per CTA when that still gives every SM a tile, else 64
+    int bn = 128;
+    if (int64_t((a.rows + (pair ? 63 : 127)) / (pair ? 64 : 128)) * mblk < sms) bn = 64;
+    const int outs = pair ? bn / 2 : bn;
+    const int ntile = (a.rows + outs - 1) / outs;
+    const int64_t tiles = int64_t(ntile) * mblk;
+    int ks = 1;
+    if (tiles < sms) ks = int(std::min<int64_t>({(sms + tiles - 1) / tiles, int64_t(kUMaxSplit), std::max(1, nst / 2)}));
+    UmmaSplit sp;
+    sp.sper = (nst + ks - 1) / ks;
+    sp.ksplit = (nst + sp.sper - 1) / sp.sper;
+    sp.xh = xh;
+    sp.xl = xl;
+    UmmaFn k = a.fmt == kFP8 ? pick_umma<kFP8>(bn, pair) : pick_umma<kFP4>(bn, pair);
+    const size_t smem = a.fmt == kFP8 ? umma_smem<kFP8>(bn, pair) : umma_smem<kFP4>(bn, pair);
+    if (smem > 227 * 1024) return cudaErrorNotSupported;
+    static int attr_set[2][2][2][8] = {};  // per (format, BN, pair, device < 8)
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int* set = dev < 8 ? &attr_set[a.fmt == kFP8 ? 0 : 1][bn == 128][pair][dev] : nullptr;
+    if (!set || *set < int(smem)) {
+        if (cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+            e != cudaSuccess)
+            return e;
+        if (set) *set = int(smem);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ntile, mblk, sp.ksplit);
+    cfg.blockDim = dim3(kUThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (sp.ksplit > 1) {  // the K splits of a tile form one cluster
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = sp.ksplit;
+        na++;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, k, a, sp);
+}
+
+}  // namespace neko

@@ -1,6 +1,7 @@
 // Internal host-side declarations shared by the CUDA translation units of libneko_cuda.so.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -95,6 +96,9 @@ cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, bool pdl, int max_ctas = 0)
 cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl);
 // The tensor-core kernel for 5+ activation rows (k_mma.cu); cudaErrorNotSupported when the call does not fit.
 cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl);
+// The tcgen05 kernel (k_umma.cu) for 128+ rows on activations split into f16 hi / lo ([M][K] each);
+// cudaErrorNotSupported when the call does not fit.
+cudaError_t launch_gemm_umma(const GemvArgs& a, const __half* xh, const __half* xl, cudaStream_t st, bool pdl);
 // Workspace (floats, tickets) with which launch_gemm_tc splits this matmul's activations once (norm: with the
 // norm prologue applied); 0, 0 when it needs none or the tensor-core path does not apply.
 void gemm_tc_scratch(int fmt, int rows, int K, int M, bool pair, bool norm, int64_t* floats, int64_t* tickets);
