@@ -15,7 +15,7 @@
 // gate + BN / 2 up rows), K in stages of 64 (one 128-byte swizzle atom of f16). Eight warps: every thread stages
 // the activations (cp.async into the 128B-swizzled K-major layout) and converts the weight codes of a stage into
 // the same layout; thread 0 issues the UMMAs and commits them to the stage's mbarrier, which frees the stage's
-// buffers for the stage three ahead. K is split over a thread-block cluster (<= 8 CTAs) when the tiles leave SMs
+// buffers for a later stage (3 buffers at BN = 128, 4 at BN = 64: the copies run 2 or 3 stages ahead). K is split over a thread-block cluster (<= 8 CTAs) when the tiles leave SMs
 // idle: each CTA moves its fp32 tile from TMEM to shared memory and CTA z sums rows z, z + ks, ... over the
 // cluster in split order (deterministic), then runs the epilogue. All waits are bounded; TMEM is always freed.
 #include <cooperative_groups.h>
@@ -33,7 +33,7 @@ namespace {
 
 constexpr int kUM = 128;       // activation rows per CTA (UMMA M)
 constexpr int kUK = 64;        // K per stage: 64 f16 = one 128-byte swizzle atom
-constexpr int kUBufs = 3;      // f16 operand buffers
+constexpr int kUMaxBufs = 4;   // f16 operand buffers (3 at BN = 128, 4 at BN = 64: shared memory)
 constexpr int kUThreads = 256;
 constexpr int kUMaxSplit = 8;  // CTAs of a cluster (portable limit)
 // Below 128 rows the mma.sync kernel is faster (measured: M = 64 decode-layer shapes 27-31 us there vs 33 us
@@ -98,18 +98,22 @@ struct UmmaSmem {
     static constexpr int kATile = kUM * kUK * 2;                         // bytes of one f16 A tile
     static constexpr int kBTile = BN * kUK * 2;                          // bytes of one f16 B tile
     static constexpr int kBuf = 2 * kATile + 2 * kBTile;                 // A hi, A lo, B hi, B lo
+    static constexpr int NB = BN == 64 ? 4 : 3;                          // operand buffers
+    static constexpr int P = NB - 1;                                     // stages in flight ahead
     static constexpr int kRaw = BN * kCode + BN * 4;                     // codes + 2 scales per row
-    static constexpr int kRawOff = kUBufs * kBuf;
-    static constexpr int kBytes = kRawOff + 2 * kRaw;                    // + two raw code buffers
+    static constexpr int kRawOff = NB * kBuf;
+    static constexpr int kBytes = kRawOff + P * kRaw;                    // + P raw code buffers
     static constexpr int kTilePitch = BN + 4;                            // epilogue fp32 tile pitch
-    static_assert(kUM * kTilePitch * 4 <= kUBufs * kBuf, "epilogue tile fits the operand buffers");
+    static_assert(NB <= kUMaxBufs, "barriers");
+    static_assert(kUM * kTilePitch * 4 <= NB * kBuf, "epilogue tile fits the operand buffers");
 };
 
 template <int FMT, int BN, bool PAIR>
 __global__ void __launch_bounds__(kUThreads, 1) umma_gemm_kernel(const GemvArgs a, const UmmaSplit sp) {
     using L = UmmaSmem<FMT, BN, PAIR>;
     extern __shared__ uint8_t usm_raw[];
-    __shared__ uint64_t mma_bar[kUBufs];
+    __shared__ uint64_t mma_bar[kUMaxBufs];
+    constexpr int NB = L::NB, P = L::P;
     __shared__ uint32_t tmem_base;
     __shared__ int s_fail;
     // operand tiles need 1024-byte alignment (the swizzle pattern is anchored on address bits 7..9)
@@ -128,7 +132,7 @@ __global__ void __launch_bounds__(kUThreads, 1) umma_gemm_kernel(const GemvArgs 
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        for (int b = 0; b < kUBufs; b++) mbar_init(&mma_bar[b], 1);
+        for (int b = 0; b < NB; b++) mbar_init(&mma_bar[b], 1);
         fence_barrier_init();
         s_fail = 0;
     }
@@ -143,9 +147,9 @@ __global__ void __launch_bounds__(kUThreads, 1) umma_gemm_kernel(const GemvArgs 
         const int nc = min(n, a.rows - 1);
         return a.W + (int64_t(nc) + (PAIR && r >= BN / 2 ? a.pair_off : 0)) * a.row_bytes;
     };
-    auto buf = [&](int i) { return usm + (i % kUBufs) * L::kBuf; };
-    auto raw = [&](int i) { return usm + L::kRawOff + (i & 1) * L::kRaw; };
-    // weight codes + scales of stage i (index within this CTA's range) -> raw buffer i & 1
+    auto buf = [&](int i) { return usm + (i % NB) * L::kBuf; };
+    auto raw = [&](int i) { return usm + L::kRawOff + (i % P) * L::kRaw; };
+    // weight codes + scales of stage i (index within this CTA's range) -> raw buffer i % P
     auto issue_w = [&](int i) {
         const int s = s_begin + i;
         uint8_t* rb = raw(i);
@@ -167,13 +171,13 @@ __global__ void __launch_bounds__(kUThreads, 1) umma_gemm_kernel(const GemvArgs 
         }
     };
     if (mv < kUM) {  // A rows past M: zero in every buffer, never written again
-        for (int j = tid; j < kUBufs * 2 * (kUM - mv) * 8; j += kUThreads) {
+        for (int j = tid; j < NB * 2 * (kUM - mv) * 8; j += kUThreads) {
             const int b = j / (2 * (kUM - mv) * 8), jj = j - b * 2 * (kUM - mv) * 8;
             const int h = jj >= (kUM - mv) * 8 ? 1 : 0, k2 = jj - h * (kUM - mv) * 8, r = mv + (k2 >> 3), q = k2 & 7;
             *reinterpret_cast<uint4*>(usm + b * L::kBuf + h * L::kATile + sw128_off(r, q)) = make_uint4(0, 0, 0, 0);
         }
     }
-    // raw buffer i & 1 -> B hi / lo tiles of buffer i: w = code x scale split into two f16
+    // raw buffer i % P -> B hi / lo tiles of buffer i: w = code x scale split into two f16
     auto convert = [&](int i) {
         const uint8_t* rb = raw(i);
         uint8_t* bb = buf(i) + 2 * L::kATile;
@@ -213,21 +217,24 @@ __global__ void __launch_bounds__(kUThreads, 1) umma_gemm_kernel(const GemvArgs 
     };
     // bounded wait for the UMMAs of stage i (their commit): their buffer is free / their results are in TMEM
     auto mma_wait = [&](int i) {
-        if (!mbar_wait(&mma_bar[i % kUBufs], uint32_t(i / kUBufs) & 1u)) s_fail = 1;
+        if (!mbar_wait(&mma_bar[i % NB], uint32_t(i / NB) & 1u)) s_fail = 1;
     };
 
-    // prologue: stages 0 and 1 (weights before the dependency wait: they never depend on the previous kernel)
-    if (nst > 0) issue_w(0);
-    if (nst > 1) issue_w(1);
+    // prologue: stages 0 .. P - 1 (weights before the dependency wait: they never depend on the previous kernel;
+    // one commit group per stage's activations, the first also holding every prologue weight copy)
+#pragma unroll
+    for (int j = 0; j < P; j++)
+        if (j < nst) issue_w(j);
     pdl_wait();
-    if (nst > 0) issue_x(0);
-    cp_commit();
-    if (nst > 1) issue_x(1);
-    cp_commit();
+#pragma unroll
+    for (int j = 0; j < P; j++) {
+        if (j < nst) issue_x(j);
+        cp_commit();
+    }
     for (int i = 0; i < nst; i++) {
-        cp_wait<1>();  // stage i landed (this thread's copies)
+        cp_wait<P - 1>();  // stage i landed (this thread's copies)
         __syncthreads();
-        if (i >= kUBufs) mma_wait(i - kUBufs);  // buffer i % 3 was last read by the UMMAs of stage i - 3
+        if (i >= NB) mma_wait(i - NB);  // buffer i % NB was last read by the UMMAs of stage i - NB
         convert(i);
         fence_proxy_async();  // generic-proxy writes (conversions, cp.async) -> visible to the tensor cores
         __syncthreads();
@@ -242,14 +249,14 @@ __global__ void __launch_bounds__(kUThreads, 1) umma_gemm_kernel(const GemvArgs 
                 umma_f16(tmem, sw128_desc(al + o), sw128_desc(bh + o), kIdesc, 1u);
                 umma_f16(tmem, sw128_desc(ah + o), sw128_desc(bl + o), kIdesc, 1u);
             }
-            umma_commit(&mma_bar[i % kUBufs]);
+            umma_commit(&mma_bar[i % NB]);
         }
-        // stage i + 2: its weights into the raw buffer just converted, its activations into buffer (i + 2) % 3,
+        // stage i + P: its weights into the raw buffer just converted, its activations into buffer (i + P) % NB,
         // last read by the UMMAs of stage i - 1
-        if (i + 2 < nst) {
+        if (i + P < nst) {
             if (i >= 1) mma_wait(i - 1);
-            issue_w(i + 2);
-            issue_x(i + 2);
+            issue_w(i + P);
+            issue_x(i + P);
         }
         cp_commit();
     }
