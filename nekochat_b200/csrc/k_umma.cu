@@ -15,9 +15,9 @@
 // gate + BN / 2 up rows), K in stages of 64 (one 128-byte swizzle atom of f16). Eight warps: every thread stages
 // the activations (cp.async into the 128B-swizzled K-major layout) and converts the weight codes of a stage into
 // the same layout; thread 0 issues the UMMAs and commits them to the stage's mbarrier, which frees the stage's
-// buffers for a later stage (3 buffers at BN = 128, 4 at BN = 64: the copies run 2 or 3 stages ahead). K is split over a thread-block cluster (<= 8 CTAs) when the tiles leave SMs
-// idle: each CTA moves its fp32 tile from TMEM to shared memory and CTA z sums rows z, z + ks, ... over the
-// cluster in split order (deterministic), then runs the epilogue. All waits are bounded; TMEM is always freed.
+// buffers for a later stage (3 buffers at BN = 128, 4 at BN = 64: the copies run 2 or 3 stages ahead). K is split over a thread-block cluster when the tiles leave SMs
+// idle (clusters of up to 4): each CTA moves its fp32 tile from TMEM to shared memory and CTA z sums rows z,
+// z + ks, ... over the cluster in split order (deterministic), then runs the epilogue. All waits are bounded; TMEM is always freed.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -35,7 +35,10 @@ constexpr int kUM = 128;       // activation rows per CTA (UMMA M)
 constexpr int kUK = 64;        // K per stage: 64 f16 = one 128-byte swizzle atom
 constexpr int kUMaxBufs = 4;   // f16 operand buffers (3 at BN = 128, 4 at BN = 64: shared memory)
 constexpr int kUThreads = 256;
-constexpr int kUMaxSplit = 8;  // CTAs of a cluster (portable limit)
+// CTAs of a split-K cluster. At ~210 KB of shared memory a CTA fills an SM, and clusters of 8 such CTAs only
+// find room a few per GPC (measured: SMs active 38% of the kernel at M = 128, K = 3072, N = 1024); clusters of 4
+// schedule freely (that shape 36.5 -> 30.3 us, M = 256: 47.5 -> 31.2 us).
+constexpr int kUMaxSplit = 4;
 // Below 128 rows the mma.sync kernel is faster (measured: M = 64 decode-layer shapes 27-31 us there vs 33 us
 // here, where two stages of prefetch leave the pipeline latency-bound); from 128 rows on, this one (M = 512:
 // 1.3-1.5x).
