@@ -555,8 +555,10 @@ Geometry plan(int rows, int n_kv, int max_pos, int G, int hd) {
     const int sms = num_sms();
     Geometry g;
     g.chunk = chunk_for(hd);
-    // about eight CTAs per SM (several waves, so the last one is short), at least two chunks of keys per split
-    const int want = std::max(1, std::min((8 * sms + rows * n_kv - 1) / (rows * n_kv), L / (2 * g.chunk)));
+    // about two CTAs per SM, at least two chunks of keys per split: a CTA's start-up and its share of the split
+    // merge are fixed costs, so long splits win (measured at batch 64, position 512: 1 split per (row, KV head)
+    // 3.25 ms per decode step, 2 splits 3.59 ms, 3 splits 3.72 ms)
+    const int want = std::max(1, std::min((2 * sms + rows * n_kv - 1) / (rows * n_kv), L / (2 * g.chunk)));
     int span = (L + want - 1) / want;
     span = std::max(g.chunk, (span + g.chunk - 1) / g.chunk * g.chunk);
     g.span = span;
