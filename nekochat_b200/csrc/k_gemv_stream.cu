@@ -292,16 +292,21 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_stream_kernel(const GemvArgs a,
 // K is permuted inside each 16-step so that lane (g, c) reads 4 contiguous code bytes of weight row g (bytes 4c..
 // 4c+3 of the step, MMA k = 2c, 2c+1, 2c+8, 2c+9) and the same 4 activations: one 32-bit load and two hardware
 // conversions feed two MMAs (the activations as hi + lo f16, about 22 bits). Codes are exact in f16; each 32-weight
-// block's partial sums are scaled in fp32, as in the CUDA-core kernel. A stage holds 8 T rows (T tiles of 8,
-// T dividing the consumer warp count); warp w takes tile w % T over part w / T of K (kSW / T parts of whole
-// 32-weight blocks), and the parts are added in order through shared memory. Its cost hardly depends on M, so
-// it takes the calls of 2..4 activation rows; one row runs the CUDA-core kernel, which needs no row padding.
-constexpr int kMmaRedBytes = 2 * kSW * 32 * 4 * 4;  // partial sums of the K parts, double-buffered by stage
-
+// block's partial sums are scaled in fp32, as in the CUDA-core kernel.
+//  * the producer copies each row into the stage at a pitch of rowBytes + 16, so the 8 rows' 4-byte loads of a
+//    warp fall on 32 different banks (at the packed pitch, 1088 bytes for K = 1024, half the rows share banks);
+//  * a stage holds T tiles of 8 rows; G groups of T consumer warps (G T <= 16) take stages round-robin, group q
+//    stages q, q + G, ..., and warp w of a group a whole tile (all of K): no reduction across warps. The ring has
+//    a multiple of G slots, so each slot belongs to one group, which waits on its phases in order (an mbarrier
+//    parity wait is only unambiguous for a waiter at most one phase ahead of the barrier).
+// About 0.09 warp instructions per FP8 weight against ~0.19 on CUDA cores; the per-row copies cost more than
+// that saves at one activation row, so it takes 2..4.
 struct MmaPlan {
     int rows_per_cta;
-    int tiles;       // 8-row tiles per stage; kSW / tiles K parts
+    int tiles;       // 8-row tiles per stage = warps per group
+    int groups;      // warp groups taking stages (groups x tiles <= 16 consumer warps; the rest idle)
     int rps;         // rows per stage = 8 tiles
+    int pitch;       // bytes per row in a stage (row_bytes + 16)
     int nslot, slot_bytes, xs_bytes;
 };
 
@@ -382,31 +387,60 @@ __device__ void stage_act_hilo(const GemvArgs& a, __half* xh, __half* xl, int wa
     ssync();
 }
 
+// The producer of the tensor-core kernel: stage s = rows r0 + s rps .. (SwiGLU: the gate rows, then the up rows),
+// one bulk copy per row into a row pitch of sp.pitch bytes.
+__device__ void stream_producer_rows(const GemvArgs& a, int r0, int r1, const MmaPlan& sp, uint64_t* full,
+                                     uint64_t* empty, uint8_t* ring, int lane) {
+    const bool pair = a.pair_off != 0;
+    const int nst = (r1 - r0 + sp.rps - 1) / sp.rps;
+    int st = 0;
+    for (; st < nst; st++) {
+        const int slot = st % sp.nslot;
+        if (st >= sp.nslot) {
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&empty[slot], ((st / sp.nslot) - 1) & 1);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        }
+        const int row = r0 + st * sp.rps, cnt = min(sp.rps, r1 - row);
+        uint8_t* dst = ring + size_t(slot) * sp.slot_bytes;
+        if (lane == 0) mbar_arrive_expect_tx(&full[slot], uint32_t((pair ? 2 : 1) * cnt) * uint32_t(a.row_bytes));
+        __syncwarp();
+        for (int c = lane; c < (pair ? 2 : 1) * cnt; c += 32) {
+            const int half = c >= cnt ? 1 : 0, r = c - half * cnt;
+            bulk_g2s(dst + size_t(half * sp.rps + r) * sp.pitch,
+                     a.W + (int64_t(row + r) + (half ? a.pair_off : 0)) * a.row_bytes, uint32_t(a.row_bytes),
+                     &full[slot]);
+        }
+    }
+    if (lane == 0)  // leave only when no copy of ours is still landing (a consumer may have given up)
+        for (int s = st > sp.nslot ? st - sp.nslot : 0; s < st; s++) mbar_wait(&full[s % sp.nslot], (s / sp.nslot) & 1);
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(kSThr, 1) gemv_mma_kernel(const GemvArgs a, const MmaPlan sp) {
     uint64_t* full = reinterpret_cast<uint64_t*>(gsm);
     uint64_t* empty = full + kSMaxSlots;
     __half* xh = reinterpret_cast<__half*>(gsm + 256);
     __half* xl = xh + a.M * a.K;
-    float* red = reinterpret_cast<float*>(gsm + 256 + sp.xs_bytes);  // [2][kSW][32][4] K-part partial sums
-    uint8_t* ring = gsm + 256 + sp.xs_bytes + kMmaRedBytes;
+    uint8_t* ring = gsm + 256 + sp.xs_bytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const bool pair = a.pair_off != 0;
     const int r0 = blockIdx.x * sp.rows_per_cta, r1 = min(a.rows, r0 + sp.rows_per_cta);
     pdl_trigger();
     if (r0 >= r1) return;
     const int n = r1 - r0, rps = sp.rps, nst = (n + rps - 1) / rps;
+    const int T = sp.tiles, ngroups = sp.groups;
     if (threadIdx.x == 0) {
         for (int s = 0; s < sp.nslot; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kSW);
+            mbar_init(&empty[s], T);  // the T warps of the group that takes the stage
         }
         fence_barrier_init();
     }
     if (threadIdx.x < kDecodeMaxSeqs) t_key[threadIdx.x] = 0ull;
     __syncthreads();
     if (warp == kSW) {  // producer: weights only, so it never waits for the previous kernel
-        stream_producer(a, r0, r1, rps, sp.nslot, sp.slot_bytes, full, empty, ring, lane);
+        stream_producer_rows(a, r0, r1, sp, full, empty, ring, lane);
         return;
     }
 
@@ -415,31 +449,31 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_mma_kernel(const GemvArgs a, co
     stage_act_hilo(a, xh, xl, warp, lane);
     constexpr float kF = FMT == kFP8 ? kFp8HwFactor : kFp4Factor;
     const int cbytes = code_bytes(FMT, a.K), nblk = a.K / kQuantBlock;
-    const int tiles = sp.tiles, parts = kSW / tiles, tile = warp % tiles, part = warp / tiles;
-    const int b_begin = part * nblk / parts, b_end = (part + 1) * nblk / parts;
+    const int group = warp / T, tile = warp % T;  // warps of group >= ngroups take no stage
     const bool xrow = g < a.M;  // this lane's activation row exists (MMA rows past M stay zero)
     const __half* xhr = xh + (xrow ? g : 0) * a.K + 4 * c;
     const __half* xlr = xl + (xrow ? g : 0) * a.K + 4 * c;
     unsigned long long best = 0ull;  // this lane's activation row g
-    int slot = 0, par = 0;
-    for (int st = 0; st < nst; st++) {
+    for (int st = group; group < ngroups && st < nst; st += ngroups) {
+        const int slot = st % sp.nslot;
         int ok = 1;
-        if (lane == 0) ok = mbar_wait(&full[slot], par);
+        if (lane == 0) ok = mbar_wait(&full[slot], uint32_t(st / sp.nslot) & 1u);
         ok = __shfl_sync(0xffffffffu, ok, 0);  // a wait that gave up is a device error; the stage is skipped
         const int srow = st * rps, in_stage = min(rps, n - srow);
         const uint8_t* base = ring + size_t(slot) * sp.slot_bytes;
         // this lane's weight row (B operand) and the two rows whose outputs it holds (D columns 2c, 2c + 1)
         const int qb = min(8 * tile + g, in_stage - 1);
-        const uint8_t* wb = base + int64_t(qb) * a.row_bytes;
-        const uint8_t* wu = base + int64_t(in_stage + qb) * a.row_bytes;  // up row (SwiGLU)
+        const uint8_t* wb = base + size_t(qb) * sp.pitch;
+        const uint8_t* wu = base + size_t(rps + qb) * sp.pitch;  // up row (SwiGLU)
         const int qd0 = min(8 * tile + 2 * c, in_stage - 1), qd1 = min(8 * tile + 2 * c + 1, in_stage - 1);
-        const uint16_t* sc0 = reinterpret_cast<const uint16_t*>(base + int64_t(qd0) * a.row_bytes + cbytes);
-        const uint16_t* sc1 = reinterpret_cast<const uint16_t*>(base + int64_t(qd1) * a.row_bytes + cbytes);
-        const uint16_t* su0 = reinterpret_cast<const uint16_t*>(base + int64_t(in_stage + qd0) * a.row_bytes + cbytes);
-        const uint16_t* su1 = reinterpret_cast<const uint16_t*>(base + int64_t(in_stage + qd1) * a.row_bytes + cbytes);
+        const uint16_t* sc0 = reinterpret_cast<const uint16_t*>(base + size_t(qd0) * sp.pitch + cbytes);
+        const uint16_t* sc1 = reinterpret_cast<const uint16_t*>(base + size_t(qd1) * sp.pitch + cbytes);
+        const uint16_t* su0 = reinterpret_cast<const uint16_t*>(base + size_t(rps + qd0) * sp.pitch + cbytes);
+        const uint16_t* su1 = reinterpret_cast<const uint16_t*>(base + size_t(rps + qd1) * sp.pitch + cbytes);
         float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};  // [gate | up][column 2c + e]
         if (ok && 8 * tile < in_stage) {
-            for (int b = b_begin; b < b_end; b++) {
+#pragma unroll 2
+            for (int b = 0; b < nblk; b++) {
                 uint32_t ah0[4] = {0u, 0u, 0u, 0u}, al0[4] = {0u, 0u, 0u, 0u}, ah1[4] = {0u, 0u, 0u, 0u},
                          al1[4] = {0u, 0u, 0u, 0u};
                 if (xrow) {  // steps 2b (weights 32b + 4c ..) and 2b + 1 (32b + 16 + 4c ..)
@@ -462,14 +496,13 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_mma_kernel(const GemvArgs a, co
                         b00 = h2u(p0), b01 = h2u(p1), b10 = h2u(p2), b11 = h2u(p3);
                     } else {  // bytes 4c..4c+3 of the block: low nibbles = weights 4c.., high = 16 + 4c..
                         const uint32_t wd = *reinterpret_cast<const uint32_t*>(w + 16 * b + 4 * c);
-                        b00 = h2u(__halves2half2(__low2half(fp4x2_to_half2(wd & 0x000F000Fu)),
-                                                 __low2half(fp4x2_to_half2((wd >> 8) & 0x000F000Fu))));
-                        b01 = h2u(__halves2half2(__high2half(fp4x2_to_half2(wd & 0x000F000Fu)),
-                                                 __high2half(fp4x2_to_half2((wd >> 8) & 0x000F000Fu))));
-                        b10 = h2u(__halves2half2(__low2half(fp4x2_to_half2((wd >> 4) & 0x000F000Fu)),
-                                                 __low2half(fp4x2_to_half2((wd >> 12) & 0x000F000Fu))));
-                        b11 = h2u(__halves2half2(__high2half(fp4x2_to_half2((wd >> 4) & 0x000F000Fu)),
-                                                 __high2half(fp4x2_to_half2((wd >> 12) & 0x000F000Fu))));
+                        const __half2 e0 = fp4x2_to_half2(wd & 0x000F000Fu), o0 = fp4x2_to_half2((wd >> 8) & 0x000F000Fu);
+                        const __half2 e1 = fp4x2_to_half2((wd >> 4) & 0x000F000Fu);
+                        const __half2 o1 = fp4x2_to_half2((wd >> 12) & 0x000F000Fu);
+                        b00 = h2u(__halves2half2(__low2half(e0), __low2half(o0)));
+                        b01 = h2u(__halves2half2(__high2half(e0), __high2half(o0)));
+                        b10 = h2u(__halves2half2(__low2half(e1), __low2half(o1)));
+                        b11 = h2u(__halves2half2(__high2half(e1), __high2half(o1)));
                     }
                     float d[4], dl[4];
                     mma16816_z(d, ah0, b00, b01);
@@ -484,20 +517,8 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_mma_kernel(const GemvArgs a, co
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);  // the stage's weights are no longer read
-        // the K parts of each tile, added in order by the part-0 warp
-        float* rb = red + (st & 1) * kSW * 128;
-        if (parts > 1) {
-            *reinterpret_cast<float4*>(rb + (warp * 32 + lane) * 4) = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
-            ssync();
-        }
-        if (part == 0 && ok) {
-            float v[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
-            for (int p = 0; p < parts; p++) {
-                const float4 t = parts > 1 ? *reinterpret_cast<const float4*>(rb + ((tile + p * tiles) * 32 + lane) * 4)
-                                           : make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
-                v[0][0] += t.x, v[0][1] += t.y, v[1][0] += t.z, v[1][1] += t.w;
-            }
+        if (lane == 0) mbar_arrive(&empty[slot]);  // the stage's weights are no longer read by this warp
+        if (ok) {
 #pragma unroll
             for (int e = 0; e < 2; e++) {
                 const int q = 8 * tile + 2 * c + e;
@@ -506,10 +527,10 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_mma_kernel(const GemvArgs a, co
                 float* dst = a.y + int64_t(m) * a.y_stride + a.n_off + row;
                 float val;
                 if (pair) {
-                    const float gs = v[0][e], us = v[1][e];
+                    const float gs = acc[0][e], us = acc[1][e];
                     val = gs / (1.0f + expf(-gs)) * us;  // cpu::siluMul (cpu_ops.cpp:526-533)
                 } else {
-                    val = v[0][e];
+                    val = acc[0][e];
                     if (a.flags & kBias) val += a.bias[row];
                     if (a.flags & kGelu) val = gelu(val);
                     if (a.flags & kAccumulate) val += *dst;
@@ -517,10 +538,6 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_mma_kernel(const GemvArgs a, co
                 *dst = val;
                 if (a.argmax) best = max(best, argmax_key(val, row));
             }
-        }
-        if (++slot == sp.nslot) {
-            slot = 0;
-            par ^= 1;
         }
     }
     if (a.argmax) {  // the 4 lanes of each activation row, then per CTA, then one global atomic per row
@@ -541,45 +558,44 @@ StreamFn pick(int fmt, int M) {
 
 }  // namespace
 
-// The tensor-core streaming kernel: activations as hi / lo f16 in shared memory (<= 64 KB), stages of 8 T rows
-// with T the largest divisor of the consumer warp count that does not exceed the CTA's rows (rounded up to a
-// tile) and leaves a ring of four stages (three, then two, for wide rows).
+// The tensor-core streaming kernel: activations as hi / lo f16 in shared memory (<= 64 KB), rows at a padded
+// pitch, stages of 8 T rows (T in 4, 2, 1, at most the CTA's rows rounded up to a tile), G groups with one or
+// two ring slots each: the plan with the most busy warps (G T), then two slots per group, then the larger T.
 cudaError_t launch_gemv_mma(const GemvArgs& a, cudaStream_t st, bool pdl) {
     const int64_t xs = (int64_t(a.M) * a.K * 4 + 127) / 128 * 128;
     if (xs > 64 * 1024 || a.K % kQuantBlock) return cudaErrorNotSupported;
-    const int64_t rbe = a.row_bytes * (a.pair_off ? 2 : 1);
     MmaPlan sp;
     const int sms = num_sms();
     int ctas = std::max(1, std::min(sms, (a.rows + 3) / 4));
     sp.rows_per_cta = (a.rows + ctas - 1) / ctas;
     ctas = (a.rows + sp.rows_per_cta - 1) / sp.rows_per_cta;
     sp.xs_bytes = int(xs);
-    const int64_t budget = 227 * 1024 - kSStatic - 256 - xs - kMmaRedBytes;
+    sp.pitch = int(a.row_bytes) + 16;
+    const int64_t budget = 227 * 1024 - kSStatic - 256 - xs;
     const int tneed = (sp.rows_per_cta + 7) / 8;
-    int cap = kSW;
-    for (int t = 1; t <= kSW; t++)
-        if (kSW % t == 0 && t >= tneed) {
-            cap = t;
-            break;
-        }
     sp.tiles = 0;
-    for (int want : {4, 3, 2}) {
-        for (int t = kSW; t >= 1; t--) {
-            if (kSW % t) continue;
-            const int64_t sb = (8 * t * rbe + 127) / 128 * 128;
-            if (t <= cap && budget / sb >= want) {
+    int best = -1;
+    for (int t = 4; t >= 1; t /= 2) {
+        if (t > tneed && t > 1) continue;
+        const int64_t sb = (int64_t(8 * t) * sp.pitch * (a.pair_off ? 2 : 1) + 127) / 128 * 128;
+        const int slots = int(std::min<int64_t>(kSMaxSlots, budget / sb));
+        for (int per_group : {2, 1}) {
+            const int g = std::min(kSW / t, slots / per_group);
+            if (g < 1) continue;
+            const int score = (g * t) * 8 + per_group * 4 + t;  // busy warps, then slots per group, then T
+            if (score > best) {
+                best = score;
                 sp.tiles = t;
+                sp.groups = g;
                 sp.slot_bytes = int(sb);
-                break;
+                sp.nslot = g * per_group;
             }
         }
-        if (sp.tiles) break;
     }
-    if (!sp.tiles) return cudaErrorNotSupported;
+    if (!sp.tiles || sp.groups * sp.tiles < kSW / 2) return cudaErrorNotSupported;  // too few busy warps
     sp.rps = 8 * sp.tiles;
-    sp.nslot = int(std::min<int64_t>(kSMaxSlots, budget / sp.slot_bytes));
     auto k = a.fmt == kFP8 ? gemv_mma_kernel<kFP8> : gemv_mma_kernel<kFP4>;
-    const size_t smem = 256 + size_t(xs) + kMmaRedBytes + size_t(sp.nslot) * sp.slot_bytes;
+    const size_t smem = 256 + size_t(xs) + size_t(sp.nslot) * sp.slot_bytes;
     static int attr_set[2][32] = {};  // per (format, device < 32): the limit only grows
     int dev = 0;
     cudaGetDevice(&dev);
@@ -605,6 +621,8 @@ cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl) {
     if (a.norm != kNormNone && !gemv_norm_fusable(a.fmt, a.M, a.K)) return cudaErrorNotSupported;
     const int64_t rbe = a.row_bytes * (a.pair_off ? 2 : 1);
     if (a.row_bytes % 16) return cudaErrorNotSupported;
+    // the tensor-core variant for 2..4 rows (one row: the CUDA-core kernel is faster, 54 vs 73 us at the LM-head
+    // shape, where the tensor-core variant's one bulk copy per row limits the stream)
     if (a.M >= 2)
         if (const cudaError_t e = launch_gemv_mma(a, st, pdl); e != cudaErrorNotSupported) return e;
     StreamPlan sp;
