@@ -689,24 +689,48 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued,
             return false;
         }
         csync();
-        // 2. scores
-        for (int t = warp; t < n; t += kW) {
-            float kv[DL];
-            if (has_new && a.k0 + t == L - 1) {
+        // 2. scores, four keys x four query heads (heads past Gq are zero) per warp pass: the 16 lane partial
+        // sums are reduced together by a transposed butterfly (halves exchange 8 values, then 4, 2, 1, then one
+        // xor step), 16 shuffles instead of 5 per dot product
+        static_assert(kMaxGq == 4, "16 values per pass");
+        for (int grp = warp; 4 * grp < n; grp += kW) {
+            float v[16];
 #pragma unroll
-                for (int i = 0; i < DL; i++) kv[i] = snk[lane * DL + i];
-            } else {
-                load_half_row<DL>(kbuf + t * hd + lane * DL, kv);
+            for (int j = 0; j < 4; j++) {
+                const int t = 4 * grp + j;
+                float kv[DL];
+                if (t < n && has_new && a.k0 + t == L - 1) {
+#pragma unroll
+                    for (int i = 0; i < DL; i++) kv[i] = snk[lane * DL + i];
+                } else if (t < n) {
+                    load_half_row<DL>(kbuf + t * hd + lane * DL, kv);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < DL; i++) kv[i] = 0.0f;
+                }
+#pragma unroll
+                for (int gq = 0; gq < kMaxGq; gq++) {
+                    float d = 0.0f;
+                    if (gq < Gq)
+#pragma unroll
+                        for (int i = 0; i < DL; i++) d = fmaf(sq[gq * hd + lane * DL + i], kv[i], d);
+                    v[4 * j + gq] = d;
+                }
             }
 #pragma unroll
-            for (int gq = 0; gq < kMaxGq; gq++) {
-                if (gq >= Gq) break;
-                float d = 0.0f;
+            for (int w = 8; w >= 1; w >>= 1) {  // exchange halves: lane bit (16 >> k) picks which half it keeps
+                const bool up = lane & (2 * w);
 #pragma unroll
-                for (int i = 0; i < DL; i++) d = fmaf(sq[gq * hd + lane * DL + i], kv[i], d);
-                d = warp_sum(d);
-                if (lane == 0) sc[gq * span + t] = d * p.scale;
+                for (int i = 0; i < w; i++) {
+                    const float keep = up ? v[i + w] : v[i], send = up ? v[i] : v[i + w];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2 * w);
+                }
             }
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+            // lane L holds value ((L >> 4) & 1) 8 + ((L >> 3) & 1) 4 + ((L >> 2) & 1) 2 + ((L >> 1) & 1)
+            const int idx = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+            const int t = 4 * grp + (idx >> 2), gq = idx & 3;
+            if (!(lane & 1) && gq < Gq && t < n) sc[gq * span + t] = v[0] * p.scale;
         }
         csync();
         // 3. softmax of each query head over the item's keys
