@@ -11,10 +11,12 @@
 // the partial (max, sum, acc) go to scratch and the last CTA of the (row, KV head) to finish merges them,
 // elected by a ticket counter that it resets (so the kernel can be replayed from a CUDA graph).
 #include <algorithm>
+#include <cstdlib>
 
 #include "mma_frag.cuh"
 #include "neko_common.cuh"
 #include "neko_internal.h"
+#include "tma_host.h"
 
 namespace neko {
 
@@ -330,21 +332,39 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
 //    of the P.V step. The four warps' (max, sum, acc) are merged once at the end of the split;
 //  * all threads stage the chunks with 16-byte cp.async into padded shared-memory rows (pitch hd + 8 halves,
 //    conflict-free ldmatrix; rows past the last key are zero-filled), three buffers, one barrier per chunk.
+//  * TMA variant (caches whose positions are contiguous rows of hd halves, e.g. [slot][kv head][pos][hd]): one
+//    thread stages each chunk as 2D tensor copies of 64 keys x 64 dims (128-byte swizzle: 16-byte piece q of row
+//    j sits at piece q ^ (j & 7), so the ldmatrix row groups stay conflict-free without padding) completing on one
+//    mbarrier per buffer; the copies read the rows past the chunk's last key too (cache memory, or zeros past the
+//    tensor's end), whose values are zeroed in shared memory before use.
 constexpr int kTcChunk = 64;
 constexpr int kTcBufs = 3;
+constexpr int kTmaBox = 8192;  // bytes of one 64 x 64 f16 box
 
-template <int HD>
+template <int HD, bool TMA>
 constexpr int tc_attn_smem() {
-    return kTcBufs * 2 * kTcChunk * (HD + 8) * 2;
+    // the buffers, then (TMA) kTcBufs mbarriers, then two flags; TMA adds up to 1024 bytes to align the buffers
+    return TMA ? kTcBufs * 2 * (HD / 64) * kTmaBox + 64 + 1024 : kTcBufs * 2 * kTcChunk * (HD + 8) * 2 + 64;
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kAttnThreads, 2) attention_tc_kernel(const AttnArgs a, const Geometry geo) {
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+template <int HD, bool TMA>
+__global__ void __launch_bounds__(kAttnThreads, 2)
+    attention_tc_kernel(const AttnArgs a, const Geometry geo, const __grid_constant__ CUtensorMap tk,
+                        const __grid_constant__ CUtensorMap tv) {
     constexpr int P = HD + 8;  // padded row pitch (halves)
-    constexpr int CH = kTcChunk, KS = HD / 16, NTO = HD / 8;
-    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int CH = kTcChunk, KS = HD / 16, NTO = HD / 8, NB = HD / 64;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    // TMA boxes with the 128-byte swizzle need 1024-byte aligned destinations
+    uint8_t* smem = TMA ? smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023) : smem_raw;
     uint16_t* kvb = reinterpret_cast<uint16_t*>(smem);  // [kTcBufs][2][CH][P]: keys, then values
-    __shared__ int last;
 
     const int split = blockIdx.x, kvh = blockIdx.y, r = blockIdx.z;
     const int G = a.n_head / a.n_kv;
@@ -366,22 +386,71 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_tc_kernel(const Att
     const uint16_t* vbase = a.vc + int64_t(slot) * a.slot_stride + int64_t(kvh) * a.head_stride;
     // every thread: its 16-byte pieces of chunk cc's key and value rows into buffer cc % kTcBufs (one commit group
     // per chunk); rows past the chunk's last key are zero-filled without reading memory
+    constexpr int BUF = TMA ? 2 * NB * kTmaBox : 2 * CH * P * 2;  // bytes per buffer
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcBufs * BUF);  // TMA: one mbarrier per buffer
+    // flags in dynamic shared memory (the kernel declares no static shared variables)
+    int& last = *reinterpret_cast<int*>(smem + kTcBufs * BUF + 32);
+    int& tma_ok = *reinterpret_cast<int*>(smem + kTcBufs * BUF + 36);
+    // row of this (slot, KV head)'s position 0 in the tensor maps' [rows][hd] view
+    const int row0 = TMA ? int((int64_t(slot) * a.slot_stride + int64_t(kvh) * a.head_stride) / HD) : 0;
     auto issue = [&](int cc) {
         const int j0 = j_begin + cc * CH, n = min(CH, j_end - j0);
-        uint16_t* dk = kvb + (cc % kTcBufs) * 2 * CH * P;
-        constexpr int PR = HD / 8;  // pieces per row
+        uint8_t* dst = smem + (cc % kTcBufs) * BUF;
+        if constexpr (TMA) {  // thread 0 only
+            uint64_t* bar = &bars[cc % kTcBufs];
+            mbar_arrive_expect_tx(bar, uint32_t(BUF));
+#pragma unroll
+            for (int bx = 0; bx < NB; bx++) {
+                tma_load_2d(dst + bx * kTmaBox, &tk, 64 * bx, row0 + j0, bar);
+                tma_load_2d(dst + (NB + bx) * kTmaBox, &tv, 64 * bx, row0 + j0, bar);
+            }
+        } else {
+            uint16_t* dk = reinterpret_cast<uint16_t*>(dst);
+            constexpr int PR = HD / 8;  // pieces per row
 #pragma unroll 4
-        for (int i = tid; i < 2 * CH * PR; i += kAttnThreads) {
-            const int v = i >= CH * PR ? 1 : 0, j = (i - v * CH * PR) / PR, q = i - v * CH * PR - j * PR;
-            const uint16_t* src = (v ? vbase : kbase) + int64_t(j0 + min(j, n - 1)) * a.pos_stride + 8 * q;
-            cp16(dk + (v * CH + j) * P + 8 * q, src, j < n ? 16 : 0);
+            for (int i = tid; i < 2 * CH * PR; i += kAttnThreads) {
+                const int v = i >= CH * PR ? 1 : 0, j = (i - v * CH * PR) / PR, q = i - v * CH * PR - j * PR;
+                const uint16_t* src = (v ? vbase : kbase) + int64_t(j0 + min(j, n - 1)) * a.pos_stride + 8 * q;
+                cp16(dk + (v * CH + j) * P + 8 * q, src, j < n ? 16 : 0);
+            }
         }
     };
+    if constexpr (TMA) {
+        if (tid == 0) {
+            // the copies need a 1024-byte aligned destination, 8-byte aligned barriers and 64-byte aligned maps:
+            // anything else is recorded and the copies are skipped (the outputs are then invalid)
+            tma_ok = 1;
+            if ((smem_u32(smem) & 1023u) || (smem_u32(bars) & 7u)) {
+                set_device_error(kErrMisalignedSmem);
+                tma_ok = 0;
+            } else if ((reinterpret_cast<uintptr_t>(&tk) & 63u) || (reinterpret_cast<uintptr_t>(&tv) & 63u)) {
+                set_device_error(kErrMisalignedMap);
+                tma_ok = 0;
+            }
 #pragma unroll
-    for (int cc = 0; cc < kTcBufs - 1; cc++) {
-        if (cc < nchunks) issue(cc);
-        cp_commit();
+            for (int b = 0; b < kTcBufs; b++) mbar_init(&bars[b], 1);
+            fence_barrier_init();
+            if (tma_ok) {
+#pragma unroll
+                for (int cc = 0; cc < kTcBufs - 1; cc++)
+                    if (cc < nchunks) issue(cc);
+            }
+        }
+        __syncthreads();  // barrier initialisation visible before any thread waits
+    } else {
+#pragma unroll
+        for (int cc = 0; cc < kTcBufs - 1; cc++) {
+            if (cc < nchunks) issue(cc);
+            cp_commit();
+        }
     }
+    // shared-memory address of (row, 8-half piece q) of the key (v = 0) or value (v = 1) tile in buffer b
+    auto tile_addr = [&](int b, int v, int row, int q) -> const void* {
+        if constexpr (TMA)
+            return smem + b * BUF + (v * NB + (q >> 3)) * kTmaBox + row * 128 + (((q & 7) ^ (row & 7)) << 4);
+        else
+            return kvb + (b * 2 + v) * CH * P + row * P + 8 * q;
+    };
 
     // query fragments (row gr = query head gr of the group; rows 8..15 and heads past G are zero)
     uint32_t qh[KS][2], ql[KS][2];
@@ -404,20 +473,32 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_tc_kernel(const Att
 
     for (int cc = 0; cc < nchunks; cc++) {
         const int b = cc % kTcBufs, n = min(CH, j_end - (j_begin + cc * CH));
-        cp_wait<kTcBufs - 2>();  // chunk cc landed (this thread's pieces)
-        __syncthreads();         // ... every thread's; and every warp is done with chunk cc - 1's buffer
-        if (cc + kTcBufs - 1 < nchunks) issue(cc + kTcBufs - 1);
-        cp_commit();
+        if constexpr (TMA) {
+            if (tma_ok) mbar_wait(&bars[b], uint32_t(cc / kTcBufs) & 1u);  // chunk cc landed (bounded)
+            if (n < CH) {  // value rows past the last key: zeros (0 x inf or NaN in stale rows would poison P.V)
+                uint8_t* vz = smem + b * BUF + NB * kTmaBox;
+                for (int i = tid; i < NB * (CH - n) * 8; i += kAttnThreads) {
+                    const int bx = i / ((CH - n) * 8), rem = i - bx * (CH - n) * 8;
+                    *reinterpret_cast<uint4*>(vz + bx * kTmaBox + (n + (rem >> 3)) * 128 + 16 * (rem & 7)) =
+                        make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            __syncthreads();  // zeroed rows visible; every warp is done with chunk cc - 1's buffer
+            if (tid == 0 && tma_ok && cc + kTcBufs - 1 < nchunks) issue(cc + kTcBufs - 1);
+        } else {
+            cp_wait<kTcBufs - 2>();  // chunk cc landed (this thread's pieces)
+            __syncthreads();         // ... every thread's; and every warp is done with chunk cc - 1's buffer
+            if (cc + kTcBufs - 1 < nchunks) issue(cc + kTcBufs - 1);
+            cp_commit();
+        }
         if (k0 < n) {
-            const uint16_t* kb = kvb + b * 2 * CH * P;
-            const uint16_t* vb = kb + CH * P;
             // scores of keys k0..k0+15: two n8 tiles
             // four independent accumulators (tile x hi/lo) so consecutive MMAs do not wait on each other
             float s[2][4], sl[2][4];
 #pragma unroll
             for (int ks = 0; ks < KS; ks++) {
                 uint32_t bf[4];
-                ldsm_x4(bf, kb + (k0 + 8 * (lane >> 4) + (lane & 7)) * P + 16 * ks + 8 * ((lane >> 3) & 1));
+                ldsm_x4(bf, tile_addr(b, 0, k0 + 8 * (lane >> 4) + (lane & 7), 2 * ks + ((lane >> 3) & 1)));
                 const uint32_t ah[4] = {qh[ks][0], 0u, qh[ks][1], 0u}, al[4] = {ql[ks][0], 0u, ql[ks][1], 0u};
                 if (ks == 0) {
                     mma16816_z(s[0], ah, bf[0], bf[1]);
@@ -472,7 +553,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_tc_kernel(const Att
 #pragma unroll
             for (int t2 = 0; t2 < NTO / 2; t2++) {
                 uint32_t vf[4];
-                ldsm_x4_trans(vf, vb + (k0 + (lane & 7) + 8 * ((lane >> 3) & 1)) * P + 16 * t2 + 8 * (lane >> 4));
+                ldsm_x4_trans(vf, tile_addr(b, 1, k0 + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * t2 + (lane >> 4)));
                 mma16816(o[2 * t2], ph, vf[0], vf[1]);
                 mma16816(o[2 * t2 + 1], ph, vf[2], vf[3]);
                 mma16816(o[2 * t2], pl, vf[0], vf[1]);
@@ -591,18 +672,33 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl) {
     }
     const int G = a.n_head / a.n_kv;
     if ((a.hd == 64 || a.hd == 128) && G <= 8 && kTcChunk == g.chunk) {  // tensor-core kernel
-        auto k = a.hd == 128 ? attention_tc_kernel<128> : attention_tc_kernel<64>;
-        const int smem = a.hd == 128 ? tc_attn_smem<128>() : tc_attn_smem<64>();
-        static int attr_tc[2][8] = {};  // per head_dim, device < 8
+        // TMA staging when every (slot, KV head) holds its positions as consecutive hd-element rows of a known
+        // [cache_rows][hd] array, and both tensor maps encode
+        CUtensorMap tk{}, tv{};
+        static const bool tma_on = [] {
+            const char* e = std::getenv("NEKO_ATTN_TMA");
+            return !(e && e[0] == '0');
+        }();
+        const bool tma = tma_on && a.pos_stride == a.hd && a.cache_rows > 0 && a.cache_rows < (int64_t(1) << 31) &&
+                         a.slot_stride % a.hd == 0 && a.head_stride % a.hd == 0 &&
+                         encode_f16_2d_sw128(&tk, a.kc, uint64_t(a.hd), uint64_t(a.cache_rows), uint64_t(a.hd) * 2,
+                                             64, kTcChunk) &&
+                         encode_f16_2d_sw128(&tv, a.vc, uint64_t(a.hd), uint64_t(a.cache_rows), uint64_t(a.hd) * 2,
+                                             64, kTcChunk);
+        auto k = a.hd == 128 ? (tma ? attention_tc_kernel<128, true> : attention_tc_kernel<128, false>)
+                             : (tma ? attention_tc_kernel<64, true> : attention_tc_kernel<64, false>);
+        const int smem = a.hd == 128 ? (tma ? tc_attn_smem<128, true>() : tc_attn_smem<128, false>())
+                                     : (tma ? tc_attn_smem<64, true>() : tc_attn_smem<64, false>());
+        static int attr_tc[2][2][8] = {};  // per head_dim, staging, device < 8
         int dev = 0;
         cudaGetDevice(&dev);
-        if (dev >= 8 || !attr_tc[a.hd == 128][dev]) {
+        if (dev >= 8 || !attr_tc[a.hd == 128][tma][dev]) {
             if (cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
                 e != cudaSuccess)
                 return e;
-            if (dev < 8) attr_tc[a.hd == 128][dev] = 1;
+            if (dev < 8) attr_tc[a.hd == 128][tma][dev] = 1;
         }
-        return launch_ex(k, dim3(g.splits, a.n_kv, a.rows), dim3(kAttnThreads), size_t(smem), st, pdl, a, g);
+        return launch_ex(k, dim3(g.splits, a.n_kv, a.rows), dim3(kAttnThreads), size_t(smem), st, pdl, a, g, tk, tv);
     }
     static unsigned attr_done = 0u;  // bit d: device d (< 32); function attributes are per device
     int dev = 0;

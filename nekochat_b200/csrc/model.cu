@@ -372,6 +372,7 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         a.tickets = m->tickets;
         a.part_capacity = m->part_cap;
         a.ticket_capacity = m->tick_cap;
+        a.cache_rows = m->kv_layer / hd;
         CK(launch_attention(a, st, pdl()), "attention");
         if (dump(l, m->qwen ? 4 : 3, m->att, H * hd)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
         CK(gemv(L.wo, C, m->att, int64_t(H) * hd, R, kNormNone, nullptr, nullptr, L.bo,

@@ -27,7 +27,13 @@ __host__ __device__ inline int64_t scale_offset(int fmt, int64_t K) { return fmt
 // ----------------------------------------------------------------------------------------------- errors
 // Device-side error word: bounded waits that give up record a code here instead of trapping, and the host
 // reads it after every synchronisation (neko_device_error in backend.cu).
-enum DeviceError : unsigned { kErrNone = 0, kErrMbarTimeout = 1, kErrBadIndex = 2 };
+enum DeviceError : unsigned {
+    kErrNone = 0,
+    kErrMbarTimeout = 1,
+    kErrBadIndex = 2,
+    kErrMisalignedSmem = 3,  // a tensor-copy destination or mbarrier off its required alignment (copies skipped)
+    kErrMisalignedMap = 4,   // a tensor map whose address is not 64-byte aligned (copies skipped)
+};
 extern __device__ unsigned g_device_error;
 __device__ inline void set_device_error(unsigned code) { atomicCAS(&g_device_error, 0u, code); }
 

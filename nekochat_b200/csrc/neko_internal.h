@@ -167,6 +167,9 @@ struct AttnArgs {
     unsigned* tickets = nullptr;
     int64_t part_capacity = 0;       // floats available in part
     int64_t ticket_capacity = 0;
+    // rows of hd elements in each of kc and vc (0: unknown). Known, with positions hd apart, it lets the kernel
+    // stage key / value chunks with 2D tensor copies bounded by the arrays.
+    int64_t cache_rows = 0;
 };
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl);
 // Scratch the split-KV attention needs for rows x n_head heads up to position max_pos.
