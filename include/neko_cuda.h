@@ -208,6 +208,9 @@ int neko_model_memory(neko_model* m, int64_t* weights, int64_t* kv, int64_t* wor
 int neko_model_set_debug(neko_model* m, int layers, int stage);
 /* Kernel launches one decode step of n sequences issues (for the bench's launch count). */
 int neko_model_step_launches(neko_model* m, int n);
+/* Kernel nodes in the most recently captured step graph (each step shape is captured on first use), 0 before any
+ * capture: the launch count a step really issues. */
+int neko_model_graph_kernels(neko_model* m);
 /* Decode steps of 1..4 sequences (decode, step, and forward of one token) run as ONE persistent kernel by
  * default: enable = 0 makes them use the per-operator kernel chain instead (same results; for comparison).
  * enable = 2 is a test of the kernel's bounded waits: the next steps wait for a CTA that does not exist, give

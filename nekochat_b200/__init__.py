@@ -106,6 +106,7 @@ _SIGS = {
     "neko_model_tokens": (C.c_int, [_vp, C.c_int, _vp, _vp]),
     "neko_model_memory": (C.c_int, [_vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "neko_model_step_launches": (C.c_int, [_vp, C.c_int]),
+    "neko_model_graph_kernels": (C.c_int, [_vp]),
     "neko_model_set_decode_kernel": (C.c_int, [_vp, C.c_int]),
     "neko_model_set_debug": (C.c_int, [_vp, C.c_int, C.c_int]),
     "neko_model_matrix": (C.c_int, [_vp, C.c_char_p, C.POINTER(C.c_void_p), C.POINTER(C.c_int),

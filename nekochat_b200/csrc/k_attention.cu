@@ -339,6 +339,16 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
 //    tensor's end), whose values are zeroed in shared memory before use.
 constexpr int kTcChunk = 64;
 constexpr int kTcBufs = 3;
+
+// Output element e (= head * hd + d) of row r, and (when asked) its f16 hi + lo split for the next matmul.
+__device__ __forceinline__ void store_out(const AttnArgs& a, int r, int e, float v) {
+    a.out[int64_t(r) * a.out_stride + e] = v;
+    if (a.out_hi) {
+        const __half h = __float2half_rn(v);
+        a.out_hi[int64_t(r) * a.out_hl_stride + e] = h;
+        a.out_lo[int64_t(r) * a.out_hl_stride + e] = __float2half_rn(v - __half2float(h));
+    }
+}
 constexpr int kTmaBox = 8192;  // bytes of one 64 x 64 f16 box
 
 template <int HD, bool TMA>
@@ -594,7 +604,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
             den += f * wl[w * 8 + g];
         }
         if (!split_mode) {
-            a.out[int64_t(r) * a.out_stride + int64_t(kvh * G + g) * HD + d] = num / den;
+            store_out(a, r, (kvh * G + g) * HD + d, num / den);
         } else {
             float* pr = a.part + ((int64_t(r) * a.n_head + kvh * G + g) * geo.splits + split) * rec;
             if (d == 0) {
@@ -627,7 +637,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
             den += __ldcg(base + sp * rec + 1) * w;
             num += __ldcg(base + sp * rec + 2 + d) * w;
         }
-        a.out[int64_t(r) * a.out_stride + int64_t(kvh * G + g) * HD + d] = num / den;
+        store_out(a, r, (kvh * G + g) * HD + d, num / den);
     }
 }
 
@@ -671,7 +681,9 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl) {
             return cudaErrorInvalidValue;
     }
     const int G = a.n_head / a.n_kv;
-    if ((a.hd == 64 || a.hd == 128) && G <= 8 && kTcChunk == g.chunk) {  // tensor-core kernel
+    const bool tc = (a.hd == 64 || a.hd == 128) && G <= 8 && kTcChunk == g.chunk;
+    if (a.out_hi && (!tc || !a.out_lo || a.out_hl_stride < int64_t(a.n_head) * a.hd)) return cudaErrorInvalidValue;
+    if (tc) {  // tensor-core kernel
         // TMA staging when every (slot, KV head) holds its positions as consecutive hd-element rows of a known
         // [cache_rows][hd] array, and both tensor maps encode
         CUtensorMap tk{}, tv{};

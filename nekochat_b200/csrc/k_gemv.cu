@@ -331,6 +331,10 @@ int gemv_launch_count() { return 1; }
 
 cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, bool pdl, int max_ctas) {
     if (a.rows <= 0 || a.M <= 0) return cudaSuccess;
+    if (a.x_hi || a.in_ss || a.out_hi || a.out_ss) {  // matmul chaining: the tensor-core kernel or nothing
+        const cudaError_t e = max_ctas <= 0 ? launch_gemm_tc(a, st, pdl) : cudaErrorNotSupported;
+        return e == cudaErrorNotSupported ? cudaErrorInvalidValue : e;
+    }
     if (max_ctas <= 0) {  // 1..4 activation rows: the streaming kernel; 5+: tensor cores (when the call fits)
         cudaError_t e = launch_gemv_stream(a, st, pdl);
         if (e != cudaErrorNotSupported) return e;

@@ -341,6 +341,19 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
         peer[zz] = zz < ks ? (ks > 1 ? cg::this_cluster().map_shared_rank(tile, zz) : tile) : tile;
     const int nrow = (mv - z + ks - 1) / ks;  // rows of this CTA
     static_assert(OC % 32 == 0, "a warp's 32 elements share a row");
+    // RMSNorm as a row scale (the activations held x * gamma): rstd of each row from the producer's per-tile
+    // sums of squares, summed in tile order (deterministic)
+    __shared__ float rs[kTM];
+    __shared__ float ssp[kTM][OC / 32];  // per row and 32-column group: sum of squares of the outputs
+    if (a.in_ss) {
+        for (int r = tid; r < nrow; r += kTThreads) {
+            const int row = z + ks * r;
+            double s2 = 0.0;
+            for (int t = 0; t < a.in_ss_tiles; t++) s2 += double(a.in_ss[int64_t(t) * a.M + m0 + row]);
+            rs[row] = float(1.0 / sqrt(s2 / a.K + double(a.eps)));
+        }
+        __syncthreads();
+    }
     for (int i = tid; i < nrow * OC; i += kTThreads) {
         const int row = z + ks * (i / OC), col = i - (i / OC) * OC;
         const int m = m0 + row, n = n0 + col;
@@ -351,7 +364,12 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
             v += peer[zz][row * TPF + col];
             if (PAIR) u += peer[zz][row * TPF + BN + col];
         }
+        if (a.in_ss) {
+            v *= rs[row];
+            u *= rs[row];
+        }
         unsigned long long key = 0ull;
+        float sq = 0.0f;
         if (n < a.rows) {
             float* dst = a.y + int64_t(m) * a.y_stride + a.n_off + n;
             float val = v;
@@ -364,11 +382,32 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
             }
             *dst = val;
             key = argmax_key(val, n);
+            if (a.out_hi) {  // the next matmul's activations: val * gamma as f16 hi + lo
+                const float yv = a.out_gamma ? val * a.out_gamma[n] : val;
+                const __half h = __float2half_rn(yv);
+                a.out_hi[int64_t(m) * a.out_ld + n] = h;
+                a.out_lo[int64_t(m) * a.out_ld + n] = __float2half_rn(yv - __half2float(h));
+            }
+            sq = val * val;
+        }
+        if (a.out_ss) {  // the warp's 32 columns of the row
+            sq = warp_sum(sq);
+            if (lane == 0) ssp[row][col >> 5] = sq;
         }
         if (a.argmax) {  // the warp's 32 columns of the row, then one shared atomic
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
             if (lane == 0 && key) atomicMax(&keys[row], key);
+        }
+    }
+    if (a.out_ss) {  // one partial per (column tile, row), the column groups summed in order
+        __syncthreads();
+        for (int r = tid; r < nrow; r += kTThreads) {
+            const int row = z + ks * r;
+            float s2 = 0.0f;
+#pragma unroll
+            for (int h = 0; h < OC / 32; h++) s2 += ssp[row][h];
+            a.out_ss[int64_t(blockIdx.x) * a.M + m0 + row] = s2;
         }
     }
     if (a.argmax) {  // one global atomic per row of this CTA
@@ -468,12 +507,22 @@ void gemm_tc_scratch(int fmt, int rows, int K, int M, bool pair, bool norm, int6
 cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl) {
     if (!gemm_tc_fits(a)) return cudaErrorNotSupported;
     const bool pair = a.pair_off != 0;
-    const TcPlan pl = tc_plan(a, a.ws ? a.ws_floats : 0);
+    TcPlan pl = tc_plan(a, a.ws ? a.ws_floats : 0);
+    const bool chained = a.x_hi || a.in_ss || a.out_hi || a.out_ss;
+    if (chained) {  // this kernel only (not tcgen05); norms only as row scales
+        if (a.norm != kNormNone || (a.x_hi && !a.x_lo) || (a.in_ss && a.in_ss_tiles <= 0) ||
+            (a.out_hi && (!a.out_lo || a.out_ld < a.rows)))
+            return cudaErrorInvalidValue;
+        if (a.x_hi) pl.presplit = true;
+    }
     if (a.norm != kNormNone && !pl.presplit) return cudaErrorNotSupported;
     TcSplit sp{};
     sp.ksplit = pl.ksplit;
     sp.sper = pl.sper;
-    if (pl.presplit) {
+    if (a.x_hi) {
+        sp.xh = a.x_hi;
+        sp.xl = a.x_lo;
+    } else if (pl.presplit) {
         sp.xh = reinterpret_cast<const __half*>(a.ws);
         sp.xl = sp.xh + int64_t(a.M) * a.K;
         cudaError_t e;
@@ -488,8 +537,10 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl) {
         }
         if (e != cudaSuccess) return e;
         // 128+ rows: the tcgen05 kernel (TMEM accumulators) on the split activations
-        e = launch_gemm_umma(a, sp.xh, sp.xl, st, true);
-        if (e != cudaErrorNotSupported) return e;
+        if (!chained) {
+            e = launch_gemm_umma(a, sp.xh, sp.xl, st, true);
+            if (e != cudaErrorNotSupported) return e;
+        }
     }
     const bool pre = pl.presplit;
     TcFn k = a.fmt == kFP8 ? (pre ? pick<kFP8, true>(pair) : pick<kFP8, false>(pair))
@@ -511,7 +562,7 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl) {
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     int na = 0;
-    if (pdl || pl.presplit) {
+    if (pdl || (pl.presplit && !a.x_hi)) {  // after the split kernel of this call, or as asked
         attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[na].val.programmaticStreamSerializationAllowed = 1;
         na++;

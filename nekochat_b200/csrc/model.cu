@@ -102,6 +102,12 @@ struct neko_model {
     float* part = nullptr;
     unsigned* tickets = nullptr;
     int64_t part_cap = 0, tick_cap = 0;
+    // matmul chaining at 5..127 rows (Qwen3): split activations in two ping-pong buffers, A [2][rows][C] (the
+    // normed residual stream times gamma) and B [2][rows][max(H * hd, F)] (attention output, SwiGLU product), and
+    // the residual stream's per-tile sums of squares [C / 64][rows]
+    __half *ch_a = nullptr, *ch_b = nullptr;
+    float* ch_ss = nullptr;
+    int ch_rows = 0;
     float* mm_ws = nullptr;          // tensor-core matmul workspace (K splits, split activations)
     unsigned* mm_tickets = nullptr;
     int64_t mm_ws_floats = 0, mm_tickets_n = 0;
@@ -126,6 +132,7 @@ struct neko_model {
     int debug_stage = 0;    // > 0: stop inside layer debug_layers after this stage (debugStages numbering)
     // graphs keyed by (rows, nout, bucket, mode)
     std::map<std::tuple<int, int, int, int>, cudaGraphExec_t> graphs;
+    int graph_kernels = 0;  // kernel nodes of the most recently captured step graph
     // single-kernel decode steps (k_decode.cu)
     bool dec_enabled = true;
     int dec_stall_test = 0;    // the next single-kernel step waits for a CTA that does not exist (50 ms limit)
@@ -236,6 +243,23 @@ std::vector<float> rope_table(int ctx, int hd, double theta) {
     return t;
 }
 
+// Matmul chaining: activation rows, the column tile of the per-tile sums of squares (the tensor-core kernel's
+// 64-column CTA tile), and the inputs / outputs of one chained matmul.
+constexpr int kChainMaxRows = 127;
+constexpr int kChainTile = 64;
+struct ChainIO {
+    const __half *xh, *xl;  // split input activations
+    const float* in_ss;     // RMSNorm row scale from these sums of squares (null: none)
+    __half *oh, *ol;        // split output * og for the next matmul (null: none)
+    int64_t old;
+    const float* og;
+    float* oss;             // per-tile sums of squares of the output (null: none)
+};
+// Whether a step of R rows chains its matmuls: Qwen3, every layer matmul on the tensor-core kernel, attention
+// on its tensor-core kernel.
+bool chain_ok(const neko_model* m, int R);
+bool chain_head_ok(const neko_model* m, int R);
+
 int bucket_for(neko_model* m, int max_pos) {
     int b = 256;
     while (b < max_pos + 1) b *= 2;
@@ -263,7 +287,7 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
     const bool x_fits = gemv_norm_fusable(fmt_for(C, m->fmt), R, C);
     auto gemv = [&](const Mat& W, int nrows, const float* x, int64_t xs, int M, int norm, const float* g,
                     const float* b, const float* bias, int flags, float* y, int64_t ys, int64_t pair,
-                    unsigned long long* keys = nullptr) -> cudaError_t {
+                    unsigned long long* keys = nullptr, const ChainIO* io = nullptr) -> cudaError_t {
         GemvArgs a;
         a.W = W.w;
         a.row_bytes = W.rb;
@@ -287,9 +311,26 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         a.ws_floats = m->mm_ws_floats;
         a.ws_tickets = m->mm_tickets;
         a.ws_ntickets = int(m->mm_tickets_n);
+        if (io) {
+            a.x_hi = io->xh;
+            a.x_lo = io->xl;
+            a.in_ss = io->in_ss;
+            a.in_ss_tiles = io->in_ss ? m->C / kChainTile : 0;
+            a.out_hi = io->oh;
+            a.out_lo = io->ol;
+            a.out_ld = io->old;
+            a.out_gamma = io->og;
+            a.out_ss = io->oss;
+        }
         return launch_gemv(a, st, pdl());
     };
     const bool staged = m->debug_layers >= 0 && m->debug_stage > 0;
+    // matmul chaining (5..127 rows): A holds the next normed matmul's input (x * gamma, hi / lo), B the attention
+    // output and the SwiGLU product; the RMSNorms are row scales from the per-tile sums of squares
+    const bool chain = !staged && chain_ok(m, R);
+    const int64_t BW = std::max<int64_t>(int64_t(H) * hd, m->F);
+    __half *a_hi = m->ch_a, *a_lo = m->ch_a + int64_t(R) * C;
+    __half *b_hi = m->ch_b, *b_lo = m->ch_b + int64_t(R) * BW;
     // norm: applied by the matmul call (the GEMV prologue when the activations fit in shared memory, or the
     // tensor-core path's activation split) or by a separate kernel
     auto normed = [&](const Mat& W, int rows, bool pair, const float* g, const float* b, int& norm_kind,
@@ -320,8 +361,16 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         uint16_t* vc = m->vc + int64_t(l) * m->kv_layer;
         int nk;
         const float* src;
-        CK(normed(L.wqkv, m->QW, false, L.ln1, L.ln1b, nk, src), "norm1");
-        CK(gemv(L.wqkv, m->QW, src, C, R, nk, L.ln1, L.ln1b, L.bqkv, m->qwen ? 0 : kBias, m->qkv, m->QW, 0), "qkv");
+        if (chain && l > 0) {  // the previous layer's down projection wrote x * ln1 and the sums of squares
+            const ChainIO io{a_hi, a_lo, m->ch_ss, nullptr, nullptr, 0, nullptr, nullptr};
+            CK(gemv(L.wqkv, m->QW, m->x, C, R, kNormNone, nullptr, nullptr, L.bqkv, m->qwen ? 0 : kBias, m->qkv,
+                    m->QW, 0, nullptr, &io),
+               "qkv");
+        } else {
+            CK(normed(L.wqkv, m->QW, false, L.ln1, L.ln1b, nk, src), "norm1");
+            CK(gemv(L.wqkv, m->QW, src, C, R, nk, L.ln1, L.ln1b, L.bqkv, m->qwen ? 0 : kBias, m->qkv, m->QW, 0),
+               "qkv");
+        }
         if (dump(l, 2, m->qkv, m->QW)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
         QkvPostArgs q;
         q.qkv = m->qkv;
@@ -373,8 +422,31 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         a.part_capacity = m->part_cap;
         a.ticket_capacity = m->tick_cap;
         a.cache_rows = m->kv_layer / hd;
+        if (chain) {
+            a.out_hi = b_hi;
+            a.out_lo = b_lo;
+            a.out_hl_stride = int64_t(H) * hd;
+        }
         CK(launch_attention(a, st, pdl()), "attention");
         if (dump(l, m->qwen ? 4 : 3, m->att, H * hd)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
+        if (chain) {
+            // o_proj reads the attention's split output and writes x * ln2 + sums of squares for gate / up, whose
+            // SwiGLU product (split) feeds down, which writes x * (next ln1 or the final norm) + sums of squares
+            const ChainIO io_o{b_hi, b_lo, nullptr, a_hi, a_lo, C, L.ln2, m->ch_ss};
+            CK(gemv(L.wo, C, m->att, int64_t(H) * hd, R, kNormNone, nullptr, nullptr, nullptr, kAccumulate, m->x, C,
+                    0, nullptr, &io_o),
+               "o_proj");
+            const ChainIO io_gu{a_hi, a_lo, m->ch_ss, b_hi, b_lo, m->F, nullptr, nullptr};
+            CK(gemv(L.wup, m->F, m->x, C, R, kNormNone, nullptr, nullptr, nullptr, 0, m->h, m->F, m->F, nullptr,
+                    &io_gu),
+               "gate_up");
+            const float* g_next = l + 1 < m->layers.size() ? m->layers[l + 1].ln1 : m->normf;
+            const ChainIO io_d{b_hi, b_lo, nullptr, a_hi, a_lo, C, g_next, m->ch_ss};
+            CK(gemv(L.wdown, C, m->h, m->F, R, kNormNone, nullptr, nullptr, nullptr, kAccumulate, m->x, C, 0,
+                    nullptr, &io_d),
+               "down");
+            continue;
+        }
         CK(gemv(L.wo, C, m->att, int64_t(H) * hd, R, kNormNone, nullptr, nullptr, L.bo,
                 kAccumulate | (m->qwen ? 0 : kBias), m->x, C, 0),
            "o_proj");
@@ -411,7 +483,11 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
                            gemm_tc_launches(m->embed.fmt, m->V, C, nout, false, true) > 0;
     const bool fused_argmax = do_argmax && nout <= 64;
     unsigned long long* keys = fused_argmax ? m->d_keys : nullptr;
-    if (head_fits) {
+    if (chain && outrows_identity && nout == R && chain_head_ok(m, R)) {  // x * normf split by the last down
+        const ChainIO io{a_hi, a_lo, m->ch_ss, nullptr, nullptr, 0, nullptr, nullptr};
+        CK(gemv(m->embed, m->V, m->x, C, nout, kNormNone, nullptr, nullptr, nullptr, 0, m->logits, m->V, 0, keys, &io),
+           "lm_head");
+    } else if (head_fits) {
         CK(gemv(m->embed, m->V, hx, C, nout, m->qwen ? kNormRms : kNormLayer, m->normf, m->normfb, nullptr, 0,
                 m->logits, m->V, 0, keys),
            "lm_head");
@@ -471,9 +547,31 @@ int matmul_launches(const MatShape& ms, int M, bool x_fits) {
     return tc > 0 ? tc : 1;
 }
 
+bool chain_ok(const neko_model* m, int R) {
+    if (!m->qwen || !m->ch_a || R < 5 || R > std::min(kChainMaxRows, m->ch_rows) || m->C % kChainTile) return false;
+    if ((m->hd != 64 && m->hd != 128) || m->KV <= 0 || m->H % m->KV || m->H / m->KV > 8) return false;
+    for (const MatShape& ms : mat_shapes(m))
+        if (!ms.lm_head && gemm_tc_launches(ms.fmt, ms.rows, ms.K, R, ms.pair, false) <= 0) return false;
+    return true;
+}
+
+bool chain_head_ok(const neko_model* m, int R) {
+    return gemm_tc_launches(m->embed.fmt, m->V, m->C, R, false, false) > 0;
+}
+
 int step_launches(neko_model* m, int R, int nout, bool gather, bool do_argmax, bool advance) {
     if (!gather && nout == R && m->debug_layers < 0 && m->dec_enabled && R <= m->dec_seqs && decode_ok(m, R))
         return 1;
+    if (m->debug_layers < 0 && chain_ok(m, R)) {
+        // embedding, the first layer's norm split + qkv, then per layer qkv_post, attention, o_proj, gate / up,
+        // down and (after the first) qkv
+        const MatShape q = mat_shapes(m)[0];
+        const int nl = int(m->layers.size());
+        int n = 1 + gemm_tc_launches(q.fmt, q.rows, q.K, R, false, true) + 5 * nl + (nl - 1) + (gather ? 1 : 0);
+        if (!gather && nout == R && chain_head_ok(m, R)) n += 1;
+        else n += matmul_launches(mat_shapes(m).back(), nout, gemv_norm_fusable(m->embed.fmt, nout, m->C));
+        return n + (do_argmax ? 1 : 0) + (advance && nout > 64 ? 1 : 0);
+    }
     const bool x_fits = gemv_norm_fusable(fmt_for(m->C, m->fmt), R, m->C);
     int per_layer = 2;  // qkv_post, attention
     for (const MatShape& ms : mat_shapes(m))
@@ -603,6 +701,18 @@ int run_step(neko_model* m, int R, int nout, bool identity, int max_pos, bool do
             return rc;
         }
         if (e != cudaSuccess) return fail(m, NEKO_ERR_CUDA, cuda_msg(e, "end capture"));
+        // kernel nodes of the step (checked against neko_model_step_launches by the tests)
+        size_t nn = 0;
+        m->graph_kernels = 0;
+        if (cudaGraphGetNodes(g, nullptr, &nn) == cudaSuccess && nn > 0) {
+            std::vector<cudaGraphNode_t> nodes(nn);
+            if (cudaGraphGetNodes(g, nodes.data(), &nn) == cudaSuccess)
+                for (size_t i = 0; i < nn; i++) {
+                    cudaGraphNodeType t;
+                    if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel)
+                        m->graph_kernels++;
+                }
+        }
         cudaGraphExec_t ex = nullptr;
         e = cudaGraphInstantiate(&ex, g, 0);
         cudaGraphDestroy(g);
@@ -764,6 +874,17 @@ neko_model* neko_model_create(int device, const neko_model_config* cfg, char* er
         if (m->mm_tickets) cudaMemset(m->mm_tickets, 0, size_t(std::max<int64_t>(wt, 1)) * 4);
         m->work_bytes += size_t(wt) * 4;
     }
+    // matmul chaining buffers (Qwen3)
+    if (m->qwen) {
+        m->ch_rows = int(std::min<size_t>(R, size_t(kChainMaxRows)));
+        const int64_t bw = std::max<int64_t>(int64_t(m->H) * m->hd, m->F);
+        const size_t na = size_t(2) * m->ch_rows * m->C, nb = size_t(2) * m->ch_rows * bw;
+        const size_t nss = size_t(m->ch_rows) * ((m->C + kChainTile - 1) / kChainTile);
+        if (cudaMalloc(&m->ch_a, na * 2) != cudaSuccess || cudaMalloc(&m->ch_b, nb * 2) != cudaSuccess ||
+            falloc(&m->ch_ss, nss))
+            return bail(m, "matmul chaining buffers allocation failed");
+        m->work_bytes += (na + nb) * 2;
+    }
     // single-kernel decode steps: split-KV partials at the smallest span (32 keys), tickets, phase counters
     m->dec_seqs = std::min({kDecodeMaxSeqs, c.max_rows, c.max_seqs});
     m->dec_max_splits = (c.context + 31) / 32;
@@ -822,6 +943,7 @@ void neko_model_destroy(neko_model* m) {
                     (void*)m->att, (void*)m->h, (void*)m->hx, (void*)m->logits, (void*)m->d_tokens, (void*)m->d_slots,
                     (void*)m->d_pos, (void*)m->d_argmax, (void*)m->d_outrows, (void*)m->d_keys, (void*)m->part,
                     (void*)m->tickets, (void*)m->mm_ws, (void*)m->mm_tickets, (void*)m->dec_part, (void*)m->dec_tickets, (void*)m->dec_sync,
+                    (void*)m->ch_a, (void*)m->ch_b, (void*)m->ch_ss,
                     (void*)m->staging})
         if (p) cudaFree(p);
     if (m->h_in) cudaFreeHost(m->h_in);
@@ -1110,6 +1232,11 @@ int neko_model_set_decode_kernel(neko_model* m, int enable) {
 int neko_model_step_launches(neko_model* m, int n) {
     if (!m) return NEKO_ERR_ARG;
     return step_launches(m, n, n, false, true, true);
+}
+
+int neko_model_graph_kernels(neko_model* m) {
+    if (!m) return NEKO_ERR_ARG;
+    return m->graph_kernels;
 }
 
 int neko_model_matrix(neko_model* m, const char* which, const uint8_t** ptr, int* rows, int* cols) {

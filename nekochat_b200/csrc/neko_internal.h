@@ -63,6 +63,22 @@ struct GemvArgs {
     int64_t ws_floats = 0;
     unsigned* ws_tickets = nullptr;
     int ws_ntickets = 0;
+    // tensor-core chaining (5..127 rows, FP8 / FP4): each matmul's epilogue prepares the next one's input.
+    //  * x_hi / x_lo: the activations already split into f16 hi + lo ([M][K] each); no split kernel runs.
+    //  * in_ss: RMSNorm as a row scale. The activations hold x * gamma; y[m] is multiplied by
+    //    rstd[m] = 1 / sqrt(sum_{t < in_ss_tiles} in_ss[t * M + m] / K + eps) before the bias / activation.
+    //  * out_hi / out_lo: the epilogue also writes the output times (out_gamma ? out_gamma[n] : 1) split into
+    //    hi + lo f16 at [m * out_ld + n]; out_ss: the sums of squares of the output over each CTA's columns
+    //    (column tile t, row m) at out_ss[t * M + m], for a consumer's in_ss.
+    const __half* x_hi = nullptr;
+    const __half* x_lo = nullptr;
+    const float* in_ss = nullptr;
+    int in_ss_tiles = 0;
+    __half* out_hi = nullptr;
+    __half* out_lo = nullptr;
+    int64_t out_ld = 0;
+    const float* out_gamma = nullptr;
+    float* out_ss = nullptr;
     // launch plan (filled by plan_gemv)
     int x_smem = 0;
     int rows_per_cta = 0;
@@ -170,6 +186,11 @@ struct AttnArgs {
     // rows of hd elements in each of kc and vc (0: unknown). Known, with positions hd apart, it lets the kernel
     // stage key / value chunks with 2D tensor copies bounded by the arrays.
     int64_t cache_rows = 0;
+    // optional: the output also as f16 hi + lo (row r, head h at out_hi + r * out_hl_stride + h * hd), the next
+    // matmul's split activations (tensor-core kernel only)
+    __half* out_hi = nullptr;
+    __half* out_lo = nullptr;
+    int64_t out_hl_stride = 0;
 };
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl);
 // Scratch the split-KV attention needs for rows x n_head heads up to position max_pos.

@@ -157,6 +157,10 @@ class Model:
     def step_launches(self, n):
         return int(lib().neko_model_step_launches(self.h, n))
 
+    def graph_kernels(self):
+        """Kernel nodes of the most recently captured step graph."""
+        return int(lib().neko_model_graph_kernels(self.h))
+
     def set_decode_kernel(self, enable):
         """Run decode steps of 1..4 sequences as one persistent kernel (True, the default) or as the per-operator
         kernel chain (False); 2 makes the kernel's next steps hit a wait that runs out (timeout test). Returns

@@ -156,3 +156,43 @@ def test_device_tensor_on_another_device_is_refused():
     with pytest.raises(nb.NekoError, match="cuda:1"):
         m.set_tensor_device("embed_tokens.weight", t)
     m.close()
+
+
+def test_step_launch_count_matches_captured_graph():
+    """neko_model_step_launches (the bench's gpu_launches) == the kernel nodes of the captured step graph, on the
+    single-kernel step (1, 4 sequences) and the kernel chain with chained matmuls (8, 40, 64 sequences)."""
+    s = workload.shape("qwen3-tiny")
+    m = nmodel.build("qwen3-tiny", FP8, context=64, max_seqs=64, max_rows=64, seed=1)
+    rng = np.random.default_rng(2)
+    for n in (1, 4, 8, 40, 64):
+        slots = np.arange(n, dtype=np.int32)
+        m.stage(slots, rng.integers(0, s["vocab"], n).astype(np.int32), np.full(n, 5, np.int32))
+        m.step(n, 5)
+        assert m.graph_kernels() == m.step_launches(n), n
+    m.close()
+
+
+@pytest.mark.parametrize("n", [40, 100])
+def test_chained_batch_matches_single_sequence(n):
+    """n sequences in one step (matmuls chained: each epilogue writes the next matmul's split activations, the
+    RMSNorms applied as row scales; 100 rows take two 64-row tiles) == each sequence decoded alone on the
+    single-kernel step, to the fp32 rounding level."""
+    s = workload.shape("qwen3-tiny")
+    tensors = list(workload.weights(s, seed=7, perturb=True))
+    m = nmodel.Model(s, FP8, context=48, max_seqs=n, max_rows=n).load(tensors)
+    m2 = nmodel.Model(s, FP8, context=48, max_seqs=n, max_rows=n).load(tensors)
+    rng = np.random.default_rng(11)
+    prompts = [workload.prompt(s, int(k), seed=30 + i) for i, k in enumerate(rng.integers(2, 30, n))]
+    first = [int(np.argmax(m.prefill(p, slot))) for slot, p in enumerate(prompts)]
+    slots = np.arange(n, dtype=np.int32)
+    pos = np.array([len(p) for p in prompts], np.int32)
+    lg_b, am_b = m.decode(slots, first, pos)
+    for slot, p in enumerate(prompts):
+        m2.prefill(p, slot)
+        lg, am = m2.decode([slot], [first[slot]], [pos[slot]])
+        np.testing.assert_allclose(lg_b[slot], lg[0], rtol=1e-4, atol=1e-4)
+        if am_b[slot] != am[0]:
+            srt = np.sort(lg[0])
+            assert srt[-1] - srt[-2] <= 2e-4, "greedy token differs beyond a near-tie"
+    m.close()
+    m2.close()
