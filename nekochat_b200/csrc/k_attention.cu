@@ -326,18 +326,22 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
 // accumulation), for head_dim 64 / 128 and up to 8 query heads per KV head:
 //  * the cache rows are f16 already, so keys and values enter the MMA exactly; the query and the probabilities
 //    are split into hi + lo f16 (about 22 bits, as in the matmul), so scores and P.V keep fp32-level accuracy;
-//  * MMA rows = the group's query heads (rows past G are zero), columns = 8 keys (scores) or 8 dims (P.V);
-//  * warp w owns keys 16w..16w+15 of each 64-key chunk with its own running max / sum (online softmax per
-//    warp, no block barrier inside a chunk); the score fragments of its two key tiles are exactly the A fragment
-//    of the P.V step. The four warps' (max, sum, acc) are merged once at the end of the split;
-//  * all threads stage the chunks with 16-byte cp.async into padded shared-memory rows (pitch hd + 8 halves,
-//    conflict-free ldmatrix; rows past the last key are zero-filled), three buffers, one barrier per chunk.
-//  * TMA variant (caches whose positions are contiguous rows of hd halves, e.g. [slot][kv head][pos][hd]): one
-//    thread stages each chunk as 2D tensor copies of 64 keys x 64 dims (128-byte swizzle: 16-byte piece q of row
-//    j sits at piece q ^ (j & 7), so the ldmatrix row groups stay conflict-free without padding) completing on one
-//    mbarrier per buffer; the copies read the rows past the chunk's last key too (cache memory, or zeros past the
-//    tensor's end), whose values are zeroed in shared memory before use.
-constexpr int kTcChunk = 64;
+//  * keys and head dims are the MMA's rows, the group's query heads its 8 columns (heads past G are zero): the
+//    scores S^T[key][head] take the key rows as A (ldmatrix) and the query fragments as B; P.V accumulates
+//    O^T[dim][head] from the value rows (A, transposed by ldmatrix) and P^T as B, which 8 shuffles gather from
+//    the score fragments. With G = 2 this is half the MMAs and accumulators of putting the heads on the rows;
+//  * warp w owns keys 16w..16w+15 of each chunk with its own running max / sum per head (online softmax per
+//    warp, no block barrier inside a chunk); the warps' (max, sum, acc) are merged once at the end of the split;
+//  * cp.async variant (any cache layout): 4 warps, 64-key chunks staged by all threads with 16-byte cp.async into
+//    padded shared-memory rows (pitch hd + 8 halves, conflict-free ldmatrix; rows past the last key zero-filled),
+//    three buffers, one barrier per chunk;
+//  * TMA variant (caches whose positions are contiguous rows of hd halves, e.g. [slot][kv head][pos][hd]): 2 warps,
+//    32-key chunks that one thread stages as 2D tensor copies of 32 keys x 64 dims (128-byte swizzle: 16-byte
+//    piece q of row j sits at piece q ^ (j & 7), so the ldmatrix row groups stay conflict-free without padding)
+//    completing on one mbarrier per buffer; the copies read the rows past the chunk's last key too (cache
+//    memory, or zeros past the tensor's end), whose values are zeroed in shared memory before use. Four CTAs
+//    share an SM, so the splits are planned to fill them once (one wave).
+constexpr int kTcChunk = 64;  // keys per chunk of the cp.async variant (4 warps x 16)
 constexpr int kTcBufs = 3;
 
 // Output element e (= head * hd + d) of row r, and (when asked) its f16 hi + lo split for the next matmul.
@@ -349,13 +353,22 @@ __device__ __forceinline__ void store_out(const AttnArgs& a, int r, int e, float
         a.out_lo[int64_t(r) * a.out_hl_stride + e] = __float2half_rn(v - __half2float(h));
     }
 }
-constexpr int kTmaBox = 8192;  // bytes of one 64 x 64 f16 box
+// TMA variant: 2 warps per CTA, chunks of 32 keys (boxes of 32 keys x 64 dims), 3 buffers: about 50 KB of
+// shared memory, so four CTAs share an SM and a batch-64 layer's 512 (row, KV head) items run in one wave
+constexpr int kTmaWarps = 2;
+constexpr int kTmaChunk = 16 * kTmaWarps;
+constexpr int kTmaBox = kTmaChunk * 128;  // bytes of one box (keys x 128-byte rows)
+constexpr int kTcBufsTma = 3;             // buffers per CTA
+constexpr int kTcCtasTma = 4;             // CTAs per SM
+__host__ __device__ constexpr int tc_bufs(bool tma) { return tma ? kTcBufsTma : kTcBufs; }
+__host__ __device__ constexpr int tc_warps(bool tma) { return tma ? kTmaWarps : 4; }
 
 template <int HD, bool TMA>
 constexpr int tc_attn_smem() {
-    // the buffers, then (TMA) kTcBufs mbarriers, then two flags; TMA adds up to 1024 bytes to align the buffers
-    return TMA ? kTcBufs * 2 * (HD / 64) * kTmaBox + 64 + 1024 : kTcBufs * 2 * kTcChunk * (HD + 8) * 2 + 64;
+    // the buffers, then (TMA) their mbarriers, then two flags; TMA adds up to 1024 bytes to align the buffers
+    return TMA ? kTcBufsTma * 2 * (HD / 64) * kTmaBox + 64 + 1024 : kTcBufs * 2 * kTcChunk * (HD + 8) * 2 + 64;
 }
+static_assert(kTcCtasTma * (tc_attn_smem<128, true>() + 1024) <= 228 * 1024, "four TMA CTAs per SM");
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -366,15 +379,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 }
 
 template <int HD, bool TMA>
-__global__ void __launch_bounds__(kAttnThreads, 2)
+__global__ void __launch_bounds__(32 * tc_warps(TMA), TMA ? kTcCtasTma : 2)
     attention_tc_kernel(const AttnArgs a, const Geometry geo, const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv) {
     constexpr int P = HD + 8;  // padded row pitch (halves)
-    constexpr int CH = kTcChunk, KS = HD / 16, NTO = HD / 8, NB = HD / 64;
+    constexpr int W = tc_warps(TMA), NT = 32 * W;  // warps, threads
+    constexpr int CH = 16 * W, KS = HD / 16, MT = HD / 16, NB = HD / 64, NBUF = tc_bufs(TMA);
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // TMA boxes with the 128-byte swizzle need 1024-byte aligned destinations
     uint8_t* smem = TMA ? smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023) : smem_raw;
-    uint16_t* kvb = reinterpret_cast<uint16_t*>(smem);  // [kTcBufs][2][CH][P]: keys, then values
+    uint16_t* kvb = reinterpret_cast<uint16_t*>(smem);  // [NBUF][2][CH][P]: keys, then values
 
     const int split = blockIdx.x, kvh = blockIdx.y, r = blockIdx.z;
     const int G = a.n_head / a.n_kv;
@@ -394,20 +408,20 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     const int nchunks = (j_end - j_begin + CH - 1) / CH;
     const uint16_t* kbase = a.kc + int64_t(slot) * a.slot_stride + int64_t(kvh) * a.head_stride;
     const uint16_t* vbase = a.vc + int64_t(slot) * a.slot_stride + int64_t(kvh) * a.head_stride;
-    // every thread: its 16-byte pieces of chunk cc's key and value rows into buffer cc % kTcBufs (one commit group
+    // every thread: its 16-byte pieces of chunk cc's key and value rows into buffer cc % NBUF (one commit group
     // per chunk); rows past the chunk's last key are zero-filled without reading memory
     constexpr int BUF = TMA ? 2 * NB * kTmaBox : 2 * CH * P * 2;  // bytes per buffer
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcBufs * BUF);  // TMA: one mbarrier per buffer
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NBUF * BUF);  // TMA: one mbarrier per buffer
     // flags in dynamic shared memory (the kernel declares no static shared variables)
-    int& last = *reinterpret_cast<int*>(smem + kTcBufs * BUF + 32);
-    int& tma_ok = *reinterpret_cast<int*>(smem + kTcBufs * BUF + 36);
+    int& last = *reinterpret_cast<int*>(smem + NBUF * BUF + 32);
+    int& tma_ok = *reinterpret_cast<int*>(smem + NBUF * BUF + 36);
     // row of this (slot, KV head)'s position 0 in the tensor maps' [rows][hd] view
     const int row0 = TMA ? int((int64_t(slot) * a.slot_stride + int64_t(kvh) * a.head_stride) / HD) : 0;
     auto issue = [&](int cc) {
         const int j0 = j_begin + cc * CH, n = min(CH, j_end - j0);
-        uint8_t* dst = smem + (cc % kTcBufs) * BUF;
+        uint8_t* dst = smem + (cc % NBUF) * BUF;
         if constexpr (TMA) {  // thread 0 only
-            uint64_t* bar = &bars[cc % kTcBufs];
+            uint64_t* bar = &bars[cc % NBUF];
             mbar_arrive_expect_tx(bar, uint32_t(BUF));
 #pragma unroll
             for (int bx = 0; bx < NB; bx++) {
@@ -418,7 +432,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
             uint16_t* dk = reinterpret_cast<uint16_t*>(dst);
             constexpr int PR = HD / 8;  // pieces per row
 #pragma unroll 4
-            for (int i = tid; i < 2 * CH * PR; i += kAttnThreads) {
+            for (int i = tid; i < 2 * CH * PR; i += NT) {
                 const int v = i >= CH * PR ? 1 : 0, j = (i - v * CH * PR) / PR, q = i - v * CH * PR - j * PR;
                 const uint16_t* src = (v ? vbase : kbase) + int64_t(j0 + min(j, n - 1)) * a.pos_stride + 8 * q;
                 cp16(dk + (v * CH + j) * P + 8 * q, src, j < n ? 16 : 0);
@@ -438,18 +452,18 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
                 tma_ok = 0;
             }
 #pragma unroll
-            for (int b = 0; b < kTcBufs; b++) mbar_init(&bars[b], 1);
+            for (int b = 0; b < NBUF; b++) mbar_init(&bars[b], 1);
             fence_barrier_init();
             if (tma_ok) {
 #pragma unroll
-                for (int cc = 0; cc < kTcBufs - 1; cc++)
+                for (int cc = 0; cc < NBUF - 1; cc++)
                     if (cc < nchunks) issue(cc);
             }
         }
         __syncthreads();  // barrier initialisation visible before any thread waits
     } else {
 #pragma unroll
-        for (int cc = 0; cc < kTcBufs - 1; cc++) {
+        for (int cc = 0; cc < NBUF - 1; cc++) {
             if (cc < nchunks) issue(cc);
             cp_commit();
         }
@@ -475,130 +489,144 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
                 split_hilo(x0, x1, qh[ks][h], ql[ks][h]);
             }
     }
-    float o[NTO][4];
+    // lane (g, c) keeps heads 2c, 2c + 1 of the group: their running max and its share of the running sum, and
+    // the P.V accumulators O^T[dim][head] of dims 16t + g and 16t + g + 8
+    float o[MT][4];
 #pragma unroll
-    for (int t = 0; t < NTO; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
-    float m_run = -INFINITY, l_part = 0.0f;  // row gr: running max; this lane's share of the running sum
+    for (int t = 0; t < MT; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_part[2] = {0.0f, 0.0f};
     const int k0 = 16 * warp;
 
     for (int cc = 0; cc < nchunks; cc++) {
-        const int b = cc % kTcBufs, n = min(CH, j_end - (j_begin + cc * CH));
+        const int b = cc % NBUF, n = min(CH, j_end - (j_begin + cc * CH));
         if constexpr (TMA) {
-            if (tma_ok) mbar_wait(&bars[b], uint32_t(cc / kTcBufs) & 1u);  // chunk cc landed (bounded)
+            if (tma_ok) mbar_wait(&bars[b], uint32_t(cc / NBUF) & 1u);  // chunk cc landed (bounded)
             if (n < CH) {  // value rows past the last key: zeros (0 x inf or NaN in stale rows would poison P.V)
                 uint8_t* vz = smem + b * BUF + NB * kTmaBox;
-                for (int i = tid; i < NB * (CH - n) * 8; i += kAttnThreads) {
+                for (int i = tid; i < NB * (CH - n) * 8; i += NT) {
                     const int bx = i / ((CH - n) * 8), rem = i - bx * (CH - n) * 8;
                     *reinterpret_cast<uint4*>(vz + bx * kTmaBox + (n + (rem >> 3)) * 128 + 16 * (rem & 7)) =
                         make_uint4(0u, 0u, 0u, 0u);
                 }
             }
             __syncthreads();  // zeroed rows visible; every warp is done with chunk cc - 1's buffer
-            if (tid == 0 && tma_ok && cc + kTcBufs - 1 < nchunks) issue(cc + kTcBufs - 1);
+            if (tid == 0 && tma_ok && cc + NBUF - 1 < nchunks) issue(cc + NBUF - 1);
         } else {
-            cp_wait<kTcBufs - 2>();  // chunk cc landed (this thread's pieces)
+            cp_wait<NBUF - 2>();  // chunk cc landed (this thread's pieces)
             __syncthreads();         // ... every thread's; and every warp is done with chunk cc - 1's buffer
-            if (cc + kTcBufs - 1 < nchunks) issue(cc + kTcBufs - 1);
+            if (cc + NBUF - 1 < nchunks) issue(cc + NBUF - 1);
             cp_commit();
         }
         if (k0 < n) {
-            // scores of keys k0..k0+15: two n8 tiles
-            // four independent accumulators (tile x hi/lo) so consecutive MMAs do not wait on each other
-            float s[2][4], sl[2][4];
+            // scores S^T[key][head] of keys k0..k0+15 (the MMA's rows) and the group's heads (its columns): A = key
+            // rows by ldmatrix, B = the query fragments; hi and lo products of even and odd k-steps in four
+            // independent accumulators
+            float sa[4][4];
 #pragma unroll
             for (int ks = 0; ks < KS; ks++) {
-                uint32_t bf[4];
-                ldsm_x4(bf, tile_addr(b, 0, k0 + 8 * (lane >> 4) + (lane & 7), 2 * ks + ((lane >> 3) & 1)));
-                const uint32_t ah[4] = {qh[ks][0], 0u, qh[ks][1], 0u}, al[4] = {ql[ks][0], 0u, ql[ks][1], 0u};
-                if (ks == 0) {
-                    mma16816_z(s[0], ah, bf[0], bf[1]);
-                    mma16816_z(s[1], ah, bf[2], bf[3]);
-                    mma16816_z(sl[0], al, bf[0], bf[1]);
-                    mma16816_z(sl[1], al, bf[2], bf[3]);
+                uint32_t kf[4];
+                ldsm_x4(kf, tile_addr(b, 0, k0 + (lane & 15), 2 * ks + (lane >> 4)));
+                float(&sh)[4] = sa[2 * (ks & 1)];
+                float(&sl)[4] = sa[2 * (ks & 1) + 1];
+                if (ks < 2) {
+                    mma16816_z(sh, kf, qh[ks][0], qh[ks][1]);
+                    mma16816_z(sl, kf, ql[ks][0], ql[ks][1]);
                 } else {
-                    mma16816(s[0], ah, bf[0], bf[1]);
-                    mma16816(s[1], ah, bf[2], bf[3]);
-                    mma16816(sl[0], al, bf[0], bf[1]);
-                    mma16816(sl[1], al, bf[2], bf[3]);
+                    mma16816(sh, kf, qh[ks][0], qh[ks][1]);
+                    mma16816(sl, kf, ql[ks][0], ql[ks][1]);
                 }
             }
+            // s4[0], s4[1]: key k0 + gr, heads 2c, 2c + 1; s4[2], s4[3]: key k0 + gr + 8
+            float s4[4];
+            const bool v0 = k0 + gr < n, v1 = k0 + gr + 8 < n;
 #pragma unroll
-            for (int t = 0; t < 2; t++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) s[t][e] += sl[t][e];
-            // online softmax for row gr over this warp's keys (4 lanes share a row)
-            float mx = -INFINITY;
-#pragma unroll
-            for (int t = 0; t < 2; t++)
-#pragma unroll
-                for (int e = 0; e < 2; e++) {
-                    const int key = k0 + 8 * t + 2 * c + e;
-                    s[t][e] = key < n ? s[t][e] * a.scale : -INFINITY;
-                    mx = fmaxf(mx, s[t][e]);
-                }
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            const float m_new = fmaxf(m_run, mx);  // finite: key k0 < n is in every row's range
-            const float corr = expf(m_run - m_new);  // 0 on this warp's first keys (m_run = -inf)
-            l_part *= corr;
-#pragma unroll
-            for (int t = 0; t < NTO; t++) {
-                o[t][0] *= corr;
-                o[t][1] *= corr;
+            for (int e = 0; e < 4; e++) {
+                const float t = (sa[0][e] + sa[1][e]) + (sa[2][e] + sa[3][e]);
+                s4[e] = (e < 2 ? v0 : v1) ? t * a.scale : -INFINITY;
             }
-            float p[2][2];
+            // online softmax per head over the warp's keys (the 8 lanes of a column hold them)
+            float mx0 = fmaxf(s4[0], s4[2]), mx1 = fmaxf(s4[1], s4[3]);
 #pragma unroll
-            for (int t = 0; t < 2; t++)
+            for (int off = 4; off < 32; off <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+            }
+            const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);  // finite: key k0 < n
+            const float c0 = expf(m_run[0] - mn0), c1 = expf(m_run[1] - mn1);    // 0 on the first keys
+            l_part[0] *= c0;
+            l_part[1] *= c1;
 #pragma unroll
-                for (int e = 0; e < 2; e++) {
-                    p[t][e] = expf(s[t][e] - m_new);
-                    l_part += p[t][e];
-                }
-            m_run = m_new;
-            // P.V: A = probabilities of keys k0..k0+15 (hi + lo), B = value rows (transposed fragments)
-            uint32_t ph[4], pl[4];
-            split_hilo(p[0][0], p[0][1], ph[0], pl[0]);
-            split_hilo(p[1][0], p[1][1], ph[2], pl[2]);
-            ph[1] = ph[3] = pl[1] = pl[3] = 0u;
+            for (int t = 0; t < MT; t++) {
+                o[t][0] *= c0;
+                o[t][2] *= c0;
+                o[t][1] *= c1;
+                o[t][3] *= c1;
+            }
+            const float p0 = expf(s4[0] - mn0), p1 = expf(s4[1] - mn1), p2 = expf(s4[2] - mn0),
+                        p3 = expf(s4[3] - mn1);
+            l_part[0] += p0 + p2;
+            l_part[1] += p1 + p3;
+            m_run[0] = mn0;
+            m_run[1] = mn1;
+            // P^T as the B fragment of P.V: lane (g, c) needs P[keys 2c, 2c+1, 2c+8, 2c+9][head g], held by lanes
+            // (2c, g / 2) and (2c + 1, g / 2) in their head-(g & 1) registers
+            const int sA = 8 * c + (gr >> 1), sB = sA + 4;
+            const bool odd = gr & 1;
+            const float e0 = __shfl_sync(0xffffffffu, p0, sA), q0 = __shfl_sync(0xffffffffu, p1, sA);
+            const float e1 = __shfl_sync(0xffffffffu, p0, sB), q1 = __shfl_sync(0xffffffffu, p1, sB);
+            const float e2 = __shfl_sync(0xffffffffu, p2, sA), q2 = __shfl_sync(0xffffffffu, p3, sA);
+            const float e3 = __shfl_sync(0xffffffffu, p2, sB), q3 = __shfl_sync(0xffffffffu, p3, sB);
+            uint32_t bh0, bl0, bh1, bl1;
+            split_hilo(odd ? q0 : e0, odd ? q1 : e1, bh0, bl0);
+            split_hilo(odd ? q2 : e2, odd ? q3 : e3, bh1, bl1);
+            // O^T[dim][head] += V^T[dim][key] . P^T[key][head]: A = value rows, transposed by ldmatrix
 #pragma unroll
-            for (int t2 = 0; t2 < NTO / 2; t2++) {
+            for (int t = 0; t < MT; t++) {
                 uint32_t vf[4];
-                ldsm_x4_trans(vf, tile_addr(b, 1, k0 + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * t2 + (lane >> 4)));
-                mma16816(o[2 * t2], ph, vf[0], vf[1]);
-                mma16816(o[2 * t2 + 1], ph, vf[2], vf[3]);
-                mma16816(o[2 * t2], pl, vf[0], vf[1]);
-                mma16816(o[2 * t2 + 1], pl, vf[2], vf[3]);
+                ldsm_x4_trans(vf, tile_addr(b, 1, k0 + (lane & 7) + 8 * (lane >> 4), 2 * t + ((lane >> 3) & 1)));
+                mma16816(o[t], vf, bh0, bh1);
+                mma16816(o[t], vf, bl0, bl1);
             }
         }
     }
 
-    // merge the four warps (the buffers are free once every warp is past its last chunk)
+    // merge the warps (the buffers are free once every warp is past its last chunk)
     __syncthreads();
-    l_part += __shfl_xor_sync(0xffffffffu, l_part, 1);
-    l_part += __shfl_xor_sync(0xffffffffu, l_part, 2);
-    float* wm = reinterpret_cast<float*>(smem);  // [4][8] max
-    float* wl = wm + 32;                         // [4][8] sum
-    float* wo = wl + 32;                         // [4][8][HD] acc
-    if (gr < G) {
-        if (c == 0) {
-            wm[warp * 8 + gr] = m_run;
-            wl[warp * 8 + gr] = l_part;
-        }
 #pragma unroll
-        for (int t = 0; t < NTO; t++)
-            *reinterpret_cast<float2*>(wo + (warp * 8 + gr) * HD + 8 * t + 2 * c) = make_float2(o[t][0], o[t][1]);
+    for (int off = 4; off < 32; off <<= 1) {
+        l_part[0] += __shfl_xor_sync(0xffffffffu, l_part[0], off);
+        l_part[1] += __shfl_xor_sync(0xffffffffu, l_part[1], off);
+    }
+    float* wm = reinterpret_cast<float*>(smem);  // [W][8] max
+    float* wl = wm + 8 * W;                      // [W][8] sum
+    float* wo = wl + 8 * W;                      // [W][8][HD] acc
+    static_assert((16 * W + 8 * W * HD) * 4 <= NBUF * BUF, "the warp merge fits the buffers");
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        const int h = 2 * c + e;
+        if (h < G) {
+            if (gr == 0) {
+                wm[warp * 8 + h] = m_run[e];
+                wl[warp * 8 + h] = l_part[e];
+            }
+#pragma unroll
+            for (int t = 0; t < MT; t++) {
+                wo[(warp * 8 + h) * HD + 16 * t + gr] = o[t][e];
+                wo[(warp * 8 + h) * HD + 16 * t + gr + 8] = o[t][2 + e];
+            }
+        }
     }
     __syncthreads();
     const bool split_mode = active > 1;
     const int64_t rec = HD + 2;
-    for (int i = tid; i < G * HD; i += kAttnThreads) {
+    for (int i = tid; i < G * HD; i += NT) {
         const int g = i / HD, d = i - g * HD;
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < 4; w++) M = fmaxf(M, wm[w * 8 + g]);
+        for (int w = 0; w < W; w++) M = fmaxf(M, wm[w * 8 + g]);
         float num = 0.0f, den = 0.0f;
 #pragma unroll
-        for (int w = 0; w < 4; w++) {
+        for (int w = 0; w < W; w++) {
             const float f = expf(wm[w * 8 + g] - M);  // 0 for a warp that saw no keys (max -inf)
             num += f * wo[(w * 8 + g) * HD + d];
             den += f * wl[w * 8 + g];
@@ -626,7 +654,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     __syncthreads();
     if (!last) return;
     __threadfence();
-    for (int i = tid; i < G * HD; i += kAttnThreads) {
+    for (int i = tid; i < G * HD; i += NT) {
         const int g = i / HD, d = i - g * HD;
         const float* base = a.part + (int64_t(r) * a.n_head + kvh * G + g) * geo.splits * rec;
         float M = -INFINITY;
@@ -641,10 +669,19 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     }
 }
 
-Geometry plan(int rows, int n_kv, int max_pos, int G, int hd) {
+Geometry plan(int rows, int n_kv, int max_pos, int G, int hd, bool tma) {
     const int L = max_pos + 1;
     const int sms = num_sms();
     Geometry g;
+    if (tma) {  // TMA tensor-core kernel: splits that fill the four CTAs per SM once, at least 128 keys each
+        g.chunk = kTmaChunk;
+        const int items = std::max(1, rows * n_kv);
+        const int want = std::max(1, std::min(kTcCtasTma * sms / items, L / 128));
+        g.span = std::max(g.chunk, ((L + want - 1) / want + g.chunk - 1) / g.chunk * g.chunk);
+        g.splits = (L + g.span - 1) / g.span;
+        g.smem = 0;
+        return g;
+    }
     g.chunk = chunk_for(hd);
     // about two CTAs per SM, at least two chunks of keys per split: a CTA's start-up and its share of the split
     // merge are fixed costs, so long splits win (measured at batch 64, position 512: 1 split per (row, KV head)
@@ -660,9 +697,13 @@ Geometry plan(int rows, int n_kv, int max_pos, int G, int hd) {
 
 }  // namespace
 
-void attention_scratch(int rows, int n_head, int n_kv, int hd, int max_pos, int64_t* part_floats, int64_t* tickets) {
-    const Geometry g = plan(rows, n_kv, max_pos, n_head / std::max(1, n_kv), hd);
-    *part_floats = g.splits > 1 ? int64_t(rows) * n_head * g.splits * (hd + 2) : 0;
+void attention_scratch(int rows, int n_head, int n_kv, int hd, int max_pos, int64_t* part_floats, int64_t* tickets,
+                       bool tma) {
+    const int G = n_head / std::max(1, n_kv);
+    int splits = plan(rows, n_kv, max_pos, G, hd, false).splits;
+    if (tma && (hd == 64 || hd == 128) && G <= 8)
+        splits = std::max(splits, plan(rows, n_kv, max_pos, G, hd, true).splits);
+    *part_floats = splits > 1 ? int64_t(rows) * n_head * splits * (hd + 2) : 0;
     *tickets = int64_t(rows) * n_kv;
 }
 
@@ -674,29 +715,30 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl) {
     if ((a.pos_stride % 8) || (a.head_stride % 8) || (a.slot_stride % 8) ||
         (reinterpret_cast<uintptr_t>(a.kc) & 15) || (reinterpret_cast<uintptr_t>(a.vc) & 15))
         return cudaErrorInvalidValue;
-    const Geometry g = plan(a.rows, a.n_kv, a.max_pos, a.n_head / a.n_kv, a.hd);
+    const int G = a.n_head / a.n_kv;
+    const bool tc_shape = (a.hd == 64 || a.hd == 128) && G <= 8;
+    // TMA staging when every (slot, KV head) holds its positions as consecutive hd-element rows of a known
+    // [cache_rows][hd] array, and both tensor maps encode
+    CUtensorMap tk{}, tv{};
+    static const bool tma_on = [] {
+        const char* e = std::getenv("NEKO_ATTN_TMA");
+        return !(e && e[0] == '0');
+    }();
+    const bool tma = tc_shape && tma_on && a.pos_stride == a.hd && a.cache_rows > 0 &&
+                     a.cache_rows < (int64_t(1) << 31) && a.slot_stride % a.hd == 0 && a.head_stride % a.hd == 0 &&
+                     encode_f16_2d_sw128(&tk, a.kc, uint64_t(a.hd), uint64_t(a.cache_rows), uint64_t(a.hd) * 2, 64,
+                                         kTmaChunk) &&
+                     encode_f16_2d_sw128(&tv, a.vc, uint64_t(a.hd), uint64_t(a.cache_rows), uint64_t(a.hd) * 2, 64,
+                                         kTmaChunk);
+    const Geometry g = plan(a.rows, a.n_kv, a.max_pos, G, a.hd, tma);
     if (g.splits > 1) {
         const int64_t need = int64_t(a.rows) * a.n_head * g.splits * (a.hd + 2);
         if (!a.part || !a.tickets || need > a.part_capacity || int64_t(a.rows) * a.n_kv > a.ticket_capacity)
             return cudaErrorInvalidValue;
     }
-    const int G = a.n_head / a.n_kv;
-    const bool tc = (a.hd == 64 || a.hd == 128) && G <= 8 && kTcChunk == g.chunk;
+    const bool tc = tc_shape && (tma || kTcChunk == g.chunk);
     if (a.out_hi && (!tc || !a.out_lo || a.out_hl_stride < int64_t(a.n_head) * a.hd)) return cudaErrorInvalidValue;
     if (tc) {  // tensor-core kernel
-        // TMA staging when every (slot, KV head) holds its positions as consecutive hd-element rows of a known
-        // [cache_rows][hd] array, and both tensor maps encode
-        CUtensorMap tk{}, tv{};
-        static const bool tma_on = [] {
-            const char* e = std::getenv("NEKO_ATTN_TMA");
-            return !(e && e[0] == '0');
-        }();
-        const bool tma = tma_on && a.pos_stride == a.hd && a.cache_rows > 0 && a.cache_rows < (int64_t(1) << 31) &&
-                         a.slot_stride % a.hd == 0 && a.head_stride % a.hd == 0 &&
-                         encode_f16_2d_sw128(&tk, a.kc, uint64_t(a.hd), uint64_t(a.cache_rows), uint64_t(a.hd) * 2,
-                                             64, kTcChunk) &&
-                         encode_f16_2d_sw128(&tv, a.vc, uint64_t(a.hd), uint64_t(a.cache_rows), uint64_t(a.hd) * 2,
-                                             64, kTcChunk);
         auto k = a.hd == 128 ? (tma ? attention_tc_kernel<128, true> : attention_tc_kernel<128, false>)
                              : (tma ? attention_tc_kernel<64, true> : attention_tc_kernel<64, false>);
         const int smem = a.hd == 128 ? (tma ? tc_attn_smem<128, true>() : tc_attn_smem<128, false>())
@@ -710,7 +752,8 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl) {
                 return e;
             if (dev < 8) attr_tc[a.hd == 128][tma][dev] = 1;
         }
-        return launch_ex(k, dim3(g.splits, a.n_kv, a.rows), dim3(kAttnThreads), size_t(smem), st, pdl, a, g, tk, tv);
+        return launch_ex(k, dim3(g.splits, a.n_kv, a.rows), dim3(32 * tc_warps(tma)), size_t(smem), st, pdl, a, g, tk,
+                         tv);
     }
     static unsigned attr_done = 0u;  // bit d: device d (< 32); function attributes are per device
     int dev = 0;

@@ -331,16 +331,16 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
     }
     namespace cg = cooperative_groups;
     const int ks = sp.ksplit;
-    if (ks > 1) cg::this_cluster().sync();  // every split's partial tile is in place
-    else __syncthreads();
-    // rows z, z + ks, ... of the tile: sums over the splits in order, then bias / GELU / accumulate or SiLU * up
+    // rows z, z + ks, ... of the tile: sums over the splits in order, then bias / GELU / accumulate or SiLU * up.
+    // Element i of this CTA (row z + ks * (i / OC), column i % OC) belongs to thread i % kTThreads; a thread takes
+    // kEpi elements per pass with every load of the pass issued first, and the global operands of the first pass
+    // (residual, bias, gamma, the row scales) are fetched before the cluster barrier.
     constexpr int OC = PAIR ? BN : BNW;  // output columns of the tile
-    const float* peer[kTMaxSplit];
-#pragma unroll
-    for (int zz = 0; zz < kTMaxSplit; zz++)
-        peer[zz] = zz < ks ? (ks > 1 ? cg::this_cluster().map_shared_rank(tile, zz) : tile) : tile;
+    constexpr int kEpi = 4;
     const int nrow = (mv - z + ks - 1) / ks;  // rows of this CTA
+    const int total = nrow * OC;
     static_assert(OC % 32 == 0, "a warp's 32 elements share a row");
+    static_assert(kTThreads % 32 == 0, "whole warps per pass");
     // RMSNorm as a row scale (the activations held x * gamma): rstd of each row from the producer's per-tile
     // sums of squares, summed in tile order (deterministic)
     __shared__ float rs[kTM];
@@ -352,52 +352,88 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
             for (int t = 0; t < a.in_ss_tiles; t++) s2 += double(a.in_ss[int64_t(t) * a.M + m0 + row]);
             rs[row] = float(1.0 / sqrt(s2 / a.K + double(a.eps)));
         }
-        __syncthreads();
     }
-    for (int i = tid; i < nrow * OC; i += kTThreads) {
-        const int row = z + ks * (i / OC), col = i - (i / OC) * OC;
-        const int m = m0 + row, n = n0 + col;
-        float v = 0.0f, u = 0.0f;
+    float g_old[kEpi], g_bias[kEpi], g_gam[kEpi];  // residual, bias and gamma of the pass's elements
+    auto fetch = [&](int base) {
 #pragma unroll
-        for (int zz = 0; zz < kTMaxSplit; zz++) {
-            if (zz >= ks) break;
-            v += peer[zz][row * TPF + col];
-            if (PAIR) u += peer[zz][row * TPF + BN + col];
-        }
-        if (a.in_ss) {
-            v *= rs[row];
-            u *= rs[row];
-        }
-        unsigned long long key = 0ull;
-        float sq = 0.0f;
-        if (n < a.rows) {
-            float* dst = a.y + int64_t(m) * a.y_stride + a.n_off + n;
-            float val = v;
-            if (PAIR) {
-                val = val / (1.0f + expf(-val)) * u;  // cpu::siluMul (cpu_ops.cpp:526-533)
-            } else {
-                if (a.flags & kBias) val += a.bias[n];
-                if (a.flags & kGelu) val = gelu(val);
-                if (a.flags & kAccumulate) val += *dst;
+        for (int e = 0; e < kEpi; e++) {
+            const int i = base + e * kTThreads;
+            g_old[e] = 0.0f;
+            g_bias[e] = 0.0f;
+            g_gam[e] = 1.0f;
+            const int row = z + ks * (i / OC), n = n0 + (i - (i / OC) * OC);
+            if (i < total && n < a.rows) {
+                if (!PAIR && (a.flags & kAccumulate)) g_old[e] = a.y[int64_t(m0 + row) * a.y_stride + a.n_off + n];
+                if (!PAIR && (a.flags & kBias)) g_bias[e] = a.bias[n];
+                if (a.out_hi && a.out_gamma) g_gam[e] = a.out_gamma[n];
             }
-            *dst = val;
-            key = argmax_key(val, n);
-            if (a.out_hi) {  // the next matmul's activations: val * gamma as f16 hi + lo
-                const float yv = a.out_gamma ? val * a.out_gamma[n] : val;
-                const __half h = __float2half_rn(yv);
-                a.out_hi[int64_t(m) * a.out_ld + n] = h;
-                a.out_lo[int64_t(m) * a.out_ld + n] = __float2half_rn(yv - __half2float(h));
-            }
-            sq = val * val;
         }
-        if (a.out_ss) {  // the warp's 32 columns of the row
-            sq = warp_sum(sq);
-            if (lane == 0) ssp[row][col >> 5] = sq;
-        }
-        if (a.argmax) {  // the warp's 32 columns of the row, then one shared atomic
+    };
+    fetch(tid);
+    if (ks > 1) cg::this_cluster().sync();  // every split's partial tile is in place
+    else __syncthreads();                   // (both also publish rs)
+    const float* peer[kTMaxSplit];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
-            if (lane == 0 && key) atomicMax(&keys[row], key);
+    for (int zz = 0; zz < kTMaxSplit; zz++)
+        peer[zz] = zz < ks ? (ks > 1 ? cg::this_cluster().map_shared_rank(tile, zz) : tile) : tile;
+    for (int base = tid; base < total; base += kEpi * kTThreads) {
+        if (base != tid) fetch(base);
+        float v[kEpi], u[kEpi];
+#pragma unroll
+        for (int e = 0; e < kEpi; e++) {
+            const int i = base + e * kTThreads;
+            v[e] = u[e] = 0.0f;
+            if (i < total) {
+                const int row = z + ks * (i / OC), col = i - (i / OC) * OC;
+#pragma unroll
+                for (int zz = 0; zz < kTMaxSplit; zz++) {
+                    if (zz >= ks) break;
+                    v[e] += peer[zz][row * TPF + col];
+                    if (PAIR) u[e] += peer[zz][row * TPF + BN + col];
+                }
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < kEpi; e++) {
+            const int i = base + e * kTThreads;
+            if (i >= total) break;  // whole warps: total and the pass stride are multiples of 32
+            const int row = z + ks * (i / OC), col = i - (i / OC) * OC;
+            const int m = m0 + row, n = n0 + col;
+            float vv = v[e], uu = u[e];
+            if (a.in_ss) {
+                vv *= rs[row];
+                uu *= rs[row];
+            }
+            unsigned long long key = 0ull;
+            float sq = 0.0f;
+            if (n < a.rows) {
+                float val = vv;
+                if (PAIR) {
+                    val = val / (1.0f + expf(-val)) * uu;  // cpu::siluMul (cpu_ops.cpp:526-533)
+                } else {
+                    if (a.flags & kBias) val += g_bias[e];
+                    if (a.flags & kGelu) val = gelu(val);
+                    if (a.flags & kAccumulate) val += g_old[e];
+                }
+                a.y[int64_t(m) * a.y_stride + a.n_off + n] = val;
+                key = argmax_key(val, n);
+                if (a.out_hi) {  // the next matmul's activations: val * gamma as f16 hi + lo
+                    const float yv = val * g_gam[e];
+                    const __half h = __float2half_rn(yv);
+                    a.out_hi[int64_t(m) * a.out_ld + n] = h;
+                    a.out_lo[int64_t(m) * a.out_ld + n] = __float2half_rn(yv - __half2float(h));
+                }
+                sq = val * val;
+            }
+            if (a.out_ss) {  // the warp's 32 columns of the row
+                sq = warp_sum(sq);
+                if (lane == 0) ssp[row][col >> 5] = sq;
+            }
+            if (a.argmax) {  // the warp's 32 columns of the row, then one shared atomic
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+                if (lane == 0 && key) atomicMax(&keys[row], key);
+            }
         }
     }
     if (a.out_ss) {  // one partial per (column tile, row), the column groups summed in order
@@ -448,7 +484,10 @@ TcPlan tc_plan(const GemvArgs& a, int64_t ws_floats) {
     // activations split once when at least 8 tiles share them
     p.x_floats = int64_t(a.M) * a.K;  // hi + lo halves
     p.presplit = (p.ntile >= 8 || a.norm != kNormNone || a.M >= 64) && ws_floats >= p.x_floats;
-    // K splits (one cluster per tile): about two CTAs per SM, each with at least 2 stages
+    // K splits (one cluster per tile): about two CTAs per SM, each with at least 2 stages. Rounding down (one
+    // wave on paper) measured slower for the SwiGLU matmul of a batch-64 step: 3 splits of 6 stages left 3
+    // clusters unplaced until others finished (the previous kernel's CTAs still hold SMs when it launches),
+    // 4 splits of 4 stages run in 1.3 waves of shorter CTAs.
     p.ksplit = 1;
     if (tiles < 2 * sms)
         p.ksplit = int(std::min<int64_t>({(2 * sms + tiles - 1) / tiles, int64_t(kTMaxSplit), std::max(1, nst / 2)}));

@@ -843,11 +843,11 @@ neko_model* neko_model_create(int device, const neko_model_config* cfg, char* er
         return bail(m, "workspace allocation failed");
     cudaMemset(m->d_keys, 0, nout * sizeof(unsigned long long));
     int64_t pf = 0, tk = 0;
-    attention_scratch(int(R), m->H, m->KV, m->hd, c.context - 1, &pf, &tk);
+    attention_scratch(int(R), m->H, m->KV, m->hd, c.context - 1, &pf, &tk, true);
     // fewer rows split more: size for the worst case over every row count 1..R
     for (int r = 1; r <= int(R); r++) {
         int64_t p2 = 0, t2 = 0;
-        attention_scratch(r, m->H, m->KV, m->hd, c.context - 1, &p2, &t2);
+        attention_scratch(r, m->H, m->KV, m->hd, c.context - 1, &p2, &t2, true);
         pf = std::max(pf, p2);
         tk = std::max(tk, t2);
     }

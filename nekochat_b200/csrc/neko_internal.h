@@ -193,9 +193,10 @@ struct AttnArgs {
     int64_t out_hl_stride = 0;
 };
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl);
-// Scratch the split-KV attention needs for rows x n_head heads up to position max_pos.
+// Scratch the split-KV attention needs for rows x n_head heads up to position max_pos (tma: the caller may pass
+// cache_rows, so the TMA variant's plan is covered too).
 void attention_scratch(int rows, int n_head, int n_kv, int hd, int max_pos, int64_t* part_floats,
-                       int64_t* tickets);
+                       int64_t* tickets, bool tma = false);
 
 // ------------------------------------------------------------------ decode-step kernel (k_decode.cu)
 // One whole decode step (embedding, every layer, final norm, LM head, greedy argmax) of 1..4 sequences in a
