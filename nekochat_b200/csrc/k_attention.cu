@@ -365,10 +365,18 @@ __host__ __device__ constexpr int tc_warps(bool tma) { return tma ? kTmaWarps : 
 
 template <int HD, bool TMA>
 constexpr int tc_attn_smem() {
-    // the buffers, then (TMA) their mbarriers, then two flags; TMA adds up to 1024 bytes to align the buffers
-    return TMA ? kTcBufsTma * 2 * (HD / 64) * kTmaBox + 64 + 1024 : kTcBufs * 2 * kTcChunk * (HD + 8) * 2 + 64;
+    // the buffers, then (TMA) their mbarriers, then two flags; TMA: the fused decode's q / k / v rows
+    // ([kMaxGroup + 2][HD] floats) and up to 1024 bytes to align the buffers
+    return TMA ? kTcBufsTma * 2 * (HD / 64) * kTmaBox + 64 + (kMaxGroup + 2) * HD * 4 + 1024
+               : kTcBufs * 2 * kTcChunk * (HD + 8) * 2 + 64;
 }
 static_assert(kTcCtasTma * (tc_attn_smem<128, true>() + 1024) <= 228 * 1024, "four TMA CTAs per SM");
+
+__device__ __forceinline__ double warp_sum_dbl(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -394,7 +402,6 @@ __global__ void __launch_bounds__(32 * tc_warps(TMA), TMA ? kTcCtasTma : 2)
     const int G = a.n_head / a.n_kv;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gr = lane >> 2, c = lane & 3;
     pdl_wait();  // q and the newest cache rows come from the previous kernels
-    pdl_trigger();
     const int pos = a.row_pos ? a.row_pos[r] : a.pos0 + r;
     const int slot = a.row_slot ? a.row_slot[r] : a.slot0;
     const int L = pos + 1;
@@ -468,6 +475,73 @@ __global__ void __launch_bounds__(32 * tc_warps(TMA), TMA ? kTcCtasTma : 2)
             cp_commit();
         }
     }
+    // Fused decode (qkv_post's arithmetic, k_ops.cu): the group's query heads, and in the split that holds
+    // position pos the new key and value, prepared into shared memory; the key / value rows also go to the caches
+    float* qs = reinterpret_cast<float*>(smem + NBUF * BUF + 64);  // [kMaxGroup + 2][HD]: q heads, k, v
+    const bool fused = TMA && a.fuse_post;
+    const bool owns_new = fused && j_end == L;
+    if (fused) {
+        // tasks: the G query heads, then (the split holding pos) the key and the value head; warp w takes tasks
+        // w, w + W, ... Lane l holds dims l + 32j (j < J), so each rotation pair (i, i + HD / 2) is in one lane
+        // (j and j + J / 2). Every load is issued before the arithmetic.
+        constexpr int J = HD / 32, TMAX = (kMaxGroup + 2 + W - 1) / W;
+        const float* qkv_row = a.q + int64_t(r) * a.q_stride;
+        const int tasks = G + (owns_new ? 2 : 0);
+        float x[TMAX][J], wq[J], wk[J], co[J / 2], sn[J / 2];
+#pragma unroll
+        for (int k = 0; k < TMAX; k++) {
+            const int t = warp + k * W;
+            if (t < tasks) {
+                const int col = t < G ? (kvh * G + t) * HD : (t == G ? a.k_off : a.v_off) + kvh * HD;
+#pragma unroll
+                for (int j = 0; j < J; j++) x[k][j] = qkv_row[col + lane + 32 * j];
+            }
+        }
+        const float* cs = a.post_cs + int64_t(pos) * HD;
+#pragma unroll
+        for (int j = 0; j < J; j++) {
+            wq[j] = a.post_wn[lane + 32 * j];
+            wk[j] = a.post_wn[HD + lane + 32 * j];
+        }
+#pragma unroll
+        for (int j = 0; j < J / 2; j++) {
+            co[j] = cs[2 * (lane + 32 * j)];
+            sn[j] = cs[2 * (lane + 32 * j) + 1];
+        }
+#pragma unroll
+        for (int k = 0; k < TMAX; k++) {
+            const int t = warp + k * W;
+            if (t >= tasks) break;  // warp-uniform
+            const bool isq = t < G, isk = t == G;
+            float* v = qs + (isq ? t : kMaxGroup + (isk ? 0 : 1)) * HD;
+            float y[J];
+#pragma unroll
+            for (int j = 0; j < J; j++) y[j] = x[k][j];
+            if (isq || isk) {  // per-head RMSNorm (sum of squares in double), then the NeoX rotation
+                double ss = 0.0;
+#pragma unroll
+                for (int j = 0; j < J; j++) ss += double(y[j]) * y[j];
+                const float sc = float(1.0 / sqrt(warp_sum_dbl(ss) / HD + double(a.post_eps)));
+#pragma unroll
+                for (int j = 0; j < J; j++) y[j] = __fmul_rn(__fmul_rn(y[j], sc), isq ? wq[j] : wk[j]);
+#pragma unroll
+                for (int j = 0; j < J / 2; j++) {
+                    const float x0 = y[j], x1 = y[j + J / 2];
+                    y[j] = __fsub_rn(__fmul_rn(x0, co[j]), __fmul_rn(x1, sn[j]));
+                    y[j + J / 2] = __fadd_rn(__fmul_rn(x0, sn[j]), __fmul_rn(x1, co[j]));
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < J; j++) v[lane + 32 * j] = y[j];
+            if (!isq) {  // the new cache row
+                uint16_t* dst = const_cast<uint16_t*>(isk ? a.kc : a.vc) + int64_t(slot) * a.slot_stride +
+                                int64_t(pos) * a.pos_stride + int64_t(kvh) * a.head_stride;
+#pragma unroll
+                for (int j = 0; j < J; j++) dst[lane + 32 * j] = __half_as_ushort(__float2half_rn(y[j]));
+            }
+        }
+        __syncthreads();
+    }
     // shared-memory address of (row, 8-half piece q) of the key (v = 0) or value (v = 1) tile in buffer b
     auto tile_addr = [&](int b, int v, int row, int q) -> const void* {
         if constexpr (TMA)
@@ -479,7 +553,7 @@ __global__ void __launch_bounds__(32 * tc_warps(TMA), TMA ? kTcCtasTma : 2)
     // query fragments (row gr = query head gr of the group; rows 8..15 and heads past G are zero)
     uint32_t qh[KS][2], ql[KS][2];
     {
-        const float* qrow = a.q + int64_t(r) * a.q_stride + int64_t(kvh * G + gr) * HD;
+        const float* qrow = fused ? qs + gr * HD : a.q + int64_t(r) * a.q_stride + int64_t(kvh * G + gr) * HD;
 #pragma unroll
         for (int ks = 0; ks < KS; ks++)
 #pragma unroll
@@ -509,7 +583,20 @@ __global__ void __launch_bounds__(32 * tc_warps(TMA), TMA ? kTcCtasTma : 2)
                         make_uint4(0u, 0u, 0u, 0u);
                 }
             }
-            __syncthreads();  // zeroed rows visible; every warp is done with chunk cc - 1's buffer
+            if (owns_new && pos - (j_begin + cc * CH) < CH) {  // the new key / value row, as the caches now hold
+                const int jr = pos - (j_begin + cc * CH);
+                for (int i = tid; i < 2 * (HD / 8); i += NT) {
+                    const int vs = i / (HD / 8), q = i - vs * (HD / 8);
+                    const float* src = qs + (kMaxGroup + vs) * HD + 8 * q;
+                    uint4 pk;
+                    pk.x = h2u(__floats2half2_rn(src[0], src[1]));
+                    pk.y = h2u(__floats2half2_rn(src[2], src[3]));
+                    pk.z = h2u(__floats2half2_rn(src[4], src[5]));
+                    pk.w = h2u(__floats2half2_rn(src[6], src[7]));
+                    *reinterpret_cast<uint4*>(const_cast<void*>(tile_addr(b, vs, jr, q))) = pk;
+                }
+            }
+            __syncthreads();  // zeroed and new rows visible; every warp is done with chunk cc - 1's buffer
             if (tid == 0 && tma_ok && cc + NBUF - 1 < nchunks) issue(cc + NBUF - 1);
         } else {
             cp_wait<NBUF - 2>();  // chunk cc landed (this thread's pieces)
@@ -590,6 +677,9 @@ __global__ void __launch_bounds__(32 * tc_warps(TMA), TMA ? kTcCtasTma : 2)
         }
     }
 
+    // The next kernel may launch now: earlier, its CTAs (waiting on this grid) would take the shared memory that
+    // lets four of these CTAs share an SM.
+    pdl_trigger();
     // merge the warps (the buffers are free once every warp is past its last chunk)
     __syncthreads();
 #pragma unroll
@@ -737,6 +827,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl) {
             return cudaErrorInvalidValue;
     }
     const bool tc = tc_shape && (tma || kTcChunk == g.chunk);
+    if (a.fuse_post && (!tma || !a.post_wn || !a.post_cs || a.k_off < 0 || a.v_off < 0)) return cudaErrorNotSupported;
     if (a.out_hi && (!tc || !a.out_lo || a.out_hl_stride < int64_t(a.n_head) * a.hd)) return cudaErrorInvalidValue;
     if (tc) {  // tensor-core kernel
         auto k = a.hd == 128 ? (tma ? attention_tc_kernel<128, true> : attention_tc_kernel<128, false>)

@@ -328,6 +328,9 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
     // matmul chaining (5..127 rows): A holds the next normed matmul's input (x * gamma, hi / lo), B the attention
     // output and the SwiGLU product; the RMSNorms are row scales from the per-tile sums of squares
     const bool chain = !staged && chain_ok(m, R);
+    // decode steps (decode and stage refuse a slot twice; a prompt runs one slot with nout = 1) of a chained
+    // Qwen3 step: the attention kernel does qkv_post's work itself
+    const bool fuse_post = chain && outrows_identity && nout == R;
     const int64_t BW = std::max<int64_t>(int64_t(H) * hd, m->F);
     __half *a_hi = m->ch_a, *a_lo = m->ch_a + int64_t(R) * C;
     __half *b_hi = m->ch_b, *b_lo = m->ch_b + int64_t(R) * BW;
@@ -396,7 +399,7 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
         q.v_off = (H + KV) * hd;
         q.pos_limit = m->cfg.context;
         q.write_back_k = staged ? 1 : 0;
-        CK(launch_qkv_post(q, st, pdl()), "qkv_post");
+        if (!fuse_post) CK(launch_qkv_post(q, st, pdl()), "qkv_post");
         if (m->qwen && dump(l, 3, m->qkv, m->QW)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
         AttnArgs a;
         a.q = m->qkv;
@@ -426,6 +429,14 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
             a.out_hi = b_hi;
             a.out_lo = b_lo;
             a.out_hl_stride = int64_t(H) * hd;
+        }
+        if (fuse_post) {  // QK-norm, rotation and the cache store inside the attention kernel
+            a.fuse_post = 1;
+            a.post_wn = L.qknorm;
+            a.post_cs = m->rope;
+            a.post_eps = eps;
+            a.k_off = H * hd;
+            a.v_off = (H + KV) * hd;
         }
         CK(launch_attention(a, st, pdl()), "attention");
         if (dump(l, m->qwen ? 4 : 3, m->att, H * hd)) return dumped == cudaSuccess ? NEKO_OK : fail(m, NEKO_ERR_CUDA, "dump");
@@ -567,7 +578,10 @@ int step_launches(neko_model* m, int R, int nout, bool gather, bool do_argmax, b
         // down and (after the first) qkv
         const MatShape q = mat_shapes(m)[0];
         const int nl = int(m->layers.size());
-        int n = 1 + gemm_tc_launches(q.fmt, q.rows, q.K, R, false, true) + 5 * nl + (nl - 1) + (gather ? 1 : 0);
+        // (qkv_post folded into attention on decode steps: every row its own slot, all rows output)
+        const bool fused = !gather && nout == R;
+        int n = 1 + gemm_tc_launches(q.fmt, q.rows, q.K, R, false, true) + (fused ? 4 : 5) * nl + (nl - 1) +
+                (gather ? 1 : 0);
         if (!gather && nout == R && chain_head_ok(m, R)) n += 1;
         else n += matmul_launches(mat_shapes(m).back(), nout, gemv_norm_fusable(m->embed.fmt, nout, m->C));
         return n + (do_argmax ? 1 : 0) + (advance && nout > 64 ? 1 : 0);

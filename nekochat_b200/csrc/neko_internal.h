@@ -191,6 +191,16 @@ struct AttnArgs {
     __half* out_hi = nullptr;
     __half* out_lo = nullptr;
     int64_t out_hl_stride = 0;
+    // Qwen3 decode steps (every row a different slot, one new position each; TMA variant only): q, k, v arrive
+    // raw in the qkv rows (q at q, k at q + k_off, v at q + v_off, per row q_stride) and the kernel applies the
+    // per-head RMSNorm (post_wn: q gains [hd], then k gains [hd]; post_eps) and the NeoX rotation (post_cs
+    // [pos][hd] cos / sin pairs) itself, stores the new key / value rows into the caches and uses them in place
+    // of the cache rows it reads (which qkv_post would otherwise have written before the launch)
+    int fuse_post = 0;
+    const float* post_wn = nullptr;
+    const float* post_cs = nullptr;
+    float post_eps = 0.0f;
+    int k_off = 0, v_off = 0;
 };
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl);
 // Scratch the split-KV attention needs for rows x n_head heads up to position max_pos (tma: the caller may pass
