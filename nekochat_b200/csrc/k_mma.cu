@@ -353,89 +353,202 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
             rs[row] = float(1.0 / sqrt(s2 / a.K + double(a.eps)));
         }
     }
-    float g_old[kEpi], g_bias[kEpi], g_gam[kEpi];  // residual, bias and gamma of the pass's elements
-    auto fetch = [&](int base) {
-#pragma unroll
-        for (int e = 0; e < kEpi; e++) {
-            const int i = base + e * kTThreads;
-            g_old[e] = 0.0f;
-            g_bias[e] = 0.0f;
-            g_gam[e] = 1.0f;
-            const int row = z + ks * (i / OC), n = n0 + (i - (i / OC) * OC);
-            if (i < total && n < a.rows) {
-                if (!PAIR && (a.flags & kAccumulate)) g_old[e] = a.y[int64_t(m0 + row) * a.y_stride + a.n_off + n];
-                if (!PAIR && (a.flags & kBias)) g_bias[e] = a.bias[n];
-                if (a.out_hi && a.out_gamma) g_gam[e] = a.out_gamma[n];
-            }
-        }
-    };
-    fetch(tid);
-    if (ks > 1) cg::this_cluster().sync();  // every split's partial tile is in place
-    else __syncthreads();                   // (both also publish rs)
+    // 16-byte path: 4 consecutive columns per thread (distributed-shared-memory, residual, bias and gamma loads
+    // of 16 bytes, f16 hi / lo stores of 8 bytes) when the output layout allows it; a row is OC / 4 lanes
+    const auto al = [](const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) & (n - 1)) == 0; };
+    const bool vec = a.y_stride % 4 == 0 && a.n_off % 4 == 0 && a.rows % 4 == 0 && al(a.y, 16) &&
+                     (!(a.flags & kBias) || al(a.bias, 16)) &&
+                     (!a.out_hi || (a.out_ld % 4 == 0 && al(a.out_hi, 8) && al(a.out_lo, 8) &&
+                                    (!a.out_gamma || al(a.out_gamma, 16))));
     const float* peer[kTMaxSplit];
+    if (vec) {
+        constexpr int G4 = OC / 4;  // lanes per row
+        static_assert(32 % G4 == 0, "a row's lanes lie in one warp");
+        const int total4 = nrow * G4;
+        float4 v_old = make_float4(0.f, 0.f, 0.f, 0.f), v_bias = v_old, v_gam = make_float4(1.f, 1.f, 1.f, 1.f);
+        auto fetch4 = [&](int i) {  // global operands of group i
+            v_old = make_float4(0.f, 0.f, 0.f, 0.f);
+            v_bias = v_old;
+            v_gam = make_float4(1.f, 1.f, 1.f, 1.f);
+            const int row = z + ks * (i / G4), n = n0 + 4 * (i - (i / G4) * G4);
+            if (i < total4 && n < a.rows) {
+                if (!PAIR && (a.flags & kAccumulate))
+                    v_old = *reinterpret_cast<const float4*>(a.y + int64_t(m0 + row) * a.y_stride + a.n_off + n);
+                if (!PAIR && (a.flags & kBias)) v_bias = *reinterpret_cast<const float4*>(a.bias + n);
+                if (a.out_hi && a.out_gamma) v_gam = *reinterpret_cast<const float4*>(a.out_gamma + n);
+            }
+        };
+        fetch4(tid);
+        if (ks > 1) cg::this_cluster().sync();  // every split's partial tile is in place
+        else __syncthreads();                   // (both also publish rs)
 #pragma unroll
-    for (int zz = 0; zz < kTMaxSplit; zz++)
-        peer[zz] = zz < ks ? (ks > 1 ? cg::this_cluster().map_shared_rank(tile, zz) : tile) : tile;
-    for (int base = tid; base < total; base += kEpi * kTThreads) {
-        if (base != tid) fetch(base);
-        float v[kEpi], u[kEpi];
-#pragma unroll
-        for (int e = 0; e < kEpi; e++) {
-            const int i = base + e * kTThreads;
-            v[e] = u[e] = 0.0f;
-            if (i < total) {
-                const int row = z + ks * (i / OC), col = i - (i / OC) * OC;
+        for (int zz = 0; zz < kTMaxSplit; zz++)
+            peer[zz] = zz < ks ? (ks > 1 ? cg::this_cluster().map_shared_rank(tile, zz) : tile) : tile;
+        // every lane of a warp runs the same passes (the row reductions shuffle across the warp)
+        for (int i = tid; i - lane < total4; i += kTThreads) {
+            if (i != tid) fetch4(i);
+            const bool live = i < total4;
+            const int row = z + ks * ((live ? i : 0) / G4), col = 4 * ((live ? i : 0) % G4);
+            float vv[4] = {0.f, 0.f, 0.f, 0.f}, uu[4] = {0.f, 0.f, 0.f, 0.f};
+            if (live) {
+                float4 pv[kTMaxSplit], pu[kTMaxSplit];
 #pragma unroll
                 for (int zz = 0; zz < kTMaxSplit; zz++) {
-                    if (zz >= ks) break;
-                    v[e] += peer[zz][row * TPF + col];
-                    if (PAIR) u[e] += peer[zz][row * TPF + BN + col];
+                    if (zz < ks) {
+                        pv[zz] = *reinterpret_cast<const float4*>(peer[zz] + row * TPF + col);
+                        if (PAIR) pu[zz] = *reinterpret_cast<const float4*>(peer[zz] + row * TPF + BN + col);
+                    }
+                }
+#pragma unroll
+                for (int zz = 0; zz < kTMaxSplit; zz++) {
+                    if (zz < ks) {
+                        vv[0] += pv[zz].x; vv[1] += pv[zz].y; vv[2] += pv[zz].z; vv[3] += pv[zz].w;
+                        if (PAIR) { uu[0] += pu[zz].x; uu[1] += pu[zz].y; uu[2] += pu[zz].z; uu[3] += pu[zz].w; }
+                    }
                 }
             }
-        }
-#pragma unroll
-        for (int e = 0; e < kEpi; e++) {
-            const int i = base + e * kTThreads;
-            if (i >= total) break;  // whole warps: total and the pass stride are multiples of 32
-            const int row = z + ks * (i / OC), col = i - (i / OC) * OC;
             const int m = m0 + row, n = n0 + col;
-            float vv = v[e], uu = u[e];
-            if (a.in_ss) {
-                vv *= rs[row];
-                uu *= rs[row];
-            }
+            const bool out = live && n < a.rows;
             unsigned long long key = 0ull;
             float sq = 0.0f;
-            if (n < a.rows) {
-                float val = vv;
-                if (PAIR) {
-                    val = val / (1.0f + expf(-val)) * uu;  // cpu::siluMul (cpu_ops.cpp:526-533)
-                } else {
-                    if (a.flags & kBias) val += g_bias[e];
-                    if (a.flags & kGelu) val = gelu(val);
-                    if (a.flags & kAccumulate) val += g_old[e];
-                }
-                a.y[int64_t(m) * a.y_stride + a.n_off + n] = val;
-                key = argmax_key(val, n);
-                if (a.out_hi) {  // the next matmul's activations: val * gamma as f16 hi + lo
-                    const float yv = val * g_gam[e];
-                    const __half h = __float2half_rn(yv);
-                    a.out_hi[int64_t(m) * a.out_ld + n] = h;
-                    a.out_lo[int64_t(m) * a.out_ld + n] = __float2half_rn(yv - __half2float(h));
-                }
-                sq = val * val;
-            }
-            if (a.out_ss) {  // the warp's 32 columns of the row
-                sq = warp_sum(sq);
-                if (lane == 0) ssp[row][col >> 5] = sq;
-            }
-            if (a.argmax) {  // the warp's 32 columns of the row, then one shared atomic
+            if (out) {
+                const float old[4] = {v_old.x, v_old.y, v_old.z, v_old.w};
+                const float bia[4] = {v_bias.x, v_bias.y, v_bias.z, v_bias.w};
+                const float gam[4] = {v_gam.x, v_gam.y, v_gam.z, v_gam.w};
+                float val[4];
+                __half h[4], l[4];
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
-                if (lane == 0 && key) atomicMax(&keys[row], key);
+                for (int e = 0; e < 4; e++) {
+                    float x = vv[e], u = uu[e];
+                    if (a.in_ss) {
+                        x *= rs[row];
+                        u *= rs[row];
+                    }
+                    if (PAIR) {
+                        x = x / (1.0f + expf(-x)) * u;  // cpu::siluMul (cpu_ops.cpp:526-533)
+                    } else {
+                        if (a.flags & kBias) x += bia[e];
+                        if (a.flags & kGelu) x = gelu(x);
+                        if (a.flags & kAccumulate) x += old[e];
+                    }
+                    val[e] = x;
+                    key = max(key, argmax_key(x, n + e));
+                    sq += x * x;
+                    const float yv = x * gam[e];
+                    h[e] = __float2half_rn(yv);
+                    l[e] = __float2half_rn(yv - __half2float(h[e]));
+                }
+                *reinterpret_cast<float4*>(a.y + int64_t(m) * a.y_stride + a.n_off + n) =
+                    make_float4(val[0], val[1], val[2], val[3]);
+                if (a.out_hi) {  // the next matmul's activations: val * gamma as f16 hi + lo
+                    *reinterpret_cast<uint2*>(a.out_hi + int64_t(m) * a.out_ld + n) =
+                        make_uint2(h2u(__halves2half2(h[0], h[1])), h2u(__halves2half2(h[2], h[3])));
+                    *reinterpret_cast<uint2*>(a.out_lo + int64_t(m) * a.out_ld + n) =
+                        make_uint2(h2u(__halves2half2(l[0], l[1])), h2u(__halves2half2(l[2], l[3])));
+                }
+            }
+            if (a.out_ss) {  // the row's G4 lanes, in a fixed order; the whole row lands in its first column group
+#pragma unroll
+                for (int o = G4 / 2; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+                if (live && (lane % G4) == 0) {
+                    ssp[row][0] = sq;
+#pragma unroll
+                    for (int hh = 1; hh < OC / 32; hh++) ssp[row][hh] = 0.0f;
+                }
+            }
+            if (a.argmax) {
+#pragma unroll
+                for (int o = G4 / 2; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+                if (live && (lane % G4) == 0 && key) atomicMax(&keys[row], key);
+            }
+        }
+    } else {
+        float g_old[kEpi], g_bias[kEpi], g_gam[kEpi];  // residual, bias and gamma of the pass's elements
+        auto fetch = [&](int base) {
+    #pragma unroll
+            for (int e = 0; e < kEpi; e++) {
+                const int i = base + e * kTThreads;
+                g_old[e] = 0.0f;
+                g_bias[e] = 0.0f;
+                g_gam[e] = 1.0f;
+                const int row = z + ks * (i / OC), n = n0 + (i - (i / OC) * OC);
+                if (i < total && n < a.rows) {
+                    if (!PAIR && (a.flags & kAccumulate)) g_old[e] = a.y[int64_t(m0 + row) * a.y_stride + a.n_off + n];
+                    if (!PAIR && (a.flags & kBias)) g_bias[e] = a.bias[n];
+                    if (a.out_hi && a.out_gamma) g_gam[e] = a.out_gamma[n];
+                }
+            }
+        };
+        fetch(tid);
+        if (ks > 1) cg::this_cluster().sync();  // every split's partial tile is in place
+        else __syncthreads();                   // (both also publish rs)
+    #pragma unroll
+        for (int zz = 0; zz < kTMaxSplit; zz++)
+            peer[zz] = zz < ks ? (ks > 1 ? cg::this_cluster().map_shared_rank(tile, zz) : tile) : tile;
+        for (int base = tid; base < total; base += kEpi * kTThreads) {
+            if (base != tid) fetch(base);
+            float v[kEpi], u[kEpi];
+    #pragma unroll
+            for (int e = 0; e < kEpi; e++) {
+                const int i = base + e * kTThreads;
+                v[e] = u[e] = 0.0f;
+                if (i < total) {
+                    const int row = z + ks * (i / OC), col = i - (i / OC) * OC;
+    #pragma unroll
+                    for (int zz = 0; zz < kTMaxSplit; zz++) {
+                        if (zz >= ks) break;
+                        v[e] += peer[zz][row * TPF + col];
+                        if (PAIR) u[e] += peer[zz][row * TPF + BN + col];
+                    }
+                }
+            }
+    #pragma unroll
+            for (int e = 0; e < kEpi; e++) {
+                const int i = base + e * kTThreads;
+                if (i >= total) break;  // whole warps: total and the pass stride are multiples of 32
+                const int row = z + ks * (i / OC), col = i - (i / OC) * OC;
+                const int m = m0 + row, n = n0 + col;
+                float vv = v[e], uu = u[e];
+                if (a.in_ss) {
+                    vv *= rs[row];
+                    uu *= rs[row];
+                }
+                unsigned long long key = 0ull;
+                float sq = 0.0f;
+                if (n < a.rows) {
+                    float val = vv;
+                    if (PAIR) {
+                        val = val / (1.0f + expf(-val)) * uu;  // cpu::siluMul (cpu_ops.cpp:526-533)
+                    } else {
+                        if (a.flags & kBias) val += g_bias[e];
+                        if (a.flags & kGelu) val = gelu(val);
+                        if (a.flags & kAccumulate) val += g_old[e];
+                    }
+                    a.y[int64_t(m) * a.y_stride + a.n_off + n] = val;
+                    key = argmax_key(val, n);
+                    if (a.out_hi) {  // the next matmul's activations: val * gamma as f16 hi + lo
+                        const float yv = val * g_gam[e];
+                        const __half h = __float2half_rn(yv);
+                        a.out_hi[int64_t(m) * a.out_ld + n] = h;
+                        a.out_lo[int64_t(m) * a.out_ld + n] = __float2half_rn(yv - __half2float(h));
+                    }
+                    sq = val * val;
+                }
+                if (a.out_ss) {  // the warp's 32 columns of the row
+                    sq = warp_sum(sq);
+                    if (lane == 0) ssp[row][col >> 5] = sq;
+                }
+                if (a.argmax) {  // the warp's 32 columns of the row, then one shared atomic
+    #pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+                    if (lane == 0 && key) atomicMax(&keys[row], key);
+                }
             }
         }
     }
+    // this CTA's reads of its peers' tiles are done: the cluster barrier's arrival now, its wait at exit (no CTA
+    // leaves while a peer may still read its tile)
+    if (ks > 1) cg::this_cluster().barrier_arrive();
     if (a.out_ss) {  // one partial per (column tile, row), the column groups summed in order
         __syncthreads();
         for (int r = tid; r < nrow; r += kTThreads) {
@@ -450,7 +563,7 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
         __syncthreads();
         if (tid < nrow && keys[z + ks * tid]) atomicMax(a.argmax + m0 + z + ks * tid, keys[z + ks * tid]);
     }
-    if (ks > 1) cg::this_cluster().sync();  // no CTA leaves while a peer may still read its tile
+    if (ks > 1) cg::this_cluster().barrier_wait();
 }
 
 using TcFn = void (*)(const GemvArgs, const TcSplit);
