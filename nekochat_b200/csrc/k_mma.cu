@@ -215,13 +215,15 @@ __global__ void __launch_bounds__(kTThreads, 2) tc_gemm_kernel(const GemvArgs a,
     }
     pdl_wait();
 #pragma unroll
-    for (int s = 0; s < kTStages - 1; s++)
+    for (int s = 0; s < kTStages - 1; s++) {  // one group per stage, so stage 0 waits for its own activations only
         if (s < nst) issue_x(s);
-    cp_commit();
+        cp_commit();
+    }
     for (int s = 0; s < nst; s++) {
-        // stage s landed (this thread's copies): everything of the prologue for s = 0; then one group per stage
-        if (s == 0) cp_wait<0>();
-        else cp_wait<kTStages - 2>();
+        // stage s landed (this thread's copies): groups are the prologue's weights of stages 0..2, their
+        // activations one group each, then one group per stage issued in the loop; all but the newest
+        // kTStages - 2 are complete
+        cp_wait<kTStages - 2>();
         __syncthreads();  // ... every thread's; and every warp is done with stage s - 1 (its buffer, which
                           // pre-split activations feed to the mma directly, and wh / xhi / xlo)
         if (s + kTStages - 1 < nst) {  // into the buffer of stage s - 1
