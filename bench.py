@@ -32,7 +32,10 @@ sys.path.insert(0, ROOT)
 
 # --model: the headline configuration or the FP4 one
 MODELS = {"qwen3-0.6b-fp8": ("qwen3-0.6b", 1, 512, "Qwen3-0.6B FP8 decode tok/s"),
-          "qwen3-1.7b-fp4": ("qwen3-1.7b", 2, 1024, "Qwen3-1.7B FP4 decode tok/s")}
+          "qwen3-1.7b-fp4": ("qwen3-1.7b", 2, 1024, "Qwen3-1.7B FP4 decode tok/s"),
+          # BASELINE's data-parallel config: 512 sequences of a 256-token prompt + 128 steps per GPU
+          "qwen3-4b-fp8": ("qwen3-4b", 1, 256, "Qwen3-4B FP8 decode tok/s"),
+          "qwen3-4b-fp4": ("qwen3-4b", 2, 256, "Qwen3-4B FP4 decode tok/s")}
 SHAPE, FMT, PROMPT, METRIC = MODELS["qwen3-0.6b-fp8"]
 FMT_NAME = {1: "FP8", 2: "FP4"}
 
@@ -44,9 +47,11 @@ def parse():
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--model", choices=sorted(MODELS), default="qwen3-0.6b-fp8",
-                   help="qwen3-0.6b-fp8 (512-token prompt, the headline) or qwen3-1.7b-fp4 (1024-token prompt)")
+                   help="qwen3-0.6b-fp8 (512-token prompt, the headline), qwen3-1.7b-fp4 (1024-token prompt), "
+                        "qwen3-4b-fp8 / qwen3-4b-fp4 (256-token prompt; BASELINE runs them at --batch 512 "
+                        "--steps 128)")
     p.add_argument("--prompt", type=int, default=None,
-                   help="prompt tokens (default: the model's, 512 / 1024; 32 with --profile)")
+                   help="prompt tokens (default: the model's, 512 / 1024 / 256; 32 with --profile)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -112,6 +117,28 @@ def peaks():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def tensor_peak():
+    """Dense bf16 TFLOP/s for a kernel timed inside a long step: MEASURED_PEAKS.json's sustained figure, else the
+    profiling recipe's fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops_sustained"]), "measured (bf16_tflops_sustained)"
+    except Exception:
+        return 1400.0, "fallback (sustained figure of the profiling recipe)"
+
+
+def matmul_macs_per_token(s):
+    """Multiply-adds of one token's matmuls (every layer matrix and the LM head; attention excluded)."""
+    C, L, V = s["embd"], s["layers"], s["vocab"]
+    if s["arch"] == "qwen3":
+        H, KV, hd, F = s["heads"], s["kv_heads"], s["head_dim"], s["ff"]
+        per = (H + 2 * KV) * hd * C + C * H * hd + 2 * F * C + C * F
+    else:
+        F = s["ff"]
+        per = 3 * C * C + C * C + 2 * F * C
+    return L * per + V * C
 
 
 def dist_setup(args):
@@ -301,7 +328,7 @@ def run_ours(args):
     cpu_on = (rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile
               and os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libneko_ref.so")))
     h16 = [] if cpu_on else None
-    m = nmodel.Model(s, FMT, context=context, max_seqs=B, max_rows=64, device=local)
+    m = nmodel.Model(s, FMT, context=context, max_seqs=B, max_rows=max(64, B), device=local)
     m.load_random_device(seed=0, host_copy=(lambda n, a: h16.append((n, a))) if cpu_on else None)
 
     # prefill every sequence (different prompts per rank and sequence)
@@ -368,6 +395,14 @@ def run_ours(args):
                 "peak_source": psrc, "traffic": None, "bytes_per_launch": bytes_step if single else None,
                 "launch_us": t / steps * 1e6 if single else None,
                 "timing": "CUDA events on the launch stream around the timed steps (graph replays back to back)"}
+        if B >= 128:  # layer matmuls and LM head on tcgen05 (128+ rows): the step is bound by the tensor pipe
+            tpk, tsrc = tensor_peak()
+            tfl = 2 * matmul_macs_per_token(s) * B / (t / steps) / 1e12
+            roof.update({"bound": "tensor", "kernel": "decode step as a kernel chain (umma_gemm_kernel dominant)",
+                         "achieved": round(tfl, 1), "peak": tpk, "unit": "TFLOP/s", "frac": round(tfl / tpk, 4),
+                         "peak_source": tsrc, "hbm_achieved_gbs": round(ach, 1),
+                         "flops_note": "2 x (layer + LM-head weights) x batch per step, useful FLOPs; the kernels "
+                                       "issue 3 f16 MMAs per product (hi / lo split operands)"})
         tf = os.path.join(ROOT, "profiles", "traffic.json")
         key = f"decode_{FMT_NAME[FMT].lower()}_b{B}" + ("" if SHAPE == "qwen3-0.6b" else "_" + SHAPE)
         if single and os.path.exists(tf):
@@ -391,7 +426,8 @@ def run_ours(args):
     if cpu_on:
         with tempfile.TemporaryDirectory() as tmp:
             try:
-                cpu = cpu_baseline(args, s, tmp, h16)
+                # bounded sample: fewer steps for the larger shapes (the scalar CPU path takes seconds per token)
+                cpu = cpu_baseline(args, s, tmp, h16, steps=8 if s["embd"] <= 1024 else 3)
             except Exception as e:  # the baseline is reported, never required
                 cpu = {"value": None, "unit": "tok/s", "error": str(e)[:200]}
     m.close()

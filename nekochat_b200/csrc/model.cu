@@ -71,6 +71,17 @@ __global__ void argmax_finalize_kernel(unsigned long long* keys, int* argmax, in
     }
 }
 
+// Device-side greedy loop past 64 sequences (argmax by its own kernel): the token becomes the next input token
+// with position + 1, as argmax_finalize_kernel does.
+__global__ void advance_kernel(const int* argmax, int* tokens, int* pos, int n, int context) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    pdl_wait();
+    if (i >= n) return;
+    tokens[i] = argmax[i];
+    if (pos[i] + 1 < context) pos[i] += 1;
+    else set_device_error(kErrBadIndex);
+}
+
 __global__ void gather_rows_kernel(const float* x, int C, const int* rows, int n, float* out) {
     pdl_wait();
     const int r = blockIdx.y;
@@ -513,7 +524,9 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
                      m->d_argmax, m->d_tokens, m->d_pos, nout, m->cfg.context, advance ? 1 : 0),
            "argmax finalize");
     else if (advance)
-        return fail(m, NEKO_ERR_UNSUPPORTED, "device greedy loop supports at most 64 sequences per step");
+        CK(launch_ex(advance_kernel, dim3((nout + 127) / 128), dim3(128), 0, st, pdl(), m->d_argmax, m->d_tokens,
+                     m->d_pos, nout, m->cfg.context),
+           "advance");
     return NEKO_OK;
 }
 

@@ -160,16 +160,45 @@ def test_device_tensor_on_another_device_is_refused():
 
 def test_step_launch_count_matches_captured_graph():
     """neko_model_step_launches (the bench's gpu_launches) == the kernel nodes of the captured step graph, on the
-    single-kernel step (1, 4 sequences) and the kernel chain with chained matmuls (8, 40, 64 sequences)."""
+    single-kernel step (1, 4 sequences), the kernel chain with chained matmuls (8, 40, 64 sequences; 72 with the
+    argmax and the token advance as kernels of their own) and without (130 rows: tcgen05 matmuls)."""
     s = workload.shape("qwen3-tiny")
-    m = nmodel.build("qwen3-tiny", FP8, context=64, max_seqs=64, max_rows=64, seed=1)
+    m = nmodel.build("qwen3-tiny", FP8, context=64, max_seqs=130, max_rows=130, seed=1)
     rng = np.random.default_rng(2)
-    for n in (1, 4, 8, 40, 64):
+    for n in (1, 4, 8, 40, 64, 72, 130):
         slots = np.arange(n, dtype=np.int32)
         m.stage(slots, rng.integers(0, s["vocab"], n).astype(np.int32), np.full(n, 5, np.int32))
         m.step(n, 5)
         assert m.graph_kernels() == m.step_launches(n), n
     m.close()
+
+
+def test_device_greedy_loop_past_64_sequences():
+    """stage + step for 72 sequences (greedy argmax and the token / position advance as separate kernels past
+    64 output rows) == decode with host feedback."""
+    s = workload.shape("qwen3-tiny")
+    tensors = list(workload.weights(s, seed=8, perturb=True))
+    n, steps = 72, 4
+    a = nmodel.Model(s, FP8, context=48, max_seqs=n, max_rows=n).load(tensors)
+    b = nmodel.Model(s, FP8, context=48, max_seqs=n, max_rows=n).load(tensors)
+    toks = []
+    for i in range(n):
+        p = workload.prompt(s, 8, seed=40 + i)
+        toks.append(int(np.argmax(a.prefill(p, i))))
+        b.prefill(p, i)
+    slots = np.arange(n, dtype=np.int32)
+    pos = np.full(n, 8, np.int32)
+    a.stage(slots, toks, pos)
+    for k in range(steps):
+        a.step(n, 8 + k)
+    dev_tokens, dev_pos = a.tokens(n)
+    host = np.array(toks, np.int32)
+    for k in range(steps):
+        _, host = b.decode(slots, host, pos + k, want_logits=False)
+    assert np.array_equal(dev_tokens, host)
+    assert np.array_equal(dev_pos, pos + steps)
+    a.close()
+    b.close()
 
 
 @pytest.mark.parametrize("n", [40, 100])
