@@ -653,6 +653,8 @@ void gemm_tc_scratch(int fmt, int rows, int K, int M, bool pair, bool norm, int6
     if (!gemm_tc_fits(a)) return;
     const TcPlan p = tc_plan(a, int64_t(1) << 40);
     *floats = p.presplit ? p.x_floats : 0;
+    // 256+ rows: room for the dequantised hi / lo weight rows after the activations (SwiGLU: gate and up rows)
+    if (p.presplit && M >= kGemmDqMinRows) *floats += int64_t(pair ? 2 * rows : rows) * K;
 }
 
 // The tensor-core kernel takes 5+ activation rows of FP8 / FP4 weights, K a multiple of 64; cudaErrorNotSupported
@@ -690,8 +692,11 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl) {
                           const_cast<__half*>(sp.xh), const_cast<__half*>(sp.xl));
         }
         if (e != cudaSuccess) return e;
-        // 128+ rows: the tcgen05 kernel (TMEM accumulators) on the split activations
+        // 256+ rows: weights dequantised once, then the TMA-fed tcgen05 GEMM; 128+ rows: the tcgen05 kernel that
+        // converts the codes per CTA (both TMEM accumulators, on the split activations)
         if (!chained) {
+            e = launch_gemm_umma_dq(a, sp.xh, sp.xl, st, true);
+            if (e != cudaErrorNotSupported) return e;
             e = launch_gemm_umma(a, sp.xh, sp.xl, st, true);
             if (e != cudaErrorNotSupported) return e;
         }

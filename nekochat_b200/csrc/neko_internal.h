@@ -115,6 +115,10 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl);
 // The tcgen05 kernel (k_umma.cu) for 128+ rows on activations split into f16 hi / lo ([M][K] each);
 // cudaErrorNotSupported when the call does not fit.
 cudaError_t launch_gemm_umma(const GemvArgs& a, const __half* xh, const __half* xl, cudaStream_t st, bool pdl);
+// 256+ rows: the weights dequantised once into hi / lo f16 rows in a.ws (after M x K floats of split activations;
+// needs (M + matrix rows) x K floats), then a TMA-fed tcgen05 GEMM. cudaErrorNotSupported when it does not apply.
+cudaError_t launch_gemm_umma_dq(const GemvArgs& a, const __half* xh, const __half* xl, cudaStream_t st, bool pdl);
+constexpr int kGemmDqMinRows = 256;
 // Workspace (floats, tickets) with which launch_gemm_tc splits this matmul's activations once (norm: with the
 // norm prologue applied); 0, 0 when it needs none or the tensor-core path does not apply.
 void gemm_tc_scratch(int fmt, int rows, int K, int M, bool pair, bool norm, int64_t* floats, int64_t* tickets);

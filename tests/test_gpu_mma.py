@@ -175,3 +175,63 @@ def test_umma_deterministic(torch, R):
     first = ops.matmul(FP8, xt, qt, K).cpu().numpy()
     for _ in range(3):
         assert np.array_equal(ops.matmul(FP8, xt, qt, K).cpu().numpy(), first)
+
+
+# ---------------------------------------------------------------------- dequantise, then tcgen05 GEMM (256+ rows)
+@pytest.mark.parametrize("fmt", [FP8, FP4])
+@pytest.mark.parametrize("M,K,N", [(256, 1024, 3072), (300, 2048, 700), (512, 3072, 1024), (384, 64, 200)])
+def test_dq_gemm_shapes(torch, R, fmt, M, K, N):
+    """256+ rows: the weights dequantised once into hi / lo f16 rows, then the TMA-fed tcgen05 GEMM; partial row
+    and column tiles (zero-filled tensor copies past the matrices), K split over clusters, a single K stage."""
+    from nekochat_b200 import ops
+    rng = np.random.default_rng(M * 5 + K + N + fmt)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    q = R.quantize(fmt, w)
+    y = ops.matmul(fmt, cu(torch, x), cu(torch, q), K)
+    torch.cuda.synchronize()
+    close(y.cpu().numpy(), R.matmul(fmt, x, q, K))
+
+
+@pytest.mark.parametrize("fmt", [FP8, FP4])
+@pytest.mark.parametrize("flags", [GELU, ACCUMULATE])
+def test_dq_gemm_epilogues(torch, R, fmt, flags):
+    from nekochat_b200 import ops
+    rng = np.random.default_rng(flags + 30 * fmt)
+    M, K, N, ys, off = 320, 1024, 200, 260, 37
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    y0 = rng.standard_normal((M, ys)).astype(np.float32)
+    q = R.quantize(fmt, w)
+    y = cu(torch, y0.copy())
+    ops.matmul(fmt, cu(torch, x), cu(torch, q), K, bias=cu(torch, bias), y=y, y_stride=ys, n_off=off, flags=flags)
+    torch.cuda.synchronize()
+    want = y0.copy()
+    R.matmul(fmt, x, q, K, bias, want, ys, flags, off)
+    close(y.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("fmt", [FP8, FP4])
+def test_dq_gemm_swiglu_pair(torch, R, fmt):
+    from nekochat_b200 import ops
+    rng = np.random.default_rng(50 + fmt)
+    M, K, F = 300, 1024, 320
+    w = (rng.standard_normal((2 * F, K)) * 0.05).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    q = R.quantize(fmt, w)
+    y = ops.matmul_fused(fmt, cu(torch, x), cu(torch, q), K, F, 0, None, None, 1e-6, swiglu=True)
+    torch.cuda.synchronize()
+    close(y.cpu().numpy(), R.silu_mul(R.matmul(fmt, x, q, K), F))
+
+
+def test_dq_gemm_deterministic(torch, R):
+    """Repeated calls (cluster split-K summed in split order) give bit-identical results."""
+    from nekochat_b200 import ops
+    rng = np.random.default_rng(19)
+    M, K, N = 512, 3072, 1024
+    xt = cu(torch, rng.standard_normal((M, K)).astype(np.float32))
+    qt = cu(torch, R.quantize(FP8, (rng.standard_normal((N, K)) * 0.02).astype(np.float32)))
+    first = ops.matmul(FP8, xt, qt, K).cpu().numpy()
+    for _ in range(2):
+        assert np.array_equal(ops.matmul(FP8, xt, qt, K).cpu().numpy(), first)
