@@ -534,16 +534,32 @@ int neko_op_matmul_fused(int format, const float* x, int T, int K, const uint8_t
     NEKO_OP_RETURN(launch_gemv_op(a, static_cast<cudaStream_t>(stream), (flags & NEKO_PDL) != 0));
 }
 
+namespace {
+// RMSNorm / softmax over wide rows, fewer than the SMs: the split-row kernels with their partials in pool scratch.
+cudaError_t wide_rows_op(const float* x, float* y, const float* gamma, int rows, int C, float eps, bool softmax,
+                         int S, cudaStream_t st) {
+    void* part = nullptr;
+    if (cudaError_t e = scratch_alloc(&part, size_t(rows) * S * 2 * sizeof(double), st); e != cudaSuccess) return e;
+    const cudaError_t e = launch_wide_rows(x, C, y, C, gamma, rows, C, eps, softmax, static_cast<double*>(part), S, st);
+    cudaFreeAsync(part, st);
+    return e;
+}
+}  // namespace
+
 int neko_op_norm(const float* x, float* y, const float* gamma, const float* beta, int rows, int C, float eps,
                  void* stream) {
     if (!x || !y || !gamma || rows < 0 || C <= 0) return set_err(nullptr, NEKO_ERR_ARG, "norm args");
-    NEKO_OP_RETURN(launch_norm(x, C, y, C, gamma, beta, rows, C, eps, beta == nullptr,
-                               static_cast<cudaStream_t>(stream), false));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (const int S = beta == nullptr ? wide_row_chunks(rows, C) : 0; S > 0)
+        NEKO_OP_RETURN(wide_rows_op(x, y, gamma, rows, C, eps, false, S, st));
+    NEKO_OP_RETURN(launch_norm(x, C, y, C, gamma, beta, rows, C, eps, beta == nullptr, st, false));
 }
 
 int neko_op_softmax(const float* x, float* y, int rows, int C, void* stream) {
     if (!x || !y || rows < 0 || C <= 0) return set_err(nullptr, NEKO_ERR_ARG, "softmax args");
-    NEKO_OP_RETURN(launch_softmax(x, y, rows, C, static_cast<cudaStream_t>(stream)));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (const int S = wide_row_chunks(rows, C); S > 0) NEKO_OP_RETURN(wide_rows_op(x, y, nullptr, rows, C, 0.0f, true, S, st));
+    NEKO_OP_RETURN(launch_softmax(x, y, rows, C, st));
 }
 
 int neko_op_argmax(const float* x, int rows, int C, int* out, void* stream) {

@@ -111,6 +111,95 @@ __global__ void __launch_bounds__(kNormThreads) softmax_kernel(const float* __re
     for (int c = threadIdx.x; c < C; c += blockDim.x) yr[c] = (cached ? row[c] : expf(xr[c] - mx)) * inv;
 }
 
+// Wide rows, few of them (the LM-head width at 1..sms rows): one CTA per row leaves most SMs idle, so each row is
+// split into S chunks over CTAs across the GPU, in two kernels: per-chunk partial statistics (RMS: the sum of
+// squares in double; softmax: the chunk's max and float sum of exp(x - max)), then every chunk CTA combines its
+// row's partials in chunk order (deterministic) and writes its outputs. The second pass re-reads x from L2.
+__global__ void __launch_bounds__(kNormThreads) wide_partial_kernel(const float* __restrict__ x, int64_t xs, int C,
+                                                                    int chunk, int softmax, double* __restrict__ part) {
+    __shared__ double red[kNormThreads / 32];
+    __shared__ float redf[kNormThreads / 32];
+    pdl_wait();
+    const int j = blockIdx.x, r = blockIdx.y, S = gridDim.x;
+    const float* xr = x + int64_t(r) * xs;
+    const int c0 = j * chunk, c1 = min(C, c0 + chunk);
+    double* pr = part + (int64_t(r) * S + j) * 2;
+    if (!softmax) {
+        double s2 = 0.0;
+#pragma unroll 4
+        for (int c = c0 + threadIdx.x; c < c1; c += kNormThreads) {
+            const float v = xr[c];
+            s2 += double(v) * v;
+        }
+        s2 = block_sum_d(s2, red);
+        if (threadIdx.x == 0) pr[0] = s2;
+    } else {
+        float mx = -INFINITY;
+#pragma unroll 4
+        for (int c = c0 + threadIdx.x; c < c1; c += kNormThreads) mx = fmaxf(mx, xr[c]);
+        mx = warp_max(mx);
+        const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+        if (l == 0) redf[w] = mx;
+        __syncthreads();
+        mx = l < kNormThreads / 32 ? redf[l] : -INFINITY;
+        mx = warp_max(mx);
+        float sum = 0.0f;
+#pragma unroll 4
+        for (int c = c0 + threadIdx.x; c < c1; c += kNormThreads) sum += expf(xr[c] - mx);
+        sum = block_sum<kNormThreads>(sum, redf);
+        if (threadIdx.x == 0) {
+            pr[0] = mx;
+            pr[1] = sum;
+        }
+    }
+    pdl_trigger();
+}
+
+__global__ void __launch_bounds__(kNormThreads) wide_apply_kernel(const float* __restrict__ x, int64_t xs,
+                                                                  float* __restrict__ y, int64_t ys,
+                                                                  const float* __restrict__ g, int C, int chunk,
+                                                                  int softmax, float eps,
+                                                                  const double* __restrict__ part) {
+    __shared__ float stat[2];
+    pdl_wait();
+    const int j = blockIdx.x, r = blockIdx.y, S = gridDim.x;
+    const double* pr = part + int64_t(r) * S * 2;
+    if (threadIdx.x < 32) {  // the row statistic from its S partials: lanes take chunks l, l + 32, ... in order
+        const int l = threadIdx.x;
+        if (!softmax) {
+            double t = 0.0;
+            for (int k = l; k < S; k += 32) t += pr[2 * k];
+            t = warp_sum_d(t);
+            if (l == 0) stat[0] = float(1.0 / sqrt(t / C + double(eps)));
+        } else {
+            float M = -INFINITY;
+            for (int k = l; k < S; k += 32) M = fmaxf(M, float(pr[2 * k]));
+            M = warp_max(M);
+            float t = 0.0f;
+            for (int k = l; k < S; k += 32) t += float(pr[2 * k + 1]) * expf(float(pr[2 * k]) - M);
+            t = warp_sum(t);
+            if (l == 0) {
+                stat[0] = M;
+                stat[1] = 1.0f / t;
+            }
+        }
+    }
+    __syncthreads();
+    pdl_trigger();
+    const float* xr = x + int64_t(r) * xs;
+    float* yr = y + int64_t(r) * ys;
+    const int c0 = j * chunk, c1 = min(C, c0 + chunk);
+    if (!softmax) {
+        const float rs = stat[0];
+#pragma unroll 4
+        for (int c = c0 + threadIdx.x; c < c1; c += kNormThreads) yr[c] = __fmul_rn(__fmul_rn(xr[c], rs), g[c]);
+    } else {
+        const float M = stat[0], inv = stat[1];
+#pragma unroll 4
+        for (int c = c0 + threadIdx.x; c < c1; c += kNormThreads) yr[c] = expf(xr[c] - M) * inv;
+    }
+}
+
 // First index of the maximum of each row (std::max_element: strict '<' keeps the earliest).
 __global__ void __launch_bounds__(kNormThreads) argmax_kernel(const float* __restrict__ x, int64_t stride, int C,
                                                               int* __restrict__ out) {
@@ -288,6 +377,25 @@ cudaError_t launch_norm(const float* x, int64_t x_stride, float* y, int64_t y_st
     if (cudaError_t e = row_cache_attr(norm_kernel); e != cudaSuccess) return e;
     return launch_ex(norm_kernel, dim3(rows), dim3(kNormThreads), smem, st, pdl, x, x_stride, y, y_stride, gamma, beta,
                      C, eps, rms ? 1 : 0);
+}
+
+int wide_row_chunks(int rows, int C) {
+    if (rows <= 0 || C < kWideRowMinC || rows >= num_sms()) return 0;
+    // about two CTAs per SM over the rows' chunks, each chunk at least 512 columns
+    return std::max(1, std::min((2 * num_sms() + rows - 1) / rows, C / 512));
+}
+
+cudaError_t launch_wide_rows(const float* x, int64_t x_stride, float* y, int64_t y_stride, const float* gamma,
+                             int rows, int C, float eps, bool softmax, double* part, int S, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    if (S <= 0 || !part) return cudaErrorInvalidValue;
+    const int chunk = (C + S - 1) / S;
+    if (cudaError_t e = launch_ex(wide_partial_kernel, dim3(S, rows), dim3(kNormThreads), 0, st, false, x, x_stride,
+                                  C, chunk, softmax ? 1 : 0, part);
+        e != cudaSuccess)
+        return e;
+    return launch_ex(wide_apply_kernel, dim3(S, rows), dim3(kNormThreads), 0, st, true, x, x_stride, y, y_stride,
+                     gamma, C, chunk, softmax ? 1 : 0, eps, static_cast<const double*>(part));
 }
 
 cudaError_t launch_softmax(const float* x, float* y, int rows, int C, cudaStream_t st) {

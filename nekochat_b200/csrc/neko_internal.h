@@ -131,6 +131,12 @@ int gemv_launch_count();  // number of launches launch_gemv issues per call (1)
 cudaError_t launch_norm(const float* x, int64_t x_stride, float* y, int64_t y_stride, const float* gamma,
                         const float* beta, int rows, int C, float eps, bool rms, cudaStream_t st, bool pdl);
 cudaError_t launch_softmax(const float* x, float* y, int rows, int C, cudaStream_t st);
+// Wide rows, fewer than the SMs (RMSNorm or softmax): chunks per row for launch_wide_rows, 0 when one CTA per row
+// is the better plan. launch_wide_rows needs rows x S x 2 doubles of scratch in part.
+constexpr int kWideRowMinC = 16384;
+int wide_row_chunks(int rows, int C);
+cudaError_t launch_wide_rows(const float* x, int64_t x_stride, float* y, int64_t y_stride, const float* gamma,
+                             int rows, int C, float eps, bool softmax, double* part, int S, cudaStream_t st);
 cudaError_t launch_argmax(const float* x, int64_t stride, int rows, int C, int* out, cudaStream_t st, bool pdl);
 cudaError_t launch_silu_mul(const float* h, float* g, int T, int I, cudaStream_t st);
 // Embedding gather (embed.comp semantics + the native runner's f32 position table):

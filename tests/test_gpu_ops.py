@@ -94,7 +94,10 @@ def test_matmul_many_rows(torch, R, M):
     close(run_matmul(torch, FP8, x, q, K), R.matmul(FP8, x, q, K))
 
 
-@pytest.mark.parametrize("C,rows", [(96, 3), (1024, 7), (2560, 2), (151936, 2)])
+# (151936, 1..2) and (20000, 100): wide rows, fewer than the SMs, split over CTAs (RMSNorm; LayerNorm keeps one
+# CTA per row); (16384, 150): one CTA per row
+@pytest.mark.parametrize("C,rows", [(96, 3), (1024, 7), (2560, 2), (151936, 2), (151936, 1), (20000, 100),
+                                    (16384, 150)])
 def test_norms(torch, R, C, rows):
     from nekochat_b200 import ops
     rng = np.random.default_rng(C)
@@ -106,7 +109,8 @@ def test_norms(torch, R, C, rows):
     close(ops.norm(tx, tg, tb, 1e-5).cpu().numpy(), R.layer_norm(x, g, b, 1e-5), 1e-5)
 
 
-@pytest.mark.parametrize("C,rows", [(1024, 5), (2048, 3), (2560, 1), (151936, 2), (1000, 4)])
+@pytest.mark.parametrize("C,rows", [(1024, 5), (2048, 3), (2560, 1), (151936, 2), (1000, 4), (151936, 1),
+                                    (20000, 100), (16384, 150)])
 def test_softmax_argmax(torch, R, C, rows):
     from nekochat_b200 import ops
     rng = np.random.default_rng(C + 1)
