@@ -1,6 +1,8 @@
 // Elementwise and reduction kernels around the matmuls: LayerNorm/RMSNorm, row softmax, argmax, embedding
 // gather, Qwen3 QK-norm + RoPE + KV-cache store, KV store, SwiGLU. All memory-bound; each reads its inputs
 // once where the row fits on chip and keeps fp32 (fp64 for the norm sums, like cpu_ops.cpp) arithmetic.
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <cfloat>
 
@@ -167,6 +169,124 @@ __global__ void __launch_bounds__(kNormThreads) rows_warp_kernel(const float* __
         yr[c] = kind == 0 ? __fmul_rn(__fmul_rn(v, rs), g[c])
                           : __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, m), rs), g[c]), b[c]);
     }
+}
+
+// Rows wider than the row cache, sms or more of them: a thread-block cluster of CL CTAs per row, each caching its
+// chunk (at most kRowCacheFloats) in shared memory; the chunks' partial statistics go through distributed shared
+// memory and every CTA sums them in rank order (deterministic), so x is read from memory once. kind: 0 RMSNorm,
+// 1 LayerNorm (mean, then the centred sum of squares), 2 softmax (max, then the float sum of exp(x - max)).
+__device__ __forceinline__ float block_max_f(float v, float* red) {
+    v = warp_max(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    v = l < kNormThreads / 32 ? red[l] : -INFINITY;
+    return warp_max(v);
+}
+
+__global__ void __launch_bounds__(kNormThreads) rows_cluster_kernel(const float* __restrict__ x, int64_t xs,
+                                                                    float* __restrict__ y, int64_t ys,
+                                                                    const float* __restrict__ g,
+                                                                    const float* __restrict__ b, int C, int chunk,
+                                                                    float eps, int kind, int bulk) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(16) float cache[];
+    __shared__ double red[kNormThreads / 32];
+    __shared__ float redf[kNormThreads / 32];
+    __shared__ double xch[2];  // this CTA's partial of exchange round 0 / 1
+    __shared__ __align__(8) uint64_t bar;
+    pdl_wait();
+    cg::cluster_group cl = cg::this_cluster();
+    const int CL = int(cl.num_blocks()), rank = int(cl.block_rank()), r = blockIdx.y;
+    const float* xr = x + int64_t(r) * xs;
+    float* yr = y + int64_t(r) * ys;
+    const int c0 = rank * chunk, n = max(0, min(C, c0 + chunk) - c0);
+    // 1. the chunk into shared memory (bulk: one asynchronous copy of n floats, 16-byte aligned, multiple of 4)
+    if (bulk) {
+        if (threadIdx.x == 0) {
+            mbar_init(&bar, 1);
+            fence_barrier_init();
+            mbar_arrive_expect_tx(&bar, uint32_t(n) * 4u);
+            if (n > 0) bulk_g2s(cache, xr + c0, uint32_t(n) * 4u, &bar);
+        }
+        __syncthreads();
+        mbar_wait(&bar, 0);  // bounded; a timeout is recorded
+    } else {
+#pragma unroll 4
+        for (int i = threadIdx.x; i < n; i += kNormThreads) cache[i] = xr[c0 + i];
+        __syncthreads();
+    }
+    // the first partial
+    double p1 = 0.0;
+    float pm = -INFINITY;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n; i += kNormThreads) {
+        const float v = cache[i];
+        if (kind == 2) pm = fmaxf(pm, v);
+        else p1 += kind == 0 ? double(v) * v : double(v);
+    }
+    if (kind == 2) pm = block_max_f(pm, redf);
+    else p1 = block_sum_d(p1, red);
+    if (threadIdx.x == 0) xch[0] = kind == 2 ? double(pm) : p1;
+    cl.sync();
+    // 2. the row's first statistic from every rank's partial, in rank order
+    double s0 = kind == 2 ? -INFINITY : 0.0;
+    for (int k = 0; k < CL; k++) {
+        const double v = *cl.map_shared_rank(&xch[0], k);
+        s0 = kind == 2 ? fmax(s0, v) : s0 + v;
+    }
+    float rs = 0.0f, mean = 0.0f, mx = 0.0f, inv = 0.0f;
+    if (kind == 0) {
+        rs = float(1.0 / sqrt(s0 / C + double(eps)));
+    } else {
+        // second partial: centred squares (LayerNorm) or exp sums (softmax)
+        const double mu = s0 / C;
+        mx = float(s0);
+        double p2 = 0.0;
+        float ps = 0.0f;
+#pragma unroll 4
+        for (int i = threadIdx.x; i < n; i += kNormThreads) {
+            if (kind == 1) {
+                const double d = cache[i] - mu;
+                p2 += d * d;
+            } else {
+                ps += expf(cache[i] - mx);
+            }
+        }
+        if (kind == 1) p2 = block_sum_d(p2, red);
+        else ps = block_sum<kNormThreads>(ps, redf);
+        if (threadIdx.x == 0) xch[1] = kind == 1 ? p2 : double(ps);
+        cl.sync();
+        if (kind == 1) {
+            double v2 = 0.0;
+            for (int k = 0; k < CL; k++) v2 += *cl.map_shared_rank(&xch[1], k);
+            rs = float(1.0 / sqrt(v2 / C + double(eps)));
+            mean = float(mu);
+        } else {
+            float t = 0.0f;
+            for (int k = 0; k < CL; k++) t += float(*cl.map_shared_rank(&xch[1], k));
+            inv = 1.0f / t;
+        }
+    }
+    // reads of the peers' partials are done: arrive now, wait before leaving (a peer may still read ours)
+    cl.barrier_arrive();
+    pdl_trigger();
+    auto out = [&](float v, int c) {
+        return kind == 0   ? __fmul_rn(__fmul_rn(v, rs), g[c])
+               : kind == 1 ? __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, mean), rs), g[c]), b[c])
+                           : expf(v - mx) * inv;
+    };
+    if (bulk) {  // y rows are 16-byte aligned too (the host checks): float4 stores
+        for (int i = 4 * threadIdx.x; i < n; i += 4 * kNormThreads) {
+            const float4 v = *reinterpret_cast<const float4*>(cache + i);
+            const int c = c0 + i;
+            *reinterpret_cast<float4*>(yr + c) = make_float4(out(v.x, c), out(v.y, c + 1), out(v.z, c + 2), out(v.w, c + 3));
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += kNormThreads) yr[c0 + i] = out(cache[i], c0 + i);
+    }
+    cl.barrier_wait();
 }
 
 // Wide rows, few of them (the LM-head width at 1..sms rows): one CTA per row leaves most SMs idle, so each row is
@@ -428,6 +548,9 @@ cudaError_t row_cache_attr(K kernel) {
     return e;
 }
 
+cudaError_t launch_rows_cluster(const float* x, int64_t xs, float* y, int64_t ys, const float* g, const float* b,
+                                int rows, int C, float eps, int kind, cudaStream_t st, bool pdl);
+
 cudaError_t launch_norm(const float* x, int64_t x_stride, float* y, int64_t y_stride, const float* gamma,
                         const float* beta, int rows, int C, float eps, bool rms, cudaStream_t st, bool pdl) {
     if (rows <= 0) return cudaSuccess;
@@ -437,6 +560,9 @@ cudaError_t launch_norm(const float* x, int64_t x_stride, float* y, int64_t y_st
         return launch_ex(rows_warp_kernel, dim3((rows + kNormThreads / 32 - 1) / (kNormThreads / 32)),
                          dim3(kNormThreads), 0, st, pdl, x, x_stride, y, y_stride, gamma, beta, rows, C, eps,
                          rms ? 0 : 1);
+    if (cudaError_t e = launch_rows_cluster(x, x_stride, y, y_stride, gamma, beta, rows, C, eps, rms ? 0 : 1, st, pdl);
+        e != cudaErrorNotSupported)
+        return e;
     const size_t smem = C <= kRowCacheFloats ? size_t(C) * 4 : 0;
     if (cudaError_t e = row_cache_attr(norm_kernel); e != cudaSuccess) return e;
     return launch_ex(norm_kernel, dim3(rows), dim3(kNormThreads), smem, st, pdl, x, x_stride, y, y_stride, gamma, beta,
@@ -462,6 +588,46 @@ cudaError_t launch_wide_rows(const float* x, int64_t x_stride, float* y, int64_t
                      gamma, C, chunk, softmax ? 1 : 0, eps, static_cast<const double*>(part));
 }
 
+// Cluster per row for rows wider than the row cache (up to 8 x kRowCacheFloats); cudaErrorNotSupported otherwise.
+cudaError_t launch_rows_cluster(const float* x, int64_t xs, float* y, int64_t ys, const float* g, const float* b,
+                                int rows, int C, float eps, int kind, cudaStream_t st, bool pdl) {
+    const int CL = (C + kRowCacheFloats - 1) / kRowCacheFloats;
+    if (C <= kRowCacheFloats || CL > 8 || rows > 65535) return cudaErrorNotSupported;
+    const int chunk = ((C + CL - 1) / CL + 3) / 4 * 4;  // a multiple of 4, at most kRowCacheFloats
+    const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const int bulk = C % 4 == 0 && xs % 4 == 0 && ys % 4 == 0 && al16(x) && al16(y) ? 1 : 0;
+    static unsigned done = 0u;  // bit d: device d (< 32); function attributes are per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 32 || !((done >> dev) & 1u)) {
+        if (cudaError_t e = cudaFuncSetAttribute(rows_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 kRowCacheFloats * 4);
+            e != cudaSuccess)
+            return e;
+        if (dev < 32) done |= 1u << dev;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(CL, rows);
+    cfg.blockDim = dim3(kNormThreads);
+    cfg.dynamicSmemBytes = size_t(chunk) * 4;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = CL;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    na++;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, rows_cluster_kernel, x, xs, y, ys, g, b, C, chunk, eps, kind, bulk);
+}
+
 cudaError_t launch_softmax(const float* x, float* y, int rows, int C, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
     // a warp per row only for many rows of at most 1024 (wider rows: the CTA kernel's float4 loads and row cache
@@ -470,6 +636,9 @@ cudaError_t launch_softmax(const float* x, float* y, int rows, int C, cudaStream
         return launch_ex(rows_warp_kernel, dim3((rows + kNormThreads / 32 - 1) / (kNormThreads / 32)),
                          dim3(kNormThreads), 0, st, false, x, int64_t(C), y, int64_t(C), static_cast<const float*>(nullptr),
                          static_cast<const float*>(nullptr), rows, C, 0.0f, 2);
+    if (cudaError_t e = launch_rows_cluster(x, C, y, C, nullptr, nullptr, rows, C, 0.0f, 2, st, false);
+        e != cudaErrorNotSupported)
+        return e;
     const size_t smem = C <= kRowCacheFloats ? size_t(C) * 4 : 0;
     if (cudaError_t e = row_cache_attr(softmax_kernel); e != cudaSuccess) return e;
     softmax_kernel<<<rows, kNormThreads, smem, st>>>(x, y, C);

@@ -95,9 +95,10 @@ def test_matmul_many_rows(torch, R, M):
 
 
 # (151936, 1..2) and (20000, 100): wide rows, fewer than the SMs, split over CTAs (RMSNorm; LayerNorm keeps one
-# CTA per row); (16384, 150): one CTA per row; (1024, 300), (2500, 400): a warp per row
+# CTA per row, or a cluster per row past the row cache); (16384, 150): one CTA per row; (1024, 300),
+# (2500, 400): a warp per row; (40000, 160): a cluster of 2 CTAs per row
 @pytest.mark.parametrize("C,rows", [(96, 3), (1024, 7), (2560, 2), (151936, 2), (151936, 1), (20000, 100),
-                                    (16384, 150), (1024, 300), (2500, 400)])
+                                    (16384, 150), (1024, 300), (2500, 400), (40000, 160)])
 def test_norms(torch, R, C, rows):
     from nekochat_b200 import ops
     rng = np.random.default_rng(C)
@@ -110,7 +111,7 @@ def test_norms(torch, R, C, rows):
 
 
 @pytest.mark.parametrize("C,rows", [(1024, 5), (2048, 3), (2560, 1), (151936, 2), (1000, 4), (151936, 1),
-                                    (20000, 100), (16384, 150), (1000, 300)])
+                                    (20000, 100), (16384, 150), (1000, 300), (40000, 160)])
 def test_softmax_argmax(torch, R, C, rows):
     from nekochat_b200 import ops
     rng = np.random.default_rng(C + 1)
