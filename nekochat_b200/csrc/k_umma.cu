@@ -219,7 +219,9 @@ __global__ void __launch_bounds__(kUThreads, 1) umma_gemm_kernel(const GemvArgs 
     if (tid == 0) {
         for (int b = 0; b < NB; b++) mbar_init(&mma_bar[b], 1);
         fence_barrier_init();
-        s_fail = 0;
+        // the descriptors assume 1024-byte aligned tiles; a misaligned base (static shared variables sit beside
+        // the run-time aligned dynamic block) is recorded and the UMMAs are skipped
+        s_fail = (smem_u32(usm) & 1023u) ? 1 : 0;
     }
     tc_fence_before();
     __syncthreads();
@@ -300,9 +302,11 @@ __global__ void __launch_bounds__(kUThreads, 1) umma_gemm_kernel(const GemvArgs 
             *reinterpret_cast<uint4*>(bb + L::kBTile + sw128_off(r, q)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
     };
-    // bounded wait for the UMMAs of stage i (their commit): their buffer is free / their results are in TMEM
+    // bounded wait for the UMMAs of stage i (their commit): their buffer is free / their results are in TMEM;
+    // nothing to wait for when the alignment check failed (no UMMA is issued then)
+    const bool issuing = !s_fail;
     auto mma_wait = [&](int i) {
-        if (!mbar_wait(&mma_bar[i % NB], uint32_t(i / NB) & 1u)) s_fail = 1;
+        if (issuing && !mbar_wait(&mma_bar[i % NB], uint32_t(i / NB) & 1u)) s_fail = 1;
     };
 
     // prologue: stages 0 .. P - 1 (weights before the dependency wait: they never depend on the previous kernel;
