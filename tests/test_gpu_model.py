@@ -225,3 +225,35 @@ def test_chained_batch_matches_single_sequence(n):
             assert srt[-1] - srt[-2] <= 2e-4, "greedy token differs beyond a near-tie"
     m.close()
     m2.close()
+
+
+def test_generate_reuses_the_cached_prefix_and_stops():
+    """nekochat_b200.generate (Engine::generate semantics): a second turn whose prompt extends the first reuses the
+    slot's cache (all but the last sampled token, which was never run) and samples from logits that match a fresh
+    run of the whole prompt; a stop id ends generation before it; a full context ends it with reason 3."""
+    from nekochat_b200.generate import SlotGenerator
+    s = workload.shape("qwen3-tiny")
+    tensors = list(workload.weights(s, seed=12, perturb=True))
+    p1 = [int(t) for t in workload.prompt(s, 20, seed=50)]
+    a = nmodel.Model(s, FP8, context=96, max_seqs=1, max_rows=16).load(tensors)
+    ga = SlotGenerator(a)
+    out1, st1 = ga.generate(p1, 6)
+    assert st1["reused_tokens"] == 0 and st1["generated_tokens"] == 6 and st1["stop_reason"] == 0
+    p2 = p1 + out1 + [7, 8, 9]
+    out2, st2 = ga.generate(p2, 4, keep_logits=True)
+    assert st2["reused_tokens"] == len(p1) + len(out1) - 1
+    b = nmodel.Model(s, FP8, context=96, max_seqs=1, max_rows=16).load(tensors)
+    out_b, stb = SlotGenerator(b).generate(p2, 4, keep_logits=True)
+    assert stb["reused_tokens"] == 0
+    np.testing.assert_allclose(st2["logits"][0], stb["logits"][0], rtol=1e-4, atol=1e-4)
+    # stop id: the token a plain run produces third ends generation after two tokens
+    c = nmodel.Model(s, FP8, context=32, max_seqs=1, max_rows=16).load(tensors)
+    plain, _ = SlotGenerator(c).generate(p1, 5)
+    if plain[2] not in plain[:2]:
+        stopped, stc = SlotGenerator(c, stop_ids=[plain[2]]).generate(p1, 5)
+        assert stopped == plain[:2] and stc["stop_reason"] == 1
+    # a full context: 20 prompt tokens + 12 decoded fill the 32 positions
+    full, stf = SlotGenerator(c).generate(p1, 40)
+    assert stf["stop_reason"] == 3 and len(full) == 32 - 20 + 1
+    for mm in (a, b, c):
+        mm.close()
