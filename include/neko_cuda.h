@@ -145,6 +145,22 @@ int neko_op_attention_noalloc(const float* q, int q_stride, const uint16_t* k_ca
                               float* out, int T, int n_head, int n_kv, int hd, int pos0, void* stream);
 /* Index of the first maximum of each row (std::max_element in Sampler::sample, sampler.cpp:24). */
 int neko_op_argmax(const float* x, int rows, int C, int* out, void* stream);
+/* SamplingParams (sampler.h:12-19) without the seed: the random draw is an input of neko_op_sample. */
+typedef struct neko_sampling {
+    float temperature;    /* <= 0: greedy */
+    int top_k;            /* 0: every token (then at most NEKO_MAX_TOP_K tokens, unless greedy) */
+    float top_p;
+    float repeat_penalty; /* 1: off */
+    int repeat_last_n;
+} neko_sampling;
+#define NEKO_MAX_TOP_K 1024
+/* Sampler::sample (sampler.cpp:14-55) for each of `rows` rows of `logits` [rows][V] (device, modified in place
+ * by the repetition penalty, as the engine's are): history [rows][hist_stride] with hist_len[r] valid tokens
+ * (device; may be NULL when the penalty is off), u [rows] uniform draws in [0, 1) (device doubles; the engine's
+ * draw is u times the kept candidates' sum), out [rows] token ids (device). Candidates that tie in value are
+ * ordered by index. top_k above NEKO_MAX_TOP_K (or 0 with V above it) with temperature > 0: NEKO_ERR_UNSUPPORTED. */
+int neko_op_sample(float* logits, int rows, int V, const int* history, const int* hist_len, int hist_stride,
+                   const double* u, const neko_sampling* params, int* out, void* stream);
 
 /* ------------------------------------------------------------------ 3. native model runner */
 

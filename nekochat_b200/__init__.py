@@ -91,6 +91,7 @@ _SIGS = {
     "neko_op_softmax": (C.c_int, [_vp, _vp, C.c_int, C.c_int, _vp]),
     "neko_op_attention": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
     "neko_op_argmax": (C.c_int, [_vp, C.c_int, C.c_int, _vp, _vp]),
+    "neko_op_sample": (C.c_int, [_vp, C.c_int, C.c_int, _vp, _vp, C.c_int, _vp, _vp, _vp, _vp]),
     "neko_op_attention_noalloc": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                             _vp]),
     "neko_model_create": (_vp, [C.c_int, C.POINTER(ModelConfig), C.c_char_p, C.c_size_t]),
@@ -145,3 +146,9 @@ def check(rc, what="", ctx=None):
 from .backend import Buffer, ComputeBackend  # noqa: E402
 from .model import Model  # noqa: E402
 from . import ops  # noqa: E402,F401
+
+
+class Sampling(C.Structure):
+    """neko_sampling (include/neko_cuda.h): SamplingParams without the seed."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float), ("repeat_penalty", C.c_float),
+                ("repeat_last_n", C.c_int)]

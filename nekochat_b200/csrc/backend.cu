@@ -567,6 +567,20 @@ int neko_op_argmax(const float* x, int rows, int C, int* out, void* stream) {
     NEKO_OP_RETURN(launch_argmax(x, C, rows, C, out, static_cast<cudaStream_t>(stream), false));
 }
 
+int neko_op_sample(float* logits, int rows, int V, const int* history, const int* hist_len, int hist_stride,
+                   const double* u, const neko_sampling* params, int* out, void* stream) {
+    if (!logits || !out || !params || rows < 0 || V <= 0 || hist_stride < 0)
+        return set_err(nullptr, NEKO_ERR_ARG, "sample args");
+    const neko_sampling sp = *params;
+    if (sp.temperature > 0.0f && !u) return set_err(nullptr, NEKO_ERR_ARG, "sample: u is needed when temperature > 0");
+    if (sp.repeat_penalty != 1.0f && sp.repeat_last_n > 0 && (!history || !hist_len))
+        return set_err(nullptr, NEKO_ERR_ARG, "sample: the repetition penalty needs the history");
+    if (sp.temperature > 0.0f && (sp.top_k <= 0 ? V : std::min(sp.top_k, V)) > kMaxTopK)
+        return set_err(nullptr, NEKO_ERR_UNSUPPORTED, "sample: top_k above NEKO_MAX_TOP_K");
+    NEKO_OP_RETURN(launch_sample(logits, rows, V, history, hist_len, hist_stride, u, sp, out,
+                                 static_cast<cudaStream_t>(stream)));
+}
+
 int neko_op_attention(const float* q, int q_stride, const uint16_t* k_cache, const uint16_t* v_cache, float* out,
                       int T, int n_head, int n_kv, int hd, int pos0, void* stream) {
     if (!q || !k_cache || !v_cache || !out || T <= 0 || n_kv <= 0 || n_head % n_kv || hd <= 0)

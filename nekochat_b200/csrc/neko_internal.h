@@ -4,6 +4,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "../../include/neko_cuda.h"
+
 #include <cstdint>
 #include <string>
 #include <utility>
@@ -131,6 +133,11 @@ int gemv_launch_count();  // number of launches launch_gemv issues per call (1)
 cudaError_t launch_norm(const float* x, int64_t x_stride, float* y, int64_t y_stride, const float* gamma,
                         const float* beta, int rows, int C, float eps, bool rms, cudaStream_t st, bool pdl);
 cudaError_t launch_softmax(const float* x, float* y, int rows, int C, cudaStream_t st);
+// Token sampling (k_sample.cu): Sampler::sample per row with caller-supplied uniform draws; top-k at most kMaxTopK
+// (cudaErrorNotSupported beyond, unless greedy).
+constexpr int kMaxTopK = NEKO_MAX_TOP_K;
+cudaError_t launch_sample(float* logits, int rows, int V, const int* hist, const int* hist_len, int hist_stride,
+                          const double* u, const neko_sampling& sp, int* out, cudaStream_t st);
 // Wide rows, fewer than the SMs (RMSNorm or softmax): chunks per row for launch_wide_rows, 0 when one CTA per row
 // is the better plan. launch_wide_rows needs rows x S x 2 doubles of scratch in part.
 constexpr int kWideRowMinC = 16384;

@@ -102,6 +102,22 @@ def argmax(x):
     return out
 
 
+def sample(logits, u, temperature=0.8, top_k=40, top_p=0.95, repeat_penalty=1.1, repeat_last_n=64, history=None,
+           hist_len=None):
+    """Sampler::sample per row of logits [rows][V] (modified in place by the repetition penalty) with the uniform
+    draws u [rows] (float64); history [rows][S] int32 with hist_len [rows] valid tokens. Returns int32 [rows]."""
+    import torch
+    from . import Sampling
+    rows, V = logits.shape
+    out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    sp = Sampling(temperature, top_k, top_p, repeat_penalty, repeat_last_n)
+    check(lib().neko_op_sample(_ptr(logits), rows, V, _ptr(history) if history is not None else None,
+                               _ptr(hist_len) if hist_len is not None else None,
+                               history.shape[1] if history is not None else 0,
+                               _ptr(u) if u is not None else None, C.byref(sp), _ptr(out), _stream()), "sample")
+    return out
+
+
 def attention(q, q_stride, k_cache, v_cache, T, n_head, n_kv, hd, pos0):
     """cpu::attention (cpu_ops.cpp:544-575) over engine-layout caches [ctx][n_kv * hd] (int16/uint16 f16 bits)."""
     import torch

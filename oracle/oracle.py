@@ -273,6 +273,19 @@ class Reference(_Ops):
             raise RuntimeError(self.error())
         return RefModel(self, h)
 
+    def sample(self, logits, history, temperature, top_k, top_p, repeat_penalty, repeat_last_n, seed):
+        """Sampler::sample with a fixed seed; returns (token, the logits after the repetition penalty)."""
+        x = np.ascontiguousarray(logits, dtype=np.float32).copy()
+        h = np.ascontiguousarray(history, dtype=np.int32)
+        f = self._fn("sample", C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_float, C.c_int, C.c_float,
+                     C.c_float, C.c_int, C.c_ulonglong)
+        t = f(x.ctypes.data, len(x), h.ctypes.data, len(h), temperature, top_k, top_p, repeat_penalty,
+              repeat_last_n, seed)
+        return int(t), x
+
+    def sampler_draw(self, seed):
+        """The uniform value behind the first draw of a Sampler seeded with `seed`."""
+        return float(self._fn("sampler_draw", C.c_double, C.c_ulonglong)(seed))
 
 class RefModel:
     def __init__(self, ref, h):

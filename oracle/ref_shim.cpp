@@ -8,6 +8,7 @@
 #include <cstdint>
 #include <cstring>
 #include <memory>
+#include <random>
 #include <string>
 #include <thread>
 #include <vector>
@@ -17,6 +18,7 @@
 #include "gpu/compute.h"
 #include "model.h"
 #include "quant.h"
+#include "sampler.h"
 #include "thread_pool.h"
 
 using namespace neko;
@@ -175,6 +177,29 @@ void ref_model_memory(void* m, long long* weights, long long* kvCapacity, long l
 }
 
 int ref_hardware_threads() { return int(std::thread::hardware_concurrency()); }
+
+// Sampler::sample (sampler.cpp:14-55) with a fixed seed, on host logits (modified in place, as the engine's).
+int ref_sample(float* logits, int n, const int* history, int hlen, float temperature, int top_k, float top_p,
+               float repeat_penalty, int repeat_last_n, unsigned long long seed) {
+    SamplingParams sp;
+    sp.temperature = temperature;
+    sp.topK = top_k;
+    sp.topP = top_p;
+    sp.repeatPenalty = repeat_penalty;
+    sp.repeatLastN = repeat_last_n;
+    sp.seed = seed;
+    Sampler s(sp);
+    const std::vector<int> h(history, history + hlen);
+    return s.sample(logits, n, h);
+}
+
+// The uniform value in [0, 1) behind the first draw of a Sampler seeded with `seed`: its
+// uniform_real_distribution<double>(0, total) on the same std::mt19937_64 returns total times this value.
+double ref_sampler_draw(unsigned long long seed) {
+    std::mt19937_64 rng(seed);
+    std::uniform_real_distribution<double> u(0.0, 1.0);
+    return u(rng);
+}
 
 #if defined(NEKO_REF_WITH_CUDA)
 }  // extern "C"

@@ -146,3 +146,39 @@ def test_attention_op(torch, R, H, KV, hd, T, pos0):
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16) if a.dtype == np.uint16 else a).cuda()
     got = ops.attention(t(q), stride, t(kc), t(vc), T, H, KV, hd, pos0).cpu().numpy()
     close(got, ref, 2e-3)
+
+
+SAMPLE_PARAMS = [(0.8, 40, 0.95, 1.1, 64), (1.0, 1, 1.0, 1.0, 0), (0.7, 1024, 0.9, 1.3, 32), (1.5, 0, 0.5, 1.0, 64),
+                 (0.0, 40, 0.95, 1.1, 64)]
+
+
+@pytest.mark.parametrize("params", SAMPLE_PARAMS)
+@pytest.mark.parametrize("V", [1000, 151936])
+def test_sample_matches_reference_sampler(torch, params, V):
+    """neko_op_sample against the reference's own Sampler::sample (compiled from its sources) with the same
+    seeds: the device takes each seed's uniform draw as input. Same token, same penalised logits."""
+    import nekochat_b200 as nb
+    from nekochat_b200 import ops
+    from oracle.oracle import Reference
+    R = Reference()
+    rng = np.random.default_rng(V + params[1])
+    rows, S = 4, 80
+    x = (rng.standard_normal((rows, V)) * 3).astype(np.float32)
+    hist = rng.integers(0, V, (rows, S)).astype(np.int32)
+    hist[:, -3:] = np.argmax(x, axis=1)[:, None]  # the top token repeated: the penalty moves it
+    hlen = np.array([S, 50, 10, 0], np.int32)
+    seeds = [5000 + i for i in range(rows)]
+    u = np.array([R.sampler_draw(sd) for sd in seeds])
+    tx = torch.from_numpy(x.copy()).cuda()
+    args = (torch.from_numpy(u).cuda(),) + params
+    kw = dict(history=torch.from_numpy(hist).cuda(), hist_len=torch.from_numpy(hlen).cuda())
+    if params[0] > 0 and (params[1] if params[1] > 0 else V) > 1024:
+        with pytest.raises(nb.NekoError):
+            ops.sample(tx, *args, **kw)
+        return
+    out = ops.sample(tx, *args, **kw).cpu().numpy()
+    got_x = tx.cpu().numpy()
+    for i in range(rows):
+        want, px = R.sample(x[i], hist[i, :hlen[i]], *params, seeds[i])
+        assert int(out[i]) == want, (i, params)
+        np.testing.assert_array_equal(got_x[i], px)
