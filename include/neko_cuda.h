@@ -161,6 +161,13 @@ typedef struct neko_sampling {
  * ordered by index. top_k above NEKO_MAX_TOP_K (or 0 with V above it) with temperature > 0: NEKO_ERR_UNSUPPORTED. */
 int neko_op_sample(float* logits, int rows, int V, const int* history, const int* hist_len, int hist_stride,
                    const double* u, const neko_sampling* params, int* out, void* stream);
+/* An FP8 (E4M3) checkpoint weight as f32, TensorStore::rows / toF32 (tensor_store.cpp:543-571, 578-590):
+ * out[r][c] = e4m3fn(codes[r][c]) * scales[r / bR][c / bC] (device pointers), the scale tensor being the
+ * checkpoint's "<name>_scale_inv" or "<name>_scale" as f32 [scale_rows][scale_cols] (1 x 1 for a per-tensor
+ * scale); a block spans 128 elements along an axis when ceil(n / 128) scales cover it, else ceil(n / parts).
+ * Codes 0x7F / 0xFF decode to +-480 as in the reference's table. */
+int neko_op_fp8_block_dequant(const uint8_t* codes, int64_t rows, int64_t cols, const float* scales,
+                              int64_t scale_rows, int64_t scale_cols, float* out, void* stream);
 
 /* ------------------------------------------------------------------ 3. native model runner */
 
@@ -196,6 +203,11 @@ const char* neko_model_last_error(neko_model* m);
 int neko_model_set_tensor(neko_model* m, const char* name, const float* data, int64_t rows, int64_t cols);
 /* The same with the f32 data already in device memory of the model's device (no host copy). */
 int neko_model_set_tensor_device(neko_model* m, const char* name, const float* d_data, int64_t rows, int64_t cols);
+/* The same for an FP8 (E4M3) checkpoint weight (Qwen3-*-FP8): host codes [rows][cols] and its block scales as
+ * f32 [scale_rows][scale_cols] (a BF16 scale tensor widened to f32 first); the weight is dequantized on the GPU
+ * exactly as neko_op_fp8_block_dequant, then quantized into the engine's format like neko_model_set_tensor. */
+int neko_model_set_tensor_fp8(neko_model* m, const char* name, const uint8_t* codes, int64_t rows, int64_t cols,
+                              const float* scales, int64_t scale_rows, int64_t scale_cols);
 /* Checks that every tensor was provided. Must be called before the first forward. */
 int neko_model_finalize(neko_model* m);
 /* Model::forward (model.h:72): tokens[0..T) of sequence `slot` at positions [pos0, pos0 + T), T <= max_rows;

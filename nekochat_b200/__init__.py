@@ -92,6 +92,7 @@ _SIGS = {
     "neko_op_attention": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
     "neko_op_argmax": (C.c_int, [_vp, C.c_int, C.c_int, _vp, _vp]),
     "neko_op_sample": (C.c_int, [_vp, C.c_int, C.c_int, _vp, _vp, C.c_int, _vp, _vp, _vp, _vp]),
+    "neko_op_fp8_block_dequant": (C.c_int, [_vp, C.c_int64, C.c_int64, _vp, C.c_int64, C.c_int64, _vp, _vp]),
     "neko_op_attention_noalloc": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                             _vp]),
     "neko_model_create": (_vp, [C.c_int, C.POINTER(ModelConfig), C.c_char_p, C.c_size_t]),
@@ -99,6 +100,8 @@ _SIGS = {
     "neko_model_last_error": (C.c_char_p, [_vp]),
     "neko_model_set_tensor": (C.c_int, [_vp, C.c_char_p, _vp, C.c_int64, C.c_int64]),
     "neko_model_set_tensor_device": (C.c_int, [_vp, C.c_char_p, _vp, C.c_int64, C.c_int64]),
+    "neko_model_set_tensor_fp8": (C.c_int, [_vp, C.c_char_p, _vp, C.c_int64, C.c_int64, _vp, C.c_int64,
+                                            C.c_int64]),
     "neko_model_finalize": (C.c_int, [_vp]),
     "neko_model_forward": (C.c_int, [_vp, C.c_int, _vp, C.c_int, C.c_int, _vp]),
     "neko_model_decode": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp]),

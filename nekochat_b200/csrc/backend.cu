@@ -581,6 +581,14 @@ int neko_op_sample(float* logits, int rows, int V, const int* history, const int
                                  static_cast<cudaStream_t>(stream)));
 }
 
+int neko_op_fp8_block_dequant(const uint8_t* codes, int64_t rows, int64_t cols, const float* scales,
+                              int64_t scale_rows, int64_t scale_cols, float* out, void* stream) {
+    if (!codes || !scales || !out || rows < 0 || cols < 0 || scale_rows < 1 || scale_cols < 1)
+        return set_err(nullptr, NEKO_ERR_ARG, "fp8_block_dequant args");
+    NEKO_OP_RETURN(launch_fp8_block_dequant(codes, rows, cols, scales, scale_rows, scale_cols, out,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
 int neko_op_attention(const float* q, int q_stride, const uint16_t* k_cache, const uint16_t* v_cache, float* out,
                       int T, int n_head, int n_kv, int hd, int pos0, void* stream) {
     if (!q || !k_cache || !v_cache || !out || T <= 0 || n_kv <= 0 || n_head % n_kv || hd <= 0)

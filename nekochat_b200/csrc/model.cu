@@ -138,6 +138,8 @@ struct neko_model {
     std::set<std::string> need;
     float* staging = nullptr;  // f32 upload buffer for matrices
     size_t staging_floats = 0;
+    uint8_t* staging8 = nullptr;  // FP8 checkpoint codes + their f32 block scales
+    size_t staging8_bytes = 0;
     bool final_ok = false;
     int debug_layers = -1;  // Model::setDebugLayers: stop after this many layers and output the hidden states
     int debug_stage = 0;    // > 0: stop inside layer debug_layers after this stage (debugStages numbering)
@@ -971,7 +973,7 @@ void neko_model_destroy(neko_model* m) {
                     (void*)m->d_pos, (void*)m->d_argmax, (void*)m->d_outrows, (void*)m->d_keys, (void*)m->part,
                     (void*)m->tickets, (void*)m->mm_ws, (void*)m->mm_tickets, (void*)m->dec_part, (void*)m->dec_tickets, (void*)m->dec_sync,
                     (void*)m->ch_a, (void*)m->ch_b, (void*)m->ch_ss,
-                    (void*)m->staging})
+                    (void*)m->staging, (void*)m->staging8})
         if (p) cudaFree(p);
     if (m->h_in) cudaFreeHost(m->h_in);
     if (m->h_logits) cudaFreeHost(m->h_logits);
@@ -1110,6 +1112,39 @@ int neko_model_set_tensor(neko_model* m, const char* name, const float* data, in
 
 int neko_model_set_tensor_device(neko_model* m, const char* name, const float* d_data, int64_t rows, int64_t cols) {
     return set_tensor_entry(m, name, d_data, rows, cols, true);
+}
+
+int neko_model_set_tensor_fp8(neko_model* m, const char* name, const uint8_t* codes, int64_t rows, int64_t cols,
+                              const float* scales, int64_t scale_rows, int64_t scale_cols) {
+    if (!m) return NEKO_ERR_ARG;
+    if (!name || !codes || !scales || rows <= 0 || cols <= 0 || scale_rows < 1 || scale_cols < 1)
+        return fail(m, NEKO_ERR_ARG, "set_tensor_fp8: bad argument");
+    Guard g(m->device);
+    const size_t n = size_t(rows) * size_t(cols), ns = size_t(scale_rows) * size_t(scale_cols);
+    const size_t scale_off = (n + 255) & ~size_t(255);
+    if (scale_off + ns * 4 > m->staging8_bytes) {
+        CK(cudaStreamSynchronize(m->stream), "staging8");
+        cudaFree(m->staging8);
+        m->staging8 = nullptr;
+        m->staging8_bytes = 0;
+        CK(cudaMalloc(&m->staging8, scale_off + ns * 4), "staging8");
+        m->staging8_bytes = scale_off + ns * 4;
+    }
+    if (n > m->staging_floats) {
+        CK(cudaStreamSynchronize(m->stream), "staging");
+        cudaFree(m->staging);
+        m->staging = nullptr;
+        m->staging_floats = 0;
+        CK(cudaMalloc(&m->staging, n * 4), "staging");
+        m->staging_floats = n;
+    }
+    float* d_scales = reinterpret_cast<float*>(m->staging8 + scale_off);
+    CK(cudaMemcpyAsync(m->staging8, codes, n, cudaMemcpyHostToDevice, m->stream), "upload fp8 codes");
+    CK(cudaMemcpyAsync(d_scales, scales, ns * 4, cudaMemcpyHostToDevice, m->stream), "upload fp8 scales");
+    CK(launch_fp8_block_dequant(m->staging8, rows, cols, d_scales, scale_rows, scale_cols, m->staging, m->stream),
+       "fp8 dequant");
+    // the f32 tensor is device memory of the model's device, ordered on its stream: the device-data path
+    return set_tensor(m, name, m->staging, rows, cols, true);
 }
 
 int neko_model_finalize(neko_model* m) {

@@ -136,6 +136,10 @@ cudaError_t launch_softmax(const float* x, float* y, int rows, int C, cudaStream
 // Token sampling (k_sample.cu): Sampler::sample per row with caller-supplied uniform draws; top-k at most kMaxTopK
 // (cudaErrorNotSupported beyond, unless greedy).
 constexpr int kMaxTopK = NEKO_MAX_TOP_K;
+// FP8 (E4M3) checkpoint codes times their block scales, to f32 (tensor_store.cpp:543-571)
+int64_t fp8_block_of(int64_t n, int64_t parts);
+cudaError_t launch_fp8_block_dequant(const uint8_t* codes, int64_t rows, int64_t cols, const float* scales,
+                                     int64_t sR, int64_t sC, float* out, cudaStream_t st);
 cudaError_t launch_sample(float* logits, int rows, int V, const int* hist, const int* hist_len, int hist_stride,
                           const double* u, const neko_sampling& sp, int* out, cudaStream_t st);
 // Wide rows, fewer than the SMs (RMSNorm or softmax): chunks per row for launch_wide_rows, 0 when one CTA per row

@@ -56,6 +56,15 @@ class Model:
         rows, cols = (a.shape[0], int(np.prod(a.shape[1:]))) if a.ndim > 1 else (1, a.shape[0])
         self._check(lib().neko_model_set_tensor(self.h, name.encode(), _p(a), rows, cols), f"set_tensor {name}")
 
+    def set_tensor_fp8(self, name, codes, scales):
+        """An FP8 (E4M3) checkpoint weight: codes uint8 [rows][cols] and its block scales [sR][sC] (any float
+        dtype, widened to f32; a 0-d or 1-element scale is per tensor), dequantized and quantized on the GPU."""
+        q = np.ascontiguousarray(codes, dtype=np.uint8)
+        sc = np.ascontiguousarray(scales, dtype=np.float32)
+        s2 = sc.reshape(sc.shape[0] if sc.ndim else 1, -1)
+        self._check(lib().neko_model_set_tensor_fp8(self.h, name.encode(), _p(q), q.shape[0], q.shape[1], _p(s2),
+                                                    s2.shape[0], s2.shape[1]), f"set_tensor_fp8 {name}")
+
     def set_tensor_device(self, name, t):
         """t: a contiguous float32 CUDA tensor on the model's device."""
         if t.device.type != "cuda" or t.device.index != self.device:
@@ -86,9 +95,13 @@ class Model:
         return self
 
     def load(self, tensors):
-        """tensors: iterable of (name, float32 array), e.g. workload.weights(shape)."""
-        for name, a in tensors:
-            self.set_tensor(name, a)
+        """tensors: iterable of (name, float32 array), e.g. workload.weights(shape), or (name, uint8 codes,
+        scales) for an FP8 (E4M3) checkpoint weight with its block scales."""
+        for item in tensors:
+            if len(item) == 3:
+                self.set_tensor_fp8(*item)
+            else:
+                self.set_tensor(*item)
         self._check(lib().neko_model_finalize(self.h), "finalize")
         return self
 

@@ -118,6 +118,19 @@ def sample(logits, u, temperature=0.8, top_k=40, top_p=0.95, repeat_penalty=1.1,
     return out
 
 
+def fp8_block_dequant(codes, scales):
+    """An FP8 (E4M3) checkpoint weight as f32 (TensorStore::toF32, tensor_store.cpp:543-571, 578-590): codes
+    uint8 [rows][cols], scales float32 [sR][sC] (the "_scale_inv" / "_scale" tensor; 1 x 1 per tensor), both CUDA
+    tensors. Returns float32 [rows][cols]."""
+    import torch
+    rows, cols = codes.shape
+    s2 = scales.reshape(scales.shape[0] if scales.dim() else 1, -1)
+    out = torch.empty((rows, cols), dtype=torch.float32, device=codes.device)
+    check(lib().neko_op_fp8_block_dequant(_ptr(codes), rows, cols, _ptr(scales), s2.shape[0], s2.shape[1], _ptr(out),
+                                          _stream()), "fp8_block_dequant")
+    return out
+
+
 def attention(q, q_stride, k_cache, v_cache, T, n_head, n_kv, hd, pos0):
     """cpu::attention (cpu_ops.cpp:544-575) over engine-layout caches [ctx][n_kv * hd] (int16/uint16 f16 bits)."""
     import torch

@@ -12,11 +12,13 @@ _DT = {np.dtype(np.float32): "F32", np.dtype(np.float16): "F16"}
 
 
 def write_safetensors(path, tensors):
-    """tensors: list of (name, array). Arrays are written as stored (F32 or F16)."""
+    """tensors: list of (name, array) or (name, array, dtype tag). Arrays are written as stored (F32 or F16);
+    a tag names the stored type of raw bytes, e.g. (name, uint8 codes, "F8_E4M3") for an FP8 checkpoint weight."""
     header, blobs, off = {}, [], 0
-    for name, a in tensors:
-        a = np.ascontiguousarray(a)
-        header[name] = {"dtype": _DT[a.dtype], "shape": list(a.shape), "data_offsets": [off, off + a.nbytes]}
+    for item in tensors:
+        name, a = item[0], np.ascontiguousarray(item[1])
+        tag = item[2] if len(item) > 2 else _DT[a.dtype]
+        header[name] = {"dtype": tag, "shape": list(a.shape), "data_offsets": [off, off + a.nbytes]}
         blobs.append(a)
         off += a.nbytes
     h = json.dumps(header, separators=(",", ":")).encode()
@@ -50,3 +52,35 @@ def write_model(folder, s, tensors, dtype=np.float32):
         json.dump(config_json(s), f)
     write_safetensors(os.path.join(folder, "model.safetensors"), items)
     return folder
+
+
+def e4m3fn_table():
+    """The reference's FP8 checkpoint decode table (tensor_store.cpp:558-563): OCP E4M3, bias 7, no infinities
+    and no NaN code (0x7F / 0xFF give +-480); code 0x80 is -0.0."""
+    c = np.arange(256)
+    e, m = (c >> 3) & 15, c & 7
+    mag = np.where(e == 0, np.ldexp(m / 8.0, -6), np.ldexp(1.0 + m / 8.0, e - 7)).astype(np.float32)
+    return np.where(c & 0x80, -mag, mag).astype(np.float32)
+
+
+def fp8_block_of(n, parts):
+    """Block length along an axis of n elements with `parts` scales (tensor_store.cpp:550-554)."""
+    if parts <= 1:
+        return n
+    if (n + 127) // 128 == parts:
+        return 128
+    return (n + parts - 1) // parts
+
+
+def fp8_block_dequant(codes, scales):
+    """TensorStore::rows for an F8_E4M3 weight (tensor_store.cpp:543-571): table[code] * scale of its block, one
+    f32 multiply. codes uint8 [R][C]; scales as stored (0-d, [sR] or [sR][sC])."""
+    codes = np.asarray(codes, np.uint8)
+    s = np.asarray(scales, np.float32)
+    sR = s.shape[0] if s.ndim >= 1 else 1
+    sC = s.shape[1] if s.ndim >= 2 else 1
+    s = s.reshape(sR, sC)
+    R, Cn = codes.shape
+    bR, bC = fp8_block_of(R, sR), fp8_block_of(Cn, sC)
+    ri, ci = np.arange(R) // bR, np.arange(Cn) // bC
+    return (e4m3fn_table()[codes] * s[ri][:, ci]).astype(np.float32)

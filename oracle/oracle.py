@@ -283,6 +283,15 @@ class Reference(_Ops):
               repeat_last_n, seed)
         return int(t), x
 
+    def tensor_f32(self, path, name, count):
+        """TensorStore::toF32 of one tensor of a safetensors file (FP8 weights dequantized with their scales)."""
+        out = np.empty(count, np.float32)
+        f = self._fn("tensor_f32", C.c_long, C.c_char_p, C.c_char_p, C.c_void_p, C.c_long)
+        n = f(path.encode(), name.encode(), out.ctypes.data, count)
+        if n < 0:
+            raise RuntimeError(self.error())
+        return out[:n]
+
     def sampler_draw(self, seed):
         """The uniform value behind the first draw of a Sampler seeded with `seed`."""
         return float(self._fn("sampler_draw", C.c_double, C.c_ulonglong)(seed))

@@ -9,6 +9,7 @@
 #include <cstring>
 #include <memory>
 #include <random>
+#include <stdexcept>
 #include <string>
 #include <thread>
 #include <vector>
@@ -19,6 +20,7 @@
 #include "model.h"
 #include "quant.h"
 #include "sampler.h"
+#include "tensor_store.h"
 #include "thread_pool.h"
 
 using namespace neko;
@@ -199,6 +201,22 @@ double ref_sampler_draw(unsigned long long seed) {
     std::mt19937_64 rng(seed);
     std::uniform_real_distribution<double> u(0.0, 1.0);
     return u(rng);
+}
+
+// TensorStore::toF32 (tensor_store.cpp:578-590) of one tensor of a safetensors file: an FP8 (E4M3) weight comes
+// out dequantized with its "_scale_inv" / "_scale" block scales (tensor_store.cpp:543-571). Returns the element
+// count, or -1 (error text in ref_last_error).
+long ref_tensor_f32(const char* path, const char* name, float* out, long cap) {
+    long n = -1;
+    const int rc = guarded([&] {
+        TensorStore ts;
+        ts.addFile(path);
+        const std::vector<float> v = ts.toF32(name);
+        if (long(v.size()) > cap) throw std::runtime_error("ref_tensor_f32: output buffer too small");
+        std::memcpy(out, v.data(), v.size() * 4);
+        n = long(v.size());
+    });
+    return rc ? -1 : n;
 }
 
 #if defined(NEKO_REF_WITH_CUDA)

@@ -16,7 +16,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, ROOT)
 
-from oracle.checkpoint import write_model  # noqa: E402
+from oracle.checkpoint import write_model, write_safetensors  # noqa: E402
 from oracle.oracle import ACCUMULATE, FP4, FP8, F16, GELU, Reference  # noqa: E402
 from nekochat_b200 import workload  # noqa: E402
 
@@ -144,15 +144,45 @@ def models(ref, tmp):
     return out
 
 
-def main():
+# (rows, cols), scale shape: 128 x 128 blocks with ragged edges, an even split, a per-tensor 0-d scale, a 1-D
+# scale (rows only), more scale rows than weight rows, a 1 x 1 scale, odd columns
+FP8CKPT_CASES = (((136, 260), (2, 3)), ((96, 64), (4, 2)), ((40, 33), ()), ((140, 40), (2,)), ((10, 24), (20, 3)),
+                 ((8, 32), (1, 1)), ((129, 7), (2, 1)))
+
+
+def fp8ckpt(ref, tmp):
+    """FP8 (E4M3) checkpoint weights as the reference loader reads them (TensorStore::toF32 through
+    tensor_store.cpp:543-571), from safetensors files with F8_E4M3 weights and f32 "_scale_inv" tensors. Every
+    case holds all 256 codes."""
+    rng = np.random.default_rng(29)
+    out = {}
+    for i, ((R, Cn), sh) in enumerate(FP8CKPT_CASES):
+        codes = rng.integers(0, 256, (R, Cn), dtype=np.uint8)
+        codes.flat[:256] = np.arange(256, dtype=np.uint8)[:codes.size]
+        sc = (rng.random(sh) * 0.01 + 1e-4).astype(np.float32) if sh else np.float32(0.0137)
+        path = os.path.join(tmp, f"fp8_{i}.safetensors")
+        write_safetensors(path, [("w.weight", codes, "F8_E4M3"), ("w.weight_scale_inv", np.asarray(sc, np.float32))])
+        out[f"c{i}_codes"] = codes
+        out[f"c{i}_scales"] = np.asarray(sc, np.float32)
+        out[f"c{i}_f32"] = ref.tensor_f32(path, "w.weight", R * Cn).reshape(R, Cn)
+    return out
+
+
+def main(which=("codec", "ops", "models", "fp8ckpt")):
+    """Writes the named fixtures (all by default): python tests/golden/make_golden.py [name ...]"""
     ref = Reference()
-    np.savez_compressed(os.path.join(HERE, "codec.npz"), **codec(ref))
-    np.savez_compressed(os.path.join(HERE, "ops.npz"), **ops(ref))
+    if "codec" in which:
+        np.savez_compressed(os.path.join(HERE, "codec.npz"), **codec(ref))
+    if "ops" in which:
+        np.savez_compressed(os.path.join(HERE, "ops.npz"), **ops(ref))
     with tempfile.TemporaryDirectory() as tmp:
-        np.savez_compressed(os.path.join(HERE, "models.npz"), **models(ref, tmp))
-    for f in ("codec.npz", "ops.npz", "models.npz"):
-        print(f, os.path.getsize(os.path.join(HERE, f)))
+        if "models" in which:
+            np.savez_compressed(os.path.join(HERE, "models.npz"), **models(ref, tmp))
+        if "fp8ckpt" in which:
+            np.savez_compressed(os.path.join(HERE, "fp8ckpt.npz"), **fp8ckpt(ref, tmp))
+    for f in which:
+        print(f + ".npz", os.path.getsize(os.path.join(HERE, f + ".npz")))
 
 
 if __name__ == "__main__":
-    main()
+    main(tuple(sys.argv[1:]) or ("codec", "ops", "models", "fp8ckpt"))

@@ -67,3 +67,21 @@ def test_conv1d_transpose_path(torch, R, fmt):
     q = gpu_quant(torch, fmt, w, transpose=True)
     want = R.quantize(fmt, np.ascontiguousarray(w.T).astype(np.float16).astype(np.float32))
     assert np.array_equal(q, want)
+
+
+def test_fp8_checkpoint_dequant_golden(torch):
+    """neko_op_fp8_block_dequant bit-exact to the reference loader's TensorStore::toF32 (tensor_store.cpp:543-571)
+    on every golden case, through the four-codes-per-thread path and, with codes one byte off alignment, the
+    scalar one."""
+    from nekochat_b200 import ops
+    g = np.load(os.path.join(GOLD, "fp8ckpt.npz"))
+    n = len([k for k in g.files if k.endswith("_codes")])
+    for i in range(n):
+        codes, sc, want = g[f"c{i}_codes"], g[f"c{i}_scales"], g[f"c{i}_f32"]
+        d_sc = torch.from_numpy(np.ascontiguousarray(sc)).cuda()
+        got = ops.fp8_block_dequant(torch.from_numpy(codes).cuda(), d_sc).cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"case {i}"
+        buf = torch.zeros(codes.size + 1, dtype=torch.uint8, device="cuda")
+        buf[1:] = torch.from_numpy(codes.ravel()).cuda()
+        got = ops.fp8_block_dequant(buf[1:].view(codes.shape), d_sc).cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"case {i}, unaligned codes"

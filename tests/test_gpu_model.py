@@ -257,3 +257,33 @@ def test_generate_reuses_the_cached_prefix_and_stops():
     assert stf["stop_reason"] == 3 and len(full) == 32 - 20 + 1
     for mm in (a, b, c):
         mm.close()
+
+
+@pytest.mark.parametrize("fmt", [FP8, FP4])
+def test_fp8_checkpoint_weights_load_like_f32(fmt):
+    """A Qwen3-*-FP8 style checkpoint (every layer matrix as E4M3 codes with 128 x 128 block scales, ragged
+    edges included) loaded through neko_model_set_tensor_fp8 gives the same logits, bit for bit, as the same
+    weights dequantized by the reference loader's rule (tensor_store.cpp:543-571) on the host and loaded as f32."""
+    from oracle.checkpoint import fp8_block_dequant
+    s = workload.shape("qwen3-tiny")
+    rng = np.random.default_rng(6)
+    as_fp8, as_f32 = [], []
+    for name, a in workload.weights(s, seed=5):
+        if a.ndim == 2 and name.startswith("layers."):
+            R, Cn = a.shape
+            codes = (rng.integers(0x08, 0x48, (R, Cn)) | (rng.integers(0, 2, (R, Cn)) << 7)).astype(np.uint8)
+            sc = (rng.random(((R + 127) // 128, (Cn + 127) // 128)) * 0.004 + 0.001).astype(np.float32)
+            as_fp8.append((name, codes, sc))
+            as_f32.append((name, fp8_block_dequant(codes, sc)))
+        else:
+            as_fp8.append((name, a))
+            as_f32.append((name, a))
+    a = nmodel.Model(s, fmt, context=64, max_seqs=1, max_rows=64).load(as_f32)
+    b = nmodel.Model(s, fmt, context=64, max_seqs=1, max_rows=64).load(as_fp8)
+    prompt = workload.prompt(s, 12, seed=7)
+    la, lb = a.forward(prompt, 0), b.forward(prompt, 0)
+    assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+    with pytest.raises(nb.NekoError):  # the weight's shape is checked after the dequantization
+        b.set_tensor_fp8("layers.0.mlp.down_proj.weight", np.zeros((8, 8), np.uint8), np.ones((1, 1), np.float32))
+    a.close()
+    b.close()
