@@ -226,6 +226,19 @@ int neko_model_decode(neko_model* m, int n, const int* slots, const int* tokens,
 int neko_model_stage(neko_model* m, int n, const int* slots, const int* tokens, const int* pos);
 int neko_model_step(neko_model* m, int n, int max_pos, void* stream);
 int neko_model_tokens(neko_model* m, int n, int* tokens, int* pos);
+/* Stop ids and a token budget for that loop, Engine::generate's loop (engine.cpp:120-134) on the device. With
+ * max_new > 0, neko_model_stage takes each staged token as the first sample (a stop id finishes the sequence, else
+ * it is logged) and every neko_model_step adds one kernel after the step: a sampled stop id finishes the sequence
+ * (stop reason 1, not logged), else the token is logged and the sequence finishes once max_new tokens are logged
+ * (reason 0). A finished sequence stays at its last token and position, so later steps re-run that row in place
+ * and write no KV beyond it. The context limit stays the caller's (max_pos of neko_model_step). max_new = 0 turns
+ * it off. At most NEKO_MAX_STOP_IDS ids, each in [0, vocab). */
+#define NEKO_MAX_STOP_IDS 64
+int neko_model_set_stop(neko_model* m, const int* stop_ids, int n_stop, int max_new);
+/* Synchronises and reads the log of the n staged sequences: tokens [n][max_new] (-1 past each count), counts [n],
+ * reasons [n] (the engine's stopReason: 0 max_new reached, 1 stop id; -1 still running). NULL outputs are
+ * skipped. */
+int neko_model_generated(neko_model* m, int n, int* tokens, int* counts, int* reasons);
 /* Bytes held on the device: weights, KV cache, workspace (Model::memory, model.h:91). */
 int neko_model_memory(neko_model* m, int64_t* weights, int64_t* kv, int64_t* workspace);
 /* Model::setDebugLayers(n, stage) (model.h:93-104): with n >= 0, neko_model_forward writes, instead of the last

@@ -103,6 +103,8 @@ _SIGS = {
     "neko_model_set_tensor_fp8": (C.c_int, [_vp, C.c_char_p, _vp, C.c_int64, C.c_int64, _vp, C.c_int64,
                                             C.c_int64]),
     "neko_model_finalize": (C.c_int, [_vp]),
+    "neko_model_set_stop": (C.c_int, [_vp, _vp, C.c_int, C.c_int]),
+    "neko_model_generated": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp]),
     "neko_model_forward": (C.c_int, [_vp, C.c_int, _vp, C.c_int, C.c_int, _vp]),
     "neko_model_decode": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp]),
     "neko_model_stage": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp]),

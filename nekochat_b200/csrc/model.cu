@@ -82,6 +82,35 @@ __global__ void advance_kernel(const int* argmax, int* tokens, int* pos, int n, 
     else set_device_error(kErrBadIndex);
 }
 
+// Engine::generate's per-token bookkeeping (engine.cpp:120-134) after a device greedy step: the token each
+// sequence just sampled ends it when it is a stop id (reason 1, not logged), else it is logged and ends it when
+// max_new tokens are logged (reason 0). A finished sequence is frozen: its token and position are put back after
+// every later step, so those steps re-run the same row at the same position (no KV beyond it is written).
+// state: -1 running, else the stop reason; frozen: (token, position) pairs; log: [max_new][S].
+__global__ void track_kernel(int* tokens, int* pos, int n, const int* stop_ids, int n_stop, int* counts, int* state,
+                             int* frozen, int* log, int max_new, int S) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    pdl_wait();
+    if (i >= n) return;
+    if (state[i] >= 0) {
+        tokens[i] = frozen[2 * i];
+        pos[i] = frozen[2 * i + 1];
+        return;
+    }
+    const int t = tokens[i];
+    bool stop = false;
+    for (int s = 0; s < n_stop; s++) stop = stop || stop_ids[s] == t;
+    if (!stop) {
+        const int c = counts[i];
+        log[int64_t(c) * S + i] = t;
+        counts[i] = c + 1;
+        if (c + 1 < max_new) return;
+    }
+    state[i] = stop ? 1 : 0;
+    frozen[2 * i] = t;
+    frozen[2 * i + 1] = pos[i];
+}
+
 __global__ void gather_rows_kernel(const float* x, int C, const int* rows, int n, float* out) {
     pdl_wait();
     const int r = blockIdx.y;
@@ -139,6 +168,11 @@ struct neko_model {
     float* staging = nullptr;  // f32 upload buffer for matrices
     size_t staging_floats = 0;
     uint8_t* staging8 = nullptr;  // FP8 checkpoint codes + their f32 block scales
+    // stop ids for the device greedy loop (neko_model_set_stop): ids | counts [S] | state [S] | frozen [2 S] |
+    // log [max_new][S], S = max_seqs
+    int track_steps = 0;
+    std::vector<int> stop_ids;
+    int* d_track = nullptr;
     size_t staging8_bytes = 0;
     bool final_ok = false;
     int debug_layers = -1;  // Model::setDebugLayers: stop after this many layers and output the hidden states
@@ -973,7 +1007,7 @@ void neko_model_destroy(neko_model* m) {
                     (void*)m->d_pos, (void*)m->d_argmax, (void*)m->d_outrows, (void*)m->d_keys, (void*)m->part,
                     (void*)m->tickets, (void*)m->mm_ws, (void*)m->mm_tickets, (void*)m->dec_part, (void*)m->dec_tickets, (void*)m->dec_sync,
                     (void*)m->ch_a, (void*)m->ch_b, (void*)m->ch_ss,
-                    (void*)m->staging, (void*)m->staging8})
+                    (void*)m->staging, (void*)m->staging8, (void*)m->d_track})
         if (p) cudaFree(p);
     if (m->h_in) cudaFreeHost(m->h_in);
     if (m->h_logits) cudaFreeHost(m->h_logits);
@@ -1232,6 +1266,25 @@ int neko_model_stage(neko_model* m, int n, const int* slots, const int* tokens, 
     CK(cudaMemcpyAsync(m->d_tokens, m->h_in, size_t(n) * 4, cudaMemcpyHostToDevice, m->stream), "stage");
     CK(cudaMemcpyAsync(m->d_slots, m->h_in + n, size_t(n) * 4, cudaMemcpyHostToDevice, m->stream), "stage");
     CK(cudaMemcpyAsync(m->d_pos, m->h_in + 2 * n, size_t(n) * 4, cudaMemcpyHostToDevice, m->stream), "stage");
+    if (m->track_steps) {
+        // the staged token is the engine's first sample (engine.cpp:121-124): a stop id ends the sequence before
+        // any step, else it is the first logged token
+        const size_t S = size_t(m->cfg.max_seqs);
+        std::vector<int> cnt(S, 0), state(S, 0), frozen(2 * S, 0), first(S, 0);
+        for (int i = 0; i < n; i++) {
+            const bool stop = std::find(m->stop_ids.begin(), m->stop_ids.end(), tokens[i]) != m->stop_ids.end();
+            cnt[i] = stop ? 0 : 1;
+            state[i] = stop ? 1 : (m->track_steps <= 1 ? 0 : -1);
+            frozen[2 * i] = tokens[i];
+            frozen[2 * i + 1] = pos[i];
+            first[i] = tokens[i];
+        }
+        int* t = m->d_track + NEKO_MAX_STOP_IDS;
+        CK(cudaMemcpyAsync(t, cnt.data(), S * 4, cudaMemcpyHostToDevice, m->stream), "stage");
+        CK(cudaMemcpyAsync(t + S, state.data(), S * 4, cudaMemcpyHostToDevice, m->stream), "stage");
+        CK(cudaMemcpyAsync(t + 2 * S, frozen.data(), 2 * S * 4, cudaMemcpyHostToDevice, m->stream), "stage");
+        CK(cudaMemcpyAsync(t + 4 * S, first.data(), S * 4, cudaMemcpyHostToDevice, m->stream), "stage");
+    }
     CK(cudaStreamSynchronize(m->stream), "stage");
     return NEKO_OK;
 }
@@ -1242,7 +1295,63 @@ int neko_model_step(neko_model* m, int n, int max_pos, void* stream) {
     if (n <= 0 || n > m->cfg.max_rows || n > m->cfg.max_seqs) return fail(m, NEKO_ERR_ARG, "step: bad count");
     if (max_pos < 0 || max_pos >= m->cfg.context) return fail(m, NEKO_ERR_ARG, "step: context overflow");
     Guard g(m->device);
-    return run_step(m, n, n, true, max_pos, true, true, static_cast<cudaStream_t>(stream));
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (const int rc = run_step(m, n, n, true, max_pos, true, true, st); rc != NEKO_OK || !m->track_steps) return rc;
+    const int S = m->cfg.max_seqs;
+    int* t = m->d_track;
+    CK(launch_ex(track_kernel, dim3((n + 127) / 128), dim3(128), 0, st, false, m->d_tokens, m->d_pos, n, t,
+                 int(m->stop_ids.size()), t + NEKO_MAX_STOP_IDS, t + NEKO_MAX_STOP_IDS + S,
+                 t + NEKO_MAX_STOP_IDS + 2 * S, t + NEKO_MAX_STOP_IDS + 4 * S, m->track_steps, S),
+       "track");
+    return NEKO_OK;
+}
+
+int neko_model_set_stop(neko_model* m, const int* stop_ids, int n_stop, int max_new) {
+    if (!m) return NEKO_ERR_ARG;
+    if (n_stop < 0 || n_stop > NEKO_MAX_STOP_IDS || max_new < 0 || (n_stop > 0 && !stop_ids))
+        return fail(m, NEKO_ERR_ARG, "set_stop: bad argument");
+    for (int i = 0; i < n_stop; i++)
+        if (stop_ids[i] < 0 || stop_ids[i] >= m->V) return fail(m, NEKO_ERR_ARG, "set_stop: stop id out of range");
+    Guard g(m->device);
+    CK(cudaDeviceSynchronize(), "set_stop");  // no step may still use the old arrays
+    cudaFree(m->d_track);
+    m->d_track = nullptr;
+    m->track_steps = 0;
+    m->stop_ids.clear();
+    if (max_new == 0) return NEKO_OK;
+    const size_t S = size_t(m->cfg.max_seqs);
+    CK(cudaMalloc(&m->d_track, (NEKO_MAX_STOP_IDS + 4 * S + size_t(max_new) * S) * sizeof(int)), "set_stop");
+    CK(cudaMemset(m->d_track, 0, (NEKO_MAX_STOP_IDS + 2 * S) * sizeof(int)), "set_stop");
+    // every sequence counts as finished (reason 0, nothing logged, frozen at token 0 position 0) until staged
+    CK(cudaMemset(m->d_track + NEKO_MAX_STOP_IDS + 2 * S, 0, 2 * S * sizeof(int)), "set_stop");
+    m->stop_ids.assign(stop_ids, stop_ids + n_stop);
+    if (n_stop)
+        CK(cudaMemcpy(m->d_track, stop_ids, size_t(n_stop) * sizeof(int), cudaMemcpyHostToDevice), "set_stop");
+    m->track_steps = max_new;
+    return NEKO_OK;
+}
+
+int neko_model_generated(neko_model* m, int n, int* tokens, int* counts, int* reasons) {
+    if (!m || n <= 0 || n > m->cfg.max_seqs) return NEKO_ERR_ARG;
+    if (!m->track_steps) return fail(m, NEKO_ERR_ARG, "generated: call neko_model_set_stop first");
+    Guard g(m->device);
+    CK(cudaDeviceSynchronize(), "generated");
+    if (unsigned d = read_device_error(true)) {
+        decode_reset(m);
+        return fail(m, NEKO_ERR_DEVICE, "kernel reported device error " + std::to_string(d));
+    }
+    const size_t S = size_t(m->cfg.max_seqs), L = size_t(m->track_steps);
+    std::vector<int> h(4 * S + L * S);
+    CK(cudaMemcpy(h.data(), m->d_track + NEKO_MAX_STOP_IDS, h.size() * sizeof(int), cudaMemcpyDeviceToHost),
+       "generated");
+    for (int i = 0; i < n; i++) {
+        const int c = h[size_t(i)];
+        if (counts) counts[i] = c;
+        if (reasons) reasons[i] = h[S + size_t(i)];
+        if (tokens)
+            for (size_t j = 0; j < L; j++) tokens[size_t(i) * L + j] = int(j) < c ? h[4 * S + j * S + size_t(i)] : -1;
+    }
+    return NEKO_OK;
 }
 
 int neko_model_tokens(neko_model* m, int n, int* tokens, int* pos) {

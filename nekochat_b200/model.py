@@ -150,6 +150,22 @@ class Model:
         self._check(lib().neko_model_tokens(self.h, n, _p(t), _p(p)), "tokens")
         return t, p
 
+    def set_stop(self, stop_ids, max_new):
+        """Stop ids and token budget for the device greedy loop (Engine::generate's loop on the device);
+        max_new = 0 turns it off."""
+        ids = np.ascontiguousarray(stop_ids, dtype=np.int32)
+        self._check(lib().neko_model_set_stop(self.h, _p(ids) if len(ids) else None, len(ids), max_new), "set_stop")
+        self._max_new = max_new
+
+    def generated(self, n):
+        """(list of n int32 arrays of generated tokens, reasons: 0 max_new, 1 stop id, -1 running)."""
+        L = getattr(self, "_max_new", 0)
+        t = np.empty((n, L), np.int32)
+        c = np.empty(n, np.int32)
+        r = np.empty(n, np.int32)
+        self._check(lib().neko_model_generated(self.h, n, _p(t), _p(c), _p(r)), "generated")
+        return [t[i, :c[i]].copy() for i in range(n)], r
+
     def set_debug(self, layers, stage=0):
         """Model::setDebugLayers(n, stage) (model.h:101): forward() then returns the hidden states after n layers
         (stage 0) or the intermediate after `stage` inside layer n; n < 0 restores logits."""

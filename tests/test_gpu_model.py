@@ -287,3 +287,56 @@ def test_fp8_checkpoint_weights_load_like_f32(fmt):
         b.set_tensor_fp8("layers.0.mlp.down_proj.weight", np.zeros((8, 8), np.uint8), np.ones((1, 1), np.float32))
     a.close()
     b.close()
+
+
+def engine_turn(stream, stops, max_new):
+    """Engine::generate's loop (engine.cpp:120-134) over a greedy token stream: (tokens, stop reason)."""
+    out = []
+    for t in stream:
+        if t in stops:
+            return out, 1
+        out.append(t)
+        if len(out) == max_new:
+            return out, 0
+    return out, -1
+
+
+def test_device_loop_stop_ids_follow_engine_rules():
+    """neko_model_set_stop: the device greedy loop logs each sequence's tokens and ends it at a stop id (the
+    staged first token included) or after max_new tokens, exactly as the engine's loop would over the same greedy
+    streams; finished sequences stay at their token and position while the others keep decoding."""
+    s = workload.shape("qwen3-tiny")
+    m = nmodel.Model(s, FP8, context=128, max_seqs=4, max_rows=64).load(workload.weights(s, seed=8))
+    n, K, max_new = 3, 14, 9
+    prompts = [workload.prompt(s, 10 + 3 * i, seed=20 + i) for i in range(n)]
+    pos0 = [len(p) for p in prompts]
+
+    def prefill():
+        return [int(np.argmax(m.forward(p, 0, slot=i))) for i, p in enumerate(prompts)]
+
+    first = prefill()
+    m.stage(list(range(n)), first, pos0)
+    streams = [[t] for t in first]
+    for _ in range(K):
+        m.step(n, max(pos0) + K)
+        t, _ = m.tokens(n)
+        for i in range(n):
+            streams[i].append(int(t[i]))
+    stops = sorted({streams[0][5], first[2]})
+    m.set_stop(stops, max_new)
+    assert prefill() == first
+    m.stage(list(range(n)), first, pos0)
+    for _ in range(K):
+        m.step(n, max(pos0) + K)
+    got, reasons = m.generated(n)
+    for i in range(n):
+        want, why = engine_turn(streams[i], set(stops), max_new)
+        assert got[i].tolist() == want, f"sequence {i}"
+        assert reasons[i] == why, f"sequence {i}"
+    assert reasons[0] == 1 and reasons[2] == 1 and len(got[2]) == 0
+    t, p = m.tokens(n)
+    assert int(t[2]) == first[2] and int(p[2]) == pos0[2]  # frozen at its staged token and position
+    m.set_stop([], 0)
+    with pytest.raises(nb.NekoError):
+        m.generated(n)
+    m.close()
