@@ -90,3 +90,73 @@ class SlotGenerator:
         if keep_logits:
             stats["logits"] = seen
         return out, stats
+
+
+class BatchGenerator:
+    """Engine::generate for several slots at once. Each slot's prompt runs with the engine's prefix reuse and
+    prefill chunking (as SlotGenerator); then every slot decodes together on the device: neko_model_stage +
+    neko_model_step with the stop ids and token budget of neko_model_set_stop, with no per-token host round trip.
+    The device phase stops one position short of the smallest remaining context (a step cannot advance past the
+    last position); slots still running then finish on the host one token per forward, with the engine's
+    context-full stop (reason 3)."""
+
+    def __init__(self, model, stop_ids=(), eos=0):
+        self.m = model
+        self.stop_ids = [int(t) for t in stop_ids]
+        self.eos = eos
+        self.cached = {}  # slot -> the tokens its KV cache holds
+
+    def generate(self, prompts, max_new):
+        """prompts: {slot: token list}. Returns {slot: (generated tokens, stats dict as SlotGenerator's)}."""
+        ctx = self.m.cfg.context
+        slots = sorted(prompts)
+        firsts, pos, stats = [], [], {}
+        for slot in slots:
+            prompt = fit_prompt(prompts[slot], ctx, self.eos)
+            common = common_prefix(self.cached.get(slot, []), prompt)
+            cached = self.cached.get(slot, [])[:common]
+            for b, e in prefill_chunks(common, len(prompt), min(MAX_BATCH, self.m.cfg.max_rows)):
+                logits = self.m.forward(np.asarray(prompt[b:e], np.int32), len(cached), slot)
+                cached.extend(prompt[b:e])
+            self.cached[slot] = cached
+            firsts.append(int(np.argmax(logits)))
+            pos.append(len(cached))
+            stats[slot] = {"prompt_tokens": len(prompt), "reused_tokens": common}
+        if max_new <= 0:
+            return {s: ([], dict(stats[s], generated_tokens=0, stop_reason=0)) for s in slots}
+        n = len(slots)
+        steps = max(0, min(max_new - 1, min(ctx - 1 - p for p in pos)))
+        self.m.set_stop(self.stop_ids, max_new)
+        self.m.stage(slots, firsts, pos)
+        for k in range(steps):
+            self.m.step(n, max(pos) + k)
+        outs, reasons = self.m.generated(n)
+        self.m.set_stop([], 0)
+        result = {}
+        for i, slot in enumerate(slots):
+            out, why = [int(t) for t in outs[i]], int(reasons[i])
+            cached = self.cached[slot]
+            if why == 1:
+                cached.extend(out)          # every logged token was run
+            elif why == 0:
+                cached.extend(out[:-1])     # the last one never runs
+            else:                           # running: all but the last logged token were run on the device
+                cached.extend(out[:-1])
+                why = self._finish(slot, out, cached, max_new, ctx)
+            result[slot] = (out, dict(stats[slot], generated_tokens=len(out), stop_reason=why))
+        return result
+
+    def _finish(self, slot, out, cached, max_new, ctx):
+        """The rest of the engine's loop (engine.cpp:122-137) for one slot whose last token is not yet run."""
+        stops = set(self.stop_ids)
+        while True:
+            if len(cached) >= ctx:
+                return 3
+            if len(out) == max_new:
+                return 0
+            logits = self.m.forward(np.array([out[-1]], np.int32), len(cached), slot)
+            cached.append(out[-1])
+            nxt = int(np.argmax(logits))
+            if nxt in stops:
+                return 1
+            out.append(nxt)

@@ -340,3 +340,55 @@ def test_device_loop_stop_ids_follow_engine_rules():
     with pytest.raises(nb.NekoError):
         m.generated(n)
     m.close()
+
+
+def test_batch_generator_engine_semantics():
+    """BatchGenerator: three slots decoding together on the device give each slot exactly the engine's turn over
+    the plain greedy stream of the same batch (stop ids, max_new); a slot near the end of its context finishes on
+    the host with the engine's context-full stop; a second turn reuses each slot's cached prefix."""
+    from nekochat_b200.generate import BatchGenerator
+    s = workload.shape("qwen3-tiny")
+    tensors = list(workload.weights(s, seed=14, perturb=True))
+    prompts = {i: [int(t) for t in workload.prompt(s, 12 + 5 * i, seed=60 + i)] for i in range(3)}
+    K, max_new = 12, 10
+    # the plain streams: same batch, plain device steps read back one by one
+    from nekochat_b200.generate import prefill_chunks
+    b = nmodel.Model(s, FP8, context=96, max_seqs=3, max_rows=16).load(tensors)
+    first = []
+    for i in range(3):  # the generator's chunks, so the KV cache is bit-identical
+        for lo, hi in prefill_chunks(0, len(prompts[i]), 16):
+            lg = b.forward(np.array(prompts[i][lo:hi], np.int32), lo, slot=i)
+        first.append(int(np.argmax(lg)))
+    pos0 = [len(prompts[i]) for i in range(3)]
+    b.stage([0, 1, 2], first, pos0)
+    streams = [[t] for t in first]
+    for k in range(K):
+        b.step(3, max(pos0) + k)
+        t, _ = b.tokens(3)
+        for i in range(3):
+            streams[i].append(int(t[i]))
+    b.close()
+    stops = [streams[1][4]] if streams[1][4] not in streams[1][:4] else []
+    a = nmodel.Model(s, FP8, context=96, max_seqs=3, max_rows=16).load(tensors)
+    g = BatchGenerator(a, stop_ids=stops)
+    res = g.generate(prompts, max_new)
+    for i in range(3):
+        want, why = engine_turn(streams[i], set(stops), max_new)
+        out, st = res[i]
+        assert out == want and st["stop_reason"] == why, f"slot {i}"
+        assert st["reused_tokens"] == 0
+    # second turn: each prompt extends the first turn's prompt and reply
+    p2 = {i: prompts[i] + res[i][0] + [5, 6] for i in range(3)}
+    res2 = g.generate(p2, 3)
+    for i in range(3):
+        out1, st1 = res[i]
+        ran = len(out1) if st1["stop_reason"] == 1 else len(out1) - 1
+        assert res2[i][1]["reused_tokens"] == len(prompts[i]) + ran
+        assert len(res2[i][0]) == res2[i][1]["generated_tokens"] <= 3
+    a.close()
+    # context-full: a 40-position context and a 30-token prompt give 40 - 30 + 1 tokens, stop reason 3
+    c = nmodel.Model(s, FP8, context=40, max_seqs=2, max_rows=16).load(tensors)
+    res3 = BatchGenerator(c).generate({0: prompts[0], 1: [int(t) for t in workload.prompt(s, 30, seed=70)]}, 20)
+    assert res3[1][1]["stop_reason"] == 3 and len(res3[1][0]) == 40 - 30 + 1
+    assert res3[0][1]["stop_reason"] == 0 and len(res3[0][0]) == 20
+    c.close()
