@@ -361,21 +361,26 @@ def run_ours(args):
     # end to end through the host API (host token ids in, host logits out, every step)
     e2e = None
     if e2e_on:
-        toks, p0 = m.tokens(B)
+        # the same positions (and so the same greedy chain) as the device-resident leg: restart at the prompt's end
+        m.tokens(B)
+        toks, p0 = first.copy(), pos.copy()
         h2d = B * 3 * 4
         d2h = B * s["vocab"] * 4 + B * 4
         tok = toks.copy()
+        lg_host = np.empty((B, s["vocab"]), np.float32)  # one host logits buffer, reused like the engine's
         for k in range(warm):
-            _, tok = m.decode(slots, tok, p0 + k)
+            _, tok = m.decode(slots, tok, p0 + k, out=lg_host)
         barrier(world)
         t0 = time.perf_counter()
         for k in range(steps):
-            lg, tok = m.decode(slots, tok, p0 + warm + k)
+            lg, tok = m.decode(slots, tok, p0 + warm + k, out=lg_host)
         t_e2e = reduce_max(time.perf_counter() - t0, world)
         e2e = {"value": world * B * steps / t_e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h,
-               "path": "neko_model_decode: pinned-staged H2D of token/slot/position, CUDA graph step, D2H of the "
-                       "full logits and the greedy token, host synchronisation, every step"}
+               "positions": "the device-resident leg's (the same greedy chain from the prompt's end)",
+               "path": "neko_model_decode: pinned-staged H2D of token/slot/position (one copy), CUDA graph step, "
+                       "D2H of the full logits into one reused host buffer and the greedy token, host "
+                       "synchronisation, every step"}
 
     roof = None
     if rank == 0 and not args.profile:

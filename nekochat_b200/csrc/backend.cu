@@ -30,6 +30,10 @@ std::string cuda_msg(cudaError_t e, const char* what) {
     return std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
 }
 
+cudaError_t enqueue_device_error_read(unsigned* host, cudaStream_t st) {
+    return cudaMemcpyFromSymbolAsync(host, g_device_error, sizeof(unsigned), 0, cudaMemcpyDeviceToHost, st);
+}
+
 unsigned read_device_error(bool clear) {
     unsigned v = 0;
     if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof v) != cudaSuccess) return 0;

@@ -156,6 +156,7 @@ struct neko_model {
     int* h_in = nullptr;     // tokens | slots | pos | outrows  (4 * max_rows)
     float* h_logits = nullptr;
     int* h_argmax = nullptr;
+    unsigned* h_err = nullptr;  // the device error flag, read with each synchronous step
     // weights
     Mat embed;               // also the tied LM head
     float* normf = nullptr;  // Qwen3 final RMSNorm / GPT-2 ln_f gamma
@@ -808,8 +809,12 @@ void decode_reset(neko_model* m) {
 }
 
 int wait_model(neko_model* m) {
-    cudaError_t e = cudaStreamSynchronize(m->stream);
+    // the error flag rides on the step's own stream and synchronisation (no second blocking copy per step)
+    *m->h_err = 0;
+    cudaError_t e = enqueue_device_error_read(m->h_err, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
     if (e != cudaSuccess) return fail(m, NEKO_ERR_CUDA, cuda_msg(e, "step"));
+    if (*reinterpret_cast<volatile unsigned*>(m->h_err) == 0) return NEKO_OK;
     if (unsigned d = read_device_error(true)) {
         decode_reset(m);
         return fail(m, NEKO_ERR_DEVICE, "kernel reported device error " + std::to_string(d));
@@ -900,11 +905,14 @@ neko_model* neko_model_create(int device, const neko_model_config* cfg, char* er
     };
     if (falloc(&m->x, R * m->C) || falloc(&m->xn, nout * m->C) || falloc(&m->qkv, R * m->QW) ||
         falloc(&m->att, R * m->H * m->hd) || falloc(&m->h, R * std::max(m->F, m->UPW)) || falloc(&m->hx, nout * m->C) ||
-        falloc(&m->logits, nout * size_t(m->V)) || ialloc(&m->d_tokens, nout) || ialloc(&m->d_slots, nout) ||
-        ialloc(&m->d_pos, nout) || ialloc(&m->d_argmax, nout) || ialloc(&m->d_outrows, nout) ||
+        falloc(&m->logits, nout * size_t(m->V)) || ialloc(&m->d_tokens, 3 * nout) ||
+        ialloc(&m->d_argmax, nout) || ialloc(&m->d_outrows, nout) ||
         cudaMalloc(&m->d_keys, nout * sizeof(unsigned long long)) != cudaSuccess)
         return bail(m, "workspace allocation failed");
     cudaMemset(m->d_keys, 0, nout * sizeof(unsigned long long));
+    // tokens | slots | positions in one block (nout apart), so a decode step's inputs arrive in one copy
+    m->d_slots = m->d_tokens + nout;
+    m->d_pos = m->d_tokens + 2 * nout;
     int64_t pf = 0, tk = 0;
     attention_scratch(int(R), m->H, m->KV, m->hd, c.context - 1, &pf, &tk, true);
     // fewer rows split more: size for the worst case over every row count 1..R
@@ -969,7 +977,7 @@ neko_model* neko_model_create(int device, const neko_model_config* cfg, char* er
         cudaMemset(m->dec_sync, 0, size_t(m->dec_sync_n) * 4);
     }
     if (cudaMallocHost(&m->h_in, 4 * nout * sizeof(int)) || cudaMallocHost(&m->h_logits, nout * size_t(m->V) * 4) ||
-        cudaMallocHost(&m->h_argmax, nout * sizeof(int)))
+        cudaMallocHost(&m->h_argmax, nout * sizeof(int)) || cudaMallocHost(&m->h_err, sizeof(unsigned)))
         return bail(m, "pinned host allocation failed");
     if (m->qwen) {
         std::vector<float> t = rope_table(c.context, m->hd, c.rope_theta);
@@ -1003,8 +1011,8 @@ void neko_model_destroy(neko_model* m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     for (void* p : {(void*)m->warena, (void*)m->kc, (void*)m->vc, (void*)m->x, (void*)m->xn, (void*)m->qkv,
-                    (void*)m->att, (void*)m->h, (void*)m->hx, (void*)m->logits, (void*)m->d_tokens, (void*)m->d_slots,
-                    (void*)m->d_pos, (void*)m->d_argmax, (void*)m->d_outrows, (void*)m->d_keys, (void*)m->part,
+                    (void*)m->att, (void*)m->h, (void*)m->hx, (void*)m->logits, (void*)m->d_tokens,
+                    (void*)m->d_argmax, (void*)m->d_outrows, (void*)m->d_keys, (void*)m->part,
                     (void*)m->tickets, (void*)m->mm_ws, (void*)m->mm_tickets, (void*)m->dec_part, (void*)m->dec_tickets, (void*)m->dec_sync,
                     (void*)m->ch_a, (void*)m->ch_b, (void*)m->ch_ss,
                     (void*)m->staging, (void*)m->staging8, (void*)m->d_track})
@@ -1012,6 +1020,7 @@ void neko_model_destroy(neko_model* m) {
     if (m->h_in) cudaFreeHost(m->h_in);
     if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->h_argmax) cudaFreeHost(m->h_argmax);
+    if (m->h_err) cudaFreeHost(m->h_err);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -1231,13 +1240,13 @@ int neko_model_decode(neko_model* m, int n, const int* slots, const int* tokens,
         max_pos = std::max(max_pos, pos[i]);
     }
     Guard g(m->device);
+    // the device block's layout (tokens | slots | positions, nout apart) in the pinned staging: one copy
+    const size_t nout = size_t(m->d_slots - m->d_tokens);
     int* hi = m->h_in;
     std::memcpy(hi, tokens, size_t(n) * 4);
-    std::memcpy(hi + n, slots, size_t(n) * 4);
-    std::memcpy(hi + 2 * n, pos, size_t(n) * 4);
-    CK(cudaMemcpyAsync(m->d_tokens, hi, size_t(n) * 4, cudaMemcpyHostToDevice, m->stream), "h2d");
-    CK(cudaMemcpyAsync(m->d_slots, hi + n, size_t(n) * 4, cudaMemcpyHostToDevice, m->stream), "h2d");
-    CK(cudaMemcpyAsync(m->d_pos, hi + 2 * n, size_t(n) * 4, cudaMemcpyHostToDevice, m->stream), "h2d");
+    std::memcpy(hi + nout, slots, size_t(n) * 4);
+    std::memcpy(hi + 2 * nout, pos, size_t(n) * 4);
+    CK(cudaMemcpyAsync(m->d_tokens, hi, (2 * nout + size_t(n)) * 4, cudaMemcpyHostToDevice, m->stream), "h2d");
     if (int rc = run_step(m, n, n, true, max_pos, argmax != nullptr, false, m->stream); rc != NEKO_OK) return rc;
     if (logits)
         CK(cudaMemcpyAsync(m->h_logits, m->logits, size_t(n) * m->V * 4, cudaMemcpyDeviceToHost, m->stream), "d2h");

@@ -277,5 +277,7 @@ cudaError_t decode_clear_abort();  // after a wait of the kernel gave up (device
 std::string cuda_msg(cudaError_t e, const char* what);
 void set_last_error(const std::string& msg);  // the thread-local message behind neko_last_error()
 unsigned read_device_error(bool clear);
+// Copies the device error flag into `host` (pinned) on `st`: read after the stream's own synchronisation
+cudaError_t enqueue_device_error_read(unsigned* host, cudaStream_t st);
 
 }  // namespace neko

@@ -122,13 +122,20 @@ class Model:
             logits = self.forward(tokens[i:i + chunk], pos0 + i, slot)
         return logits
 
-    def decode(self, slots, tokens, pos, want_logits=True):
-        """One decode step for n sequences. Returns (logits [n][vocab] or None, argmax [n])."""
+    def decode(self, slots, tokens, pos, want_logits=True, out=None):
+        """One decode step for n sequences. Returns (logits [n][vocab] or None, argmax [n]). `out`: a float32
+        C-contiguous array of at least n * vocab floats to receive the logits, reused across steps the way the
+        engine reuses its logits vector (engine.cpp:56)."""
         slots = np.ascontiguousarray(slots, dtype=np.int32)
         tokens = np.ascontiguousarray(tokens, dtype=np.int32)
         pos = np.ascontiguousarray(pos, dtype=np.int32)
         n = len(slots)
-        logits = np.empty((n, self.vocab), np.float32) if want_logits else None
+        if out is not None and want_logits:
+            if out.dtype != np.float32 or not out.flags.c_contiguous or out.size < n * self.vocab:
+                raise NekoError("decode: out must be a C-contiguous float32 array of n * vocab floats")
+            logits = out.reshape(-1)[:n * self.vocab].reshape(n, self.vocab)
+        else:
+            logits = np.empty((n, self.vocab), np.float32) if want_logits else None
         am = np.empty(n, np.int32)
         self._check(lib().neko_model_decode(self.h, n, _p(slots), _p(tokens), _p(pos), _p(logits), _p(am)),
                     "decode")
