@@ -367,7 +367,7 @@ def run_ours(args):
         h2d = B * 3 * 4
         d2h = B * s["vocab"] * 4 + B * 4
         tok = toks.copy()
-        lg_host = np.empty((B, s["vocab"]), np.float32)  # one host logits buffer, reused like the engine's
+        lg_host = m.host_logits(B)  # one (pinned) host logits buffer, reused like the engine's
         for k in range(warm):
             _, tok = m.decode(slots, tok, p0 + k, out=lg_host)
         barrier(world)
@@ -379,7 +379,7 @@ def run_ours(args):
                "d2h_bytes_per_step": d2h,
                "positions": "the device-resident leg's (the same greedy chain from the prompt's end)",
                "path": "neko_model_decode: pinned-staged H2D of token/slot/position (one copy), CUDA graph step, "
-                       "D2H of the full logits into one reused host buffer and the greedy token, host "
+                       "D2H of the full logits into one reused pinned host buffer and the greedy token, host "
                        "synchronisation, every step"}
 
     roof = None

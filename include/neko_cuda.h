@@ -233,6 +233,10 @@ int neko_model_tokens(neko_model* m, int n, int* tokens, int* pos);
  * (reason 0). A finished sequence stays at its last token and position, so later steps re-run that row in place
  * and write no KV beyond it. The context limit stays the caller's (max_pos of neko_model_step). max_new = 0 turns
  * it off. At most NEKO_MAX_STOP_IDS ids, each in [0, vocab). */
+/* The runner's pinned host logits buffer (*floats of them; valid until neko_model_destroy). Passed as the
+ * `logits` output of neko_model_forward / neko_model_decode it receives the logits straight from the device
+ * copy, with no second host copy; each call overwrites it, as the engine's forward overwrites its logits vector. */
+float* neko_model_host_logits(neko_model* m, size_t* floats);
 #define NEKO_MAX_STOP_IDS 64
 int neko_model_set_stop(neko_model* m, const int* stop_ids, int n_stop, int max_new);
 /* Synchronises and reads the log of the n staged sequences: tokens [n][max_new] (-1 past each count), counts [n],

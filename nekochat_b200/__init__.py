@@ -104,6 +104,7 @@ _SIGS = {
                                             C.c_int64]),
     "neko_model_finalize": (C.c_int, [_vp]),
     "neko_model_set_stop": (C.c_int, [_vp, _vp, C.c_int, C.c_int]),
+    "neko_model_host_logits": (_vp, [_vp, C.POINTER(C.c_size_t)]),
     "neko_model_generated": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp]),
     "neko_model_forward": (C.c_int, [_vp, C.c_int, _vp, C.c_int, C.c_int, _vp]),
     "neko_model_decode": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp]),

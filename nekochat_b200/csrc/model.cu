@@ -155,6 +155,7 @@ struct neko_model {
     // host pinned staging for the synchronous API
     int* h_in = nullptr;     // tokens | slots | pos | outrows  (4 * max_rows)
     float* h_logits = nullptr;
+    size_t h_logits_floats = 0;
     int* h_argmax = nullptr;
     unsigned* h_err = nullptr;  // the device error flag, read with each synchronous step
     // weights
@@ -976,6 +977,7 @@ neko_model* neko_model_create(int device, const neko_model_config* cfg, char* er
         cudaMemset(m->dec_tickets, 0, size_t(m->dec_tickets_n) * 4);
         cudaMemset(m->dec_sync, 0, size_t(m->dec_sync_n) * 4);
     }
+    m->h_logits_floats = nout * size_t(m->V);
     if (cudaMallocHost(&m->h_in, 4 * nout * sizeof(int)) || cudaMallocHost(&m->h_logits, nout * size_t(m->V) * 4) ||
         cudaMallocHost(&m->h_argmax, nout * sizeof(int)) || cudaMallocHost(&m->h_err, sizeof(unsigned)))
         return bail(m, "pinned host allocation failed");
@@ -1221,7 +1223,7 @@ int neko_model_forward(neko_model* m, int slot, const int* tokens, int T, int po
     const size_t nout = m->debug_layers >= 0 ? size_t(T) * size_t(debug_width(m)) : size_t(m->V);
     CK(cudaMemcpyAsync(m->h_logits, m->logits, nout * 4, cudaMemcpyDeviceToHost, m->stream), "d2h");
     if (int rc = wait_model(m); rc != NEKO_OK) return rc;
-    std::memcpy(logits, m->h_logits, nout * 4);
+    if (logits != m->h_logits) std::memcpy(logits, m->h_logits, nout * 4);
     return NEKO_OK;
 }
 
@@ -1252,7 +1254,7 @@ int neko_model_decode(neko_model* m, int n, const int* slots, const int* tokens,
         CK(cudaMemcpyAsync(m->h_logits, m->logits, size_t(n) * m->V * 4, cudaMemcpyDeviceToHost, m->stream), "d2h");
     if (argmax) CK(cudaMemcpyAsync(m->h_argmax, m->d_argmax, size_t(n) * 4, cudaMemcpyDeviceToHost, m->stream), "d2h");
     if (int rc = wait_model(m); rc != NEKO_OK) return rc;
-    if (logits) std::memcpy(logits, m->h_logits, size_t(n) * m->V * 4);
+    if (logits && logits != m->h_logits) std::memcpy(logits, m->h_logits, size_t(n) * m->V * 4);
     if (argmax) std::memcpy(argmax, m->h_argmax, size_t(n) * 4);
     return NEKO_OK;
 }
@@ -1313,6 +1315,12 @@ int neko_model_step(neko_model* m, int n, int max_pos, void* stream) {
                  t + NEKO_MAX_STOP_IDS + 2 * S, t + NEKO_MAX_STOP_IDS + 4 * S, m->track_steps, S),
        "track");
     return NEKO_OK;
+}
+
+float* neko_model_host_logits(neko_model* m, size_t* floats) {
+    if (!m) return nullptr;
+    if (floats) *floats = m->h_logits_floats;
+    return m->h_logits;
 }
 
 int neko_model_set_stop(neko_model* m, const int* stop_ids, int n_stop, int max_new) {

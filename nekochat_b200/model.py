@@ -157,6 +157,15 @@ class Model:
         self._check(lib().neko_model_tokens(self.h, n, _p(t), _p(p)), "tokens")
         return t, p
 
+    def host_logits(self, rows):
+        """A [rows][vocab] float32 view of the runner's pinned logits buffer: as decode's `out` it takes the
+        logits with no second host copy, and the next call overwrites it."""
+        n = C.c_size_t(0)
+        ptr = lib().neko_model_host_logits(self.h, C.byref(n))
+        if not ptr or rows * self.vocab > n.value:
+            raise NekoError("host_logits: buffer unavailable or too small")
+        return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_float)), shape=(rows, self.vocab))
+
     def set_stop(self, stop_ids, max_new):
         """Stop ids and token budget for the device greedy loop (Engine::generate's loop on the device);
         max_new = 0 turns it off."""

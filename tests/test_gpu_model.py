@@ -392,3 +392,20 @@ def test_batch_generator_engine_semantics():
     assert res3[1][1]["stop_reason"] == 3 and len(res3[1][0]) == 40 - 30 + 1
     assert res3[0][1]["stop_reason"] == 0 and len(res3[0][0]) == 20
     c.close()
+
+
+def test_decode_into_the_pinned_host_logits_buffer():
+    """decode with out = host_logits() (no second host copy) returns the same logits and tokens as decode into a
+    fresh array; the view is overwritten by the next call."""
+    s = workload.shape("qwen3-tiny")
+    m = nmodel.Model(s, FP8, context=64, max_seqs=2, max_rows=16).load(workload.weights(s, seed=4))
+    for i in range(2):
+        m.prefill(workload.prompt(s, 10, seed=80 + i), i)
+    buf = m.host_logits(2)
+    la, aa = m.decode([0, 1], [3, 4], [10, 10])
+    lb, ab = m.decode([0, 1], [3, 4], [10, 10], out=buf)
+    assert lb.ctypes.data == buf.ctypes.data
+    assert np.array_equal(la, lb) and np.array_equal(aa, ab)
+    m.decode([0, 1], [5, 6], [10, 10], out=buf)
+    assert not np.array_equal(buf, la)
+    m.close()
