@@ -228,31 +228,66 @@ def gemv_roofline(model, s, stream, reps=3):
     return nbytes / len(mats), t, reps * len(mats)
 
 
-def cpu_baseline(args, s, tmpdir, h16, steps=8, prompt=32):
-    """The reference engine's CPU backend on this host (oracle/_ref/libneko_ref.so): loadModel with all host
-    threads (the engine's pool caps at 16), a short prompt, then `steps` timed greedy decode steps."""
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            return next((ln.split(":", 1)[1].strip() for ln in f if ln.startswith("model name")), "unknown")
+    except OSError:
+        return "unknown"
+
+
+def reference_decode(s, h16, tmpdir, prompt_len, warm, steps, budget_s=20.0):
+    """The reference engine's CPU backend on this host, on the GPU arm's workload: loadModel (CPU backend, the
+    timing build for this host's ISA level, all host threads up to the engine's pool cap of 16) of an f16
+    checkpoint of `h16`, the same `prompt_len`-token prompt fed in chunks of 64 (Model::kMaxBatch, as
+    Engine::generate feeds it), `warm` untimed greedy steps, then greedy steps at the GPU arm's positions,
+    timed until `steps` are done or `budget_s` has passed (a bounded sample; at least 2 steps). Returns
+    (tok/s, timed steps, description)."""
+    from nekochat_b200 import workload
     from oracle.checkpoint import write_model
-    from oracle.oracle import Reference
-    ref = Reference()
+    from oracle.oracle import Reference, native_build
+    ref = Reference(native=True)
     folder = write_model(os.path.join(tmpdir, "ckpt"), s, h16, dtype=np.float16)
     threads = min(16, os.cpu_count() or 1)
     m = ref.load_model(folder, FMT, threads=threads)
-    from nekochat_b200 import workload
-    toks = workload.prompt(s, prompt)
-    logits = m.forward(toks, 0)
-    tok, pos = int(np.argmax(logits)), prompt
-    logits = m.forward(np.array([tok], np.int32), pos)  # warm-up step
-    tok, pos = int(np.argmax(logits)), pos + 1
-    t0 = time.perf_counter()
-    for _ in range(steps):
+    toks = workload.prompt(s, prompt_len)
+    for i in range(0, prompt_len, 64):
+        logits = m.forward(toks[i:i + 64], i)
+    tok, pos = int(np.argmax(logits)), prompt_len
+    for _ in range(warm):
         logits = m.forward(np.array([tok], np.int32), pos)
         tok, pos = int(np.argmax(logits)), pos + 1
+    p0 = pos
+    k = 0
+    t0 = time.perf_counter()
+    while k < steps and (k < 2 or time.perf_counter() - t0 < budget_s):
+        logits = m.forward(np.array([tok], np.int32), pos)
+        tok, pos = int(np.argmax(logits)), pos + 1
+        k += 1
     dt = time.perf_counter() - t0
     m.close()
-    return {"value": steps / dt, "unit": "tok/s", "cores": threads, "kind": "reference",
-            "sample": f"reference CPU engine (x86 scalar path, {threads} threads), batch 1, {prompt}-token prompt, "
-                      f"{steps} timed greedy decode steps after 1 warm-up; the engine has no multi-sequence "
-                      f"batching, so its aggregate rate equals this single-sequence rate"}
+    build = native_build()[1]
+    desc = (f"reference CPU engine (oracle/_ref/{ref.build}: {build}; x86 portable matmulGeneric path) on "
+            f"{threads} threads of '{cpu_model()}' ({os.cpu_count()} logical CPUs), batch 1, the GPU arm's "
+            f"{prompt_len}-token prompt prefilled in chunks of 64, {warm} warm-up steps, then {k} timed greedy "
+            f"decode steps at positions {p0}..{pos - 1} (a bounded sample of {budget_s:.0f} s at most of the "
+            f"{steps}-step run); the engine runs sequences one at a time, so this is also its aggregate rate")
+    return k / dt, k, threads, desc
+
+
+def random_h16(s, seed=0):
+    """N(0, 0.02) f16 weights from torch's seeded CPU generator (numpy's is ~10x slower here), gains 1, biases 0."""
+    import torch
+    from nekochat_b200 import workload
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for name, shp, kind in workload.tensor_specs(s):
+        if kind == "w":
+            a = (torch.randn(shp, generator=g) * 0.02).half().numpy()
+        else:
+            a = (np.ones if kind == "g" else np.zeros)(shp, np.float16)
+        out.append((name, a))
+    return out
 
 
 # ---------------------------------------------------------------------------------------------- reference arm
@@ -263,51 +298,17 @@ def run_reference(args):
         return
     from nekochat_b200 import workload
     s = workload.shape(SHAPE)
-    import torch
+    prompt_len = args.prompt or PROMPT
     with tempfile.TemporaryDirectory() as tmp:
-        # weights: N(0, 0.02) f16 checkpoint from torch's seeded CPU generator (numpy's is ~10x slower here)
-        g = torch.Generator().manual_seed(0)
-        h16 = []
-        for name, shp, kind in workload.tensor_specs(s):
-            if kind == "w":
-                a = (torch.randn(shp, generator=g) * 0.02).half().numpy()
-            else:
-                a = (np.ones if kind == "g" else np.zeros)(shp, np.float16)
-            h16.append((name, a))
-        n_prompt = 32
-        steps, warm = args.steps, args.warmup
-        from oracle.checkpoint import write_model
-        from oracle.oracle import Reference
-        ref = Reference()
-        folder = write_model(os.path.join(tmp, "ckpt"), s, h16, dtype=np.float16)
-        del h16
-        threads = min(16, os.cpu_count() or 1)
-        m = ref.load_model(folder, FMT, threads=threads)
-        toks = workload.prompt(s, n_prompt)
-        logits = m.forward(toks, 0)
-        tok, pos = int(np.argmax(logits)), n_prompt
-        # bounded sample: at most 24 timed steps per run so K/W-sized runs finish in minutes
-        k = min(steps, 24)
-        w = min(warm, 3)
-        for _ in range(w):
-            logits = m.forward(np.array([tok], np.int32), pos)
-            tok, pos = int(np.argmax(logits)), pos + 1
-        t0 = time.perf_counter()
-        for _ in range(k):
-            logits = m.forward(np.array([tok], np.int32), pos)
-            tok, pos = int(np.argmax(logits)), pos + 1
-        dt = time.perf_counter() - t0
-        m.close()
-    v = k / dt
-    sample = (f"reference CPU engine (oracle/_ref, x86 scalar path, {threads} threads), batch 1, {n_prompt}-token "
-              f"prompt, {w} warm-up + {k} timed greedy decode steps (bounded sample of the {args.steps}-step run); "
-              f"the engine runs sequences one at a time, so this is also its aggregate rate")
+        v, k, threads, sample = reference_decode(s, random_h16(s), tmp, prompt_len, args.warmup, args.steps)
+    B = args.batch
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world, "steps": k,
-        "warmup": w, "ms_per_step": dt / k * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{SHAPE} {FMT_NAME[FMT].lower()} greedy decode, batch 1", "batch": 1,
-                   "prompt": n_prompt},
+        "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{SHAPE} {FMT_NAME[FMT].lower()} (engine {FMT_NAME[FMT]} format), {prompt_len}-token "
+                               f"random prompt, greedy decode, batch {B} per GPU", "batch": B, "prompt": prompt_len,
+                   "positions": [prompt_len + args.warmup, prompt_len + args.warmup + k]},
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -430,9 +431,9 @@ def run_ours(args):
     cpu = None
     if cpu_on:
         with tempfile.TemporaryDirectory() as tmp:
-            try:
-                # bounded sample: fewer steps for the larger shapes (the scalar CPU path takes seconds per token)
-                cpu = cpu_baseline(args, s, tmp, h16, steps=8 if s["embd"] <= 1024 else 3)
+            try:  # the same routine, prompt and positions as --impl reference, on this run's weights
+                v, k, threads, sample = reference_decode(s, h16, tmp, prompt_len, warm, steps)
+                cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample}
             except Exception as e:  # the baseline is reported, never required
                 cpu = {"value": None, "unit": "tok/s", "error": str(e)[:200]}
     m.close()

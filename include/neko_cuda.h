@@ -6,7 +6,7 @@
  *  1. neko_cuda_*   the engine's gpu::ComputeBackend contract (app/architecture/shared/cpp/gpu/compute.h:24-48):
  *                   buffers, upload/download, and dispatch of the nine kernels of compute.h:17 with the same
  *                   parameter blocks the GLSL shaders take. nekochat_b200/csrc/cuda_compute.cpp wraps it as a
- *                   C++ ComputeBackend subclass so Model::startGpu can pick it.
+ *                   C++ ComputeBackend subclass so Model::startGpu (model.cpp:137-148) can pick it.
  *  2. neko_op_*     single operators on device pointers (weight codec, dequant matmul, norms, softmax,
  *                   attention), for the operator sweep and for callers that manage their own memory.
  *  3. neko_model_*  a native GPT-2 / Qwen3 runner built on the same kernels: fused decode steps replayed as

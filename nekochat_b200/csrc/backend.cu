@@ -595,7 +595,7 @@ int neko_op_fp8_block_dequant(const uint8_t* codes, int64_t rows, int64_t cols, 
 
 int neko_op_attention(const float* q, int q_stride, const uint16_t* k_cache, const uint16_t* v_cache, float* out,
                       int T, int n_head, int n_kv, int hd, int pos0, void* stream) {
-    if (!q || !k_cache || !v_cache || !out || T <= 0 || n_kv <= 0 || n_head % n_kv || hd <= 0)
+    if (!q || !k_cache || !v_cache || !out || T <= 0 || !attention_shape_ok(n_head, n_kv, hd))
         return set_err(nullptr, NEKO_ERR_ARG, "attention args");
     AttnArgs a;
     a.q = q;

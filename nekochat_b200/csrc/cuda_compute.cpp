@@ -1,7 +1,7 @@
 // CUDA implementation of the engine's gpu::ComputeBackend (app/architecture/shared/cpp/gpu/compute.h:24-45).
 //
-// This file is written to be added to the engine's own source tree next to vk_compute.cpp / gl_compute.cpp
-// (see INTEGRATION.md): it includes the engine's "gpu/compute.h" and "common.h" and calls the B200 kernels
+// This file is written to be added to the engine's own source tree next to vk_compute.cpp / gl_compute.cpp,
+// with a createCuda() slot in Model::startGpu (model.cpp:137-148): it includes the engine's "gpu/compute.h" and "common.h" and calls the B200 kernels
 // only through the C ABI of libneko_cuda.so (include/neko_cuda.h). Semantics follow the Vulkan backend:
 // buffers are owned by the backend until it is destroyed, every dispatch is ordered after the previous one,
 // flush() submits nothing extra (CUDA streams already run ahead of the host), submitAndWait() blocks until

@@ -797,10 +797,14 @@ void attention_scratch(int rows, int n_head, int n_kv, int hd, int max_pos, int6
     *tickets = int64_t(rows) * n_kv;
 }
 
+bool attention_shape_ok(int n_head, int n_kv, int hd) {
+    return n_kv > 0 && n_head > 0 && n_head % n_kv == 0 && n_head / n_kv <= kMaxGroup && hd > 0 && hd <= kMaxHd &&
+           hd % 8 == 0;
+}
+
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl) {
     if (a.rows <= 0) return cudaSuccess;
-    if (a.n_kv <= 0 || a.n_head % a.n_kv != 0 || a.n_head / a.n_kv > kMaxGroup || a.hd > kMaxHd || (a.hd % 8))
-        return cudaErrorInvalidValue;
+    if (!attention_shape_ok(a.n_head, a.n_kv, a.hd)) return cudaErrorInvalidValue;
     // bulk copies need 16-byte aligned key rows
     if ((a.pos_stride % 8) || (a.head_stride % 8) || (a.slot_stride % 8) ||
         (reinterpret_cast<uintptr_t>(a.kc) & 15) || (reinterpret_cast<uintptr_t>(a.vc) & 15))

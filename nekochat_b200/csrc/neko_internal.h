@@ -228,6 +228,9 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl);
 // cache_rows, so the TMA variant's plan is covered too).
 void attention_scratch(int rows, int n_head, int n_kv, int hd, int max_pos, int64_t* part_floats,
                        int64_t* tickets, bool tma = false);
+// Head counts and head dim the attention kernels take: n_head a multiple of n_kv, at most 8 query heads per
+// KV head, hd a multiple of 8 up to 256.
+bool attention_shape_ok(int n_head, int n_kv, int hd);
 
 // ------------------------------------------------------------------ decode-step kernel (k_decode.cu)
 // One whole decode step (embedding, every layer, final norm, LM head, greedy argmax) of 1..4 sequences in a

@@ -76,10 +76,13 @@ using namespace neko;
 extern "C" int neko_op_attention_noalloc(const float* q, int q_stride, const uint16_t* k_cache,
                                          const uint16_t* v_cache, float* out, int T, int n_head, int n_kv, int hd,
                                          int pos0, void* stream) {
-    if (!q || !k_cache || !v_cache || !out || T <= 0 || n_kv <= 0 || n_head % n_kv || hd <= 0 || pos0 < 0)
-        return noalloc_fail(NEKO_ERR_ARG, "attention_noalloc: bad arguments");
+    if (!q || !k_cache || !v_cache || !out || T <= 0 || pos0 < 0 || !attention_shape_ok(n_head, n_kv, hd))
+        return noalloc_fail(NEKO_ERR_ARG, "attention_noalloc: bad arguments (at most 8 query heads per KV head, "
+                                          "head_dim a multiple of 8 up to 256)");
     int64_t need_part = 0, need_tickets = 0;
     attention_scratch(T, n_head, n_kv, hd, pos0 + T - 1, &need_part, &need_tickets);
+    // A single-split plan uses no scratch at all (no partials, no tickets), whatever its size.
+    if (need_part == 0) need_tickets = 0;
     if (need_part > kNoAllocPartFloats || need_tickets > kNoAllocTickets)
         return noalloc_fail(NEKO_ERR_UNSUPPORTED,
                             "attention_noalloc: this shape needs " + std::to_string(need_part) +
@@ -89,8 +92,10 @@ extern "C" int neko_op_attention_noalloc(const float* q, int q_stride, const uin
     if (cudaError_t e = scratch_for_current_device(&s); e != cudaSuccess)
         return noalloc_fail(NEKO_ERR_CUDA, cuda_msg(e, "attention_noalloc scratch address"));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (cudaError_t e = cudaMemsetAsync(s.tickets, 0, size_t(need_tickets) * sizeof(unsigned), st); e != cudaSuccess)
-        return noalloc_fail(NEKO_ERR_CUDA, cuda_msg(e, "attention_noalloc ticket clear"));
+    if (need_tickets) {
+        if (cudaError_t e = cudaMemsetAsync(s.tickets, 0, size_t(need_tickets) * sizeof(unsigned), st); e != cudaSuccess)
+            return noalloc_fail(NEKO_ERR_CUDA, cuda_msg(e, "attention_noalloc ticket clear"));
+    }
     AttnArgs a;
     a.q = q;
     a.q_stride = q_stride;

@@ -73,10 +73,11 @@ class Model:
         self._check(lib().neko_model_set_tensor_device(self.h, name.encode(), C.c_void_p(t.data_ptr()), rows, cols),
                     f"set_tensor_device {name}")
 
-    def load_random_device(self, seed=0, host_copy=None):
+    def load_random_device(self, seed=0, host_copy=None, f16_exact=False):
         """Random-init weights generated on the GPU (torch, seeded): N(0, 0.02) matrices, unit norm gains, zero
         biases, in workload.tensor_specs order. host_copy(name, f16 numpy array) receives each tensor for a CPU
-        baseline checkpoint when given."""
+        baseline checkpoint when given. f16_exact rounds every tensor through f16 before it is loaded, so the
+        runner's weights equal the f16 checkpoint written from host_copy (parity runs against the reference)."""
         import torch
         dev = torch.device("cuda", self.device)
         g = torch.Generator(device=dev).manual_seed(seed)
@@ -87,6 +88,8 @@ class Model:
                 t = torch.ones(shp, device=dev, dtype=torch.float32)
             else:
                 t = torch.zeros(shp, device=dev, dtype=torch.float32)
+            if f16_exact:
+                t = t.half().float()
             self.set_tensor_device(name, t)
             if host_copy is not None:
                 host_copy(name, t.half().cpu().numpy())

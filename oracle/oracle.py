@@ -183,14 +183,46 @@ class Restatement(_Ops):
         return np.array([self._h(float(v)) for v in a], np.uint16)
 
 
+def host_isa_level():
+    """The x86-64 ISA level of this host's CPU from /proc/cpuinfo: 4 (AVX-512 F/BW/CD/DQ/VL), 3 (AVX2 + FMA +
+    BMI2), else 1."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            flags = next((ln.split(":", 1)[1].split() for ln in f if ln.startswith("flags")), [])
+    except OSError:
+        return 1
+    fl = set(flags)
+    if {"avx2", "fma", "bmi2", "movbe"} <= fl:
+        if {"avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl"} <= fl:
+            return 4
+        return 3
+    return 1
+
+
+def native_build():
+    """(library name, description) of the reference CPU engine built for timing on this host: the x86-64-v4 or
+    -v3 build of oracle/Makefile's ref_native target, or the portable checker build when neither fits."""
+    lvl = host_isa_level()
+    for v in (4, 3):
+        name = f"libneko_ref_native_v{v}.so"
+        if lvl >= v and os.path.exists(os.path.join(HERE, "_ref", name)):
+            return name, f"-O3 -march=x86-64-v{v} (FMA contraction on)"
+    return "libneko_ref.so", "-O3, no -march, -ffp-contract=off (portable checker build)"
+
+
 class Reference(_Ops):
     """The reference engine compiled from its own sources (oracle/_ref). cuda=True loads the variant whose
     first GPU backend slot is the B200 backend (needs nekochat_b200/libneko_cuda.so and a GPU)."""
 
     prefix = "ref_"
 
-    def __init__(self, cuda=False, path=None):
+    def __init__(self, cuda=False, path=None, native=False):
+        """native=True loads the timing build for this host's ISA level (native_build()) instead of the
+        deterministic checker; use it only to time the reference, never to check results."""
         name = "libneko_ref_cuda.so" if cuda else "libneko_ref.so"
+        if native and not cuda and path is None:
+            name = native_build()[0]
+        self.build = name
         path = path or os.path.join(HERE, "_ref", name)
         if not os.path.exists(path):
             raise FileNotFoundError(f"{path} is missing: build it with `make -C oracle` where the reference exists")

@@ -5,7 +5,8 @@ forbid allocator calls once decoding has started).
 
 Checked through the C ABI against the allocating entry point neko_op_attention, on two calls in a row (the
 second must not be affected by what the first left in the shared scratch), with the tolerance the other
-attention tests use. This file is collected last so a failure here cannot hide another test's result."""
+attention tests use, and against the C restatement of the reference's cpu::attention (cpu_ops.cpp:544-575). This
+file is collected last so a failure here cannot hide another test's result."""
 import ctypes as C
 
 import numpy as np
@@ -13,6 +14,11 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-3
+
+
+def _oracle(q, kc, vc, H, KV, hd, T, pos0):
+    from oracle.oracle import Restatement
+    return Restatement().attention(q, q.shape[1], kc.view(np.uint16), vc.view(np.uint16), T, H, KV, hd, pos0)
 
 
 def _case(rng, H, KV, hd, T, pos0):
@@ -47,6 +53,36 @@ def test_noalloc_matches_allocating_attention_twice(H, KV, hd, T, pos0):
         assert np.all(np.isfinite(got))
         d = np.abs(got - want)
         assert np.all(d <= TOL * (1 + np.abs(want))), f"call {call}: max err {d.max()}"
+        ref = _oracle(q, kc, vc, H, KV, hd, T, pos0 + 37 * call)
+        d = np.abs(got - ref)
+        assert np.all(d <= TOL * (1 + np.abs(ref))), f"call {call}: max err vs oracle {d.max()}"
+
+
+def test_noalloc_single_split_needs_no_scratch():
+    """Many rows x KV heads (more than the fixed ticket count) in a single-split plan: no scratch is used, so the
+    call runs, and matches the allocating entry point and the oracle."""
+    import torch
+    H, KV, hd, T, pos0 = 16, 8, 128, 1025, 0
+    q, kc, vc = _case(np.random.default_rng(3), H, KV, hd, T, pos0)
+    want = _run("neko_op_attention", torch, q, kc, vc, H, KV, hd, T, pos0)
+    got = _run("neko_op_attention_noalloc", torch, q, kc, vc, H, KV, hd, T, pos0)
+    d = np.abs(got - want)
+    assert np.all(d <= TOL * (1 + np.abs(want))), f"max err {d.max()}"
+    for r in (0, 1, 511, 1024):  # the oracle is a scalar loop: row r alone is query r at position r
+        ref = _oracle(q[r:r + 1], kc, vc, H, KV, hd, 1, r)[0]
+        d = np.abs(got[r] - ref)
+        assert np.all(d <= TOL * (1 + np.abs(ref))), f"row {r}: max err vs oracle {d.max()}"
+
+
+def test_noalloc_rejects_unsupported_group_as_bad_argument():
+    """Sixteen query heads per KV head is beyond the kernels: a bad argument, reported before any work."""
+    import torch
+    import nekochat_b200 as nb
+    tiny = torch.zeros(16, device="cuda")
+    rc = nb.lib().neko_op_attention_noalloc(C.c_void_p(tiny.data_ptr()), 18 * 64, C.c_void_p(tiny.data_ptr()),
+                                            C.c_void_p(tiny.data_ptr()), C.c_void_p(tiny.data_ptr()), 1, 16, 1, 64,
+                                            0, None)
+    assert rc == -1  # NEKO_ERR_ARG
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
