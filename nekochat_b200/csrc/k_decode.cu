@@ -8,17 +8,27 @@
 //  * every CTA owns a fixed row range of every matrix; its producer warp streams those rows, phase after phase
 //    and layer after layer, through a ring of shared-memory slots with cp.async.bulk (TMA), gated only by free
 //    slots, so the next matrices are already on chip while the current phase waits for its inputs;
-//  * phases (qkv, attention, o_proj, gate/up, down, LM head) hand their activations over through global memory;
-//    a phase waits on a counter that the producing phase's CTAs bump after their writes (release / acquire at
-//    GPU scope), so a step costs one on-chip hand-off per phase instead of a launch;
-//  * attention folds in the per-head QK RMSNorm, RoPE and the f16 KV store (split-KV items, merged by the last
-//    item of a (sequence, KV head) through a ticket).
-// The dot products, activation staging, norm prologue and epilogues are the ones of the GEMV kernel (same
-// summation order), so both paths give the same logits.
+//  * phases hand their outputs over as tagged words: every output element is stored as one 64-bit word, the
+//    float's bits in the low half and the exchange's tag (step epoch + layer + phase) in the high half, with a
+//    single-copy-atomic 64-bit store. A consumer issues all of its loads at once and reloads only the words whose
+//    tag is not the expected one yet, so the data carries its own readiness: one L2 round trip per hand-off, no
+//    counters, fences or tickets (measured on B200: 1.2 us per grid-wide hand-off of a 1024-float vector, against
+//    2.5 us for a release counter followed by the data reads);
+//  * attention items (sequence, KV head, key span) fold in the per-head QK RMSNorm, RoPE and the f16 KV store;
+//    when a head's keys are split over several items, their partial softmax states are merged by idle warps of
+//    other CTAs in a separate hand-off;
+//  * the residual stream: the CTA that owns rows of x (the o_proj / down rows) keeps them in shared memory and
+//    publishes each update;
+//  * Qwen3's RMSNorm before a matrix is applied in the GEMV epilogue: the staged activations are x * gamma and
+//    the row's dot product is multiplied by rstd = 1 / sqrt(mean(x^2) + eps), which is the same RMSNorm since
+//    W (x rstd gamma) = rstd (W (x gamma)); the sums of squares ride on the staging pass, so it needs one barrier.
+// The dot products and activation layout are the GEMV kernel's (same summation order).
 //
 // Every wait is bounded (DecodeParams::wait_ns on %globaltimer, 2 s by default): on expiry the kernel records
-// kErrMbarTimeout, raises an abort flag that makes every other wait return at once, and the producer waits (bounded) for its copies in flight
-// before leaving. The last CTA to finish resets the counters, so the launch can be replayed from a CUDA graph.
+// kErrMbarTimeout, raises an abort flag that makes every other wait return at once, and the producer waits
+// (bounded) for its copies in flight before leaving. Waits that can fail are combined over the CTA's consumer
+// threads with a reducing barrier, so the threads leave together. The last CTA to finish finalises the greedy
+// tokens, resets the step counter and advances the epoch, so the launch replays from a CUDA graph.
 #include <algorithm>
 
 #include "gemv_core.cuh"
@@ -32,17 +42,21 @@ namespace {
 constexpr int kW = 12;                 // consumer warps (12 + 1 warps: at most 128 registers a thread)
 constexpr int kNT = kW * 32;           // consumer threads
 constexpr int kThr = kNT + 32;         // + the producer warp
-constexpr int kMaxGroupRows = kW * 4;  // rows the CTA consumes per pass, at most (kRows<1> warps x 4)
 constexpr int kMaxSlots = 16;
 constexpr int kSlotBytes = 32768;      // bigger stages stream faster (fewer producer / consumer hand-offs)
-constexpr int kMaxStatSlots = 256;     // 32-float4 groups with a norm partial (M * C / 128)
+constexpr int kMaxGroupRows = kW * 4;  // rows the CTA consumes per pass, at most (kRows<1> warps x 4)
+constexpr int kMaxStatSlots = 256;     // LayerNorm partial-sum slots (kGatherE * kW used)
 constexpr int kChunk = 8192;           // bytes per bulk copy
-constexpr int kPhases = 5;             // per layer: qkv, attention, o_proj, up, down
 constexpr int kMaxGq = 4;              // query heads per KV head
 constexpr int kMaxSpan = 64;           // keys per attention item (staged in shared memory)
 constexpr int kStaticSmem = 8192;      // upper bound of the kernel's static shared memory
+constexpr int kOwnRows = 32;           // residual rows a CTA owns, at most (C <= 32 * grid)
+constexpr int kGatherE = 2;            // float4 groups a thread has in flight per gather batch
+constexpr int kMergeS = 16;            // split states a merge warp has in flight per batch
 
 enum Ph : int { kQkv = 0, kAttn = 1, kO = 2, kUp = 3, kDown = 4, kHead = 5 };
+// Exchanges (tag offsets) per layer. The LM head reads x under layer L's kXIn.
+enum Xch : unsigned { kXIn = 0, kXQkv = 1, kXPart = 2, kXAtt = 3, kXMid = 4, kXH = 5, kXPer = 8 };
 
 __device__ unsigned g_dec_abort;  // raised by the first wait that gives up
 
@@ -52,10 +66,18 @@ __device__ __forceinline__ uint64_t gtimer() {
     return t;
 }
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kNT) : "memory"); }
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+// Consumer barrier that also ANDs a predicate over the consumer threads.
+__device__ __forceinline__ bool csync_and(bool ok) {
+    unsigned r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.and.pred p, 1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(ok ? 1u : 0u), "n"(kNT)
+        : "memory");
+    return r != 0;
 }
 __device__ __forceinline__ bool aborted() { return *reinterpret_cast<volatile unsigned*>(&g_dec_abort) != 0u; }
 __device__ __forceinline__ void give_up() {
@@ -66,6 +88,99 @@ __device__ __forceinline__ double wsum_d(double v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
+}
+
+// ---------------------------------------------------------------------------------------------- tagged words
+__device__ __forceinline__ void tw_put(uint64_t* p, float v, unsigned tag) {
+    const uint64_t w = (uint64_t(tag) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ void tw_ld2(const uint64_t* p, uint64_t& a, uint64_t& b) {  // 16-byte aligned pair
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ uint64_t tw_ld(const uint64_t* p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+__device__ __forceinline__ bool tw_ok(uint64_t w, unsigned tag) { return unsigned(w >> 32) == tag; }
+__device__ __forceinline__ float tw_val(uint64_t w) { return __uint_as_float(unsigned(w)); }
+
+// Poll bookkeeping shared by the gathers: false once the wait has run past lim (reported) or another wait gave up.
+struct Poll {
+    uint64_t t0 = 0;
+    uint32_t n = 0;
+    __device__ __forceinline__ bool keep_going(uint64_t lim) {
+        if ((++n & 15u) != 1u) return true;
+        if (aborted()) return false;
+        const uint64_t t = gtimer();
+        if (n == 1u) {
+            t0 = t;
+            return true;
+        }
+        if (t - t0 > lim) {
+            give_up();
+            return false;
+        }
+        return true;
+    }
+};
+
+// E groups of 4 consecutive tagged words (group q at src + 4 q, for the q of this thread that are < nq): every
+// load in flight at once, then only the groups with a stale tag are reloaded. False on timeout or abort.
+template <int E>
+__device__ bool gather4(const uint64_t* src, const int (&q)[E], int nq, unsigned tag, float4 (&out)[E],
+                        uint64_t lim) {
+    uint64_t w[E][4];
+#pragma unroll
+    for (int e = 0; e < E; e++)
+        if (q[e] < nq) {
+            tw_ld2(src + 4 * int64_t(q[e]), w[e][0], w[e][1]);
+            tw_ld2(src + 4 * int64_t(q[e]) + 2, w[e][2], w[e][3]);
+        }
+    Poll pl;
+    for (;;) {
+        unsigned miss = 0;
+#pragma unroll
+        for (int e = 0; e < E; e++)
+            if (q[e] < nq && !(tw_ok(w[e][0], tag) && tw_ok(w[e][1], tag) && tw_ok(w[e][2], tag) && tw_ok(w[e][3], tag)))
+                miss |= 1u << e;
+        if (!miss) break;
+        if (!pl.keep_going(lim)) return false;
+#pragma unroll
+        for (int e = 0; e < E; e++)
+            if (miss >> e & 1u) {
+                tw_ld2(src + 4 * int64_t(q[e]), w[e][0], w[e][1]);
+                tw_ld2(src + 4 * int64_t(q[e]) + 2, w[e][2], w[e][3]);
+            }
+    }
+#pragma unroll
+    for (int e = 0; e < E; e++)
+        out[e] = make_float4(tw_val(w[e][0]), tw_val(w[e][1]), tw_val(w[e][2]), tw_val(w[e][3]));
+    return true;
+}
+
+// N tagged words src[stride * i], i < N, for one lane. False on timeout or abort.
+template <int N>
+__device__ bool gather_lane(const uint64_t* src, int stride, unsigned tag, float (&out)[N], uint64_t lim) {
+    uint64_t w[N];
+#pragma unroll
+    for (int i = 0; i < N; i++) w[i] = tw_ld(src + int64_t(i) * stride);
+    Poll pl;
+    for (;;) {
+        unsigned miss = 0;
+#pragma unroll
+        for (int i = 0; i < N; i++)
+            if (!tw_ok(w[i], tag)) miss |= 1u << i;
+        if (!miss) break;
+        if (!pl.keep_going(lim)) return false;
+#pragma unroll
+        for (int i = 0; i < N; i++)
+            if (miss >> i & 1u) w[i] = tw_ld(src + int64_t(i) * stride);
+    }
+#pragma unroll
+    for (int i = 0; i < N; i++) out[i] = tw_val(w[i]);
+    return true;
 }
 
 // try_wait with a suspend-time hint: the thread sleeps until the phase completes or hint_ns pass, instead of
@@ -96,52 +211,49 @@ __device__ bool dwait(uint64_t* bar, uint32_t parity, uint64_t lim, uint32_t hin
     }
 }
 
-// Consumer-side wait until *ctr >= target: thread 0 polls with acquire loads, then a consumer barrier.
-__device__ bool wait_count(const unsigned* ctr, unsigned target, int* flag, const int* abort, uint64_t lim) {
-    if (threadIdx.x == 0) {
-        int ok = *reinterpret_cast<const volatile int*>(abort) == 0 ? 1 : 0;
-        if (ok && ld_acquire(ctr) < target) {
-            const uint64_t t0 = gtimer();
-            for (uint32_t i = 1;; i++) {
-                if (ld_acquire(ctr) >= target) break;
-                if ((i & 63) == 0) {
-                    if (aborted()) {
-                        ok = 0;
-                        break;
-                    }
-                    if (gtimer() - t0 > lim) {
-                        give_up();
-                        ok = 0;
-                        break;
-                    }
-                }
-            }
-        }
-        *flag = ok;
-    }
-    csync();
-    return *reinterpret_cast<volatile int*>(flag) != 0;
+// ---------------------------------------------------------------------------------------------- shared memory
+// Shared-memory state of the kernel at file scope, so the phase functions address it directly (a struct of
+// pointers passed around ends up in local memory and puts a load on every access).
+extern __shared__ __align__(128) uint8_t dsm[];  // barriers | layer table | activations | keys/values | ring
+__shared__ double s_part[2 * kMaxStatSlots];      // LayerNorm prologue partial sums
+__shared__ double s_ss[kW][kDecodeMaxSeqs];       // RMSNorm: per-warp sums of squares of the staged rows
+__shared__ float s_xown[kDecodeMaxSeqs][kOwnRows];  // the residual rows this CTA owns
+__shared__ unsigned long long s_key[kDecodeMaxSeqs];  // LM head: the CTA's greedy argmax keys
+__shared__ int s_last;
+__shared__ unsigned s_epoch;
+__shared__ __align__(8) uint64_t s_attn_bar;           // an attention item's keys / values have landed
+__device__ __forceinline__ uint64_t* full_bar() { return reinterpret_cast<uint64_t*>(dsm); }
+__device__ __forceinline__ uint64_t* empty_bar() { return reinterpret_cast<uint64_t*>(dsm) + kMaxSlots; }
+__device__ __forceinline__ const DecodeLayer* layer_tab() { return reinterpret_cast<const DecodeLayer*>(dsm + 256); }
+__device__ __forceinline__ int tab_bytes(const DecodeParams& p) {
+    return (p.layers * int(sizeof(DecodeLayer)) + 127) / 128 * 128;
 }
-
-// All consumer warps are done with the phase's writes: publish them.
-__device__ __forceinline__ void signal(unsigned* ctr) {
-    csync();
-    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+__device__ __forceinline__ float* xs_buf(const DecodeParams& p) {
+    return reinterpret_cast<float*>(dsm + 256 + tab_bytes(p));
 }
+__device__ __forceinline__ uint16_t* kv_buf(const DecodeParams& p) {
+    return reinterpret_cast<uint16_t*>(dsm + 256 + tab_bytes(p) + p.xs_bytes);
+}
+__device__ __forceinline__ uint8_t* ring_buf(const DecodeParams& p) {
+    return dsm + 256 + tab_bytes(p) + p.xs_bytes + p.kv_bytes;
+}
+__device__ __forceinline__ unsigned tag_of(int l, unsigned x) { return s_epoch + unsigned(l) * kXPer + x; }
 
-// One GEMV phase of the step.
+// ---------------------------------------------------------------------------------------------- GEMV phases
 struct GemvPh {
     const uint8_t* W;
     int64_t rb;
-    int rows, K, pair;  // pair: SwiGLU, gate row n with up row n + rows
-    const float* x;
-    int64_t xs;
-    int embed_src;      // activations are the token embeddings (layer 0)
+    int rows, K, pair;   // pair: SwiGLU, gate row n with up row n + rows
+    const uint64_t* x;   // tagged input words [M][K]
+    unsigned xtag;
+    int embed;           // (LayerNorm path) unused
     int norm;
     const float *gamma, *beta, *bias;
     int flags;
-    float* y;
+    uint64_t* y;         // tagged output words [M][ys] (nullptr: the LM head's plain logits)
+    unsigned ytag;
     int64_t ys;
+    int resid;           // output rows are residual rows of x (o_proj, down): added to this CTA's copy
     int head;
 };
 
@@ -150,27 +262,29 @@ __device__ __forceinline__ GemvPh gemv_ph(const DecodeParams& p, int l, int kind
     const int lnk = p.qwen ? kNormRms : kNormLayer;
     if (kind == kHead) {
         g.W = p.embed; g.rb = p.rb_c; g.rows = p.V; g.K = p.C;
-        g.x = p.x; g.xs = p.C; g.norm = lnk; g.gamma = p.normf; g.beta = p.normfb;
-        g.y = p.logits; g.ys = p.V; g.head = 1;
+        g.x = p.x_tw; g.xtag = tag_of(p.layers, kXIn); g.norm = lnk; g.gamma = p.normf; g.beta = p.normfb;
+        g.ys = p.V; g.head = 1;
         return g;
     }
-    const DecodeLayer& L = p.layer[l];
+    const DecodeLayer& L = layer_tab()[l];
     if (kind == kQkv) {
         g.W = L.wqkv; g.rb = p.rb_c; g.rows = p.QW; g.K = p.C;
-        g.x = p.x; g.xs = p.C; g.embed_src = l == 0; g.norm = lnk; g.gamma = L.ln1; g.beta = L.ln1b;
-        g.bias = L.bqkv; g.flags = p.qwen ? 0 : kBias; g.y = p.qkv; g.ys = p.QW;
+        g.x = p.x_tw; g.xtag = tag_of(l, kXIn); g.norm = lnk; g.gamma = L.ln1; g.beta = L.ln1b;
+        g.bias = L.bqkv; g.flags = p.qwen ? 0 : kBias; g.y = p.qkv_tw; g.ytag = tag_of(l, kXQkv); g.ys = p.QW;
     } else if (kind == kO) {
         g.W = L.wo; g.rb = p.rb_att; g.rows = p.C; g.K = p.H * p.hd;
-        g.x = p.att; g.xs = int64_t(p.H) * p.hd;
-        g.bias = L.bo; g.flags = kAccumulate | (p.qwen ? 0 : kBias); g.y = p.x; g.ys = p.C;
+        g.x = p.att_tw; g.xtag = tag_of(l, kXAtt);
+        g.bias = L.bo; g.flags = p.qwen ? 0 : kBias; g.y = p.x_tw; g.ytag = tag_of(l, kXMid); g.ys = p.C;
+        g.resid = 1;
     } else if (kind == kUp) {
         g.W = L.wup; g.rb = p.rb_c; g.rows = p.F; g.K = p.C; g.pair = p.qwen;
-        g.x = p.x; g.xs = p.C; g.norm = lnk; g.gamma = L.ln2; g.beta = L.ln2b;
-        g.bias = L.bup; g.flags = p.qwen ? 0 : (kBias | kGelu); g.y = p.h; g.ys = p.F;
+        g.x = p.x_tw; g.xtag = tag_of(l, kXMid); g.norm = lnk; g.gamma = L.ln2; g.beta = L.ln2b;
+        g.bias = L.bup; g.flags = p.qwen ? 0 : (kBias | kGelu); g.y = p.h_tw; g.ytag = tag_of(l, kXH); g.ys = p.F;
     } else {
         g.W = L.wdown; g.rb = p.rb_f; g.rows = p.C; g.K = p.F;
-        g.x = p.h; g.xs = p.F;
-        g.bias = L.bdown; g.flags = kAccumulate | (p.qwen ? 0 : kBias); g.y = p.x; g.ys = p.C;
+        g.x = p.h_tw; g.xtag = tag_of(l, kXH);
+        g.bias = L.bdown; g.flags = p.qwen ? 0 : kBias; g.y = p.x_tw; g.ytag = tag_of(l + 1, kXIn); g.ys = p.C;
+        g.resid = 1;
     }
     return g;
 }
@@ -245,175 +359,155 @@ __device__ __forceinline__ int token_of(const DecodeParams& p, int m) {
     return t;
 }
 
-__device__ __forceinline__ float4 embed4(const DecodeParams& p, int m, int k) {
-    const uint8_t* row = p.embed + int64_t(token_of(p, m)) * p.rb_c;
-    float4 r = make_float4(dequant_one(p.fmt, row, p.C, k), dequant_one(p.fmt, row, p.C, k + 1),
-                           dequant_one(p.fmt, row, p.C, k + 2), dequant_one(p.fmt, row, p.C, k + 3));
-    if (p.wpe) {  // GPT-2 learned positions (f32, like the CPU path)
-        const float4 w = *reinterpret_cast<const float4*>(p.wpe + int64_t(p.pos[m]) * p.C + k);
-        r.x += w.x;
-        r.y += w.y;
-        r.z += w.z;
-        r.w += w.w;
-    }
-    return r;
-}
-
 // Weight rows a warp walks together (independent load streams): more for one sequence, where the registers of
 // the activation tiles are free.
 template <int NM>
 constexpr int kRows = NM == 1 ? 4 : 2;
 
-// Norm weights a consumer thread loads before the phase's wait (they do not depend on the previous phase).
-constexpr int kNormPre = 2;
-struct NormPre {
-    float4 g[kNormPre], b[kNormPre];
-};
-
-__device__ __forceinline__ void norm_prefetch(const DecodeParams& p, const GemvPh& g, NormPre& pre) {
-    if (g.norm == kNormNone) return;
-    const int K4 = g.K / 4, total = p.M * K4;
-#pragma unroll
-    for (int j = 0; j < kNormPre; j++) {
-        const int i = threadIdx.x + j * kNT;
-        if (i < total) {
-            const int k = 4 * (i % K4);
-            pre.g[j] = __ldg(reinterpret_cast<const float4*>(g.gamma + k));
-            if (g.norm == kNormLayer) pre.b[j] = __ldg(reinterpret_cast<const float4*>(g.beta + k));
-        }
-    }
-}
-
-// Stages the M activation rows of a phase into the permuted layout, with the norm prologue (RMSNorm /
-// LayerNorm over K, sums in double, cpu_ops.cpp:483-511). The rows come straight from L2 into shared memory
-// with cp.async (no registers held, every copy of the thread in flight at once); the token embeddings of layer
-// 0 are dequantised on the way instead.
-template <int FMT>
-__device__ void stage_x(const DecodeParams& p, const GemvPh& g, const NormPre& pre, float* xs, double* spart,
-                        float* snorm, int warp, int lane) {
+// Stages the M input rows of a phase (tagged words) into the permuted layout of the dot products: RMSNorm phases
+// store x * gamma and leave per-warp sums of squares in s_ss (the epilogue applies rstd); LayerNorm phases
+// (GPT-2) normalise in place with the row mean and variance (cpu_ops.cpp:483-500, sums in double). `ok` false:
+// this thread's earlier wait failed. Returns false, for every consumer thread alike, when any wait failed or an
+// input never arrived.
+template <int FMT, int NM>
+__device__ bool stage_x(const DecodeParams& p, const GemvPh& g, float* xs, int warp, int lane, bool ok) {
     const int tid = threadIdx.x;
-    const int K4 = g.K / 4, total = p.M * K4, xrow = seg_count(FMT, g.K) * Seg<FMT>::W;
-    const bool norm = g.norm != kNormNone;
-    if (g.embed_src) {
-        for (int i = tid; i < total; i += kNT) {
-            const int m = i / K4, k = 4 * (i - m * K4);
-            *reinterpret_cast<float4*>(xs + m * xrow + xperm<FMT>(k)) = embed4(p, m, k);
+    const int K4 = g.K / 4, nq = p.M * K4, xrow = seg_count(FMT, g.K) * Seg<FMT>::W;
+    const bool rms = g.norm == kNormRms, ln = g.norm == kNormLayer;
+    double ss[NM];
+#pragma unroll
+    for (int m = 0; m < NM; m++) ss[m] = 0.0;
+    for (int base = 0; base < nq && ok; base += kGatherE * kNT) {
+        int q[kGatherE];
+        float4 gm[kGatherE];
+#pragma unroll
+        for (int e = 0; e < kGatherE; e++) {
+            q[e] = base + tid + e * kNT;
+            if (rms && q[e] < nq) gm[e] = __ldg(reinterpret_cast<const float4*>(g.gamma + 4 * (q[e] % K4)));
         }
-    } else {
-        for (int i = tid; i < total; i += kNT) {
-            const int m = i / K4, k = 4 * (i - m * K4);
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(xs + m * xrow + xperm<FMT>(k))),
-                         "l"(g.x + int64_t(m) * g.xs + k)
-                         : "memory");
+        float4 v[kGatherE];
+        ok = gather4<kGatherE>(g.x, q, nq, g.xtag, v, p.wait_ns);
+        if (!ok) break;
+#pragma unroll
+        for (int e = 0; e < kGatherE; e++) {
+            if (q[e] >= nq) continue;
+            const int m = q[e] / K4, k = 4 * (q[e] - m * K4);
+            float4 y = v[e];
+            if (rms) {
+                const double sq = double(y.x) * y.x + double(y.y) * y.y + double(y.z) * y.z + double(y.w) * y.w;
+#pragma unroll
+                for (int mm = 0; mm < NM; mm++)
+                    if (mm == m) ss[mm] += sq;
+                y.x = __fmul_rn(y.x, gm[e].x);
+                y.y = __fmul_rn(y.y, gm[e].y);
+                y.z = __fmul_rn(y.z, gm[e].z);
+                y.w = __fmul_rn(y.w, gm[e].w);
+            }
+            *reinterpret_cast<float4*>(xs + m * xrow + xperm<FMT>(k)) = y;
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
     }
-    if (!norm) {
-        csync();
-        return;
+    if (rms) {
+#pragma unroll
+        for (int m = 0; m < NM; m++) {
+            if (m >= p.M) break;
+            const double t = wsum_d(ss[m]);
+            if (lane == 0) s_ss[warp][m] = t;
+        }
     }
-    // K % 128 == 0: the 32 float4 of a warp in one pass share a row
-    for (int base = 0; base < total; base += kNT) {
+    if (!csync_and(ok)) return false;
+    if (!ln) return true;
+    // LayerNorm: K % 128 == 0, so the 32 float4 of a warp in one pass share a row
+    for (int base = 0; base < nq; base += kNT) {
         const int i = base + tid;
         double s1 = 0.0, s2 = 0.0;
-        if (i < total) {
+        if (i < nq) {
             const int m = i / K4;
             const float4 v = *reinterpret_cast<const float4*>(xs + m * xrow + xperm<FMT>(4 * (i - m * K4)));
             s1 = double(v.x) + double(v.y) + double(v.z) + double(v.w);
             s2 = double(v.x) * v.x + double(v.y) * v.y + double(v.z) * v.z + double(v.w) * v.w;
         }
-        if (base + warp * 32 < total) {
+        if (base + warp * 32 < nq) {
             s1 = wsum_d(s1);
             s2 = wsum_d(s2);
             if (lane == 0) {
-                const int q = base / 32 + warp;
-                spart[2 * q] = s1;
-                spart[2 * q + 1] = s2;
+                const int qq = base / 32 + warp;
+                s_part[2 * qq] = s1;
+                s_part[2 * qq + 1] = s2;
             }
         }
     }
     csync();
-    // Every thread totals the partials of the rows it normalises (fixed order), so no second barrier.
     const int gpr = K4 / 32;  // partial slots per row
-    for (int i = tid, j = 0; i < total; i += kNT, j++) {
+    for (int i = tid; i < nq; i += kNT) {
         const int m = i / K4, k = 4 * (i - m * K4);
         double a1 = 0.0, a2 = 0.0;
-        for (int q = m * gpr; q < (m + 1) * gpr; q++) {
-            a1 += spart[2 * q];
-            a2 += spart[2 * q + 1];
+        for (int qq = m * gpr; qq < (m + 1) * gpr; qq++) {
+            a1 += s_part[2 * qq];
+            a2 += s_part[2 * qq + 1];
         }
-        float mean = 0.0f, r;
-        if (g.norm == kNormRms) {
-            r = float(1.0 / sqrt(a2 / g.K + double(p.eps)));
-        } else {
-            const double mu = a1 / g.K;
-            mean = float(mu);
-            r = float(1.0 / sqrt(a2 / g.K - mu * mu + double(p.eps)));
-        }
+        const double mu = a1 / g.K;
+        const float mean = float(mu);
+        const float r = float(1.0 / sqrt(a2 / g.K - mu * mu + double(p.eps)));
         float4* px = reinterpret_cast<float4*>(xs + m * xrow + xperm<FMT>(k));
         float4 y = *px;
-        float4 ga, be;
-        if (j < kNormPre) {
-            ga = j == 0 ? pre.g[0] : pre.g[kNormPre - 1];
-            be = j == 0 ? pre.b[0] : pre.b[kNormPre - 1];
-        } else {
-            ga = __ldg(reinterpret_cast<const float4*>(g.gamma + k));
-            if (g.norm == kNormLayer) be = __ldg(reinterpret_cast<const float4*>(g.beta + k));
-        }
-        if (g.norm == kNormRms) {
-            y.x = __fmul_rn(__fmul_rn(y.x, r), ga.x);
-            y.y = __fmul_rn(__fmul_rn(y.y, r), ga.y);
-            y.z = __fmul_rn(__fmul_rn(y.z, r), ga.z);
-            y.w = __fmul_rn(__fmul_rn(y.w, r), ga.w);
-        } else {
-            y.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.x, mean), r), ga.x), be.x);
-            y.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.y, mean), r), ga.y), be.y);
-            y.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.z, mean), r), ga.z), be.z);
-            y.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.w, mean), r), ga.w), be.w);
-        }
+        const float4 ga = __ldg(reinterpret_cast<const float4*>(g.gamma + k));
+        const float4 be = __ldg(reinterpret_cast<const float4*>(g.beta + k));
+        y.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.x, mean), r), ga.x), be.x);
+        y.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.y, mean), r), ga.y), be.y);
+        y.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.z, mean), r), ga.z), be.z);
+        y.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(y.w, mean), r), ga.w), be.w);
         *px = y;
     }
     csync();
+    return true;
 }
 
-// Shared-memory state of the kernel at file scope, so the phase functions address it directly (a struct of
-// pointers passed around ends up in local memory and puts a load on every access).
-extern __shared__ __align__(128) uint8_t dsm[];  // barriers | activations | attention keys/values | weight ring
-__shared__ double s_part[2 * kMaxStatSlots];      // norm prologue partial sums
-__shared__ float s_norm[2 * kDecodeMaxSeqs];
-__shared__ unsigned long long s_key[kDecodeMaxSeqs];  // LM head: the CTA's greedy argmax keys
-__shared__ int s_flag, s_ticket, s_last, s_abort;      // s_abort: a stage wait of this CTA gave up
-__shared__ __align__(8) uint64_t s_attn_bar;           // an attention item's keys / values have landed
-__device__ __forceinline__ uint64_t* full_bar() { return reinterpret_cast<uint64_t*>(dsm); }
-__device__ __forceinline__ uint64_t* empty_bar() { return reinterpret_cast<uint64_t*>(dsm) + kMaxSlots; }
-__device__ __forceinline__ float* xs_buf() { return reinterpret_cast<float*>(dsm + 256); }
-__device__ __forceinline__ uint16_t* kv_buf(const DecodeParams& p) {
-    return reinterpret_cast<uint16_t*>(dsm + 256 + p.xs_bytes);
+// rstd of row m from the staging pass's per-warp sums of squares (RMSNorm, cpu_ops.cpp:502-511).
+__device__ __forceinline__ float rms_rstd(const DecodeParams& p, int m, int K) {
+    double a = 0.0;
+#pragma unroll
+    for (int w = 0; w < kW; w++) a += s_ss[w][m];
+    return float(1.0 / sqrt(a / K + double(p.eps)));
 }
-__device__ __forceinline__ uint8_t* ring_buf(const DecodeParams& p) { return dsm + 256 + p.xs_bytes + p.kv_bytes; }
 
-
-
-// One GEMV phase on this CTA's rows: wait for the inputs, stage them, consume the producer's stages. A pass of a
-// warp takes RR rows (RR / 2 gate / up pairs for SwiGLU) spaced kW apart, so the CTA's warps walk the stages
-// together and free them in order.
+// One GEMV phase on this CTA's rows: take the first weight stage, gather and stage the inputs, consume the
+// producer's stages, store the outputs as tagged words. A pass of a warp takes RR rows (RR / 2 gate / up pairs
+// for SwiGLU) spaced kW apart, so the CTA's warps walk the stages together and free them in order. Returns false
+// when the kernel must stop (a wait failed).
 template <int FMT, int NM>
-__device__ __forceinline__ bool gemv_run(const DecodeParams& p, const GemvPh& g, const unsigned* dep,
-                                         unsigned target, uint32_t& st_base, int warp, int lane) {
+__device__ __forceinline__ bool gemv_run(const DecodeParams& p, const GemvPh& g, uint32_t& st_base, uint32_t& seen,
+                                         int warp, int lane) {
     constexpr int RR = kRows<NM>;
     int r0, r1;
     cta_rows(g.rows, p.grid, r0, r1);
     if (r0 >= r1) return true;
-    NormPre pre;
-    norm_prefetch(p, g, pre);
-    constexpr float kF = FMT == kFP8 ? kFp8HwFactor : kFp4Factor;
     const int n = r1 - r0, rps = stage_rows(p, g), nst = (n + rps - 1) / rps;
     const int cbytes = code_bytes(FMT, g.K), nseg = seg_count(FMT, g.K), xrow = nseg * Seg<FMT>::W;
     const int rpp = g.pair ? RR / 2 : RR;  // output rows per pass
+    const bool rms = g.norm == kNormRms;
+    constexpr float kF = FMT == kFP8 ? kFp8HwFactor : kFp4Factor;  // the dot products' decode factor
     RowWalk w{0, 0, int(st_base % uint32_t(p.nslot)), int((st_base / uint32_t(p.nslot)) & 1u)};
     w.advance(warp, rps, p.nslot);  // this warp's first row
     int released = 0;               // stages [0, released) of this phase that this warp has let go
-    int waited = -1;                // last stage of this phase this warp has waited for
+    // A parity wait on a slot is only unambiguous while the slot is at most one phase ahead of the waiter, and a
+    // warp need not have rows in every stage, so each warp observes the landing of every stage of the step in
+    // order (`seen`: the next one), the ones it does not read included, and lets go of a stage only after
+    // observing it. The landed ones cost one try_wait.
+    auto observe = [&](uint32_t upto) -> bool {
+        int ok = 1;
+        for (; seen <= upto && ok; seen++) {
+            const int slot = int(seen % uint32_t(p.nslot)), par = int((seen / uint32_t(p.nslot)) & 1u);
+            if (lane == 0) ok = mbar_try_wait(&full_bar()[slot], par) || dwait(&full_bar()[slot], par, p.wait_ns);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+        }
+        return ok != 0;
+    };
+    auto release_to = [&](int s) -> bool {
+        if (s > released && !observe(st_base + uint32_t(s - 1))) return false;
+        for (; released < s; released++)
+            if (lane == 0) mbar_arrive(&empty_bar()[(st_base + uint32_t(released)) % uint32_t(p.nslot)]);
+        return true;
+    };
     unsigned long long best[NM];    // LM head: this warp's greedy argmax key per sequence
 #pragma unroll
     for (int m = 0; m < NM; m++) best[m] = 0ull;
@@ -429,13 +523,7 @@ __device__ __forceinline__ bool gemv_run(const DecodeParams& p, const GemvPh& g,
         for (int r = 0; r < RR; r++) {
             if (r >= rpp) break;
             if (i0 + r * kW < n) {
-                if (v.s != waited) {
-                    int ok = 1;
-                    if (lane == 0)
-                        ok = mbar_try_wait(&full_bar()[v.slot], v.par) || dwait(&full_bar()[v.slot], v.par, p.wait_ns);
-                    if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
-                    waited = v.s;
-                }
+                if (!observe(st_base + uint32_t(v.s))) return false;
                 const uint8_t* b = ring_buf(p) + size_t(v.slot) * p.slot_bytes;
                 wr[r] = b + int64_t(v.o) * g.rb;
                 if (g.pair) wr[rpp + r] = b + int64_t(min(rps, n - v.s * rps) + v.o) * g.rb;
@@ -449,23 +537,22 @@ __device__ __forceinline__ bool gemv_run(const DecodeParams& p, const GemvPh& g,
         return true;
     };
     // The first pass's weights were streamed in during earlier phases: take them before the activations' wait.
-    // A wait that gives up stops the consumption but keeps the CTA's barriers in step; the next wait_count (or
-    // the end of the step) sees the flag and every consumer warp leaves together.
-    if (warp < n && !setup(warp)) {
-        if (lane == 0) s_abort = 1;
-        return true;
-    }
-    if (dep && !wait_count(dep, target, &s_flag, &s_abort, p.wait_ns)) return false;
-    stage_x<FMT>(p, g, pre, xs_buf(), s_part, s_norm, warp, lane);
+    // A stage wait that gives up stops this warp's consumption; the failure reaches the other consumer threads
+    // at the next reducing barrier (every consumer thread passes the same barriers), and they all leave.
+    bool ok = warp < n ? setup(warp) : true;
+    if (!stage_x<FMT, NM>(p, g, xs_buf(p), warp, lane, ok)) return false;
+    float rstd[NM];
+#pragma unroll
+    for (int m = 0; m < NM; m++) rstd[m] = (rms && m < p.M) ? rms_rstd(p, m, g.K) : 1.0f;
     for (int i0 = warp; i0 < n; i0 += kW * rpp) {
         if (i0 != warp && !setup(i0)) {
-            if (lane == 0) s_abort = 1;
-            return true;
+            ok = false;
+            break;
         }
         // SwiGLU: up row r sits at rpp + r (gate rows nr .. rpp - 1 are computed but unused)
         const int nrows = g.pair ? rpp + nr : nr;
         float acc[RR][NM];
-        dot_rows<FMT, NM, RR>(wr, nrows, cbytes, nseg, xs_buf(), xrow, p.M, lane, acc);
+        dot_rows<FMT, NM, RR>(wr, nrows, cbytes, nseg, xs_buf(p), xrow, p.M, lane, acc);
         // reductions of every row first (independent shuffle chains), then the lanes that own a row store it
         float red_[RR][NM];
 #pragma unroll
@@ -480,31 +567,39 @@ __device__ __forceinline__ bool gemv_run(const DecodeParams& p, const GemvPh& g,
                 if (m >= p.M) break;
                 if (r >= nr || lane != ((r * NM + m) & 31)) continue;
                 const int row = r0 + i0 + r * kW;
-                float* dst = g.y + int64_t(m) * g.ys + row;
-                const float gs = red_[r][m];
+                const float rs = rstd[m];
                 float val;
                 if (g.pair) {
-                    const float us = red_[rpp + r < RR ? rpp + r : 0][m];
+                    const float gs = __fmul_rn(red_[r][m], rs);
+                    const float us = __fmul_rn(red_[rpp + r < RR ? rpp + r : 0][m], rs);
                     val = gs / (1.0f + expf(-gs)) * us;  // cpu::siluMul (cpu_ops.cpp:526-533)
                 } else {
-                    val = gs;
+                    val = rms ? __fmul_rn(red_[r][m], rs) : red_[r][m];
                     if (g.flags & kBias) val += g.bias[row];
                     if (g.flags & kGelu) val = gelu(val);
-                    if (g.flags & kAccumulate) val += *dst;
+                    if (g.resid) {
+                        float& xo = s_xown[m][row - r0];
+                        val += xo;
+                        xo = val;
+                    }
                 }
-                *dst = val;
-                if (g.head) best[m] = max(best[m], argmax_key(val, row));
+                if (g.head) {
+                    p.logits[int64_t(m) * g.ys + row] = val;
+                    best[m] = max(best[m], argmax_key(val, row));
+                } else {
+                    tw_put(g.y + int64_t(m) * g.ys + row, val, g.ytag);
+                }
             }
         }
         __syncwarp();
         w = v;  // the first row of this warp's next pass
-        const int s_next = i0 + kW * rpp < n ? w.s : nst;
-        for (; released < s_next; released++)
-            if (lane == 0) mbar_arrive(&empty_bar()[(st_base + uint32_t(released)) % uint32_t(p.nslot)]);
+        if (!release_to(i0 + kW * rpp < n ? w.s : nst)) {
+            ok = false;
+            break;
+        }
     }
     __syncwarp();
-    for (; released < nst; released++)
-        if (lane == 0) mbar_arrive(&empty_bar()[(st_base + uint32_t(released)) % uint32_t(p.nslot)]);
+    if (ok) ok = release_to(nst);
     if (g.head) {  // one shared atomic per warp and sequence
 #pragma unroll
         for (int m = 0; m < NM; m++) {
@@ -516,7 +611,8 @@ __device__ __forceinline__ bool gemv_run(const DecodeParams& p, const GemvPh& g,
         }
     }
     st_base += uint32_t(nst);
-    return true;
+    // the next phase's staging overwrites the activations this phase's warps may still be reading
+    return csync_and(ok);
 }
 
 // ---------------------------------------------------------------------------------------------- attention
@@ -547,16 +643,21 @@ struct AttnItem {
 __device__ __forceinline__ AttnItem attn_item(const DecodeParams& p, const int (&Sm)[kDecodeMaxSeqs],
                                               const int (&Pm)[kDecodeMaxSeqs], int it) {
     AttnItem a;
-    int m = 0, rem = it;
-    while (rem >= p.KV * Sm[m]) {
-        rem -= p.KV * Sm[m];
-        m++;
+    int rem = it, m = 0, ns = Sm[0], pos = Pm[0];
+#pragma unroll
+    for (int mm = 0; mm < kDecodeMaxSeqs - 1; mm++) {  // unrolled walk (no dynamic indexing of the arrays)
+        if (rem >= p.KV * ns) {
+            rem -= p.KV * ns;
+            m = mm + 1;
+            ns = Sm[mm + 1];
+            pos = Pm[mm + 1];
+        }
     }
     a.m = m;
-    a.ns = Sm[m];
-    a.g = rem / a.ns;
-    a.j = rem - a.g * a.ns;
-    a.pos = Pm[m];
+    a.ns = ns;
+    a.g = rem / ns;
+    a.j = rem - a.g * ns;
+    a.pos = pos;
     a.slot = p.slots[m];
     a.k0 = a.j * p.span;
     a.n = min(a.pos + 1, a.k0 + p.span) - a.k0;
@@ -583,7 +684,7 @@ __device__ __forceinline__ int attn_items(const DecodeParams& p, int (&Sm)[kDeco
 // into shared memory with two bulk copies (a head's positions are contiguous in the cache), completing on
 // s_attn_bar. The cache rows are from earlier steps, so this is issued long before the item runs.
 __device__ __forceinline__ void attn_issue(const DecodeParams& p, int l, const AttnItem& a) {
-    const DecodeLayer& Ly = p.layer[l];
+    const DecodeLayer& Ly = layer_tab()[l];
     const int nold = min(a.n, a.pos - a.k0);  // rows that are in the cache already
     const uint32_t bytes = uint32_t(nold) * uint32_t(p.hd) * 2u;
     const int64_t base = int64_t(a.slot) * p.kv_slot + int64_t(a.g) * p.kv_head + int64_t(a.k0) * p.hd;
@@ -597,17 +698,17 @@ __device__ __forceinline__ void attn_issue(const DecodeParams& p, int l, const A
 // Items (sequence m, KV head g, split j) over keys [j * span, min(L, (j + 1) * span)), L = pos + 1. Each item
 // rebuilds the group's query heads (QK-norm + RoPE, qwen3_model.cpp:249-262) and the new key / value
 // (f16-rounded, as the cache holds them); split 0 stores them at pos (cpu::storeKv). The older keys and values
-// are copied to shared memory before the wait for this step's qkv. Lane l owns dims [l * DL, l * DL + DL) of a
-// key / value row for scores (cpu_ops.cpp:558) and P.V.
+// were copied to shared memory when the layer started. Lane l owns dims [l * DL, l * DL + DL) of a key / value
+// row for scores (cpu_ops.cpp:558) and P.V. A sequence with one split writes its heads' output; with several,
+// each item writes its partial softmax state (max, sum, unnormalised P.V) for merge_run.
 template <int DL>
 __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued, int warp, int lane) {
     const int Gq = p.H / p.KV, hd = p.hd, span = p.span;
     int Sm[kDecodeMaxSeqs], Pm[kDecodeMaxSeqs];
     const int total = attn_items(p, Sm, Pm);
     if (int(blockIdx.x) >= total) return true;
-    unsigned* sy = p.sync + l * kPhases;
-    const DecodeLayer& Ly = p.layer[l];
-    float* sq = xs_buf();             // [Gq][hd]
+    const DecodeLayer& Ly = layer_tab()[l];
+    float* sq = xs_buf(p);            // [Gq][hd]
     float* snk = sq + Gq * hd;        // [hd]
     float* snv = snk + hd;            // [hd]
     float* sc = snv + hd;             // [Gq][span]
@@ -615,9 +716,9 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued,
     float* sst = red + kW * Gq * hd;  // [Gq](max, sum)
     const uint16_t* kbuf = kv_buf(p);  // [span][hd]
     const uint16_t* vbuf = kv_buf(p) + span * hd;
+    // stall_test: the queries wait for a tag no phase writes (timeout path test)
+    const unsigned qtag = tag_of(l, kXQkv) ^ (p.stall_test ? 0x80000000u : 0u);
 
-    // The first item's keys / values were requested at the start of the layer (attn_issue); before the wait,
-    // the rotation and norm weights it needs.
     AttnItem a = attn_item(p, Sm, Pm, blockIdx.x);
     float cs_c[DL / 2], cs_s[DL / 2], wn[DL];
     auto load_rot = [&](const AttnItem& it) {
@@ -633,9 +734,6 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued,
         }
     };
     load_rot(a);
-    // stall_test: wait for one CTA more than there are, so the wait runs out (timeout path test)
-    if (!wait_count(sy + kQkv, unsigned(p.grid + (p.stall_test ? 1 : 0)), &s_flag, &s_abort, p.wait_ns))
-        return false;
 
     for (int it = blockIdx.x; it < total; it += p.grid) {
         if (it != int(blockIdx.x)) {  // later items of this CTA (long contexts): requested after the previous
@@ -644,51 +742,47 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued,
         }
         const int L = a.pos + 1, n = a.n, g = a.g, m = a.m;
         const bool has_new = a.k0 + n == L;
-        const float* row = p.qkv + int64_t(m) * p.QW;
-        // 1. query heads of the group, the new key and value
+        bool ok = true;
+        // 1. query heads of the group, the new key and value: one warp per head, straight from the tagged words
         if (warp < Gq + 2) {
             const int which = warp < Gq ? 0 : warp == Gq ? 1 : 2;
             const int col = which == 0 ? (g * Gq + warp) * hd : which == 1 ? (p.H + g) * hd : (p.H + p.KV + g) * hd;
             float e[DL];
+            ok = gather_lane<DL>(p.qkv_tw + int64_t(m) * p.QW + col + lane, 32, qtag, e, p.wait_ns);
+            if (ok) {
+                if (p.qwen && which != 2) {
+                    double ss = 0.0;
 #pragma unroll
-            for (int i = 0; i < DL; i++) e[i] = __ldcg(row + col + lane + 32 * i);
-            if (p.qwen && which != 2) {
-                double ss = 0.0;
+                    for (int i = 0; i < DL; i++) ss += double(e[i]) * e[i];
+                    ss = wsum_d(ss);
+                    const float sn = float(1.0 / sqrt(ss / hd + double(p.eps)));
 #pragma unroll
-                for (int i = 0; i < DL; i++) ss += double(e[i]) * e[i];
-                ss = wsum_d(ss);
-                const float sn = float(1.0 / sqrt(ss / hd + double(p.eps)));
+                    for (int i = 0; i < DL; i++) e[i] = __fmul_rn(__fmul_rn(e[i], sn), wn[i]);
 #pragma unroll
-                for (int i = 0; i < DL; i++) e[i] = __fmul_rn(__fmul_rn(e[i], sn), wn[i]);
-#pragma unroll
-                for (int i = 0; i < DL / 2; i++) {  // NeoX pairs (d, d + hd / 2), cpu::rope
-                    const float x0 = e[i], x1 = e[i + DL / 2];
-                    e[i] = __fsub_rn(__fmul_rn(x0, cs_c[i]), __fmul_rn(x1, cs_s[i]));
-                    e[i + DL / 2] = __fadd_rn(__fmul_rn(x0, cs_s[i]), __fmul_rn(x1, cs_c[i]));
+                    for (int i = 0; i < DL / 2; i++) {  // NeoX pairs (d, d + hd / 2), cpu::rope
+                        const float x0 = e[i], x1 = e[i + DL / 2];
+                        e[i] = __fsub_rn(__fmul_rn(x0, cs_c[i]), __fmul_rn(x1, cs_s[i]));
+                        e[i + DL / 2] = __fadd_rn(__fmul_rn(x0, cs_s[i]), __fmul_rn(x1, cs_c[i]));
+                    }
                 }
-            }
-            if (which == 0) {
+                if (which == 0) {
 #pragma unroll
-                for (int i = 0; i < DL; i++) sq[warp * hd + lane + 32 * i] = e[i];
-            } else {
-                uint16_t* cache = (which == 1 ? Ly.kc : Ly.vc) + int64_t(a.slot) * p.kv_slot +
-                                  int64_t(g) * p.kv_head + int64_t(a.pos) * hd;
-                float* dsm = which == 1 ? snk : snv;
+                    for (int i = 0; i < DL; i++) sq[warp * hd + lane + 32 * i] = e[i];
+                } else {
+                    uint16_t* cache = (which == 1 ? Ly.kc : Ly.vc) + int64_t(a.slot) * p.kv_slot +
+                                      int64_t(g) * p.kv_head + int64_t(a.pos) * hd;
+                    float* dst = which == 1 ? snk : snv;
 #pragma unroll
-                for (int i = 0; i < DL; i++) {
-                    const __half hv = __float2half_rn(e[i]);
-                    dsm[lane + 32 * i] = __half2float(hv);
-                    if (a.j == 0 && p.pos[m] == a.pos) cache[lane + 32 * i] = __half_as_ushort(hv);
+                    for (int i = 0; i < DL; i++) {
+                        const __half hv = __float2half_rn(e[i]);
+                        dst[lane + 32 * i] = __half2float(hv);
+                        if (a.j == 0 && p.pos[m] == a.pos) cache[lane + 32 * i] = __half_as_ushort(hv);
+                    }
                 }
             }
         }
-        if (!dwait(&s_attn_bar, uint32_t(issued - 1) & 1u, p.wait_ns)) {
-            // the keys never landed: leave (the consumers' barriers stay in step: every thread is here)
-            if (threadIdx.x == 0) s_abort = 1;
-            csync();
-            return false;
-        }
-        csync();
+        if (threadIdx.x == 0 && !dwait(&s_attn_bar, uint32_t(issued - 1) & 1u, p.wait_ns)) ok = false;
+        if (!csync_and(ok)) return false;  // the inputs or the keys never arrived: leave together
         // 2. scores, four keys x four query heads (heads past Gq are zero) per warp pass: the 16 lane partial
         // sums are reduced together by a transposed butterfly (halves exchange 8 values, then 4, 2, 1, then one
         // xor step), 16 shuffles instead of 5 per dot product
@@ -784,60 +878,120 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued,
             if (threadIdx.x == 0) attn_issue(p, l, attn_item(p, Sm, Pm, it + p.grid));
             issued++;
         }
-        // 5. merge the warps; one split: the output, else a partial for the ticket merge
+        // 5. merge the warps; one split: the heads' output, else this split's partial state
         const int outs = Gq * hd;
-        float* att = p.att + int64_t(m) * p.H * hd + int64_t(g) * Gq * hd;
         for (int o = threadIdx.x; o < outs; o += kNT) {
             float sacc = 0.0f;
 #pragma unroll
             for (int w = 0; w < kW; w++) sacc += red[w * outs + o];
-            const int gq = o / hd;
+            const int gq = o / hd, d = o - gq * hd;
             if (a.ns == 1) {
-                att[o] = sacc / sst[2 * gq + 1];
+                tw_put(p.att_tw + int64_t(m) * p.H * hd + int64_t(g) * outs + o, sacc / sst[2 * gq + 1],
+                       tag_of(l, kXAtt));
             } else {
-                float* pr = p.part + (((int64_t(m) * p.KV + g) * p.max_splits + a.j) * Gq + gq) * (hd + 2);
-                pr[2 + (o - gq * hd)] = sacc;
-                if (o - gq * hd == 0) {
-                    pr[0] = sst[2 * gq];
-                    pr[1] = sst[2 * gq + 1];
+                uint64_t* pr = p.part_tw + (((int64_t(m) * p.KV + g) * p.max_splits + a.j) * Gq + gq) * (hd + 2);
+                tw_put(pr + 2 + d, sacc, tag_of(l, kXPart));
+                if (d == 0) {
+                    tw_put(pr, sst[2 * gq], tag_of(l, kXPart));
+                    tw_put(pr + 1, sst[2 * gq + 1], tag_of(l, kXPart));
                 }
             }
         }
-        if (a.ns == 1) {
-            signal(sy + kAttn);
-            csync();
-            continue;
-        }
-        __threadfence();
-        csync();
-        if (threadIdx.x == 0) {
-            unsigned* tk = p.tickets + m * p.KV + g;
-            const unsigned t = atomicAdd(tk, 1u);
-            s_ticket = t == unsigned(a.ns - 1) ? 1 : 0;
-            if (t == unsigned(a.ns - 1)) *tk = 0u;  // every item of (m, g) has its ticket: ready for the next layer
-        }
-        csync();
-        if (*reinterpret_cast<volatile int*>(&s_ticket)) {
-            __threadfence();
-            for (int o = threadIdx.x; o < outs; o += kNT) {
-                const int gq = o / hd, d = o - gq * hd;
-                const float* base = p.part + ((int64_t(m) * p.KV + g) * p.max_splits * Gq + gq) * (hd + 2);
-                const int64_t sstride = int64_t(Gq) * (hd + 2);
-                float mx = -INFINITY;
-                for (int sp = 0; sp < a.ns; sp++) mx = fmaxf(mx, __ldcg(base + sp * sstride));
-                float num = 0.0f, den = 0.0f;
-                for (int sp = 0; sp < a.ns; sp++) {
-                    const float w = expf(__ldcg(base + sp * sstride) - mx);
-                    den += __ldcg(base + sp * sstride + 1) * w;
-                    num += __ldcg(base + sp * sstride + 2 + d) * w;
-                }
-                att[o] = num / den;
-            }
-            signal(sy + kAttn);
-        }
-        csync();
+        csync();  // the scores and partial buffers are reused by the next item
     }
     return true;
+}
+
+// Split-KV merge: one warp per (sequence, KV head, query head, block of 32 dims) of a sequence with several
+// splits, on warps of CTAs that hold no attention item when there are enough of them; lane l owns dim 32 b + l.
+// The splits are merged in order with the softmax rescaling of their states (max m_s, sum l_s, unnormalised
+// P.V a_s): out = sum_s exp(m_s - M) a_s / sum_s exp(m_s - M) l_s, M = max_s m_s (cpu_ops.cpp:556-572 over all
+// keys). A merge that cannot finish (timeout or abort) is skipped: the next phase's inputs then never arrive and
+// every CTA leaves through its own failed wait.
+__device__ __noinline__ void merge_run(const DecodeParams& p, int l, int warp, int lane) {
+    const int Gq = p.H / p.KV, hd = p.hd, nb = hd / 32;
+    int Sm[kDecodeMaxSeqs], Pm[kDecodeMaxSeqs];
+    const int total = attn_items(p, Sm, Pm);
+    const int per_seq = p.KV * Gq * nb;
+    int units = 0;
+#pragma unroll
+    for (int m = 0; m < kDecodeMaxSeqs; m++)
+        if (m < p.M && Sm[m] > 1) units += per_seq;
+    if (!units) return;
+    // CTAs without an attention item first (the last ones), then all CTAs; unit u on warp u / ctas
+    const int idle = max(0, p.grid - total);
+    const int ctas = idle * kW >= units ? idle : p.grid;
+    const int first = idle * kW >= units ? total : 0;
+    const int cta = int(blockIdx.x) - first;
+    if (cta < 0) return;
+    const unsigned ptag = tag_of(l, kXPart), atag = tag_of(l, kXAtt);
+    for (int u = cta + warp * ctas; u < units; u += kW * ctas) {
+        // unit u -> (m, g, gq, b) over the sequences that have several splits
+        int rem = u, m = 0;
+#pragma unroll
+        for (int mm = 0; mm < kDecodeMaxSeqs; mm++) {
+            const int c = (mm < p.M && Sm[mm] > 1) ? per_seq : 0;
+            if (m == mm && rem >= c) {
+                rem -= c;
+                m = mm + 1;
+            }
+        }
+        int ns = Sm[0];
+#pragma unroll
+        for (int mm = 1; mm < kDecodeMaxSeqs; mm++)
+            if (m == mm) ns = Sm[mm];
+        const int gh = rem / nb, b = rem - gh * nb, g = gh / Gq, gq = gh - g * Gq;
+        const uint64_t* base = p.part_tw + ((int64_t(m) * p.KV + g) * p.max_splits * Gq + gq) * (hd + 2);
+        const int64_t sstride = int64_t(Gq) * (hd + 2);
+        const int d = 32 * b + lane;
+        float M = -INFINITY, den = 0.0f, num = 0.0f;
+        bool ok = true;
+        for (int s0 = 0; s0 < ns && ok; s0 += kMergeS) {
+            // kMergeS splits at a time, every load in flight at once: lane j < kMergeS also holds the (max, sum)
+            // of split s0 + j
+            const int cnt = min(kMergeS, ns - s0);
+            const bool have = lane < cnt;
+            const int64_t so = int64_t(s0 + (have ? lane : 0)) * sstride;
+            uint64_t w[kMergeS], wm = tw_ld(base + so), wl = tw_ld(base + so + 1);
+#pragma unroll
+            for (int j = 0; j < kMergeS; j++) w[j] = j < cnt ? tw_ld(base + int64_t(s0 + j) * sstride + 2 + d) : 0ull;
+            Poll pl;
+            for (;;) {
+                unsigned miss = 0;
+#pragma unroll
+                for (int j = 0; j < kMergeS; j++)
+                    if (j < cnt && !tw_ok(w[j], ptag)) miss |= 1u << j;
+                const bool stm = have && !(tw_ok(wm, ptag) && tw_ok(wl, ptag));
+                if (!__any_sync(0xffffffffu, miss || stm)) break;
+                if (!pl.keep_going(p.wait_ns)) {
+                    ok = false;
+                    break;
+                }
+                if (stm) {
+                    wm = tw_ld(base + so);
+                    wl = tw_ld(base + so + 1);
+                }
+#pragma unroll
+                for (int j = 0; j < kMergeS; j++)
+                    if (miss >> j & 1u) w[j] = tw_ld(base + int64_t(s0 + j) * sstride + 2 + d);
+            }
+            if (!ok) break;
+            const float ms = tw_val(wm), ls = tw_val(wl);
+            // in split order: the running max, then the rescaled sums
+#pragma unroll
+            for (int j = 0; j < kMergeS; j++) {
+                if (j >= cnt) break;
+                const float mj = __shfl_sync(0xffffffffu, ms, j), lj = __shfl_sync(0xffffffffu, ls, j);
+                const float Mn = fmaxf(M, mj);
+                const float a = expf(M - Mn), e = expf(mj - Mn);  // exp(-inf) = 0 for the first split
+                den = den * a + lj * e;
+                num = num * a + tw_val(w[j]) * e;
+                M = Mn;
+            }
+        }
+        if (!ok) return;
+        tw_put(p.att_tw + int64_t(m) * p.H * hd + int64_t(g * Gq + gq) * hd + d, num / den, atag);
+    }
 }
 
 // ---------------------------------------------------------------------------------------------- the kernel
@@ -851,9 +1005,17 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
         }
         mbar_init(&s_attn_bar, 1);
         fence_barrier_init();
+        s_epoch = *reinterpret_cast<volatile const unsigned*>(p.epoch);
+    }
+    // the per-layer pointers, once, into shared memory (indexing the parameter block by layer would go through
+    // the constant cache on every phase)
+    {
+        const int words = p.layers * int(sizeof(DecodeLayer) / 8);
+        const uint64_t* src = reinterpret_cast<const uint64_t*>(p.layer);
+        uint64_t* dst = reinterpret_cast<uint64_t*>(dsm + 256);
+        for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
     }
     if (threadIdx.x < kDecodeMaxSeqs) s_key[threadIdx.x] = 0ull;
-    if (threadIdx.x == 0) s_abort = 0;
     __syncthreads();
     if (warp == kW) {
         producer(p, full_bar(), empty_bar(), ring_buf(p), lane);
@@ -862,8 +1024,8 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
 
     for (int m = threadIdx.x; m < p.M; m += kNT)
         if (p.pos[m] < 0 || p.pos[m] >= p.context) set_device_error(kErrBadIndex);
-    // The residual stream starts as the token embeddings (+ positions); each CTA writes the rows it owns in the
-    // o_proj / down phases, which are the only phases that read them back.
+    // The residual stream starts as the token embeddings (+ positions): each CTA computes the rows it owns (the
+    // o_proj / down rows), keeps them and publishes them for layer 0.
     {
         int n0, n1;
         cta_rows(p.C, p.grid, n0, n1);
@@ -872,31 +1034,29 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
             const int m = i / w, c = n0 + (i - m * w);
             float v = dequant_one(p.fmt, p.embed + int64_t(token_of(p, m)) * p.rb_c, p.C, c);
             if (p.wpe) v += p.wpe[int64_t(p.pos[m]) * p.C + c];
-            p.x[int64_t(m) * p.C + c] = v;
+            s_xown[m][c - n0] = v;
+            tw_put(p.x_tw + int64_t(m) * p.C + c, v, tag_of(0, kXIn));
         }
     }
-    // Phases in order: per layer qkv, attention, o_proj, up, down; then the LM head. Each GEMV phase waits for the
-    // counter of the phase that produced its activations (the attention counter counts (sequence, KV head)
-    // merges, the others CTAs) and bumps its own.
-    uint32_t st = 0;
+    // Phases in order: per layer qkv, attention, split merge, o_proj, up, down; then the LM head.
+    uint32_t st = 0, seen = 0;  // weight stages of the step: consumed by the phases so far, landings observed
     int issued = 0;  // attention copies requested so far (the parity of s_attn_bar)
     int Sm[kDecodeMaxSeqs], Pm[kDecodeMaxSeqs];
     const bool attn_cta = int(blockIdx.x) < attn_items(p, Sm, Pm);
+    // Leaving early (a wait gave up): no attention copy of ours may still be landing in shared memory.
+    auto drain = [&]() {
+        if (threadIdx.x == 0 && issued > 0) {
+            const uint64_t t0 = gtimer();
+            while (!mbar_try_wait(&s_attn_bar, uint32_t(issued - 1) & 1u) && gtimer() - t0 < p.wait_ns) {
+            }
+        }
+    };
     for (int l = 0; l <= p.layers; l++) {
-        unsigned* sy = p.sync + l * kPhases;
-        for (int k = 0; k < (l == p.layers ? 1 : kPhases); k++) {
+        for (int k = 0; k < (l == p.layers ? 1 : 5); k++) {
             if (k == kQkv && l < p.layers && attn_cta) {  // this layer's first attention item: keys / values now
                 if (threadIdx.x == 0) attn_issue(p, l, attn_item(p, Sm, Pm, blockIdx.x));
                 issued++;
             }
-            // Leaving early (a wait gave up): no attention copy of ours may still be landing in shared memory.
-            auto drain = [&]() {
-                if (threadIdx.x == 0 && issued > 0) {
-                    const uint64_t t0 = gtimer();
-                    while (!mbar_try_wait(&s_attn_bar, uint32_t(issued - 1) & 1u) && gtimer() - t0 < p.wait_ns) {
-                    }
-                }
-            };
             if (k == kAttn) {
                 const bool ok = p.hd == 128 ? attn_run<4>(p, l, issued, warp, lane)
                                             : attn_run<2>(p, l, issued, warp, lane);
@@ -904,29 +1064,24 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
                     drain();
                     return;
                 }
+                merge_run(p, l, warp, lane);
                 continue;
             }
             const int kind = l == p.layers ? int(kHead) : k;
-            const unsigned* dep = kind == kQkv ? (l ? sy - kPhases + kDown : nullptr)
-                                : kind == kHead ? sy - kPhases + kDown : sy + k - 1;
-            const unsigned target = kind == kO ? unsigned(p.M * p.KV) : unsigned(p.grid);
-            if (!gemv_run<FMT, NM>(p, gemv_ph(p, l, kind), dep, target, st, warp, lane)) {
+            if (!gemv_run<FMT, NM>(p, gemv_ph(p, l, kind), st, seen, warp, lane)) {
                 drain();
                 return;
             }
-            if (kind != kHead) signal(sy + k);
         }
     }
-    csync();
-    if (*reinterpret_cast<volatile int*>(&s_abort)) return;
     if (threadIdx.x < p.M && s_key[threadIdx.x]) atomicMax(p.keys + threadIdx.x, s_key[threadIdx.x]);
     __threadfence();
     csync();
-    if (threadIdx.x == 0) s_last = atomicAdd(p.sync + p.layers * kPhases, 1u) == unsigned(p.grid - 1) ? 1 : 0;
+    if (threadIdx.x == 0) s_last = atomicAdd(p.sync, 1u) == unsigned(p.grid - 1) ? 1 : 0;
     csync();
     if (!s_last) return;
     // Last CTA: every other CTA has passed its last wait. Greedy token per sequence (argmax_finalize_kernel
-    // semantics), then reset the counters for the next launch.
+    // semantics), then reset the step counter and advance the epoch for the next launch.
     __threadfence();
     if (threadIdx.x < p.M) {
         const int m = threadIdx.x;
@@ -943,7 +1098,10 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
             else set_device_error(kErrBadIndex);
         }
     }
-    for (int i = threadIdx.x; i <= p.layers * kPhases; i += kNT) p.sync[i] = 0u;
+    if (threadIdx.x == 0) {
+        *p.sync = 0u;
+        *p.epoch = s_epoch + decode_epoch_stride(p.layers);
+    }
 }
 
 using DecodeFn = void (*)(const DecodeParams);
@@ -958,6 +1116,12 @@ int64_t padded_x_bytes(int fmt, int M, int K) { return gemv_x_bytes(fmt, M, K); 
 int attn_scratch_floats(const DecodeParams& p) {
     const int Gq = p.H / p.KV;
     return Gq * p.hd + 2 * p.hd + Gq * p.span + kW * Gq * p.hd + 2 * Gq;
+}
+
+int64_t table_bytes(const DecodeParams& p) { return (int64_t(p.layers) * int64_t(sizeof(DecodeLayer)) + 127) / 128 * 128; }
+
+size_t smem_bytes(const DecodeParams& p) {
+    return 256 + size_t(table_bytes(p)) + size_t(p.xs_bytes) + size_t(p.kv_bytes) + size_t(p.nslot) * p.slot_bytes;
 }
 
 }  // namespace
@@ -977,6 +1141,9 @@ bool plan_decode(DecodeParams& p, std::string* why) {
     if (p.span < 32 || p.span > kMaxSpan || p.span % 32 || p.max_splits < (p.context + p.span - 1) / p.span)
         return no("attention split");
     p.grid = num_sms();
+    if ((p.C + p.grid - 1) / p.grid > kOwnRows) return no("residual rows per CTA");
+    if (!p.x_tw || !p.qkv_tw || !p.att_tw || !p.h_tw || !p.part_tw || !p.epoch || !p.sync)
+        return no("exchange buffers");
     int64_t xs = std::max({padded_x_bytes(p.fmt, p.M, p.C), padded_x_bytes(p.fmt, p.M, p.H * p.hd),
                            padded_x_bytes(p.fmt, p.M, p.F), int64_t(attn_scratch_floats(p)) * 4});
     xs = (xs + 127) / 128 * 128;
@@ -984,7 +1151,8 @@ bool plan_decode(DecodeParams& p, std::string* why) {
     int64_t slot = std::max<int64_t>(kSlotBytes, (rb_max + 1023) / 1024 * 1024);
     // A warp's pass touches rows up to kMaxGroupRows - 1 apart; while it waits for the last of their stages it
     // holds the first, so the ring must hold every stage a pass can span plus one being refilled (fewer when the
-    // CTA's share of the matrix has fewer stages).
+    // CTA's share of the matrix has fewer stages). Every warp walks every stage of a phase in order, so no warp
+    // waits on a slot more than one phase ahead of it.
     auto need_for = [&](int64_t rows, int64_t rbe) {
         const int64_t rps = slot / rbe, share = (rows + p.grid - 1) / p.grid;
         const int64_t nst = (share + rps - 1) / rps, span = (kMaxGroupRows - 1) / rps + 2;
@@ -994,7 +1162,7 @@ bool plan_decode(DecodeParams& p, std::string* why) {
                                need_for(p.F, p.rb_c * (p.qwen ? 2 : 1)), need_for(p.C, p.rb_f),
                                need_for(p.V, p.rb_c), 2});
     const int64_t kvb = int64_t(2) * kMaxSpan * p.hd * 2;
-    const int64_t budget = 227 * 1024 - kStaticSmem - 256 - xs - kvb;
+    const int64_t budget = 227 * 1024 - kStaticSmem - 256 - table_bytes(p) - xs - kvb;
     const int nslot = int(std::min<int64_t>(kMaxSlots, budget / slot));
     if (nslot < need) return no("shared memory: weight rows too wide for the slot ring");
     p.xs_bytes = int(xs);
@@ -1002,7 +1170,7 @@ bool plan_decode(DecodeParams& p, std::string* why) {
     p.slot_bytes = int(slot);
     p.nslot = nslot;
     DecodeFn k = pick(p.fmt, p.M);
-    const size_t smem = 256 + size_t(p.xs_bytes) + size_t(p.kv_bytes) + size_t(p.nslot) * p.slot_bytes;
+    const size_t smem = smem_bytes(p);
     int per_sm = 0;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThr, smem) != cudaSuccess || per_sm < 1) {
@@ -1017,20 +1185,21 @@ cudaError_t decode_clear_abort() {
     return cudaMemcpyToSymbol(g_dec_abort, &zero, sizeof(zero));
 }
 
-void decode_scratch(const DecodeParams& p, int64_t* part_floats, int64_t* tickets, int64_t* counters) {
+void decode_scratch(const DecodeParams& p, DecodeScratch* s) {
     const int Gq = p.H / std::max(1, p.KV);
-    if (part_floats) *part_floats = int64_t(p.M) * p.KV * p.max_splits * Gq * (p.hd + 2);
-    if (tickets) *tickets = int64_t(p.M) * p.KV;
-    if (counters) *counters = int64_t(p.layers) * kPhases + 1;
+    s->part_words = int64_t(p.M) * p.KV * p.max_splits * Gq * (p.hd + 2);
+    s->x_words = int64_t(p.M) * p.C;
+    s->qkv_words = int64_t(p.M) * p.QW;
+    s->att_words = int64_t(p.M) * p.H * p.hd;
+    s->h_words = int64_t(p.M) * p.F;
 }
 
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t st) {
     DecodeFn k = pick(p.fmt, p.M);
-    const size_t smem = 256 + size_t(p.xs_bytes) + size_t(p.kv_bytes) + size_t(p.nslot) * p.slot_bytes;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
     cfg.blockDim = dim3(kThr);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = smem_bytes(p);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;

@@ -187,10 +187,11 @@ struct neko_model {
     int dec_stall_test = 0;    // the next single-kernel step waits for a CTA that does not exist (50 ms limit)
     int dec_seqs = 0;          // most sequences one launch serves
     int dec_max_splits = 0;    // attention splits per (sequence, KV head) at the smallest span
-    float* dec_part = nullptr;
-    unsigned* dec_tickets = nullptr;
-    unsigned* dec_sync = nullptr;
-    int64_t dec_sync_n = 0, dec_tickets_n = 0;
+    // single-kernel decode step: tagged-word exchange buffers (one allocation), tag epoch and the step counter
+    uint64_t* dec_tw = nullptr;
+    DecodeScratch dec_sz;
+    int64_t dec_tw_words = 0;
+    unsigned* dec_sync = nullptr;  // [0] CTAs done with the step, [1] the tag epoch
     int dec_ok[kDecodeMaxSeqs + 1] = {-1, -1, -1, -1, -1};  // per sequence count: -1 not planned yet
 };
 
@@ -684,10 +685,17 @@ bool fill_decode(neko_model* m, int R, int bucket, bool advance, DecodeParams& p
     p.wpe = m->wpe;
     p.kv_slot = m->kv_slot;
     p.kv_head = m->kv_head;
-    p.x = m->x;
-    p.qkv = m->qkv;
-    p.att = m->att;
-    p.h = m->h;
+    {
+        auto pad = [](int64_t w) { return (w + 31) / 32 * 32; };
+        const DecodeScratch& z = m->dec_sz;
+        uint64_t* b = m->dec_tw;
+        p.x_tw = b;
+        p.qkv_tw = b += pad(z.x_words);
+        p.att_tw = b += pad(z.qkv_words);
+        p.h_tw = b += pad(z.att_words);
+        p.part_tw = b += pad(z.h_words);
+    }
+    p.epoch = m->dec_sync + 1;
     p.logits = m->logits;
     p.tokens = m->d_tokens;
     p.slots = m->d_slots;
@@ -695,8 +703,6 @@ bool fill_decode(neko_model* m, int R, int bucket, bool advance, DecodeParams& p
     p.argmax = m->d_argmax;
     p.keys = m->d_keys;
     p.advance = advance ? 1 : 0;
-    p.part = m->dec_part;
-    p.tickets = m->dec_tickets;
     p.sync = m->dec_sync;
     // keys per attention item: about one item per SM over the sequences' KV heads at this context bucket
     const int per = std::max(1, num_sms() / std::max(1, R * m->KV));
@@ -799,11 +805,15 @@ int debug_width(const neko_model* m) {
     }
 }
 
-// After a device error the single-kernel step may have stopped between its phases: clear its counters,
-// tickets, argmax keys and abort flag so the next step starts clean.
+// After a device error the single-kernel step may have stopped between its phases (its epoch not advanced, some
+// exchange words written under its tags): clear the exchange buffers, the step counter, the argmax keys and the
+// abort flag, and restart the epoch, so the next step starts clean.
 void decode_reset(neko_model* m) {
-    if (m->dec_sync) cudaMemset(m->dec_sync, 0, size_t(m->dec_sync_n) * 4);
-    if (m->dec_tickets) cudaMemset(m->dec_tickets, 0, size_t(m->dec_tickets_n) * 4);
+    if (m->dec_tw) cudaMemset(m->dec_tw, 0, size_t(m->dec_tw_words) * 8);
+    if (m->dec_sync) {
+        const unsigned init[2] = {0u, 1u};
+        cudaMemcpy(m->dec_sync, init, sizeof(init), cudaMemcpyHostToDevice);
+    }
     cudaMemset(m->d_keys, 0, size_t(std::max(m->cfg.max_rows, m->cfg.max_seqs)) * sizeof(unsigned long long));
     decode_clear_abort();
     cudaDeviceSynchronize();
@@ -957,25 +967,33 @@ neko_model* neko_model_create(int device, const neko_model_config* cfg, char* er
             return bail(m, "matmul chaining buffers allocation failed");
         m->work_bytes += (na + nb) * 2;
     }
-    // single-kernel decode steps: split-KV partials at the smallest span (32 keys), tickets, phase counters
+    // single-kernel decode steps: exchange buffers sized for the most sequences a launch serves and split-KV
+    // partials at the smallest span (32 keys); the step counter and the tag epoch (starting at 1, so the zeroed
+    // buffers hold no tag a step waits for)
     m->dec_seqs = std::min({kDecodeMaxSeqs, c.max_rows, c.max_seqs});
     m->dec_max_splits = (c.context + 31) / 32;
     {
         DecodeParams dp;
         dp.M = m->dec_seqs;
+        dp.C = m->C;
+        dp.QW = m->QW;
+        dp.F = m->qwen ? m->F : m->UPW;
         dp.H = m->H;
         dp.KV = m->KV;
         dp.hd = m->hd;
         dp.layers = c.layers;
         dp.max_splits = m->dec_max_splits;
-        int64_t pf2 = 0;
-        decode_scratch(dp, &pf2, &m->dec_tickets_n, &m->dec_sync_n);
-        if (falloc(&m->dec_part, size_t(pf2)) || cudaMalloc(&m->dec_tickets, size_t(m->dec_tickets_n) * 4) ||
-            cudaMalloc(&m->dec_sync, size_t(m->dec_sync_n) * 4))
-            return bail(m, "decode scratch allocation failed");
-        m->work_bytes += size_t(m->dec_tickets_n + m->dec_sync_n) * 4;
-        cudaMemset(m->dec_tickets, 0, size_t(m->dec_tickets_n) * 4);
-        cudaMemset(m->dec_sync, 0, size_t(m->dec_sync_n) * 4);
+        decode_scratch(dp, &m->dec_sz);
+        const DecodeScratch& z = m->dec_sz;
+        auto pad = [](int64_t w) { return (w + 31) / 32 * 32; };  // 256-byte aligned sections
+        m->dec_tw_words = pad(z.x_words) + pad(z.qkv_words) + pad(z.att_words) + pad(z.h_words) + pad(z.part_words);
+        if (cudaMalloc(&m->dec_tw, size_t(m->dec_tw_words) * 8) != cudaSuccess ||
+            cudaMalloc(&m->dec_sync, 2 * sizeof(unsigned)) != cudaSuccess)
+            return bail(m, "decode exchange buffers allocation failed");
+        m->work_bytes += size_t(m->dec_tw_words) * 8 + 8;
+        cudaMemset(m->dec_tw, 0, size_t(m->dec_tw_words) * 8);
+        const unsigned init[2] = {0u, 1u};
+        cudaMemcpy(m->dec_sync, init, sizeof(init), cudaMemcpyHostToDevice);
     }
     m->h_logits_floats = nout * size_t(m->V);
     if (cudaMallocHost(&m->h_in, 4 * nout * sizeof(int)) || cudaMallocHost(&m->h_logits, nout * size_t(m->V) * 4) ||
@@ -1015,7 +1033,7 @@ void neko_model_destroy(neko_model* m) {
     for (void* p : {(void*)m->warena, (void*)m->kc, (void*)m->vc, (void*)m->x, (void*)m->xn, (void*)m->qkv,
                     (void*)m->att, (void*)m->h, (void*)m->hx, (void*)m->logits, (void*)m->d_tokens,
                     (void*)m->d_argmax, (void*)m->d_outrows, (void*)m->d_keys, (void*)m->part,
-                    (void*)m->tickets, (void*)m->mm_ws, (void*)m->mm_tickets, (void*)m->dec_part, (void*)m->dec_tickets, (void*)m->dec_sync,
+                    (void*)m->tickets, (void*)m->mm_ws, (void*)m->mm_tickets, (void*)m->dec_tw, (void*)m->dec_sync,
                     (void*)m->ch_a, (void*)m->ch_b, (void*)m->ch_ss,
                     (void*)m->staging, (void*)m->staging8, (void*)m->d_track})
         if (p) cudaFree(p);

@@ -255,13 +255,17 @@ struct DecodeParams {
     const uint8_t* embed = nullptr;  // [V] rows, also the tied LM head
     const float *normf = nullptr, *normfb = nullptr, *rope = nullptr, *wpe = nullptr;
     int64_t kv_slot = 0, kv_head = 0;  // cache element strides (positions are hd apart)
-    float *x = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+    // Exchange buffers of tagged words (float bits | tag << 32), one per hand-off: x [M][C], q|k|v [M][QW],
+    // attention output [M][H * hd], SwiGLU / GELU output [M][F], split-KV partials
+    // [M][KV][max_splits][group][hd + 2] (max, sum, unnormalised P.V). Any initial content whose tags the epoch
+    // never produces (zeros with the epoch starting at 1).
+    uint64_t *x_tw = nullptr, *qkv_tw = nullptr, *att_tw = nullptr, *h_tw = nullptr, *part_tw = nullptr;
+    unsigned* epoch = nullptr;           // tag base of the next step; the kernel advances it by the stride
+    float* logits = nullptr;
     int *tokens = nullptr, *slots = nullptr, *pos = nullptr, *argmax = nullptr;
     unsigned long long* keys = nullptr;  // greedy argmax keys (zero between steps)
     int advance = 0;                     // device greedy loop: next token = argmax, position + 1
-    float* part = nullptr;               // split-KV partials [seq][kv head][split][group][hd + 2]
-    unsigned* tickets = nullptr;         // [seq][kv head], zero between steps
-    unsigned* sync = nullptr;            // phase counters [layers * 5 + 1], zero between steps
+    unsigned* sync = nullptr;            // one counter: CTAs done with the step (zero between steps)
     int span = 0, max_splits = 0;        // keys per attention split; splits per (seq, kv head) at most
     uint64_t wait_ns = 2000000000ull;    // a wait of the kernel gives up after this long (device error)
     int stall_test = 0;                  // 1: a wait that nothing satisfies (exercises the timeout path)
@@ -271,8 +275,13 @@ struct DecodeParams {
 };
 // Checks that the step fits the kernel and plans its shared memory; false (with a reason) when it does not.
 bool plan_decode(DecodeParams& p, std::string* why);
-// Scratch the kernel needs: partial floats, tickets and phase counters.
-void decode_scratch(const DecodeParams& p, int64_t* part_floats, int64_t* tickets, int64_t* counters);
+// Exchange-buffer sizes (64-bit words) for p.M sequences.
+struct DecodeScratch {
+    int64_t part_words = 0, x_words = 0, qkv_words = 0, att_words = 0, h_words = 0;
+};
+void decode_scratch(const DecodeParams& p, DecodeScratch* s);
+// Tag values one step uses: the epoch advances by this much per step.
+__host__ __device__ inline unsigned decode_epoch_stride(int layers) { return unsigned(layers + 2) * 8u; }
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t st);  // p planned by plan_decode
 cudaError_t decode_clear_abort();  // after a wait of the kernel gave up (device error reported)
 

@@ -5,6 +5,7 @@
 cannot express; ``stage`` + ``step`` run greedy decoding entirely on the device (the bench's inner loop).
 """
 import ctypes as C
+import weakref
 
 import numpy as np
 
@@ -43,6 +44,7 @@ class Model:
         self.fmt = fmt
         self.context = context
         err = C.create_string_buffer(1024)
+        self._views = []  # weak references to the host_logits views handed out
         self.h = lib().neko_model_create(device, C.byref(cfg), err, 1024)
         if not self.h:
             raise NekoError("neko_model_create: " + err.value.decode())
@@ -129,6 +131,8 @@ class Model:
         """One decode step for n sequences. Returns (logits [n][vocab] or None, argmax [n]). `out`: a float32
         C-contiguous array of at least n * vocab floats to receive the logits, reused across steps the way the
         engine reuses its logits vector (engine.cpp:56)."""
+        if not self.h:
+            raise NekoError("decode: the model is closed")
         slots = np.ascontiguousarray(slots, dtype=np.int32)
         tokens = np.ascontiguousarray(tokens, dtype=np.int32)
         pos = np.ascontiguousarray(pos, dtype=np.int32)
@@ -162,12 +166,18 @@ class Model:
 
     def host_logits(self, rows):
         """A [rows][vocab] float32 view of the runner's pinned logits buffer: as decode's `out` it takes the
-        logits with no second host copy, and the next call overwrites it."""
+        logits with no second host copy, and the next call overwrites it. The buffer belongs to the runner: after
+        close() the model no longer runs, and the runner (with this buffer) is destroyed only once every view
+        handed out here has been released, so a view never points at freed memory."""
+        if not self.h:
+            raise NekoError("host_logits: the model is closed")
         n = C.c_size_t(0)
         ptr = lib().neko_model_host_logits(self.h, C.byref(n))
         if not ptr or rows * self.vocab > n.value:
             raise NekoError("host_logits: buffer unavailable or too small")
-        return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_float)), shape=(rows, self.vocab))
+        view = np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_float)), shape=(rows, self.vocab)).view(np.ndarray)
+        self._views.append(weakref.ref(view))
+        return view
 
     def set_stop(self, stop_ids, max_new):
         """Stop ids and token budget for the device greedy loop (Engine::generate's loop on the device);
@@ -226,9 +236,24 @@ class Model:
         return p.value, r.value, c.value, fmt
 
     def close(self):
-        if self.h:
-            lib().neko_model_destroy(self.h)
-            self.h = None
+        """Ends the model. The runner is destroyed now, or, while host_logits views are still referenced, when
+        the last of them is released."""
+        if not self.h:
+            return
+        h, self.h = self.h, None
+        alive = [v for v in (r() for r in getattr(self, "_views", [])) if v is not None]
+        self._views = []
+        if not alive:
+            lib().neko_model_destroy(h)
+            return
+        left = [len(alive)]
+
+        def release():
+            left[0] -= 1
+            if left[0] == 0:
+                lib().neko_model_destroy(h)
+        for v in alive:
+            weakref.finalize(v, release)
 
     def __enter__(self):
         return self

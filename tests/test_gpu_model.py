@@ -409,3 +409,23 @@ def test_decode_into_the_pinned_host_logits_buffer():
     m.decode([0, 1], [5, 6], [10, 10], out=buf)
     assert not np.array_equal(buf, la)
     m.close()
+
+
+def test_host_logits_view_outlives_close():
+    """A host_logits view stays readable after close(): the runner is destroyed only once the last view is
+    released; the closed model refuses to decode or hand out new views."""
+    import gc
+    s = workload.shape("qwen3-tiny")
+    m = nmodel.Model(s, FP8, context=64, max_seqs=1, max_rows=16).load(workload.weights(s, seed=4))
+    m.prefill(workload.prompt(s, 10, seed=80), 0)
+    buf = m.host_logits(1)
+    want, _ = m.decode([0], [3], [10], out=buf)
+    want = want.copy()
+    m.close()
+    assert np.array_equal(buf, want)  # still the runner's pinned buffer, not freed memory
+    with pytest.raises(nb.NekoError, match="closed"):
+        m.decode([0], [3], [10], out=buf)
+    with pytest.raises(nb.NekoError, match="closed"):
+        m.host_logits(1)
+    del buf
+    gc.collect()  # the last view is gone: the deferred destroy has run
