@@ -52,7 +52,7 @@ constexpr int kMaxSpan = 64;           // keys per attention item (staged in sha
 constexpr int kStaticSmem = 8192;      // upper bound of the kernel's static shared memory
 constexpr int kOwnRows = 32;           // residual rows a CTA owns, at most (C <= 32 * grid)
 constexpr int kGatherE = 2;            // float4 groups a thread has in flight per gather batch
-constexpr int kMergeS = 16;            // split states a merge warp has in flight per batch
+constexpr int kMergeS = 8;             // split states a merge warp has in flight per batch
 
 enum Ph : int { kQkv = 0, kAttn = 1, kO = 2, kUp = 3, kDown = 4, kHead = 5 };
 // Exchanges (tag offsets) per layer. The LM head reads x under layer L's kXIn.
@@ -107,18 +107,19 @@ __device__ __forceinline__ bool tw_ok(uint64_t w, unsigned tag) { return unsigne
 __device__ __forceinline__ float tw_val(uint64_t w) { return __uint_as_float(unsigned(w)); }
 
 // Poll bookkeeping shared by the gathers: false once the wait has run past lim (reported) or another wait gave up.
+// The clock is read at the first retry and checked with the abort flag (a global load) every 16th retry only, so
+// a retry costs no more than the reload itself.
 struct Poll {
     uint64_t t0 = 0;
     uint32_t n = 0;
     __device__ __forceinline__ bool keep_going(uint64_t lim) {
-        if ((++n & 15u) != 1u) return true;
-        if (aborted()) return false;
-        const uint64_t t = gtimer();
-        if (n == 1u) {
-            t0 = t;
+        if (n++ == 0u) {
+            t0 = gtimer();
             return true;
         }
-        if (t - t0 > lim) {
+        if (n & 15u) return true;
+        if (aborted()) return false;
+        if (gtimer() - t0 > lim) {
             give_up();
             return false;
         }
@@ -197,8 +198,9 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
     return ok != 0;
 }
 
-// Bounded mbarrier wait for the decode kernel (gives up on abort or after lim ns).
-__device__ bool dwait(uint64_t* bar, uint32_t parity, uint64_t lim, uint32_t hint_ns = 20000) {
+// Bounded mbarrier wait for the decode kernel (gives up on abort or after lim ns). Out of line: callers try the
+// barrier once first, and the kernel's code is kept small (instruction fetch is on its critical path).
+__device__ __noinline__ bool dwait(uint64_t* bar, uint32_t parity, uint64_t lim, uint32_t hint_ns = 20000) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = gtimer();
     for (;;) {
@@ -257,9 +259,10 @@ struct GemvPh {
     int head;
 };
 
+template <int QW>
 __device__ __forceinline__ GemvPh gemv_ph(const DecodeParams& p, int l, int kind) {
     GemvPh g{};
-    const int lnk = p.qwen ? kNormRms : kNormLayer;
+    const int lnk = QW ? kNormRms : kNormLayer;
     if (kind == kHead) {
         g.W = p.embed; g.rb = p.rb_c; g.rows = p.V; g.K = p.C;
         g.x = p.x_tw; g.xtag = tag_of(p.layers, kXIn); g.norm = lnk; g.gamma = p.normf; g.beta = p.normfb;
@@ -270,20 +273,20 @@ __device__ __forceinline__ GemvPh gemv_ph(const DecodeParams& p, int l, int kind
     if (kind == kQkv) {
         g.W = L.wqkv; g.rb = p.rb_c; g.rows = p.QW; g.K = p.C;
         g.x = p.x_tw; g.xtag = tag_of(l, kXIn); g.norm = lnk; g.gamma = L.ln1; g.beta = L.ln1b;
-        g.bias = L.bqkv; g.flags = p.qwen ? 0 : kBias; g.y = p.qkv_tw; g.ytag = tag_of(l, kXQkv); g.ys = p.QW;
+        g.bias = L.bqkv; g.flags = QW ? 0 : kBias; g.y = p.qkv_tw; g.ytag = tag_of(l, kXQkv); g.ys = p.QW;
     } else if (kind == kO) {
         g.W = L.wo; g.rb = p.rb_att; g.rows = p.C; g.K = p.H * p.hd;
         g.x = p.att_tw; g.xtag = tag_of(l, kXAtt);
-        g.bias = L.bo; g.flags = p.qwen ? 0 : kBias; g.y = p.x_tw; g.ytag = tag_of(l, kXMid); g.ys = p.C;
+        g.bias = L.bo; g.flags = QW ? 0 : kBias; g.y = p.x_tw; g.ytag = tag_of(l, kXMid); g.ys = p.C;
         g.resid = 1;
     } else if (kind == kUp) {
-        g.W = L.wup; g.rb = p.rb_c; g.rows = p.F; g.K = p.C; g.pair = p.qwen;
+        g.W = L.wup; g.rb = p.rb_c; g.rows = p.F; g.K = p.C; g.pair = QW;
         g.x = p.x_tw; g.xtag = tag_of(l, kXMid); g.norm = lnk; g.gamma = L.ln2; g.beta = L.ln2b;
-        g.bias = L.bup; g.flags = p.qwen ? 0 : (kBias | kGelu); g.y = p.h_tw; g.ytag = tag_of(l, kXH); g.ys = p.F;
+        g.bias = L.bup; g.flags = QW ? 0 : (kBias | kGelu); g.y = p.h_tw; g.ytag = tag_of(l, kXH); g.ys = p.F;
     } else {
         g.W = L.wdown; g.rb = p.rb_f; g.rows = p.C; g.K = p.F;
         g.x = p.h_tw; g.xtag = tag_of(l, kXH);
-        g.bias = L.bdown; g.flags = p.qwen ? 0 : kBias; g.y = p.x_tw; g.ytag = tag_of(l + 1, kXIn); g.ys = p.C;
+        g.bias = L.bdown; g.flags = QW ? 0 : kBias; g.y = p.x_tw; g.ytag = tag_of(l + 1, kXIn); g.ys = p.C;
         g.resid = 1;
     }
     return g;
@@ -303,12 +306,13 @@ __device__ __forceinline__ int mat_kind(const DecodeParams& p, int l, int k) {
 }
 
 // ---------------------------------------------------------------------------------------------- producer
+template <int QW>
 __device__ void producer(const DecodeParams& p, uint64_t* full, uint64_t* empty, uint8_t* ring, int lane) {
     uint32_t st = 0;
     bool ok = true;
     for (int l = 0; l <= p.layers && ok; l++) {
         for (int k = 0; k < (l == p.layers ? 1 : 4) && ok; k++) {
-            const GemvPh g = gemv_ph(p, l, mat_kind(p, l, k));
+            const GemvPh g = gemv_ph<QW>(p, l, mat_kind(p, l, k));
             int r0, r1;
             cta_rows(g.rows, p.grid, r0, r1);
             const int rps = stage_rows(p, g);
@@ -462,12 +466,19 @@ __device__ bool stage_x(const DecodeParams& p, const GemvPh& g, float* xs, int w
     return true;
 }
 
+// 1 / sqrt(ss / n + eps) in double, rounded to float (the norms of cpu_ops.cpp:483-511), with CUDA's double
+// reciprocal square root: its result differs from the reference's correctly rounded divide and square root by
+// far less than the float rounding that follows.
+__device__ __forceinline__ float inv_rms(double ss, double inv_n, float eps) {
+    return float(rsqrt(ss * inv_n + double(eps)));
+}
+
 // rstd of row m from the staging pass's per-warp sums of squares (RMSNorm, cpu_ops.cpp:502-511).
 __device__ __forceinline__ float rms_rstd(const DecodeParams& p, int m, int K) {
     double a = 0.0;
 #pragma unroll
     for (int w = 0; w < kW; w++) a += s_ss[w][m];
-    return float(1.0 / sqrt(a / K + double(p.eps)));
+    return inv_rms(a, 1.0 / K, p.eps);
 }
 
 // One GEMV phase on this CTA's rows: take the first weight stage, gather and stage the inputs, consume the
@@ -572,7 +583,7 @@ __device__ __forceinline__ bool gemv_run(const DecodeParams& p, const GemvPh& g,
                 if (g.pair) {
                     const float gs = __fmul_rn(red_[r][m], rs);
                     const float us = __fmul_rn(red_[rpp + r < RR ? rpp + r : 0][m], rs);
-                    val = gs / (1.0f + expf(-gs)) * us;  // cpu::siluMul (cpu_ops.cpp:526-533)
+                    val = __fdividef(gs, 1.0f + expf(-gs)) * us;  // cpu::siluMul (cpu_ops.cpp:526-533)
                 } else {
                     val = rms ? __fmul_rn(red_[r][m], rs) : red_[r][m];
                     if (g.flags & kBias) val += g.bias[row];
@@ -701,7 +712,7 @@ __device__ __forceinline__ void attn_issue(const DecodeParams& p, int l, const A
 // were copied to shared memory when the layer started. Lane l owns dims [l * DL, l * DL + DL) of a key / value
 // row for scores (cpu_ops.cpp:558) and P.V. A sequence with one split writes its heads' output; with several,
 // each item writes its partial softmax state (max, sum, unnormalised P.V) for merge_run.
-template <int DL>
+template <int DL, int QW>
 __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued, int warp, int lane) {
     const int Gq = p.H / p.KV, hd = p.hd, span = p.span;
     int Sm[kDecodeMaxSeqs], Pm[kDecodeMaxSeqs];
@@ -722,7 +733,7 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued,
     AttnItem a = attn_item(p, Sm, Pm, blockIdx.x);
     float cs_c[DL / 2], cs_s[DL / 2], wn[DL];
     auto load_rot = [&](const AttnItem& it) {
-        if (p.qwen && warp <= Gq) {
+        if (QW && warp <= Gq) {
             const float* cs = p.rope + int64_t(it.pos) * hd;
 #pragma unroll
             for (int i = 0; i < DL / 2; i++) {
@@ -750,12 +761,12 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued,
             float e[DL];
             ok = gather_lane<DL>(p.qkv_tw + int64_t(m) * p.QW + col + lane, 32, qtag, e, p.wait_ns);
             if (ok) {
-                if (p.qwen && which != 2) {
+                if (QW && which != 2) {
                     double ss = 0.0;
 #pragma unroll
                     for (int i = 0; i < DL; i++) ss += double(e[i]) * e[i];
                     ss = wsum_d(ss);
-                    const float sn = float(1.0 / sqrt(ss / hd + double(p.eps)));
+                    const float sn = inv_rms(ss, 1.0 / hd, p.eps);
 #pragma unroll
                     for (int i = 0; i < DL; i++) e[i] = __fmul_rn(__fmul_rn(e[i], sn), wn[i]);
 #pragma unroll
@@ -886,7 +897,7 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued,
             for (int w = 0; w < kW; w++) sacc += red[w * outs + o];
             const int gq = o / hd, d = o - gq * hd;
             if (a.ns == 1) {
-                tw_put(p.att_tw + int64_t(m) * p.H * hd + int64_t(g) * outs + o, sacc / sst[2 * gq + 1],
+                tw_put(p.att_tw + int64_t(m) * p.H * hd + int64_t(g) * outs + o, __fdividef(sacc, sst[2 * gq + 1]),
                        tag_of(l, kXAtt));
             } else {
                 uint64_t* pr = p.part_tw + (((int64_t(m) * p.KV + g) * p.max_splits + a.j) * Gq + gq) * (hd + 2);
@@ -978,24 +989,26 @@ __device__ __noinline__ void merge_run(const DecodeParams& p, int l, int warp, i
             if (!ok) break;
             const float ms = tw_val(wm), ls = tw_val(wl);
             // in split order: the running max, then the rescaled sums
+            float wv[kMergeS];
 #pragma unroll
-            for (int j = 0; j < kMergeS; j++) {
-                if (j >= cnt) break;
+            for (int j = 0; j < kMergeS; j++) wv[j] = tw_val(w[j]);
+#pragma unroll 1
+            for (int j = 0; j < cnt; j++) {
                 const float mj = __shfl_sync(0xffffffffu, ms, j), lj = __shfl_sync(0xffffffffu, ls, j);
                 const float Mn = fmaxf(M, mj);
                 const float a = expf(M - Mn), e = expf(mj - Mn);  // exp(-inf) = 0 for the first split
                 den = den * a + lj * e;
-                num = num * a + tw_val(w[j]) * e;
+                num = num * a + wv[j] * e;
                 M = Mn;
             }
         }
         if (!ok) return;
-        tw_put(p.att_tw + int64_t(m) * p.H * hd + int64_t(g * Gq + gq) * hd + d, num / den, atag);
+        tw_put(p.att_tw + int64_t(m) * p.H * hd + int64_t(g * Gq + gq) * hd + d, __fdividef(num, den), atag);
     }
 }
 
 // ---------------------------------------------------------------------------------------------- the kernel
-template <int FMT, int NM>
+template <int FMT, int NM, int QW, int DL>
 __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -1018,7 +1031,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
     if (threadIdx.x < kDecodeMaxSeqs) s_key[threadIdx.x] = 0ull;
     __syncthreads();
     if (warp == kW) {
-        producer(p, full_bar(), empty_bar(), ring_buf(p), lane);
+        producer<QW>(p, full_bar(), empty_bar(), ring_buf(p), lane);
         return;
     }
 
@@ -1058,8 +1071,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
                 issued++;
             }
             if (k == kAttn) {
-                const bool ok = p.hd == 128 ? attn_run<4>(p, l, issued, warp, lane)
-                                            : attn_run<2>(p, l, issued, warp, lane);
+                const bool ok = attn_run<DL, QW>(p, l, issued, warp, lane);
                 if (!ok) {
                     drain();
                     return;
@@ -1068,7 +1080,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
                 continue;
             }
             const int kind = l == p.layers ? int(kHead) : k;
-            if (!gemv_run<FMT, NM>(p, gemv_ph(p, l, kind), st, seen, warp, lane)) {
+            if (!gemv_run<FMT, NM>(p, gemv_ph<QW>(p, l, kind), st, seen, warp, lane)) {
                 drain();
                 return;
             }
@@ -1106,9 +1118,16 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
 
 using DecodeFn = void (*)(const DecodeParams);
 
-DecodeFn pick(int fmt, int M) {
-    if (fmt == kFP8) return M == 1 ? decode_kernel<kFP8, 1> : decode_kernel<kFP8, kDecodeMaxSeqs>;
-    return M == 1 ? decode_kernel<kFP4, 1> : decode_kernel<kFP4, kDecodeMaxSeqs>;
+// One instantiation per weight format, sequence count (1, or up to 4), model family and head dim (hd 128: four
+// dims a lane, 64: two), so each holds only the code its model executes.
+template <int QW, int DL>
+DecodeFn pick_fm(int fmt, int M) {
+    if (fmt == kFP8) return M == 1 ? decode_kernel<kFP8, 1, QW, DL> : decode_kernel<kFP8, kDecodeMaxSeqs, QW, DL>;
+    return M == 1 ? decode_kernel<kFP4, 1, QW, DL> : decode_kernel<kFP4, kDecodeMaxSeqs, QW, DL>;
+}
+DecodeFn pick(const DecodeParams& p) {
+    if (!p.qwen) return p.hd == 64 ? pick_fm<0, 2>(p.fmt, p.M) : nullptr;
+    return p.hd == 128 ? pick_fm<1, 4>(p.fmt, p.M) : p.hd == 64 ? pick_fm<1, 2>(p.fmt, p.M) : nullptr;
 }
 
 int64_t padded_x_bytes(int fmt, int M, int K) { return gemv_x_bytes(fmt, M, K); }
@@ -1169,7 +1188,8 @@ bool plan_decode(DecodeParams& p, std::string* why) {
     p.kv_bytes = int(kvb);
     p.slot_bytes = int(slot);
     p.nslot = nslot;
-    DecodeFn k = pick(p.fmt, p.M);
+    DecodeFn k = pick(p);
+    if (!k) return no("GPT-2 with head_dim 64, Qwen3 with head_dim 64 or 128");
     const size_t smem = smem_bytes(p);
     int per_sm = 0;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess ||
@@ -1195,7 +1215,8 @@ void decode_scratch(const DecodeParams& p, DecodeScratch* s) {
 }
 
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t st) {
-    DecodeFn k = pick(p.fmt, p.M);
+    DecodeFn k = pick(p);
+    if (!k) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
     cfg.blockDim = dim3(kThr);
