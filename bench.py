@@ -13,8 +13,9 @@ oracle/_ref) on this host's cores.
 
     python bench.py [--gpus N --steps K --warmup W --batch B --impl ours|reference --model M]
 
---model qwen3-1.7b-fp4 runs BASELINE configs[2] instead (Qwen3-1.7B shape, the engine's FP4 weights, a
-1024-token prompt); the default is the headline configuration above.
+--model selects another BASELINE configuration: gpt2-fp8 (configs[0]: GPT-2 small, FP8, 32-token prompt),
+qwen3-1.7b-fp4 (configs[2]: Qwen3-1.7B shape, the engine's FP4 weights, a 1024-token prompt), qwen3-4b-fp8 /
+qwen3-4b-fp4 (configs[3]'s per-GPU batch: run with --batch 512); the default is the headline configuration above.
 """
 import argparse
 import json
@@ -30,8 +31,9 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-# --model: the headline configuration or the FP4 one
+# --model: the headline configuration and the other measured configurations
 MODELS = {"qwen3-0.6b-fp8": ("qwen3-0.6b", 1, 512, "Qwen3-0.6B FP8 decode tok/s"),
+          "gpt2-fp8": ("gpt2", 1, 32, "GPT-2 small FP8 decode tok/s"),
           "qwen3-1.7b-fp4": ("qwen3-1.7b", 2, 1024, "Qwen3-1.7B FP4 decode tok/s"),
           # BASELINE's data-parallel config: 512 sequences of a 256-token prompt + 128 steps per GPU
           "qwen3-4b-fp8": ("qwen3-4b", 1, 256, "Qwen3-4B FP8 decode tok/s"),
@@ -47,7 +49,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--model", choices=sorted(MODELS), default="qwen3-0.6b-fp8",
-                   help="qwen3-0.6b-fp8 (512-token prompt, the headline), qwen3-1.7b-fp4 (1024-token prompt), "
+                   help="qwen3-0.6b-fp8 (512-token prompt, the headline), gpt2-fp8 (32-token prompt), "
+                        "qwen3-1.7b-fp4 (1024-token prompt), "
                         "qwen3-4b-fp8 / qwen3-4b-fp4 (256-token prompt; BASELINE runs them at --batch 512 "
                         "--steps 128)")
     p.add_argument("--prompt", type=int, default=None,
