@@ -331,9 +331,18 @@ def run_ours(args):
     context = (context + 255) // 256 * 256
     cpu_on = (rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile
               and os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libneko_ref.so")))
-    h16 = [] if cpu_on else None
+    cpu = None
+    if cpu_on:
+        # First, before the GPU work starts threads of its own on this host: the same routine, weights
+        # generator, prompt and positions as --impl reference, so the two CPU figures measure the same thing.
+        with tempfile.TemporaryDirectory() as tmp:
+            try:
+                v, k, threads, sample = reference_decode(s, random_h16(s), tmp, prompt_len, warm, steps)
+                cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample}
+            except Exception as e:  # the baseline is reported, never required
+                cpu = {"value": None, "unit": "tok/s", "error": str(e)[:200]}
     m = nmodel.Model(s, FMT, context=context, max_seqs=B, max_rows=max(64, B), device=local)
-    m.load_random_device(seed=0, host_copy=(lambda n, a: h16.append((n, a))) if cpu_on else None)
+    m.load_random_device(seed=0)
 
     # prefill every sequence (different prompts per rank and sequence)
     first = np.zeros(B, np.int32)
@@ -431,14 +440,6 @@ def run_ours(args):
                            "achieved": round(per_launch / t_launch / 1e9, 1), "bytes_per_launch": per_launch,
                            "launch_us": t_launch * 1e6}
 
-    cpu = None
-    if cpu_on:
-        with tempfile.TemporaryDirectory() as tmp:
-            try:  # the same routine, prompt and positions as --impl reference, on this run's weights
-                v, k, threads, sample = reference_decode(s, h16, tmp, prompt_len, warm, steps)
-                cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample}
-            except Exception as e:  # the baseline is reported, never required
-                cpu = {"value": None, "unit": "tok/s", "error": str(e)[:200]}
     m.close()
     if rank == 0:
         line = {
