@@ -621,8 +621,11 @@ cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl) {
     if (a.norm != kNormNone && !gemv_norm_fusable(a.fmt, a.M, a.K)) return cudaErrorNotSupported;
     const int64_t rbe = a.row_bytes * (a.pair_off ? 2 : 1);
     if (a.row_bytes % 16) return cudaErrorNotSupported;
-    // the tensor-core variant for 2..4 rows (one row: the CUDA-core kernel is faster, 54 vs 73 us at the LM-head
-    // shape, where the tensor-core variant's one bulk copy per row limits the stream)
+    // FP8: the direct-load tensor-core kernel (k_gemv_fp8tc.cu) when it fits
+    if (a.fmt == kFP8)
+        if (const cudaError_t e = launch_gemv_fp8_tc(a, st, pdl); e != cudaErrorNotSupported) return e;
+    // the f16 tensor-core variant for 2..4 rows (one row: the CUDA-core kernel is faster, 54 vs 73 us at the
+    // LM-head shape, where this variant's one bulk copy per row limits the stream)
     if (a.M >= 2)
         if (const cudaError_t e = launch_gemv_mma(a, st, pdl); e != cudaErrorNotSupported) return e;
     StreamPlan sp;

@@ -112,6 +112,9 @@ cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, bool pdl, int max_ctas = 0)
 // The streaming kernel for 1..4 FP8 / FP4 activation rows (k_gemv_stream.cu); cudaErrorNotSupported when the
 // call does not fit it (launch_gemv then uses the general kernel).
 cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl);
+// The direct-load tensor-core GEMV for 1..4 FP8 activation rows (k_gemv_fp8tc.cu); cudaErrorNotSupported when the
+// call does not fit it.
+cudaError_t launch_gemv_fp8_tc(const GemvArgs& a, cudaStream_t st, bool pdl);
 // The tensor-core kernel for 5+ activation rows (k_mma.cu); cudaErrorNotSupported when the call does not fit.
 cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl);
 // The tcgen05 kernel (k_umma.cu) for 128+ rows on activations split into f16 hi / lo ([M][K] each);
