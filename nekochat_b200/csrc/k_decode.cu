@@ -257,6 +257,7 @@ struct GemvPh {
     int64_t ys;
     int resid;           // output rows are residual rows of x (o_proj, down): added to this CTA's copy
     int head;
+    float* xout;         // plain output rows [M][ys] instead of tagged words (the last down with x_final)
 };
 
 template <int QW>
@@ -288,6 +289,7 @@ __device__ __forceinline__ GemvPh gemv_ph(const DecodeParams& p, int l, int kind
         g.x = p.h_tw; g.xtag = tag_of(l, kXH);
         g.bias = L.bdown; g.flags = QW ? 0 : kBias; g.y = p.x_tw; g.ytag = tag_of(l + 1, kXIn); g.ys = p.C;
         g.resid = 1;
+        if (l == p.layers - 1) g.xout = p.x_final;
     }
     return g;
 }
@@ -310,7 +312,8 @@ template <int QW>
 __device__ void producer(const DecodeParams& p, uint64_t* full, uint64_t* empty, uint8_t* ring, int lane) {
     uint32_t st = 0;
     bool ok = true;
-    for (int l = 0; l <= p.layers && ok; l++) {
+    const int last = p.x_final ? p.layers - 1 : p.layers;  // the LM head's weights too unless it runs apart
+    for (int l = 0; l <= last && ok; l++) {
         for (int k = 0; k < (l == p.layers ? 1 : 4) && ok; k++) {
             const GemvPh g = gemv_ph<QW>(p, l, mat_kind(p, l, k));
             int r0, r1;
@@ -597,6 +600,8 @@ __device__ __forceinline__ bool gemv_run(const DecodeParams& p, const GemvPh& g,
                 if (g.head) {
                     p.logits[int64_t(m) * g.ys + row] = val;
                     best[m] = max(best[m], argmax_key(val, row));
+                } else if (g.xout) {
+                    g.xout[int64_t(m) * g.ys + row] = val;
                 } else {
                     tw_put(g.y + int64_t(m) * g.ys + row, val, g.ytag);
                 }
@@ -1064,7 +1069,8 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
             }
         }
     };
-    for (int l = 0; l <= p.layers; l++) {
+    const int last = p.x_final ? p.layers - 1 : p.layers;  // the LM head runs apart when x_final is set
+    for (int l = 0; l <= last; l++) {
         for (int k = 0; k < (l == p.layers ? 1 : 5); k++) {
             if (k == kQkv && l < p.layers && attn_cta) {  // this layer's first attention item: keys / values now
                 if (threadIdx.x == 0) attn_issue(p, l, attn_item(p, Sm, Pm, blockIdx.x));
@@ -1087,6 +1093,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
         }
     }
     if (threadIdx.x < p.M && s_key[threadIdx.x]) atomicMax(p.keys + threadIdx.x, s_key[threadIdx.x]);
+    // (No early trigger of the dependent LM-head launch: releasing it here measured 60 us slower per step.)
     __threadfence();
     csync();
     if (threadIdx.x == 0) s_last = atomicAdd(p.sync, 1u) == unsigned(p.grid - 1) ? 1 : 0;
@@ -1095,7 +1102,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
     // Last CTA: every other CTA has passed its last wait. Greedy token per sequence (argmax_finalize_kernel
     // semantics), then reset the step counter and advance the epoch for the next launch.
     __threadfence();
-    if (threadIdx.x < p.M) {
+    if (threadIdx.x < p.M && !p.x_final) {  // (with x_final the separate LM head and its finalize do this)
         const int m = threadIdx.x;
         const unsigned long long key = atomicExch(p.keys + m, 0ull);
         int idx = int(0xFFFFFFFFu - unsigned(key & 0xFFFFFFFFull));

@@ -614,6 +614,10 @@ cudaError_t launch_gemv_mma(const GemvArgs& a, cudaStream_t st, bool pdl) {
 // when it fits; the CUDA-core one otherwise.
 cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl) {
     if (a.M < 1 || a.M > kDecodeMaxSeqs || (a.fmt != kFP8 && a.fmt != kFP4)) return cudaErrorNotSupported;
+    // FP8: the direct-load tensor-core kernel (k_gemv_fp8tc.cu) when it fits (any norm width: it reads the
+    // activations from global memory)
+    if (a.fmt == kFP8)
+        if (const cudaError_t e = launch_gemv_fp8_tc(a, st, pdl); e != cudaErrorNotSupported) return e;
     if (a.x_stride % 4 || (reinterpret_cast<uintptr_t>(a.x) & 15) || a.K % 4) return cudaErrorNotSupported;
     if (a.argmax && a.pair_off) return cudaErrorNotSupported;
     const int64_t xs = (gemv_x_bytes(a.fmt, a.M, a.K) + 127) / 128 * 128;
@@ -621,9 +625,6 @@ cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl) {
     if (a.norm != kNormNone && !gemv_norm_fusable(a.fmt, a.M, a.K)) return cudaErrorNotSupported;
     const int64_t rbe = a.row_bytes * (a.pair_off ? 2 : 1);
     if (a.row_bytes % 16) return cudaErrorNotSupported;
-    // FP8: the direct-load tensor-core kernel (k_gemv_fp8tc.cu) when it fits
-    if (a.fmt == kFP8)
-        if (const cudaError_t e = launch_gemv_fp8_tc(a, st, pdl); e != cudaErrorNotSupported) return e;
     // the f16 tensor-core variant for 2..4 rows (one row: the CUDA-core kernel is faster, 54 vs 73 us at the
     // LM-head shape, where this variant's one bulk copy per row limits the stream)
     if (a.M >= 2)

@@ -570,6 +570,7 @@ int enqueue_step(neko_model* m, int R, int nout, bool outrows_identity, int max_
 }
 
 bool fill_decode(neko_model* m, int R, int bucket, bool advance, DecodeParams& p, std::string* why);
+bool head_split_ok(const neko_model* m, int R);
 
 // Whether decode steps of R sequences can run as the single kernel (planned once per R).
 bool decode_ok(neko_model* m, int R) {
@@ -624,7 +625,7 @@ bool chain_head_ok(const neko_model* m, int R) {
 
 int step_launches(neko_model* m, int R, int nout, bool gather, bool do_argmax, bool advance) {
     if (!gather && nout == R && m->debug_layers < 0 && m->dec_enabled && R <= m->dec_seqs && decode_ok(m, R))
-        return 1;
+        return head_split_ok(m, R) ? 3 : 1;  // the decode kernel (+ the LM head and argmax finalize)
     if (m->debug_layers < 0 && chain_ok(m, R)) {
         // embedding, the first layer's norm split + qkv, then per layer qkv_post, attention, o_proj, gate / up,
         // down and (after the first) qkv
@@ -650,6 +651,12 @@ int step_launches(neko_model* m, int R, int nout, bool gather, bool do_argmax, b
 
 // Parameters of the single-kernel decode step for R sequences (tokens / slots / positions in the device arrays);
 // false when the model or the step does not fit that kernel.
+// The LM head of a single-kernel decode step as a launch of its own: the direct-load tensor-core GEMV streams the
+// head at about twice the rate of the in-kernel phase (FP8 heads that it takes: C a multiple of 128).
+bool head_split_ok(const neko_model* m, int R) {
+    return m->embed.fmt == kFP8 && R <= kDecodeMaxSeqs && m->C % 128 == 0 && m->embed.rb % 16 == 0;
+}
+
 bool fill_decode(neko_model* m, int R, int bucket, bool advance, DecodeParams& p, std::string* why) {
     if (!m->dec_enabled || R < 1 || R > m->dec_seqs || size_t(m->layers.size()) > size_t(kDecodeMaxLayers)) {
         if (why) *why = "disabled or too many sequences / layers";
@@ -697,6 +704,7 @@ bool fill_decode(neko_model* m, int R, int bucket, bool advance, DecodeParams& p
     }
     p.epoch = m->dec_sync + 1;
     p.logits = m->logits;
+    p.x_final = head_split_ok(m, R) ? m->x : nullptr;  // m->x is free during single-kernel steps
     p.tokens = m->d_tokens;
     p.slots = m->d_slots;
     p.pos = m->d_pos;
@@ -760,7 +768,29 @@ int run_step(neko_model* m, int R, int nout, bool identity, int max_pos, bool do
         if (single && !fill_decode(m, R, bucket, advance, dp, nullptr))
             rc = fail(m, NEKO_ERR_CUDA, "decode kernel plan");
         else if (single) {
-            const cudaError_t le = launch_decode(dp, cap);
+            cudaError_t le = launch_decode(dp, cap);
+            if (le == cudaSuccess && dp.x_final) {  // final norm + LM head + greedy argmax, then the token / position
+                GemvArgs a;
+                a.W = m->embed.w;
+                a.row_bytes = m->embed.rb;
+                a.rows = m->V;
+                a.K = m->C;
+                a.fmt = m->embed.fmt;
+                a.x = dp.x_final;
+                a.x_stride = m->C;
+                a.M = R;
+                a.norm = m->qwen ? kNormRms : kNormLayer;
+                a.gamma = m->normf;
+                a.beta = m->normfb;
+                a.eps = m->cfg.eps;
+                a.y = m->logits;
+                a.y_stride = m->V;
+                a.argmax = m->d_keys;
+                le = launch_gemv(a, cap, true);
+                if (le == cudaSuccess)
+                    le = launch_ex(argmax_finalize_kernel, dim3(1), dim3(128), 0, cap, true, m->d_keys, m->d_argmax,
+                                   m->d_tokens, m->d_pos, R, m->cfg.context, advance ? 1 : 0);
+            }
             if (le != cudaSuccess) rc = fail(m, NEKO_ERR_CUDA, cuda_msg(le, "decode kernel"));
         } else {
             rc = enqueue_step(m, R, nout, identity, bucket - 1, do_argmax, advance, cap);

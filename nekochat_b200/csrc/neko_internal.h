@@ -265,6 +265,8 @@ struct DecodeParams {
     uint64_t *x_tw = nullptr, *qkv_tw = nullptr, *att_tw = nullptr, *h_tw = nullptr, *part_tw = nullptr;
     unsigned* epoch = nullptr;           // tag base of the next step; the kernel advances it by the stride
     float* logits = nullptr;
+    float* x_final = nullptr;            // non-null: no LM head phase; the last layer's residual rows go here as
+                                         // plain floats [M][C] for a separate LM-head launch (and no argmax)
     int *tokens = nullptr, *slots = nullptr, *pos = nullptr, *argmax = nullptr;
     unsigned long long* keys = nullptr;  // greedy argmax keys (zero between steps)
     int advance = 0;                     // device greedy loop: next token = argmax, position + 1
