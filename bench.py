@@ -453,7 +453,8 @@ def run_ours(args):
                 rec = json.load(open(tf)).get(key)
                 if rec:  # ncu DRAM bytes of one launch, scaled from the captured position to this run's mean
                     roof["traffic"] = round(rec["dram_bytes"] * bytes_step / rec["algorithmic_bytes"])
-                    roof["traffic_note"] = (f"ncu dram__bytes_read+write of one launch at position {rec['position']} "
+                    what = rec.get("launches", "one launch")
+                    roof["traffic_note"] = (f"ncu dram__bytes_read+write of {what} at position {rec['position']} "
                                             f"({rec['dram_bytes']} B vs {rec['algorithmic_bytes']} B algorithmic), "
                                             "scaled by the algorithmic bytes to the mean timed position")
             except Exception:
