@@ -32,6 +32,7 @@
 #include <algorithm>
 
 #include "gemv_core.cuh"
+#include "mma_frag.cuh"
 #include "neko_common.cuh"
 #include "neko_internal.h"
 
@@ -49,7 +50,6 @@ constexpr int kMaxStatSlots = 256;     // LayerNorm partial-sum slots (kGatherE 
 constexpr int kChunk = 8192;           // bytes per bulk copy
 constexpr int kMaxGq = 4;              // query heads per KV head
 constexpr int kMaxSpan = 64;           // keys per attention item (staged in shared memory)
-constexpr int kStaticSmem = 8192;      // upper bound of the kernel's static shared memory
 constexpr int kOwnRows = 32;           // residual rows a CTA owns, at most (C <= 32 * grid)
 constexpr int kGatherE = 2;            // float4 groups a thread has in flight per gather batch
 constexpr int kMergeS = 8;             // split states a merge warp has in flight per batch
@@ -299,8 +299,10 @@ __device__ __forceinline__ void cta_rows(int rows, int grid, int& r0, int& r1) {
     r0 = min(rows, int(blockIdx.x) * rpc);
     r1 = min(rows, r0 + rpc);
 }
+// Rows (SwiGLU: gate / up pairs) per ring stage: as many as a slot holds, at most 16 per consumer warp (a stage's
+// 16-row tiles are split over the warps along K).
 __device__ __forceinline__ int stage_rows(const DecodeParams& p, const GemvPh& g) {
-    return int(int64_t(p.slot_bytes) / (g.rb * (g.pair ? 2 : 1)));
+    return min(int(int64_t(p.slot_bytes) / (g.rb * (g.pair ? 2 : 1))), 16 * kW);
 }
 // GEMV phase kind of the k-th matrix of layer l (l == layers: the LM head).
 __device__ __forceinline__ int mat_kind(const DecodeParams& p, int l, int k) {
@@ -366,6 +368,22 @@ __device__ __forceinline__ int token_of(const DecodeParams& p, int m) {
     return t;
 }
 
+// 1 / sqrt(ss / n + eps) in double, rounded to float (the norms of cpu_ops.cpp:483-511), with CUDA's double
+// reciprocal square root: its result differs from the reference's correctly rounded divide and square root by
+// far less than the float rounding that follows.
+__device__ __forceinline__ float inv_rms(double ss, double inv_n, float eps) {
+    return float(rsqrt(ss * inv_n + double(eps)));
+}
+
+// rstd of row m from the staging pass's per-warp sums of squares (RMSNorm, cpu_ops.cpp:502-511).
+__device__ __forceinline__ float rms_rstd(const DecodeParams& p, int m, int K) {
+    double a = 0.0;
+#pragma unroll
+    for (int w = 0; w < kW; w++) a += s_ss[w][m];
+    return inv_rms(a, 1.0 / K, p.eps);
+}
+
+// ---------------------------------------------------------------------------------------------- GEMV phases, one sequence
 // Weight rows a warp walks together (independent load streams): more for one sequence, where the registers of
 // the activation tiles are free.
 template <int NM>
@@ -469,27 +487,13 @@ __device__ bool stage_x(const DecodeParams& p, const GemvPh& g, float* xs, int w
     return true;
 }
 
-// 1 / sqrt(ss / n + eps) in double, rounded to float (the norms of cpu_ops.cpp:483-511), with CUDA's double
-// reciprocal square root: its result differs from the reference's correctly rounded divide and square root by
-// far less than the float rounding that follows.
-__device__ __forceinline__ float inv_rms(double ss, double inv_n, float eps) {
-    return float(rsqrt(ss * inv_n + double(eps)));
-}
-
-// rstd of row m from the staging pass's per-warp sums of squares (RMSNorm, cpu_ops.cpp:502-511).
-__device__ __forceinline__ float rms_rstd(const DecodeParams& p, int m, int K) {
-    double a = 0.0;
-#pragma unroll
-    for (int w = 0; w < kW; w++) a += s_ss[w][m];
-    return inv_rms(a, 1.0 / K, p.eps);
-}
-
-// One GEMV phase on this CTA's rows: take the first weight stage, gather and stage the inputs, consume the
-// producer's stages, store the outputs as tagged words. A pass of a warp takes RR rows (RR / 2 gate / up pairs
-// for SwiGLU) spaced kW apart, so the CTA's warps walk the stages together and free them in order. Returns false
-// when the kernel must stop (a wait failed).
+// One GEMV phase of one sequence on CUDA cores: take the first weight stage, gather and stage the inputs,
+// consume the producer's stages, store the outputs as tagged words. A pass of a warp takes RR rows (RR / 2 gate /
+// up pairs for SwiGLU) spaced kW apart, so the CTA's warps walk the stages together and free them in order (no
+// barrier per stage: at one sequence this beats the tensor-core phase below, 0.85 vs 0.92 ms per Qwen3-0.6B
+// step). Returns false when the kernel must stop (a wait failed).
 template <int FMT, int NM>
-__device__ __forceinline__ bool gemv_run(const DecodeParams& p, const GemvPh& g, uint32_t& st_base, uint32_t& seen,
+__device__ __forceinline__ bool gemv_run_cc(const DecodeParams& p, const GemvPh& g, uint32_t& st_base, uint32_t& seen,
                                          int warp, int lane) {
     constexpr int RR = kRows<NM>;
     int r0, r1;
@@ -629,6 +633,355 @@ __device__ __forceinline__ bool gemv_run(const DecodeParams& p, const GemvPh& g,
     st_base += uint32_t(nst);
     // the next phase's staging overwrites the activations this phase's warps may still be reading
     return csync_and(ok);
+}
+
+// ---------------------------------------------------------------------------------------------- GEMV phases, 2..4 sequences
+// The dot products run on the tensor cores (mma.sync m16n8k16, f16 x f16 -> fp32): 16 weight rows of a ring
+// stage are the A operand, converted from their codes in registers (FP8: the hardware e4m3 -> f16 conversion;
+// FP4: bit arithmetic; both exact in f16); the activations are the B operand, column 2m the f16 rounding hi of
+// sequence m's row, column 2m + 1 the rounding lo of the remainder (about 22 bits together), each 32-element block
+// divided by a power of two s_b that puts its largest magnitude in [2^14, 2^15) (so f16's range holds any row).
+// Per block: acc += sw(row, block) * s_b * (D[hi] + D[lo]) in fp32, then the norm's rstd and the format's decode
+// factor in the epilogue, as in the CUDA-core kernels.
+//
+// B layout: row n of the staging area = column n ([2M][K] halves), then the block scales [M][K / 32] floats. Within
+// a block, lane t of an MMA reads its 8 values at halves 8t .. 8t + 7: FP8 in natural order (lane t holds code
+// bytes 8t .. 8t + 7 of the block); FP4 as weights 4t .. 4t + 3 then 16 + 4t .. 16 + 4t + 3 (code bytes 4t .. 4t
+// + 3 hold those as low / high nibbles).
+template <int FMT>
+__device__ __forceinline__ int bpos(int k) {  // half index within the row of activation k (k % 4 == 0)
+    if (FMT == kFP8) return k;
+    const int kk = k & 31;
+    return (k & ~31) + (kk < 16 ? 2 * kk : 2 * (kk - 16) + 4);
+}
+__device__ __forceinline__ int b_bytes(int M, int K) { return 4 * M * K + M * (K / 32) * 4; }
+
+// Writes 4 activations of sequence m at k (y = x / s_b is formed by the caller's block-scale exponent) as hi / lo.
+template <int FMT>
+__device__ __forceinline__ void put_hilo(__half* bx, int K, int m, int k, float4 y, float inv) {
+    uint32_t h0, l0, h1, l1;
+    split_hilo(y.x * inv, y.y * inv, h0, l0);
+    split_hilo(y.z * inv, y.w * inv, h1, l1);
+    const int o = bpos<FMT>(k);
+    *reinterpret_cast<uint2*>(bx + int64_t(2 * m) * K + o) = make_uint2(h0, h1);
+    *reinterpret_cast<uint2*>(bx + int64_t(2 * m + 1) * K + o) = make_uint2(l0, l1);
+}
+
+// The block's power-of-two scale from the 8 lanes (lanes 8j .. 8j + 7) that hold its 32 values: s (stored) and
+// 1 / s (applied). Every lane of the warp calls it.
+__device__ __forceinline__ void block_scale(float4 y, float& s, float& inv) {
+    float v = fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w)));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+    const int F = int((__float_as_uint(v) >> 23) & 0xFF) - 127;  // v in [2^F, 2^(F+1))
+    const int e = max(-126, min(127, F - 14)), ie = max(-126, min(127, -e));
+    s = __uint_as_float(uint32_t(e + 127) << 23);
+    inv = __uint_as_float(uint32_t(ie + 127) << 23);
+}
+
+// Stages the M input rows of a phase (tagged words) as the B operand: RMSNorm phases stage x * gamma and leave
+// per-warp sums of squares in s_ss (the epilogue applies rstd); LayerNorm phases (GPT-2) gather x into an f32
+// area first, then normalise with the row mean and variance (cpu_ops.cpp:483-500, sums in double). `ok` false:
+// this thread's earlier wait failed. Returns false, for every consumer thread alike, when any wait failed or an
+// input never arrived. A thread's float4 groups are base + tid + e * kNT; the 8 lanes of a block are consecutive.
+template <int FMT, int NM>
+__device__ bool stage_b(const DecodeParams& p, const GemvPh& g, int warp, int lane, bool ok) {
+    const int tid = threadIdx.x, K = g.K, K4 = K / 4, nq = p.M * K4;
+    const bool rms = g.norm == kNormRms, ln = g.norm == kNormLayer;
+    __half* bx = reinterpret_cast<__half*>(xs_buf(p));
+    float* bsc = reinterpret_cast<float*>(xs_buf(p)) + p.M * K;  // after the 2M half rows
+    float* xr = bsc + p.M * (K / 32);                             // LayerNorm: raw rows [M][K]
+    double ss[NM], s1[NM];
+#pragma unroll
+    for (int m = 0; m < NM; m++) ss[m] = s1[m] = 0.0;
+    for (int base = 0; base < nq && ok; base += kGatherE * kNT) {
+        int q[kGatherE];
+        float4 gm[kGatherE];
+#pragma unroll
+        for (int e = 0; e < kGatherE; e++) {
+            q[e] = base + tid + e * kNT;
+            if (rms && q[e] < nq) gm[e] = __ldg(reinterpret_cast<const float4*>(g.gamma + 4 * (q[e] % K4)));
+        }
+        float4 v[kGatherE];
+        ok = __all_sync(0xffffffffu, gather4<kGatherE>(g.x, q, nq, g.xtag, v, p.wait_ns));  // the block scales
+        if (!ok) break;                                                                     // shuffle the warp
+#pragma unroll
+        for (int e = 0; e < kGatherE; e++) {
+            const bool has = q[e] < nq;
+            const int m = has ? q[e] / K4 : 0, k = has ? 4 * (q[e] - m * K4) : 0;
+            float4 y = has ? v[e] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const double sq = double(y.x) * y.x + double(y.y) * y.y + double(y.z) * y.z + double(y.w) * y.w;
+            const double sm = double(y.x) + double(y.y) + double(y.z) + double(y.w);
+#pragma unroll
+            for (int mm = 0; mm < NM; mm++)
+                if (has && mm == m) {
+                    ss[mm] += sq;
+                    s1[mm] += sm;
+                }
+            if (ln) {
+                if (has) *reinterpret_cast<float4*>(xr + int64_t(m) * K + k) = y;
+                continue;
+            }
+            if (rms) {
+                y.x = __fmul_rn(y.x, gm[e].x);
+                y.y = __fmul_rn(y.y, gm[e].y);
+                y.z = __fmul_rn(y.z, gm[e].z);
+                y.w = __fmul_rn(y.w, gm[e].w);
+            }
+            float sb, inv;
+            block_scale(y, sb, inv);  // every lane (groups past nq hold zeros)
+            if (has) {
+                put_hilo<FMT>(bx, K, m, k, y, inv);
+                if ((k & 31) == 0) bsc[m * (K / 32) + k / 32] = sb;
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < NM; m++) {
+        if (m >= p.M) break;
+        const double t2 = wsum_d(ss[m]);
+        if (ln) {
+            const double t1 = wsum_d(s1[m]);
+            if (lane == 0) s_part[2 * (warp * NM + m)] = t1;
+        }
+        if (lane == 0) s_ss[warp][m] = t2;
+    }
+    if (!csync_and(ok)) return false;
+    if (!ln) return true;
+    // LayerNorm: the rows' mean and rstd from the per-warp sums, then the normalised values as the B operand
+    float mean[NM], r[NM];
+#pragma unroll
+    for (int m = 0; m < NM; m++) {
+        double a1 = 0.0, a2 = 0.0;
+        if (m < p.M)
+            for (int w = 0; w < kW; w++) {
+                a1 += s_part[2 * (w * NM + m)];
+                a2 += s_ss[w][m];
+            }
+        const double mu = a1 / K;
+        mean[m] = float(mu);
+        r[m] = m < p.M ? float(1.0 / sqrt(a2 / K - mu * mu + double(p.eps))) : 0.0f;
+    }
+    for (int base = 0; base < nq; base += kNT) {
+        const int qq = base + tid;
+        const bool has = qq < nq;
+        const int m = has ? qq / K4 : 0, k = has ? 4 * (qq - m * K4) : 0;
+        float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (has) {
+            float mm = mean[0], rr = r[0];
+#pragma unroll
+            for (int q2 = 1; q2 < NM; q2++)
+                if (q2 == m) {
+                    mm = mean[q2];
+                    rr = r[q2];
+                }
+            const float4 x = *reinterpret_cast<const float4*>(xr + int64_t(m) * K + k);
+            const float4 ga = __ldg(reinterpret_cast<const float4*>(g.gamma + k));
+            const float4 be = __ldg(reinterpret_cast<const float4*>(g.beta + k));
+            y.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x.x, mm), rr), ga.x), be.x);
+            y.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x.y, mm), rr), ga.y), be.y);
+            y.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x.z, mm), rr), ga.z), be.z);
+            y.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x.w, mm), rr), ga.w), be.w);
+        }
+        float sb, inv;
+        block_scale(y, sb, inv);
+        if (has) {
+            put_hilo<FMT>(bx, K, m, k, y, inv);
+            if ((k & 31) == 0) bsc[m * (K / 32) + k / 32] = sb;
+        }
+    }
+    csync();
+    return true;
+}
+
+// Lane (g, t)'s sums over spans [s0, s1) (64 weights: two blocks) of the 16 rows whose codes start at wg (row g)
+// and wh (row g + 8) in a ring stage: c0 (row g), c1 (row g + 8), for sequence t (B columns 2t, 2t + 1). xb: this
+// lane's B row (column g; nullptr past 2M), bs: sequence t's block scales.
+template <int FMT>
+__device__ __forceinline__ void tile_dot(const uint8_t* wg, const uint8_t* wh, int cbytes, int s0, int s1,
+                                         const __half* xb, const float* bs, int t, float& c0, float& c1) {
+#pragma unroll 2
+    for (int sp = s0; sp < s1; sp++) {
+        const __half2 swg = *reinterpret_cast<const __half2*>(wg + cbytes + 4 * sp);  // blocks 2sp, 2sp + 1
+        const __half2 swh = *reinterpret_cast<const __half2*>(wh + cbytes + 4 * sp);
+        const float2 fg = __half22float2(swg), fh = __half22float2(swh);
+        const float2 sb = *reinterpret_cast<const float2*>(bs + 2 * sp);
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int blk = 2 * sp + k;
+            uint4 xv = make_uint4(0u, 0u, 0u, 0u);
+            if (xb) xv = *reinterpret_cast<const uint4*>(xb + 32 * blk + 8 * t);
+            uint32_t ga[4], ha[4];  // (MMA j, k slots 2t, 2t + 1 | 2t + 8, 2t + 9) of rows g / g + 8
+            if (FMT == kFP8) {
+                const uint2 cg = *reinterpret_cast<const uint2*>(wg + 32 * blk + 8 * t);
+                const uint2 ch = *reinterpret_cast<const uint2*>(wh + 32 * blk + 8 * t);
+                __half2 a, b, c, d;
+                e4m3x4_to_half2(cg.x, a, b);
+                e4m3x4_to_half2(cg.y, c, d);
+                ga[0] = h2u(a), ga[1] = h2u(b), ga[2] = h2u(c), ga[3] = h2u(d);
+                e4m3x4_to_half2(ch.x, a, b);
+                e4m3x4_to_half2(ch.y, c, d);
+                ha[0] = h2u(a), ha[1] = h2u(b), ha[2] = h2u(c), ha[3] = h2u(d);
+            } else {  // code bytes 4t .. 4t + 3: low nibbles = weights 4t .., high nibbles = weights 16 + 4t ..
+                const uint32_t wdg = *reinterpret_cast<const uint32_t*>(wg + 16 * blk + 4 * t);
+                const uint32_t wdh = *reinterpret_cast<const uint32_t*>(wh + 16 * blk + 4 * t);
+                auto unpack = [](uint32_t wd, uint32_t (&o)[4]) {
+                    const __half2 e0 = fp4x2_to_half2(wd & 0x000F000Fu), o0 = fp4x2_to_half2((wd >> 8) & 0x000F000Fu);
+                    const __half2 e1 = fp4x2_to_half2((wd >> 4) & 0x000F000Fu);
+                    const __half2 o1 = fp4x2_to_half2((wd >> 12) & 0x000F000Fu);
+                    o[0] = h2u(__halves2half2(__low2half(e0), __low2half(o0)));    // weights 4t, 4t + 1
+                    o[1] = h2u(__halves2half2(__high2half(e0), __high2half(o0)));  // 4t + 2, 4t + 3
+                    o[2] = h2u(__halves2half2(__low2half(e1), __low2half(o1)));    // 16 + 4t, 16 + 4t + 1
+                    o[3] = h2u(__halves2half2(__high2half(e1), __high2half(o1)));  // 16 + 4t + 2, + 3
+                };
+                unpack(wdg, ga);
+                unpack(wdh, ha);
+            }
+            float d[4];
+            const uint32_t a0[4] = {ga[0], ha[0], ga[1], ha[1]}, a1[4] = {ga[2], ha[2], ga[3], ha[3]};
+            mma16816_z(d, a0, xv.x, xv.y);
+            mma16816(d, a1, xv.z, xv.w);
+            const float sbk = k ? sb.y : sb.x;
+            c0 = fmaf((k ? fg.y : fg.x) * sbk, d[0] + d[1], c0);
+            c1 = fmaf((k ? fh.y : fh.x) * sbk, d[2] + d[3], c1);
+        }
+    }
+}
+
+// One GEMV phase on this CTA's rows: gather and stage the inputs (the B operand), then stage by stage of the
+// producer's ring: every warp observes the stage, the stage's T tiles of 16 rows are split over the 12 warps
+// along K (Q = 12 / T warps per tile), the partial sums meet in shared memory (buffers alternate by stage) and,
+// after one barrier, one thread per (row, sequence) adds them in K order and stores the output as a tagged word.
+// Returns false when the kernel must stop (a wait failed).
+template <int FMT, int NM>
+__device__ __forceinline__ bool gemv_run_tc(const DecodeParams& p, const GemvPh& g, uint32_t& st_base, uint32_t& seen,
+                                            uint32_t& red_par, int warp, int lane) {
+    __shared__ float s_red[2][kW][2][NM][16];  // [stage parity][warp][gate | up][sequence][tile row]
+    int r0, r1;
+    cta_rows(g.rows, p.grid, r0, r1);
+    if (r0 >= r1) return true;
+    const int n = r1 - r0, rps = stage_rows(p, g), nst = (n + rps - 1) / rps;
+    const int tid = threadIdx.x, gq = lane >> 2, t = lane & 3;
+    const int cbytes = code_bytes(FMT, g.K), nsp = g.K / 64;
+    const bool rms = g.norm == kNormRms;
+    constexpr float kF = FMT == kFP8 ? kFp8HwFactor : kFp4Factor;  // the dot products' decode factor
+    // Every warp observes the landing of every stage of the step in order (`seen`: the next one) before it lets
+    // go of it: an mbarrier parity wait is only unambiguous while the slot is at most one phase ahead.
+    auto observe = [&](uint32_t upto) -> bool {
+        int ok = 1;
+        for (; seen <= upto && ok; seen++) {
+            const int slot = int(seen % uint32_t(p.nslot)), par = int((seen / uint32_t(p.nslot)) & 1u);
+            if (lane == 0) ok = mbar_try_wait(&full_bar()[slot], par) || dwait(&full_bar()[slot], par, p.wait_ns);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+        }
+        return ok != 0;
+    };
+    // The first stage's weights were streamed in during earlier phases: take them before the activations' wait.
+    // A stage wait that gives up stops this warp's consumption; the failure reaches the other consumer threads at
+    // the next reducing barrier (every consumer thread passes the same barriers), and they all leave.
+    bool ok = observe(st_base);
+    if (!stage_b<FMT, NM>(p, g, warp, lane, ok)) return false;
+    float rstd[NM];
+#pragma unroll
+    for (int m = 0; m < NM; m++) rstd[m] = (rms && m < p.M) ? rms_rstd(p, m, g.K) : 1.0f;
+    const __half* bx = reinterpret_cast<const __half*>(xs_buf(p));
+    const float* bsc = reinterpret_cast<const float*>(xs_buf(p)) + p.M * g.K;
+    const __half* xb = gq < 2 * p.M ? bx + int64_t(gq) * g.K : nullptr;
+    const float* bs = bsc + min(t, p.M - 1) * (g.K / 32);
+    unsigned long long best[NM];  // LM head: this thread's greedy argmax key per sequence
+#pragma unroll
+    for (int m = 0; m < NM; m++) best[m] = 0ull;
+    for (int s = 0; s < nst; s++) {
+        // a wait that gives up skips this warp's work but not the barrier below, which every consumer thread
+        // reaches once per stage and which then returns false to all of them
+        if (ok && !observe(st_base + uint32_t(s))) ok = false;
+        const int rows_s = min(rps, n - s * rps), T = (rows_s + 15) / 16, Q = kW / T;
+        const int tile = warp / Q, ks = warp % Q;
+        const uint8_t* base = ring_buf(p) + size_t((st_base + uint32_t(s)) % uint32_t(p.nslot)) * p.slot_bytes;
+        float c[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+        if (ok && tile < T) {
+            const int rg = min(16 * tile + gq, rows_s - 1), rh = min(16 * tile + gq + 8, rows_s - 1);
+            const int s0 = ks * nsp / Q, s1 = (ks + 1) * nsp / Q;
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                if (u == 1 && !g.pair) break;
+                const uint8_t* hb = base + int64_t(u ? rows_s : 0) * g.rb;  // SwiGLU: the up rows follow
+                tile_dot<FMT>(hb + int64_t(rg) * g.rb, hb + int64_t(rh) * g.rb, cbytes, s0, s1, xb, bs, t, c[u][0],
+                              c[u][1]);
+            }
+        }
+        if (t < p.M && t < NM) {
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                s_red[red_par][warp][u][t][gq] = c[u][0];
+                s_red[red_par][warp][u][t][gq + 8] = c[u][1];
+            }
+        }
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(&empty_bar()[(st_base + uint32_t(s)) % uint32_t(p.nslot)]);
+        // every warp's partial sums of this stage are in; the other buffer is free (its readers passed this)
+        if (!csync_and(ok)) return false;
+        for (int i = tid; i < rows_s * p.M; i += kNT) {
+            const int m = i % p.M, q = i / p.M, tq = q >> 4, a = q & 15;
+            float red_[2];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                float acc = 0.0f;
+                for (int k = 0; k < Q; k++) acc += s_red[red_par][tq * Q + k][u][m][a];
+                red_[u] = acc * kF;
+            }
+            const int row = r0 + s * rps + q;
+            const float rs = rstd[0];
+            float rsm = rs;
+#pragma unroll
+            for (int mm = 1; mm < NM; mm++)
+                if (mm == m) rsm = rstd[mm];
+            float val;
+            if (g.pair) {
+                const float gs = __fmul_rn(red_[0], rsm), us = __fmul_rn(red_[1], rsm);
+                val = __fdividef(gs, 1.0f + expf(-gs)) * us;  // cpu::siluMul (cpu_ops.cpp:526-533)
+            } else {
+                val = rms ? __fmul_rn(red_[0], rsm) : red_[0];
+                if (g.flags & kBias) val += g.bias[row];
+                if (g.flags & kGelu) val = gelu(val);
+                if (g.resid) {
+                    float& xo = s_xown[m][row - r0];
+                    val += xo;
+                    xo = val;
+                }
+            }
+            if (g.head) {
+                p.logits[int64_t(m) * g.ys + row] = val;
+                const unsigned long long key = argmax_key(val, row);
+#pragma unroll
+                for (int mm = 0; mm < NM; mm++)
+                    if (mm == m) best[mm] = max(best[mm], key);
+            } else if (g.xout) {
+                g.xout[int64_t(m) * g.ys + row] = val;
+            } else {
+                tw_put(g.y + int64_t(m) * g.ys + row, val, g.ytag);
+            }
+        }
+        red_par ^= 1u;
+    }
+    if (g.head) {  // one shared atomic per thread and sequence; the barrier orders them before the CTA's read
+#pragma unroll
+        for (int m = 0; m < NM; m++)
+            if (m < p.M && best[m]) atomicMax(&s_key[m], best[m]);
+        csync();
+    }
+    st_base += uint32_t(nst);
+    return ok;
+}
+
+template <int FMT, int NM>
+__device__ __forceinline__ bool gemv_run(const DecodeParams& p, const GemvPh& g, uint32_t& st_base, uint32_t& seen,
+                                         uint32_t& red_par, int warp, int lane) {
+    if constexpr (NM == 1)
+        return gemv_run_cc<FMT, 1>(p, g, st_base, seen, warp, lane);
+    else
+        return gemv_run_tc<FMT, NM>(p, g, st_base, seen, red_par, warp, lane);
 }
 
 // ---------------------------------------------------------------------------------------------- attention
@@ -1058,6 +1411,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
     }
     // Phases in order: per layer qkv, attention, split merge, o_proj, up, down; then the LM head.
     uint32_t st = 0, seen = 0;  // weight stages of the step: consumed by the phases so far, landings observed
+    uint32_t red_par = 0;       // the GEMV phases' partial-sum buffer in use (alternates by stage)
     int issued = 0;  // attention copies requested so far (the parity of s_attn_bar)
     int Sm[kDecodeMaxSeqs], Pm[kDecodeMaxSeqs];
     const bool attn_cta = int(blockIdx.x) < attn_items(p, Sm, Pm);
@@ -1086,7 +1440,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
                 continue;
             }
             const int kind = l == p.layers ? int(kHead) : k;
-            if (!gemv_run<FMT, NM>(p, gemv_ph<QW>(p, l, kind), st, seen, warp, lane)) {
+            if (!gemv_run<FMT, NM>(p, gemv_ph<QW>(p, l, kind), st, seen, red_par, warp, lane)) {
                 drain();
                 return;
             }
@@ -1170,39 +1524,58 @@ bool plan_decode(DecodeParams& p, std::string* why) {
     if ((p.C + p.grid - 1) / p.grid > kOwnRows) return no("residual rows per CTA");
     if (!p.x_tw || !p.qkv_tw || !p.att_tw || !p.h_tw || !p.part_tw || !p.epoch || !p.sync)
         return no("exchange buffers");
-    int64_t xs = std::max({padded_x_bytes(p.fmt, p.M, p.C), padded_x_bytes(p.fmt, p.M, p.H * p.hd),
-                           padded_x_bytes(p.fmt, p.M, p.F), int64_t(attn_scratch_floats(p)) * 4});
+    // GEMV inputs: one sequence, f32 rows in the CUDA-core kernel's permuted layout; 2..4, the tensor-core B
+    // operand: 2M f16 rows + block scales (+ LayerNorm's raw f32 rows)
+    auto bxs = [&](int64_t K) {
+        return p.M == 1 ? padded_x_bytes(p.fmt, p.M, int(K))
+                        : 4 * p.M * K + p.M * (K / 32) * 4 + (p.qwen ? 0 : 4 * p.M * K);
+    };
+    int64_t xs = std::max({bxs(p.C), bxs(int64_t(p.H) * p.hd), bxs(p.F), int64_t(attn_scratch_floats(p)) * 4});
     xs = (xs + 127) / 128 * 128;
     const int64_t rb_max = std::max({p.rb_c * (p.qwen ? 2 : 1), p.rb_att, p.rb_f});
     int64_t slot = std::max<int64_t>(kSlotBytes, (rb_max + 1023) / 1024 * 1024);
-    // A warp's pass touches rows up to kMaxGroupRows - 1 apart; while it waits for the last of their stages it
-    // holds the first, so the ring must hold every stage a pass can span plus one being refilled (fewer when the
-    // CTA's share of the matrix has fewer stages). Every warp walks every stage of a phase in order, so no warp
-    // waits on a slot more than one phase ahead of it.
+    // One sequence: a warp's pass touches rows up to kMaxGroupRows - 1 apart; while it waits for the last of their
+    // stages it holds the first, so the ring must hold every stage a pass can span plus one being refilled (fewer
+    // when the CTA's share of the matrix has fewer stages). 2..4 sequences: every warp takes every stage of a
+    // phase in order and lets it go before the next, so two slots keep the ring moving. Every warp walks every
+    // stage in order, so no warp waits on a slot more than one phase ahead of it.
     auto need_for = [&](int64_t rows, int64_t rbe) {
-        const int64_t rps = slot / rbe, share = (rows + p.grid - 1) / p.grid;
+        const int64_t rps = std::min<int64_t>(slot / rbe, 16 * kW), share = (rows + p.grid - 1) / p.grid;
         const int64_t nst = (share + rps - 1) / rps, span = (kMaxGroupRows - 1) / rps + 2;
         return int(std::min(nst, span) + 1);
     };
-    const int need = std::max({need_for(p.QW, p.rb_c), need_for(p.C, p.rb_att),
-                               need_for(p.F, p.rb_c * (p.qwen ? 2 : 1)), need_for(p.C, p.rb_f),
-                               need_for(p.V, p.rb_c), 2});
+    const int need = p.M > 1 ? 2
+                             : std::max({need_for(p.QW, p.rb_c), need_for(p.C, p.rb_att),
+                                         need_for(p.F, p.rb_c * (p.qwen ? 2 : 1)), need_for(p.C, p.rb_f),
+                                         need_for(p.V, p.rb_c), 2});
     const int64_t kvb = int64_t(2) * kMaxSpan * p.hd * 2;
-    const int64_t budget = 227 * 1024 - kStaticSmem - 256 - table_bytes(p) - xs - kvb;
+    DecodeFn k = pick(p);
+    if (!k) return no("GPT-2 with head_dim 64, Qwen3 with head_dim 64 or 128");
+    // the instantiation's own static shared memory against the device's per-block opt-in limit
+    cudaFuncAttributes fa{};
+    int dev = 0, optin = 0;
+    if (cudaFuncGetAttributes(&fa, k) != cudaSuccess || cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return no("kernel attributes");
+    }
+    const int64_t budget = int64_t(optin) - int64_t(fa.sharedSizeBytes) - 256 - table_bytes(p) - xs - kvb;
     const int nslot = int(std::min<int64_t>(kMaxSlots, budget / slot));
     if (nslot < need) return no("shared memory: weight rows too wide for the slot ring");
     p.xs_bytes = int(xs);
     p.kv_bytes = int(kvb);
     p.slot_bytes = int(slot);
     p.nslot = nslot;
-    DecodeFn k = pick(p);
-    if (!k) return no("GPT-2 with head_dim 64, Qwen3 with head_dim 64 or 128");
     const size_t smem = smem_bytes(p);
     int per_sm = 0;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThr, smem) != cudaSuccess || per_sm < 1) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThr, smem);
+    if (e != cudaSuccess || per_sm < 1) {
         cudaGetLastError();
-        return no("the kernel does not fit one CTA per SM");
+        if (why)
+            *why = std::string("the kernel does not fit one CTA per SM (") + cudaGetErrorString(e) + ", " +
+                   std::to_string(smem) + " B of dynamic shared memory)";
+        return false;
     }
     return true;
 }

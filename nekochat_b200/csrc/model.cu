@@ -577,7 +577,9 @@ bool decode_ok(neko_model* m, int R) {
     if (R < 1 || R > kDecodeMaxSeqs) return false;
     if (m->dec_ok[R] < 0) {
         DecodeParams dp;
-        m->dec_ok[R] = fill_decode(m, R, bucket_for(m, 0), false, dp, nullptr) ? 1 : 0;
+        std::string why;
+        m->dec_ok[R] = fill_decode(m, R, bucket_for(m, 0), false, dp, &why) ? 1 : 0;
+        if (!m->dec_ok[R]) m->err = "decode kernel not used for " + std::to_string(R) + " sequences: " + why;
     }
     return m->dec_ok[R] == 1;
 }
@@ -765,8 +767,9 @@ int run_step(neko_model* m, int R, int nout, bool identity, int max_pos, bool do
         }
         int rc = NEKO_OK;
         DecodeParams dp;
-        if (single && !fill_decode(m, R, bucket, advance, dp, nullptr))
-            rc = fail(m, NEKO_ERR_CUDA, "decode kernel plan");
+        std::string why;
+        if (single && !fill_decode(m, R, bucket, advance, dp, &why))
+            rc = fail(m, NEKO_ERR_CUDA, "decode kernel plan: " + why);
         else if (single) {
             cudaError_t le = launch_decode(dp, cap);
             if (le == cudaSuccess && dp.x_final) {  // final norm + LM head + greedy argmax, then the token / position
