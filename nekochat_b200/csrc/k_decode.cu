@@ -222,6 +222,7 @@ __shared__ double s_ss[kW][kDecodeMaxSeqs];       // RMSNorm: per-warp sums of s
 __shared__ float s_xown[kDecodeMaxSeqs][kOwnRows];  // the residual rows this CTA owns
 __shared__ unsigned long long s_key[kDecodeMaxSeqs];  // LM head: the CTA's greedy argmax keys
 __shared__ int s_last;
+__shared__ int s_span;  // keys per attention split this step (p.span is the bound the buffers are sized for)
 __shared__ unsigned s_epoch;
 __shared__ __align__(8) uint64_t s_attn_bar;           // an attention item's keys / values have landed
 __device__ __forceinline__ uint64_t* full_bar() { return reinterpret_cast<uint64_t*>(dsm); }
@@ -1028,8 +1029,8 @@ __device__ __forceinline__ AttnItem attn_item(const DecodeParams& p, const int (
     a.j = rem - a.g * ns;
     a.pos = pos;
     a.slot = p.slots[m];
-    a.k0 = a.j * p.span;
-    a.n = min(a.pos + 1, a.k0 + p.span) - a.k0;
+    a.k0 = a.j * s_span;
+    a.n = min(a.pos + 1, a.k0 + s_span) - a.k0;
     return a;
 }
 
@@ -1043,7 +1044,7 @@ __device__ __forceinline__ int attn_items(const DecodeParams& p, int (&Sm)[kDeco
         if (m >= p.M) continue;
         const int pos = max(0, min(p.pos[m], p.context - 1));  // out of range: reported at kernel start
         Pm[m] = pos;
-        Sm[m] = (pos + 1 + p.span - 1) / p.span;
+        Sm[m] = (pos + s_span) / s_span;
         total += p.KV * Sm[m];
     }
     return total;
@@ -1060,7 +1061,7 @@ __device__ __forceinline__ void attn_issue(const DecodeParams& p, int l, const A
     mbar_arrive_expect_tx(&s_attn_bar, 2u * bytes);
     if (bytes) {
         bulk_g2s(kv_buf(p), Ly.kc + base, bytes, &s_attn_bar);
-        bulk_g2s(kv_buf(p) + p.span * p.hd, Ly.vc + base, bytes, &s_attn_bar);
+        bulk_g2s(kv_buf(p) + s_span * p.hd, Ly.vc + base, bytes, &s_attn_bar);
     }
 }
 
@@ -1072,7 +1073,7 @@ __device__ __forceinline__ void attn_issue(const DecodeParams& p, int l, const A
 // each item writes its partial softmax state (max, sum, unnormalised P.V) for merge_run.
 template <int DL, int QW>
 __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued, int warp, int lane) {
-    const int Gq = p.H / p.KV, hd = p.hd, span = p.span;
+    const int Gq = p.H / p.KV, hd = p.hd, span = s_span;
     int Sm[kDecodeMaxSeqs], Pm[kDecodeMaxSeqs];
     const int total = attn_items(p, Sm, Pm);
     if (int(blockIdx.x) >= total) return true;
@@ -1377,6 +1378,15 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
         mbar_init(&s_attn_bar, 1);
         fence_barrier_init();
         s_epoch = *reinterpret_cast<volatile const unsigned*>(p.epoch);
+        // keys per attention split: the smallest multiple of 32 (up to p.span) whose items fit the grid, one item
+        // per CTA (more, smaller items finish sooner: the phase waits for its slowest item)
+        int sp = 32;
+        for (;; sp += 32) {
+            int items = 0;
+            for (int m = 0; m < p.M; m++) items += p.KV * ((max(0, min(p.pos[m], p.context - 1)) + sp) / sp);
+            if (items <= p.grid || sp >= p.span) break;
+        }
+        s_span = sp;
     }
     // the per-layer pointers, once, into shared memory (indexing the parameter block by layer would go through
     // the constant cache on every phase)

@@ -714,11 +714,10 @@ bool fill_decode(neko_model* m, int R, int bucket, bool advance, DecodeParams& p
     p.keys = m->d_keys;
     p.advance = advance ? 1 : 0;
     p.sync = m->dec_sync;
-    // keys per attention item: about one item per SM over the sequences' KV heads at this context bucket
-    const int per = std::max(1, num_sms() / std::max(1, R * m->KV));
-    int span = (bucket + per - 1) / per;
-    span = std::min(64, std::max(32, (span + 31) / 32 * 32));
-    p.span = span;
+    // keys per attention item: the bound the kernel's buffers are sized for; each step the kernel takes the
+    // smallest multiple of 32 up to it whose items fit one per CTA (bucket unused)
+    (void)bucket;
+    p.span = 64;
     p.max_splits = m->dec_max_splits;
     if (m->dec_stall_test) {
         p.stall_test = 1;
