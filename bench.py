@@ -431,7 +431,7 @@ def run_ours(args):
         roof = {"bound": "hbm",
                 "kernel": (f"{dk} (a whole decode step, one launch)" if nl == 1 else
                            f"{dk} (every layer, one launch) + gemv_fp8_tc_kernel (final norm, LM head, greedy argmax "
-                           "keys) + argmax_finalize_kernel: the step's three launches, timed together")
+                           "and token / position finalize): the step's two launches, timed together")
                 if single else "decode step as a kernel chain (tc_gemm_kernel and attention_tc_kernel dominant)",
                 "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
                 "peak_source": psrc, "traffic": None, "bytes_per_launch": bytes_step if single and nl == 1 else None,

@@ -40,6 +40,7 @@ __shared__ float e_part[kEW][2][kEMaxM][16];     // [warp][gate | up][activation
 __shared__ double e_stat[kEMaxM][kEW][2];        // norm sums per warp
 __shared__ float e_max[kEMaxM][kEW];             // largest magnitude per warp
 __shared__ unsigned long long e_key[kEMaxM];
+__shared__ int e_last;
 
 struct E4Plan {
     int tiles;       // 16-row tiles
@@ -400,6 +401,31 @@ __global__ void __launch_bounds__(kENT, 1) gemv_fp8_tc_kernel(const GemvArgs a, 
         if (g == 0 && out_lane && best) atomicMax(&e_key[t], best);
         esync();
         if (threadIdx.x < a.M && e_key[threadIdx.x]) atomicMax(a.argmax + threadIdx.x, e_key[threadIdx.x]);
+        if (a.fin_count) {  // the last CTA: every other CTA's keys are in (each fenced before counting itself)
+            __threadfence();
+            esync();
+            if (threadIdx.x == 0) e_last = atomicAdd(a.fin_count, 1u) == gridDim.x - 1 ? 1 : 0;
+            esync();
+            if (e_last) {
+                __threadfence();
+                if (threadIdx.x < a.M) {
+                    const int m = threadIdx.x;
+                    const unsigned long long key = atomicExch(a.argmax + m, 0ull);
+                    int idx = int(0xFFFFFFFFu - unsigned(key & 0xFFFFFFFFull));
+                    if (idx < 0 || idx >= a.rows) {  // no logit was reduced
+                        set_device_error(kErrBadIndex);
+                        idx = 0;
+                    }
+                    a.fin_argmax[m] = idx;
+                    if (a.fin_advance) {
+                        a.fin_tokens[m] = idx;
+                        if (a.fin_pos[m] + 1 < a.fin_context) a.fin_pos[m] += 1;
+                        else set_device_error(kErrBadIndex);
+                    }
+                }
+                if (threadIdx.x == 0) *a.fin_count = 0u;
+            }
+        }
     }
 }
 

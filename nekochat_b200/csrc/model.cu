@@ -191,7 +191,7 @@ struct neko_model {
     uint64_t* dec_tw = nullptr;
     DecodeScratch dec_sz;
     int64_t dec_tw_words = 0;
-    unsigned* dec_sync = nullptr;  // [0] CTAs done with the step, [1] the tag epoch
+    unsigned* dec_sync = nullptr;  // [0] CTAs done with the step, [1] the tag epoch, [2] LM-head CTAs done
     int dec_ok[kDecodeMaxSeqs + 1] = {-1, -1, -1, -1, -1};  // per sequence count: -1 not planned yet
 };
 
@@ -627,7 +627,7 @@ bool chain_head_ok(const neko_model* m, int R) {
 
 int step_launches(neko_model* m, int R, int nout, bool gather, bool do_argmax, bool advance) {
     if (!gather && nout == R && m->debug_layers < 0 && m->dec_enabled && R <= m->dec_seqs && decode_ok(m, R))
-        return head_split_ok(m, R) ? 3 : 1;  // the decode kernel (+ the LM head and argmax finalize)
+        return head_split_ok(m, R) ? 2 : 1;  // the decode kernel (+ the LM head, which finalizes the tokens)
     if (m->debug_layers < 0 && chain_ok(m, R)) {
         // embedding, the first layer's norm split + qkv, then per layer qkv_post, attention, o_proj, gate / up,
         // down and (after the first) qkv
@@ -788,10 +788,13 @@ int run_step(neko_model* m, int R, int nout, bool identity, int max_pos, bool do
                 a.y = m->logits;
                 a.y_stride = m->V;
                 a.argmax = m->d_keys;
+                a.fin_count = m->dec_sync + 2;  // its last CTA finalizes the greedy tokens
+                a.fin_argmax = m->d_argmax;
+                a.fin_tokens = m->d_tokens;
+                a.fin_pos = m->d_pos;
+                a.fin_context = m->cfg.context;
+                a.fin_advance = advance ? 1 : 0;
                 le = launch_gemv(a, cap, true);
-                if (le == cudaSuccess)
-                    le = launch_ex(argmax_finalize_kernel, dim3(1), dim3(128), 0, cap, true, m->d_keys, m->d_argmax,
-                                   m->d_tokens, m->d_pos, R, m->cfg.context, advance ? 1 : 0);
             }
             if (le != cudaSuccess) rc = fail(m, NEKO_ERR_CUDA, cuda_msg(le, "decode kernel"));
         } else {
@@ -843,7 +846,7 @@ int debug_width(const neko_model* m) {
 void decode_reset(neko_model* m) {
     if (m->dec_tw) cudaMemset(m->dec_tw, 0, size_t(m->dec_tw_words) * 8);
     if (m->dec_sync) {
-        const unsigned init[2] = {0u, 1u};
+        const unsigned init[4] = {0u, 1u, 0u, 0u};
         cudaMemcpy(m->dec_sync, init, sizeof(init), cudaMemcpyHostToDevice);
     }
     cudaMemset(m->d_keys, 0, size_t(std::max(m->cfg.max_rows, m->cfg.max_seqs)) * sizeof(unsigned long long));
@@ -1020,11 +1023,11 @@ neko_model* neko_model_create(int device, const neko_model_config* cfg, char* er
         auto pad = [](int64_t w) { return (w + 31) / 32 * 32; };  // 256-byte aligned sections
         m->dec_tw_words = pad(z.x_words) + pad(z.qkv_words) + pad(z.att_words) + pad(z.h_words) + pad(z.part_words);
         if (cudaMalloc(&m->dec_tw, size_t(m->dec_tw_words) * 8) != cudaSuccess ||
-            cudaMalloc(&m->dec_sync, 2 * sizeof(unsigned)) != cudaSuccess)
+            cudaMalloc(&m->dec_sync, 4 * sizeof(unsigned)) != cudaSuccess)
             return bail(m, "decode exchange buffers allocation failed");
-        m->work_bytes += size_t(m->dec_tw_words) * 8 + 8;
+        m->work_bytes += size_t(m->dec_tw_words) * 8 + 16;
         cudaMemset(m->dec_tw, 0, size_t(m->dec_tw_words) * 8);
-        const unsigned init[2] = {0u, 1u};
+        const unsigned init[4] = {0u, 1u, 0u, 0u};
         cudaMemcpy(m->dec_sync, init, sizeof(init), cudaMemcpyHostToDevice);
     }
     m->h_logits_floats = nout * size_t(m->V);

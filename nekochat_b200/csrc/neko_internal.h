@@ -60,6 +60,15 @@ struct GemvArgs {
     int n_off = 0;
     int64_t pair_off = 0;        // != 0: out n = silu(row n) * row(n + pair_off)  (SwiGLU epilogue)
     unsigned long long* argmax = nullptr;  // M <= 64: per-row atomicMax of (value, ~index) keys (fused greedy argmax)
+    // Greedy finalize by the last CTA (the FP8 tensor-core GEMV with argmax): fin_count counts the CTAs done (zero
+    // between launches); the last one turns the keys into token ids (fin_argmax), clears them and, with
+    // fin_advance, writes the next input token and position + 1 (argmax_finalize_kernel semantics)
+    unsigned* fin_count = nullptr;
+    int* fin_argmax = nullptr;
+    int* fin_tokens = nullptr;
+    int* fin_pos = nullptr;
+    int fin_context = 0;
+    int fin_advance = 0;
     // tensor-core path (5+ rows): workspace for K splits and split activations, tickets zero between launches
     float* ws = nullptr;
     int64_t ws_floats = 0;

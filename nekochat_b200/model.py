@@ -269,10 +269,10 @@ class Model:
 
 
 def decode_kernel_launches(shape, fmt):
-    """Kernel launches of a decode step on the single decode kernel: 1, or 3 when the LM head runs as its own
-    launch (FP8 heads with a hidden size that is a multiple of 128: the decode kernel, the head GEMV with the final
-    norm and the greedy argmax keys, the argmax finalize)."""
-    return 3 if fmt == 1 and shape["embd"] % 128 == 0 else 1
+    """Kernel launches of a decode step on the single decode kernel: 1, or 2 when the LM head runs as its own
+    launch (FP8 heads with a hidden size that is a multiple of 128: the decode kernel, then the head GEMV with the
+    final norm, the greedy argmax and the token / position finalize)."""
+    return 2 if fmt == 1 and shape["embd"] % 128 == 0 else 1
 
 
 def build(shape_name, fmt, context, max_seqs=1, max_rows=64, seed=0, perturb=False, device=None):

@@ -38,7 +38,7 @@ def test_single_kernel_availability():
     m = nmodel.build("qwen3-tiny", FP8, context=64, max_seqs=4, max_rows=8)
     assert m.set_decode_kernel(True)
     n = nmodel.decode_kernel_launches(workload.shape("qwen3-tiny"), FP8)
-    assert n == 3 and m.step_launches(1) == n and m.step_launches(4) == n
+    assert n == 2 and m.step_launches(1) == n and m.step_launches(4) == n
     m.set_decode_kernel(False)
     assert m.step_launches(1) > 10
     m.close()

@@ -127,14 +127,14 @@ def q06():
 def test_qwen3_06b_fp8_b1_decode_kernel(q06):
     """configs[1] at batch 1: a 120-token prompt, then 32 greedy steps on the persistent decode kernel, whose
     attention crosses from 2 to 3 key splits at position 128 (the ticket merge)."""
-    assert q06.m.set_decode_kernel(True) and q06.m.step_launches(1) == nmodel.decode_kernel_launches(q06.s, FP8) == 3
+    assert q06.m.set_decode_kernel(True) and q06.m.step_launches(1) == nmodel.decode_kernel_launches(q06.s, FP8) == 2
     prompt = workload.prompt(q06.s, 120, seed=1)
     run_batch(q06, [prompt], 32, [0], "qwen3-0.6b fp8 b1")
 
 
 def test_qwen3_06b_fp8_b4_decode_kernel(q06):
     """Four sequences in one decode_kernel<FP8, 4> launch, at different positions (1, 2 and 3 key splits)."""
-    assert q06.m.step_launches(4) == 3
+    assert q06.m.step_launches(4) == 2
     prompts = [workload.prompt(q06.s, n, seed=10 + i) for i, n in enumerate((40, 70, 100, 150))]
     run_batch(q06, prompts, 12, [0, 3], "qwen3-0.6b fp8 b4")
 
@@ -174,7 +174,7 @@ def test_gpt2_small_fp8_128_steps():
     """configs[0] exactly: GPT-2 small, FP8, 32-token prompt, 128 greedy steps (decode kernel, head_dim 64)."""
     p = Pair(workload.shape("gpt2"), FP8, context=256, max_seqs=1, max_rows=64)
     try:
-        assert p.m.set_decode_kernel(True) and p.m.step_launches(1) == nmodel.decode_kernel_launches(p.s, FP8) == 3
+        assert p.m.set_decode_kernel(True) and p.m.step_launches(1) == nmodel.decode_kernel_launches(p.s, FP8) == 2
         prompt = workload.prompt(p.s, 32, seed=1)
         run_batch(p, [prompt], 128, [0], "gpt2 small fp8")
     finally:
