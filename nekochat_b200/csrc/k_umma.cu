@@ -27,6 +27,7 @@
 #include "mma_frag.cuh"
 #include "neko_common.cuh"
 #include "neko_internal.h"
+#include "tc5_core.cuh"
 #include "tma_host.h"
 
 namespace neko {
@@ -45,51 +46,6 @@ constexpr int kUMaxSplit = 4;
 // here, where two stages of prefetch leave the pipeline latency-bound); from 128 rows on, this one (M = 512:
 // 1.3-1.5x).
 constexpr int kUMinRows = 128;
-
-// ------------------------------------------------------------------------------------------------ tcgen05 PTX
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart (SBO), version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
-    return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
-           (uint64_t(2) << 61);
-}
-// Instruction descriptor of kind::f16: f32 accumulator, f16 A and B, both K-major, N >> 3, M >> 4.
-__host__ __device__ constexpr uint32_t f16_idesc(int M, int N) {
-    return (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
-}
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                         uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-// 32 lanes x 16 columns of fp32 from TMEM (this warp's lane quarter)
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
-
-// Byte offset of f16 element (row r, k) in a K-major tile of 64-wide rows with the 128-byte swizzle (the
-// tile starts on a 1024-byte boundary): 16-byte chunk k / 8 of row r is stored at chunk (k / 8) ^ (r % 8).
-__device__ __forceinline__ uint32_t sw128_off(int r, int chunk) {
-    return uint32_t((r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4));
-}
 
 struct UmmaSplit {
     int ksplit, sper;
