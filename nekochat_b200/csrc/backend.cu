@@ -57,6 +57,54 @@ int num_sms() {
     return cache[dev];
 }
 
+namespace {
+struct DynSmem {
+    int limit = -1;  // opt-in per-block limit less the kernel's static shared memory
+    int set = 0;     // the kernel's dynamic shared memory attribute as last raised here
+};
+std::mutex g_dyn_mu;
+std::vector<std::pair<std::pair<const void*, int>, DynSmem>> g_dyn;  // (function, device) -> state
+
+DynSmem& dyn_state(const void* fn, int dev) {  // with g_dyn_mu held
+    for (auto& e : g_dyn)
+        if (e.first.first == fn && e.first.second == dev) return e.second;
+    g_dyn.push_back({{fn, dev}, DynSmem{}});
+    DynSmem& d = g_dyn.back().second;
+    int optin = 0;
+    cudaFuncAttributes fa{};
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) == cudaSuccess &&
+        cudaFuncGetAttributes(&fa, fn) == cudaSuccess)
+        d.limit = std::max(0, optin - int(fa.sharedSizeBytes));
+    else
+        d.limit = 0;
+    cudaGetLastError();
+    return d;
+}
+}  // namespace
+
+int max_dyn_smem(const void* fn) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(g_dyn_mu);
+    return dyn_state(fn, dev).limit;
+}
+
+cudaError_t ensure_dyn_smem(const void* fn, size_t bytes) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(g_dyn_mu);
+    DynSmem& d = dyn_state(fn, dev);
+    if (bytes > size_t(d.limit)) return cudaErrorNotSupported;
+    if (bytes <= size_t(d.set)) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    if (e != cudaSuccess) {
+        cudaGetLastError();  // leave no pending error for a later launch check to pick up
+        return e;
+    }
+    d.set = int(bytes);
+    return cudaSuccess;
+}
+
 }  // namespace neko
 
 using namespace neko;
@@ -322,7 +370,7 @@ int neko_cuda_dispatch(neko_ctx* c, int kernel, neko_buf* const bind[4], const i
                 return bad("embed sizes");
             e = launch_embed(static_cast<const int*>(ptr(0)), T, C, fmt, static_cast<const uint8_t*>(ptr(1)), rb, base,
                              rows, (flags & 1) ? static_cast<const uint16_t*>(ptr(2)) : nullptr, nullptr, pos0, nullptr,
-                             static_cast<float*>(ptr(3)), c->stream, false);
+                             static_cast<float*>(ptr(3)), c->stream, true);
             break;
         }
         case NEKO_K_LAYERNORM: {  // layernorm.comp
@@ -332,7 +380,7 @@ int neko_cuda_dispatch(neko_ctx* c, int kernel, neko_buf* const bind[4], const i
                 return bad("layernorm sizes");
             e = launch_norm(static_cast<const float*>(ptr(0)) + int64_t(off) * C, C, static_cast<float*>(ptr(1)), C,
                             static_cast<const float*>(ptr(2)), static_cast<const float*>(ptr(3)), rows, C, fbits(p[1]),
-                            rms != 0, c->stream, false);
+                            rms != 0, c->stream, true);
             break;
         }
         case NEKO_K_MATMUL:
@@ -360,7 +408,7 @@ int neko_cuda_dispatch(neko_ctx* c, int kernel, neko_buf* const bind[4], const i
             a.y = static_cast<float*>(ptr(3));
             a.y_stride = N;
             a.n_off = noff;
-            e = launch_gemv_op(a, c->stream, false);
+            e = launch_gemv_op(a, c->stream, true);
             break;
         }
         case NEKO_K_KVSTORE: {  // kv_store.comp
@@ -417,7 +465,7 @@ int neko_cuda_dispatch(neko_ctx* c, int kernel, neko_buf* const bind[4], const i
             a.tickets = c->tickets;
             a.part_capacity = c->part_cap;
             a.ticket_capacity = c->tick_cap;
-            e = launch_attention(a, c->stream, false);
+            e = launch_attention(a, c->stream, true);
             break;
         }
         case NEKO_K_ROPE: {  // rope.comp
@@ -441,7 +489,7 @@ int neko_cuda_dispatch(neko_ctx* c, int kernel, neko_buf* const bind[4], const i
             a.cs = static_cast<const float*>(ptr(2));
             a.pos0 = pos0;
             a.k_off = H * hd;
-            e = launch_qkv_post(a, c->stream, false);
+            e = launch_qkv_post(a, c->stream, true);
             break;
         }
         case NEKO_K_SILUMUL: {  // silu_mul.comp
@@ -454,7 +502,10 @@ int neko_cuda_dispatch(neko_ctx* c, int kernel, neko_buf* const bind[4], const i
         default:
             return bad("unknown kernel id " + std::to_string(kernel));
     }
-    if (e != cudaSuccess) return set_err(&c->err, NEKO_ERR_CUDA, cuda_msg(e, "dispatch"));
+    if (e != cudaSuccess) {
+        cudaGetLastError();  // reported here; none stays pending for the next call's launch check
+        return set_err(&c->err, NEKO_ERR_CUDA, cuda_msg(e, "dispatch"));
+    }
     return NEKO_OK;
 }
 
@@ -465,7 +516,9 @@ int64_t neko_row_bytes(int format, int cols) { return row_bytes(format, cols); }
 #define NEKO_OP_RETURN(expr)                                                        \
     do {                                                                            \
         cudaError_t e_ = (expr);                                                    \
-        return e_ == cudaSuccess ? NEKO_OK : set_err(nullptr, NEKO_ERR_CUDA, cuda_msg(e_, __func__)); \
+        if (e_ == cudaSuccess) return NEKO_OK;                                      \
+        cudaGetLastError(); /* the error is reported here; none stays pending */   \
+        return set_err(nullptr, NEKO_ERR_CUDA, cuda_msg(e_, __func__));             \
     } while (0)
 
 int neko_op_quantize(int format, const float* w, int rows, int cols, int64_t ld, int transpose_f16, uint8_t* out,

@@ -214,33 +214,40 @@ __device__ __noinline__ bool dwait(uint64_t* bar, uint32_t parity, uint64_t lim,
 }
 
 // ---------------------------------------------------------------------------------------------- shared memory
-// Shared-memory state of the kernel at file scope, so the phase functions address it directly (a struct of
-// pointers passed around ends up in local memory and puts a load on every access).
-extern __shared__ __align__(128) uint8_t dsm[];  // barriers | layer table | activations | keys/values | ring
-__shared__ double s_part[2 * kMaxStatSlots];      // LayerNorm prologue partial sums
-__shared__ double s_ss[kW][kDecodeMaxSeqs];       // RMSNorm: per-warp sums of squares of the staged rows
-__shared__ float s_xown[kDecodeMaxSeqs][kOwnRows];  // the residual rows this CTA owns
-__shared__ unsigned long long s_key[kDecodeMaxSeqs];  // LM head: the CTA's greedy argmax keys
-__shared__ int s_last;
-__shared__ int s_span;  // keys per attention split this step (p.span is the bound the buffers are sized for)
-__shared__ unsigned s_epoch;
-__shared__ __align__(8) uint64_t s_attn_bar;           // an attention item's keys / values have landed
+// Shared-memory state of the kernel at fixed offsets of the dynamic region, so the phase functions address it
+// directly (a struct of pointers passed around ends up in local memory and puts a load on every access):
+// barriers | DShared | layer table | activations | keys/values | ring. The small arrays are not file-scope
+// __shared__ variables: the device linker places those in one window shared with the other files' and the
+// kernel's static shared memory would grow with them.
+extern __shared__ __align__(128) uint8_t dsm[];
+struct DShared {
+    double part[2 * kMaxStatSlots];             // LayerNorm prologue partial sums
+    double ss[kW][kDecodeMaxSeqs];              // RMSNorm: per-warp sums of squares of the staged rows
+    float xown[kDecodeMaxSeqs][kOwnRows];       // the residual rows this CTA owns
+    unsigned long long key[kDecodeMaxSeqs];     // LM head: the CTA's greedy argmax keys
+    uint64_t attn_bar;                          // an attention item's keys / values have landed
+    int last;
+    int span;                                   // keys per attention split this step (p.span: the buffers' bound)
+    unsigned epoch;
+};
+constexpr int kDHdr = 256 + int(sizeof(DShared) + 127) / 128 * 128;  // bytes before the layer table
+__device__ __forceinline__ DShared& dsh() { return *reinterpret_cast<DShared*>(dsm + 256); }
 __device__ __forceinline__ uint64_t* full_bar() { return reinterpret_cast<uint64_t*>(dsm); }
 __device__ __forceinline__ uint64_t* empty_bar() { return reinterpret_cast<uint64_t*>(dsm) + kMaxSlots; }
-__device__ __forceinline__ const DecodeLayer* layer_tab() { return reinterpret_cast<const DecodeLayer*>(dsm + 256); }
+__device__ __forceinline__ const DecodeLayer* layer_tab() { return reinterpret_cast<const DecodeLayer*>(dsm + kDHdr); }
 __device__ __forceinline__ int tab_bytes(const DecodeParams& p) {
     return (p.layers * int(sizeof(DecodeLayer)) + 127) / 128 * 128;
 }
 __device__ __forceinline__ float* xs_buf(const DecodeParams& p) {
-    return reinterpret_cast<float*>(dsm + 256 + tab_bytes(p));
+    return reinterpret_cast<float*>(dsm + kDHdr + tab_bytes(p));
 }
 __device__ __forceinline__ uint16_t* kv_buf(const DecodeParams& p) {
-    return reinterpret_cast<uint16_t*>(dsm + 256 + tab_bytes(p) + p.xs_bytes);
+    return reinterpret_cast<uint16_t*>(dsm + kDHdr + tab_bytes(p) + p.xs_bytes);
 }
 __device__ __forceinline__ uint8_t* ring_buf(const DecodeParams& p) {
-    return dsm + 256 + tab_bytes(p) + p.xs_bytes + p.kv_bytes;
+    return dsm + kDHdr + tab_bytes(p) + p.xs_bytes + p.kv_bytes;
 }
-__device__ __forceinline__ unsigned tag_of(int l, unsigned x) { return s_epoch + unsigned(l) * kXPer + x; }
+__device__ __forceinline__ unsigned tag_of(int l, unsigned x) { return dsh().epoch + unsigned(l) * kXPer + x; }
 
 // ---------------------------------------------------------------------------------------------- GEMV phases
 struct GemvPh {
@@ -380,7 +387,7 @@ __device__ __forceinline__ float inv_rms(double ss, double inv_n, float eps) {
 __device__ __forceinline__ float rms_rstd(const DecodeParams& p, int m, int K) {
     double a = 0.0;
 #pragma unroll
-    for (int w = 0; w < kW; w++) a += s_ss[w][m];
+    for (int w = 0; w < kW; w++) a += dsh().ss[w][m];
     return inv_rms(a, 1.0 / K, p.eps);
 }
 
@@ -391,7 +398,7 @@ template <int NM>
 constexpr int kRows = NM == 1 ? 4 : 2;
 
 // Stages the M input rows of a phase (tagged words) into the permuted layout of the dot products: RMSNorm phases
-// store x * gamma and leave per-warp sums of squares in s_ss (the epilogue applies rstd); LayerNorm phases
+// store x * gamma and leave per-warp sums of squares in dsh().ss (the epilogue applies rstd); LayerNorm phases
 // (GPT-2) normalise in place with the row mean and variance (cpu_ops.cpp:483-500, sums in double). `ok` false:
 // this thread's earlier wait failed. Returns false, for every consumer thread alike, when any wait failed or an
 // input never arrived.
@@ -437,7 +444,7 @@ __device__ bool stage_x(const DecodeParams& p, const GemvPh& g, float* xs, int w
         for (int m = 0; m < NM; m++) {
             if (m >= p.M) break;
             const double t = wsum_d(ss[m]);
-            if (lane == 0) s_ss[warp][m] = t;
+            if (lane == 0) dsh().ss[warp][m] = t;
         }
     }
     if (!csync_and(ok)) return false;
@@ -457,8 +464,8 @@ __device__ bool stage_x(const DecodeParams& p, const GemvPh& g, float* xs, int w
             s2 = wsum_d(s2);
             if (lane == 0) {
                 const int qq = base / 32 + warp;
-                s_part[2 * qq] = s1;
-                s_part[2 * qq + 1] = s2;
+                dsh().part[2 * qq] = s1;
+                dsh().part[2 * qq + 1] = s2;
             }
         }
     }
@@ -468,8 +475,8 @@ __device__ bool stage_x(const DecodeParams& p, const GemvPh& g, float* xs, int w
         const int m = i / K4, k = 4 * (i - m * K4);
         double a1 = 0.0, a2 = 0.0;
         for (int qq = m * gpr; qq < (m + 1) * gpr; qq++) {
-            a1 += s_part[2 * qq];
-            a2 += s_part[2 * qq + 1];
+            a1 += dsh().part[2 * qq];
+            a2 += dsh().part[2 * qq + 1];
         }
         const double mu = a1 / g.K;
         const float mean = float(mu);
@@ -597,7 +604,7 @@ __device__ __forceinline__ bool gemv_run_cc(const DecodeParams& p, const GemvPh&
                     if (g.flags & kBias) val += g.bias[row];
                     if (g.flags & kGelu) val = gelu(val);
                     if (g.resid) {
-                        float& xo = s_xown[m][row - r0];
+                        float& xo = dsh().xown[m][row - r0];
                         val += xo;
                         xo = val;
                     }
@@ -628,7 +635,7 @@ __device__ __forceinline__ bool gemv_run_cc(const DecodeParams& p, const GemvPh&
             unsigned long long k = best[m];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) k = max(k, __shfl_xor_sync(0xffffffffu, k, o));
-            if (lane == 0 && k) atomicMax(&s_key[m], k);
+            if (lane == 0 && k) atomicMax(&dsh().key[m], k);
         }
     }
     st_base += uint32_t(nst);
@@ -682,7 +689,7 @@ __device__ __forceinline__ void block_scale(float4 y, float& s, float& inv) {
 }
 
 // Stages the M input rows of a phase (tagged words) as the B operand: RMSNorm phases stage x * gamma and leave
-// per-warp sums of squares in s_ss (the epilogue applies rstd); LayerNorm phases (GPT-2) gather x into an f32
+// per-warp sums of squares in dsh().ss (the epilogue applies rstd); LayerNorm phases (GPT-2) gather x into an f32
 // area first, then normalise with the row mean and variance (cpu_ops.cpp:483-500, sums in double). `ok` false:
 // this thread's earlier wait failed. Returns false, for every consumer thread alike, when any wait failed or an
 // input never arrived. A thread's float4 groups are base + tid + e * kNT; the 8 lanes of a block are consecutive.
@@ -744,9 +751,9 @@ __device__ bool stage_b(const DecodeParams& p, const GemvPh& g, int warp, int la
         const double t2 = wsum_d(ss[m]);
         if (ln) {
             const double t1 = wsum_d(s1[m]);
-            if (lane == 0) s_part[2 * (warp * NM + m)] = t1;
+            if (lane == 0) dsh().part[2 * (warp * NM + m)] = t1;
         }
-        if (lane == 0) s_ss[warp][m] = t2;
+        if (lane == 0) dsh().ss[warp][m] = t2;
     }
     if (!csync_and(ok)) return false;
     if (!ln) return true;
@@ -757,8 +764,8 @@ __device__ bool stage_b(const DecodeParams& p, const GemvPh& g, int warp, int la
         double a1 = 0.0, a2 = 0.0;
         if (m < p.M)
             for (int w = 0; w < kW; w++) {
-                a1 += s_part[2 * (w * NM + m)];
-                a2 += s_ss[w][m];
+                a1 += dsh().part[2 * (w * NM + m)];
+                a2 += dsh().ss[w][m];
             }
         const double mu = a1 / K;
         mean[m] = float(mu);
@@ -947,7 +954,7 @@ __device__ __forceinline__ bool gemv_run_tc(const DecodeParams& p, const GemvPh&
                 if (g.flags & kBias) val += g.bias[row];
                 if (g.flags & kGelu) val = gelu(val);
                 if (g.resid) {
-                    float& xo = s_xown[m][row - r0];
+                    float& xo = dsh().xown[m][row - r0];
                     val += xo;
                     xo = val;
                 }
@@ -969,7 +976,7 @@ __device__ __forceinline__ bool gemv_run_tc(const DecodeParams& p, const GemvPh&
     if (g.head) {  // one shared atomic per thread and sequence; the barrier orders them before the CTA's read
 #pragma unroll
         for (int m = 0; m < NM; m++)
-            if (m < p.M && best[m]) atomicMax(&s_key[m], best[m]);
+            if (m < p.M && best[m]) atomicMax(&dsh().key[m], best[m]);
         csync();
     }
     st_base += uint32_t(nst);
@@ -1029,8 +1036,8 @@ __device__ __forceinline__ AttnItem attn_item(const DecodeParams& p, const int (
     a.j = rem - a.g * ns;
     a.pos = pos;
     a.slot = p.slots[m];
-    a.k0 = a.j * s_span;
-    a.n = min(a.pos + 1, a.k0 + s_span) - a.k0;
+    a.k0 = a.j * dsh().span;
+    a.n = min(a.pos + 1, a.k0 + dsh().span) - a.k0;
     return a;
 }
 
@@ -1044,7 +1051,7 @@ __device__ __forceinline__ int attn_items(const DecodeParams& p, int (&Sm)[kDeco
         if (m >= p.M) continue;
         const int pos = max(0, min(p.pos[m], p.context - 1));  // out of range: reported at kernel start
         Pm[m] = pos;
-        Sm[m] = (pos + s_span) / s_span;
+        Sm[m] = (pos + dsh().span) / dsh().span;
         total += p.KV * Sm[m];
     }
     return total;
@@ -1052,16 +1059,16 @@ __device__ __forceinline__ int attn_items(const DecodeParams& p, int (&Sm)[kDeco
 
 // One thread: copies the item's cached keys and values (positions below pos; the newest comes from this step)
 // into shared memory with two bulk copies (a head's positions are contiguous in the cache), completing on
-// s_attn_bar. The cache rows are from earlier steps, so this is issued long before the item runs.
+// dsh().attn_bar. The cache rows are from earlier steps, so this is issued long before the item runs.
 __device__ __forceinline__ void attn_issue(const DecodeParams& p, int l, const AttnItem& a) {
     const DecodeLayer& Ly = layer_tab()[l];
     const int nold = min(a.n, a.pos - a.k0);  // rows that are in the cache already
     const uint32_t bytes = uint32_t(nold) * uint32_t(p.hd) * 2u;
     const int64_t base = int64_t(a.slot) * p.kv_slot + int64_t(a.g) * p.kv_head + int64_t(a.k0) * p.hd;
-    mbar_arrive_expect_tx(&s_attn_bar, 2u * bytes);
+    mbar_arrive_expect_tx(&dsh().attn_bar, 2u * bytes);
     if (bytes) {
-        bulk_g2s(kv_buf(p), Ly.kc + base, bytes, &s_attn_bar);
-        bulk_g2s(kv_buf(p) + s_span * p.hd, Ly.vc + base, bytes, &s_attn_bar);
+        bulk_g2s(kv_buf(p), Ly.kc + base, bytes, &dsh().attn_bar);
+        bulk_g2s(kv_buf(p) + dsh().span * p.hd, Ly.vc + base, bytes, &dsh().attn_bar);
     }
 }
 
@@ -1073,7 +1080,7 @@ __device__ __forceinline__ void attn_issue(const DecodeParams& p, int l, const A
 // each item writes its partial softmax state (max, sum, unnormalised P.V) for merge_run.
 template <int DL, int QW>
 __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued, int warp, int lane) {
-    const int Gq = p.H / p.KV, hd = p.hd, span = s_span;
+    const int Gq = p.H / p.KV, hd = p.hd, span = dsh().span;
     int Sm[kDecodeMaxSeqs], Pm[kDecodeMaxSeqs];
     const int total = attn_items(p, Sm, Pm);
     if (int(blockIdx.x) >= total) return true;
@@ -1151,7 +1158,7 @@ __device__ __noinline__ bool attn_run(const DecodeParams& p, int l, int& issued,
                 }
             }
         }
-        if (threadIdx.x == 0 && !dwait(&s_attn_bar, uint32_t(issued - 1) & 1u, p.wait_ns)) ok = false;
+        if (threadIdx.x == 0 && !dwait(&dsh().attn_bar, uint32_t(issued - 1) & 1u, p.wait_ns)) ok = false;
         if (!csync_and(ok)) return false;  // the inputs or the keys never arrived: leave together
         // 2. scores, four keys x four query heads (heads past Gq are zero) per warp pass: the 16 lane partial
         // sums are reduced together by a transposed butterfly (halves exchange 8 values, then 4, 2, 1, then one
@@ -1375,9 +1382,9 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
             mbar_init(&full_bar()[s], 1);
             mbar_init(&empty_bar()[s], kW);
         }
-        mbar_init(&s_attn_bar, 1);
+        mbar_init(&dsh().attn_bar, 1);
         fence_barrier_init();
-        s_epoch = *reinterpret_cast<volatile const unsigned*>(p.epoch);
+        dsh().epoch = *reinterpret_cast<volatile const unsigned*>(p.epoch);
         // keys per attention split: the smallest multiple of 32 (up to p.span) whose items fit the grid, one item
         // per CTA (more, smaller items finish sooner: the phase waits for its slowest item)
         int sp = 32;
@@ -1386,17 +1393,17 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
             for (int m = 0; m < p.M; m++) items += p.KV * ((max(0, min(p.pos[m], p.context - 1)) + sp) / sp);
             if (items <= p.grid || sp >= p.span) break;
         }
-        s_span = sp;
+        dsh().span = sp;
     }
     // the per-layer pointers, once, into shared memory (indexing the parameter block by layer would go through
     // the constant cache on every phase)
     {
         const int words = p.layers * int(sizeof(DecodeLayer) / 8);
         const uint64_t* src = reinterpret_cast<const uint64_t*>(p.layer);
-        uint64_t* dst = reinterpret_cast<uint64_t*>(dsm + 256);
+        uint64_t* dst = reinterpret_cast<uint64_t*>(dsm + kDHdr);
         for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
     }
-    if (threadIdx.x < kDecodeMaxSeqs) s_key[threadIdx.x] = 0ull;
+    if (threadIdx.x < kDecodeMaxSeqs) dsh().key[threadIdx.x] = 0ull;
     __syncthreads();
     if (warp == kW) {
         producer<QW>(p, full_bar(), empty_bar(), ring_buf(p), lane);
@@ -1415,21 +1422,21 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
             const int m = i / w, c = n0 + (i - m * w);
             float v = dequant_one(p.fmt, p.embed + int64_t(token_of(p, m)) * p.rb_c, p.C, c);
             if (p.wpe) v += p.wpe[int64_t(p.pos[m]) * p.C + c];
-            s_xown[m][c - n0] = v;
+            dsh().xown[m][c - n0] = v;
             tw_put(p.x_tw + int64_t(m) * p.C + c, v, tag_of(0, kXIn));
         }
     }
     // Phases in order: per layer qkv, attention, split merge, o_proj, up, down; then the LM head.
     uint32_t st = 0, seen = 0;  // weight stages of the step: consumed by the phases so far, landings observed
     uint32_t red_par = 0;       // the GEMV phases' partial-sum buffer in use (alternates by stage)
-    int issued = 0;  // attention copies requested so far (the parity of s_attn_bar)
+    int issued = 0;  // attention copies requested so far (the parity of dsh().attn_bar)
     int Sm[kDecodeMaxSeqs], Pm[kDecodeMaxSeqs];
     const bool attn_cta = int(blockIdx.x) < attn_items(p, Sm, Pm);
     // Leaving early (a wait gave up): no attention copy of ours may still be landing in shared memory.
     auto drain = [&]() {
         if (threadIdx.x == 0 && issued > 0) {
             const uint64_t t0 = gtimer();
-            while (!mbar_try_wait(&s_attn_bar, uint32_t(issued - 1) & 1u) && gtimer() - t0 < p.wait_ns) {
+            while (!mbar_try_wait(&dsh().attn_bar, uint32_t(issued - 1) & 1u) && gtimer() - t0 < p.wait_ns) {
             }
         }
     };
@@ -1456,13 +1463,13 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
             }
         }
     }
-    if (threadIdx.x < p.M && s_key[threadIdx.x]) atomicMax(p.keys + threadIdx.x, s_key[threadIdx.x]);
+    if (threadIdx.x < p.M && dsh().key[threadIdx.x]) atomicMax(p.keys + threadIdx.x, dsh().key[threadIdx.x]);
     // (No early trigger of the dependent LM-head launch: releasing it here measured 60 us slower per step.)
     __threadfence();
     csync();
-    if (threadIdx.x == 0) s_last = atomicAdd(p.sync, 1u) == unsigned(p.grid - 1) ? 1 : 0;
+    if (threadIdx.x == 0) dsh().last = atomicAdd(p.sync, 1u) == unsigned(p.grid - 1) ? 1 : 0;
     csync();
-    if (!s_last) return;
+    if (!dsh().last) return;
     // Last CTA: every other CTA has passed its last wait. Greedy token per sequence (argmax_finalize_kernel
     // semantics), then reset the step counter and advance the epoch for the next launch.
     __threadfence();
@@ -1483,7 +1490,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_kernel(const __grid_constant__
     }
     if (threadIdx.x == 0) {
         *p.sync = 0u;
-        *p.epoch = s_epoch + decode_epoch_stride(p.layers);
+        *p.epoch = dsh().epoch + decode_epoch_stride(p.layers);
     }
 }
 
@@ -1511,7 +1518,7 @@ int attn_scratch_floats(const DecodeParams& p) {
 int64_t table_bytes(const DecodeParams& p) { return (int64_t(p.layers) * int64_t(sizeof(DecodeLayer)) + 127) / 128 * 128; }
 
 size_t smem_bytes(const DecodeParams& p) {
-    return 256 + size_t(table_bytes(p)) + size_t(p.xs_bytes) + size_t(p.kv_bytes) + size_t(p.nslot) * p.slot_bytes;
+    return kDHdr + size_t(table_bytes(p)) + size_t(p.xs_bytes) + size_t(p.kv_bytes) + size_t(p.nslot) * p.slot_bytes;
 }
 
 }  // namespace
@@ -1569,7 +1576,7 @@ bool plan_decode(DecodeParams& p, std::string* why) {
         cudaGetLastError();
         return no("kernel attributes");
     }
-    const int64_t budget = int64_t(optin) - int64_t(fa.sharedSizeBytes) - 256 - table_bytes(p) - xs - kvb;
+    const int64_t budget = int64_t(optin) - int64_t(fa.sharedSizeBytes) - kDHdr - table_bytes(p) - xs - kvb;
     const int nslot = int(std::min<int64_t>(kMaxSlots, budget / slot));
     if (nslot < need) return no("shared memory: weight rows too wide for the slot ring");
     p.xs_bytes = int(xs);

@@ -35,12 +35,19 @@ constexpr int kENT = kEW * 32;
 constexpr int kEMaxM = 4;            // activation rows (2 B columns each)
 constexpr int kENB = 4;              // spans loaded ahead per warp
 
-extern __shared__ __align__(128) uint8_t esm[];  // B columns (2 M x xp bytes)
-__shared__ float e_part[kEW][2][kEMaxM][16];     // [warp][gate | up][activation row][tile row]
-__shared__ double e_stat[kEMaxM][kEW][2];        // norm sums per warp
-__shared__ float e_max[kEMaxM][kEW];             // largest magnitude per warp
-__shared__ unsigned long long e_key[kEMaxM];
-__shared__ int e_last;
+// Dynamic shared memory: EShared | B columns (2 M x xp bytes). The per-CTA arrays live in the dynamic region:
+// file-scope __shared__ arrays are placed by the device linker in one window shared with the other files' and
+// would make this kernel's static shared memory depend on them.
+extern __shared__ __align__(128) uint8_t esm[];
+struct EShared {
+    float part[kEW][2][kEMaxM][16];  // [warp][gate | up][activation row][tile row]
+    double stat[kEMaxM][kEW][2];     // norm sums per warp
+    float max[kEMaxM][kEW];          // largest magnitude per warp
+    unsigned long long key[kEMaxM];
+    int last;
+};
+constexpr int kEHdr = int(sizeof(EShared) + 127) / 128 * 128;  // bytes before the B columns
+__device__ __forceinline__ EShared& esh() { return *reinterpret_cast<EShared*>(esm); }
 
 struct E4Plan {
     int tiles;       // 16-row tiles
@@ -101,8 +108,8 @@ __device__ void stage_hilo(const GemvArgs& a, int xp, uint8_t* xh, float (&s)[kE
         for (int m = 0; m < kEMaxM; m++) {
             const double t1 = wsum_e(s1[m]), t2 = wsum_e(s2[m]);
             if (lane == 0) {
-                e_stat[m][warp][0] = t1;
-                e_stat[m][warp][1] = t2;
+                esh().stat[m][warp][0] = t1;
+                esh().stat[m][warp][1] = t2;
             }
         }
         esync();
@@ -110,8 +117,8 @@ __device__ void stage_hilo(const GemvArgs& a, int xp, uint8_t* xh, float (&s)[kE
         for (int m = 0; m < kEMaxM; m++) {
             double a1 = 0.0, a2 = 0.0;
             for (int w = 0; w < kEW; w++) {
-                a1 += e_stat[m][w][0];
-                a2 += e_stat[m][w][1];
+                a1 += esh().stat[m][w][0];
+                a2 += esh().stat[m][w][1];
             }
             if (a.norm == kNormRms) {
                 r[m] = float(1.0 / sqrt(a2 / a.K + double(a.eps)));
@@ -164,14 +171,14 @@ __device__ void stage_hilo(const GemvArgs& a, int xp, uint8_t* xh, float (&s)[kE
 #pragma unroll
     for (int m = 0; m < kEMaxM; m++) {
         const float v = warp_max(mx[m]);
-        if (lane == 0) e_max[m][warp] = v;
+        if (lane == 0) esh().max[m][warp] = v;
     }
     esync();
     float inv[kEMaxM];
 #pragma unroll
     for (int m = 0; m < kEMaxM; m++) {
         float v = 0.0f;
-        for (int w = 0; w < kEW; w++) v = fmaxf(v, e_max[m][w]);
+        for (int w = 0; w < kEW; w++) v = fmaxf(v, esh().max[m][w]);
         const int F = int((__float_as_uint(v) >> 23) & 0xFF) - 127;  // v in [2^F, 2^(F+1)) (v = 0: any scale)
         const int e = max(-126, min(127, F - 14)), ie = max(-126, min(127, -e));
         s[m] = __uint_as_float(uint32_t(e + 127) << 23);
@@ -293,11 +300,11 @@ __device__ __forceinline__ void tile_store(const GemvArgs& a, int row0, const fl
 }
 
 __global__ void __launch_bounds__(kENT, 1) gemv_fp8_tc_kernel(const GemvArgs a, const E4Plan p) {
-    uint8_t* xh = esm;
+    uint8_t* xh = esm + kEHdr;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const bool pair = a.pair_off != 0;
     const int rb = int(a.row_bytes), cbytes = a.K, ns = a.K / 64;
-    if (threadIdx.x < kEMaxM) e_key[threadIdx.x] = 0ull;
+    if (threadIdx.x < kEMaxM) esh().key[threadIdx.x] = 0ull;
     auto rows_of = [&](int tile, int u, const uint8_t*& wg, const uint8_t*& wh) {
         const int r = 16 * tile + g;
         const int64_t base = u ? a.pair_off : 0;
@@ -375,8 +382,8 @@ __global__ void __launch_bounds__(kENT, 1) gemv_fp8_tc_kernel(const GemvArgs a, 
                 if (out_lane)
 #pragma unroll
                     for (int u = 0; u < 2; u++) {
-                        e_part[warp][u][t][g] = v[u][0];
-                        e_part[warp][u][t][g + 8] = v[u][1];
+                        esh().part[warp][u][t][g] = v[u][0];
+                        esh().part[warp][u][t][g + 8] = v[u][1];
                     }
                 tile_sync(tl, p.q1 * 32);
                 if (ks == 0 && out_lane)
@@ -384,8 +391,8 @@ __global__ void __launch_bounds__(kENT, 1) gemv_fp8_tc_kernel(const GemvArgs a, 
                     for (int u = 0; u < 2; u++) {
                         float x0 = 0.0f, x1 = 0.0f;
                         for (int k = 0; k < p.q1; k++) {
-                            x0 += e_part[warp + k][u][t][g];
-                            x1 += e_part[warp + k][u][t][g + 8];
+                            x0 += esh().part[warp + k][u][t][g];
+                            x1 += esh().part[warp + k][u][t][g + 8];
                         }
                         v[u][0] = x0;
                         v[u][1] = x1;
@@ -398,15 +405,15 @@ __global__ void __launch_bounds__(kENT, 1) gemv_fp8_tc_kernel(const GemvArgs a, 
         best = max(best, __shfl_xor_sync(0xffffffffu, best, 4));
         best = max(best, __shfl_xor_sync(0xffffffffu, best, 8));
         best = max(best, __shfl_xor_sync(0xffffffffu, best, 16));
-        if (g == 0 && out_lane && best) atomicMax(&e_key[t], best);
+        if (g == 0 && out_lane && best) atomicMax(&esh().key[t], best);
         esync();
-        if (threadIdx.x < a.M && e_key[threadIdx.x]) atomicMax(a.argmax + threadIdx.x, e_key[threadIdx.x]);
+        if (threadIdx.x < a.M && esh().key[threadIdx.x]) atomicMax(a.argmax + threadIdx.x, esh().key[threadIdx.x]);
         if (a.fin_count) {  // the last CTA: every other CTA's keys are in (each fenced before counting itself)
             __threadfence();
             esync();
-            if (threadIdx.x == 0) e_last = atomicAdd(a.fin_count, 1u) == gridDim.x - 1 ? 1 : 0;
+            if (threadIdx.x == 0) esh().last = atomicAdd(a.fin_count, 1u) == gridDim.x - 1 ? 1 : 0;
             esync();
-            if (e_last) {
+            if (esh().last) {
                 __threadfence();
                 if (threadIdx.x < a.M) {
                     const int m = threadIdx.x;
@@ -449,17 +456,8 @@ cudaError_t launch_gemv_fp8_tc(const GemvArgs& a, cudaStream_t st, bool pdl) {
     p.q1 = kEW / p.tpc;
     const int ctas = p.n0 ? sms : std::max(1, std::min(sms, rem));
     p.xp = 2 * a.K + 64;
-    const size_t smem = size_t(2 * a.M) * p.xp;
-    if (smem > 200 * 1024) return cudaErrorNotSupported;
-    static int attr_set[32] = {};  // per device < 32: the limit only grows
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int* set = dev < 32 ? &attr_set[dev] : nullptr;
-    if (!set || *set < int(smem)) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_fp8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-        if (set) *set = int(smem);
-    }
+    const size_t smem = kEHdr + size_t(2 * a.M) * p.xp;
+    if (const cudaError_t e = ensure_dyn_smem(gemv_fp8_tc_kernel, smem); e != cudaSuccess) return e;
     return launch_ex(gemv_fp8_tc_kernel, dim3(ctas), dim3(kENT), smem, st, pdl, a, p);
 }
 

@@ -30,11 +30,17 @@ constexpr int kSThr = kSNT + 32;     // + the producer warp
 constexpr int kSMaxSlots = 16;
 constexpr int kSChunk = 8192;        // bytes per bulk copy
 constexpr int kSMaxStat = 64;        // norm partial slots (M * K / 128 <= 4096 / 128)
-constexpr int kSStatic = 8192;       // margin for the static shared memory and the per-block reservation
 
-extern __shared__ __align__(128) uint8_t gsm[];  // full[8] | empty[8] | activations | ring
-__shared__ double t_part[2 * kSMaxStat];
-__shared__ unsigned long long t_key[kDecodeMaxSeqs];
+// Dynamic shared memory: full[16] | empty[16] | TShared | activations | ring. The small per-CTA arrays live in
+// the dynamic region too: file-scope __shared__ arrays are placed by the device linker in one window shared
+// with the other files' and would make this kernel's static shared memory depend on them.
+extern __shared__ __align__(128) uint8_t gsm[];
+struct TShared {
+    double part[2 * kSMaxStat];                // norm partial sums
+    unsigned long long key[kDecodeMaxSeqs];    // the CTA's greedy argmax keys
+};
+constexpr int kSHdr = 256 + int(sizeof(TShared) + 127) / 128 * 128;  // bytes before the activations
+__device__ __forceinline__ TShared& tsh() { return *reinterpret_cast<TShared*>(gsm + 256); }
 
 template <int NM>
 constexpr int kSRows = NM == 1 ? 4 : 2;  // rows per warp pass
@@ -75,8 +81,8 @@ __device__ void stage_act(const GemvArgs& a, float* xs, int warp, int lane) {
             s1 = wsum_d(s1);
             s2 = wsum_d(s2);
             if (lane == 0) {
-                t_part[2 * (base / 32 + warp)] = s1;
-                t_part[2 * (base / 32 + warp) + 1] = s2;
+                tsh().part[2 * (base / 32 + warp)] = s1;
+                tsh().part[2 * (base / 32 + warp) + 1] = s2;
             }
         }
     }
@@ -86,8 +92,8 @@ __device__ void stage_act(const GemvArgs& a, float* xs, int warp, int lane) {
         const int m = i / K4, k = 4 * (i - m * K4);
         double a1 = 0.0, a2 = 0.0;
         for (int q = m * gpr; q < (m + 1) * gpr; q++) {
-            a1 += t_part[2 * q];
-            a2 += t_part[2 * q + 1];
+            a1 += tsh().part[2 * q];
+            a2 += tsh().part[2 * q + 1];
         }
         float mean = 0.0f, r;
         if (a.norm == kNormRms) {
@@ -160,8 +166,8 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_stream_kernel(const GemvArgs a,
     constexpr int RR = kSRows<NM>;
     uint64_t* full = reinterpret_cast<uint64_t*>(gsm);
     uint64_t* empty = full + kSMaxSlots;
-    float* xs = reinterpret_cast<float*>(gsm + 256);
-    uint8_t* ring = gsm + 256 + sp.xs_bytes;
+    float* xs = reinterpret_cast<float*>(gsm + kSHdr);
+    uint8_t* ring = gsm + kSHdr + sp.xs_bytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool pair = a.pair_off != 0;
     const int r0 = blockIdx.x * sp.rows_per_cta, r1 = min(a.rows, r0 + sp.rows_per_cta);
@@ -175,7 +181,7 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_stream_kernel(const GemvArgs a,
         }
         fence_barrier_init();
     }
-    if (threadIdx.x < kDecodeMaxSeqs) t_key[threadIdx.x] = 0ull;
+    if (threadIdx.x < kDecodeMaxSeqs) tsh().key[threadIdx.x] = 0ull;
     __syncthreads();
 
     if (warp == kSW) {  // producer: weights only, so it never waits for the previous kernel
@@ -279,10 +285,10 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_stream_kernel(const GemvArgs a,
             unsigned long long k = best[m];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) k = max(k, __shfl_xor_sync(0xffffffffu, k, o));
-            if (lane == 0 && k) atomicMax(&t_key[m], k);
+            if (lane == 0 && k) atomicMax(&tsh().key[m], k);
         }
         ssync();
-        if (threadIdx.x < a.M && t_key[threadIdx.x]) atomicMax(a.argmax + threadIdx.x, t_key[threadIdx.x]);
+        if (threadIdx.x < a.M && tsh().key[threadIdx.x]) atomicMax(a.argmax + threadIdx.x, tsh().key[threadIdx.x]);
     }
 }
 
@@ -331,8 +337,8 @@ __device__ void stage_act_hilo(const GemvArgs& a, __half* xh, __half* xl, int wa
         for (int m = 0; m < kDecodeMaxSeqs; m++) {
             const double t1 = wsum_d(s1[m]), t2 = wsum_d(s2[m]);
             if (lane == 0) {
-                t_part[2 * (m * kSW + warp)] = t1;
-                t_part[2 * (m * kSW + warp) + 1] = t2;
+                tsh().part[2 * (m * kSW + warp)] = t1;
+                tsh().part[2 * (m * kSW + warp) + 1] = t2;
             }
         }
         ssync();
@@ -340,8 +346,8 @@ __device__ void stage_act_hilo(const GemvArgs& a, __half* xh, __half* xl, int wa
         for (int m = 0; m < kDecodeMaxSeqs; m++) {
             double a1 = 0.0, a2 = 0.0;
             for (int w = 0; w < kSW; w++) {
-                a1 += t_part[2 * (m * kSW + w)];
-                a2 += t_part[2 * (m * kSW + w) + 1];
+                a1 += tsh().part[2 * (m * kSW + w)];
+                a2 += tsh().part[2 * (m * kSW + w) + 1];
             }
             mean[m] = 0.0f;
             if (a.norm == kNormRms) {
@@ -420,9 +426,9 @@ template <int FMT>
 __global__ void __launch_bounds__(kSThr, 1) gemv_mma_kernel(const GemvArgs a, const MmaPlan sp) {
     uint64_t* full = reinterpret_cast<uint64_t*>(gsm);
     uint64_t* empty = full + kSMaxSlots;
-    __half* xh = reinterpret_cast<__half*>(gsm + 256);
+    __half* xh = reinterpret_cast<__half*>(gsm + kSHdr);
     __half* xl = xh + a.M * a.K;
-    uint8_t* ring = gsm + 256 + sp.xs_bytes;
+    uint8_t* ring = gsm + kSHdr + sp.xs_bytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const bool pair = a.pair_off != 0;
     const int r0 = blockIdx.x * sp.rows_per_cta, r1 = min(a.rows, r0 + sp.rows_per_cta);
@@ -437,7 +443,7 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_mma_kernel(const GemvArgs a, co
         }
         fence_barrier_init();
     }
-    if (threadIdx.x < kDecodeMaxSeqs) t_key[threadIdx.x] = 0ull;
+    if (threadIdx.x < kDecodeMaxSeqs) tsh().key[threadIdx.x] = 0ull;
     __syncthreads();
     if (warp == kSW) {  // producer: weights only, so it never waits for the previous kernel
         stream_producer_rows(a, r0, r1, sp, full, empty, ring, lane);
@@ -543,9 +549,9 @@ __global__ void __launch_bounds__(kSThr, 1) gemv_mma_kernel(const GemvArgs a, co
     if (a.argmax) {  // the 4 lanes of each activation row, then per CTA, then one global atomic per row
         best = max(best, __shfl_xor_sync(0xffffffffu, best, 1));
         best = max(best, __shfl_xor_sync(0xffffffffu, best, 2));
-        if (c == 0 && xrow && best) atomicMax(&t_key[g], best);
+        if (c == 0 && xrow && best) atomicMax(&tsh().key[g], best);
         ssync();
-        if (threadIdx.x < a.M && t_key[threadIdx.x]) atomicMax(a.argmax + threadIdx.x, t_key[threadIdx.x]);
+        if (threadIdx.x < a.M && tsh().key[threadIdx.x]) atomicMax(a.argmax + threadIdx.x, tsh().key[threadIdx.x]);
     }
 }
 
@@ -571,7 +577,8 @@ cudaError_t launch_gemv_mma(const GemvArgs& a, cudaStream_t st, bool pdl) {
     ctas = (a.rows + sp.rows_per_cta - 1) / sp.rows_per_cta;
     sp.xs_bytes = int(xs);
     sp.pitch = int(a.row_bytes) + 16;
-    const int64_t budget = 227 * 1024 - kSStatic - 256 - xs;
+    auto k = a.fmt == kFP8 ? gemv_mma_kernel<kFP8> : gemv_mma_kernel<kFP4>;
+    const int64_t budget = int64_t(max_dyn_smem(k)) - kSHdr - xs;
     const int tneed = (sp.rows_per_cta + 7) / 8;
     sp.tiles = 0;
     int best = -1;
@@ -594,17 +601,8 @@ cudaError_t launch_gemv_mma(const GemvArgs& a, cudaStream_t st, bool pdl) {
     }
     if (!sp.tiles || sp.groups * sp.tiles < kSW / 2) return cudaErrorNotSupported;  // too few busy warps
     sp.rps = 8 * sp.tiles;
-    auto k = a.fmt == kFP8 ? gemv_mma_kernel<kFP8> : gemv_mma_kernel<kFP4>;
-    const size_t smem = 256 + size_t(xs) + size_t(sp.nslot) * sp.slot_bytes;
-    static int attr_set[2][32] = {};  // per (format, device < 32): the limit only grows
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int* set = dev < 32 ? &attr_set[a.fmt == kFP8 ? 0 : 1][dev] : nullptr;
-    if (!set || *set < int(smem)) {
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-        if (set) *set = int(smem);
-    }
+    const size_t smem = kSHdr + size_t(xs) + size_t(sp.nslot) * sp.slot_bytes;
+    if (const cudaError_t e = ensure_dyn_smem(k, smem); e != cudaSuccess) return e;
     return launch_ex(k, dim3(ctas), dim3(kSThr), smem, st, pdl, a, sp);
 }
 
@@ -635,7 +633,8 @@ cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl) {
     sp.rows_per_cta = (a.rows + ctas - 1) / ctas;
     ctas = (a.rows + sp.rows_per_cta - 1) / sp.rows_per_cta;
     sp.xs_bytes = int(xs);
-    const int64_t budget = 227 * 1024 - kSStatic - 256 - xs;
+    StreamFn k = pick(a.fmt, a.M);
+    const int64_t budget = int64_t(max_dyn_smem(k)) - kSHdr - xs;
     // Stage = kSW x rpw rows: the most rows per warp (up to what a pass takes) that still leaves a ring of
     // at least four stages (three, then two, for very wide rows).
     const int rpp = (a.M == 1 ? 4 : 2) / (a.pair_off ? 2 : 1);
@@ -653,18 +652,8 @@ cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl) {
     if (!sp.rpw) return cudaErrorNotSupported;
     sp.rps = kSW * sp.rpw;
     sp.nslot = int(std::min<int64_t>(kSMaxSlots, budget / sp.slot_bytes));
-    StreamFn k = pick(a.fmt, a.M);
-    const size_t smem = 256 + size_t(xs) + size_t(sp.nslot) * sp.slot_bytes;
-    // the dynamic shared-memory limit of the instantiation, raised to this call's size when needed (per device)
-    static int attr_set[4][32] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int* set = dev < 32 ? &attr_set[(a.fmt == kFP8 ? 0 : 2) + (a.M == 1 ? 0 : 1)][dev] : nullptr;
-    if (!set || *set < int(smem)) {
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-        if (set) *set = int(smem);
-    }
+    const size_t smem = kSHdr + size_t(xs) + size_t(sp.nslot) * sp.slot_bytes;
+    if (const cudaError_t e = ensure_dyn_smem(k, smem); e != cudaSuccess) return e;
     return launch_ex(k, dim3(ctas), dim3(kSThr), smem, st, pdl, a, sp);
 }
 

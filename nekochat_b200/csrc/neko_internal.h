@@ -31,6 +31,17 @@ inline cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
 }
 
 int num_sms();  // of the current device, cached per device
+// Dynamic shared memory of a kernel on the current device. The library is linked with relocatable device code,
+// so the device linker sizes each kernel's static shared memory: budgets are taken from the queried figure, never
+// from an assumed margin. max_dyn_smem: the opt-in per-block limit less the kernel's static shared memory.
+// ensure_dyn_smem: raises the kernel's attribute to bytes (the attribute only grows; cached per function and
+// device); cudaErrorNotSupported, with no CUDA call made, when bytes exceed max_dyn_smem.
+int max_dyn_smem(const void* fn);
+cudaError_t ensure_dyn_smem(const void* fn, size_t bytes);
+template <typename F>
+inline int max_dyn_smem(F* fn) { return max_dyn_smem(reinterpret_cast<const void*>(fn)); }
+template <typename F>
+inline cudaError_t ensure_dyn_smem(F* fn, size_t bytes) { return ensure_dyn_smem(reinterpret_cast<const void*>(fn), bytes); }
 
 // ------------------------------------------------------------------ weight codec (k_quant.cu)
 cudaError_t launch_quantize(int fmt, const float* w, int rows, int cols, int64_t ld, int transpose, uint8_t* out,
