@@ -25,6 +25,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <type_traits>
 
 #include "gemv_core.cuh"
@@ -700,6 +701,17 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl) {
             e = launch_gemm_umma(a, sp.xh, sp.xl, st, true);
             if (e != cudaErrorNotSupported) return e;
         }
+    }
+    // 5..64 rows on split activations: the warp-specialised tcgen05 kernel (k_umma_ws.cu), after this call's
+    // split kernel (programmatic launch) or chained to the previous matmul as asked; NEKO_GEMM_WS=0 in the
+    // environment keeps this kernel for comparison
+    static const bool ws_on = [] {
+        const char* v = std::getenv("NEKO_GEMM_WS");
+        return !(v && v[0] == '0');
+    }();
+    if (ws_on && pl.presplit && a.M <= 64) {
+        const cudaError_t e = launch_gemm_ws(a, sp.xh, sp.xl, st, a.x_hi ? pdl : true);
+        if (e != cudaErrorNotSupported) return e;
     }
     const bool pre = pl.presplit;
     TcFn k = a.fmt == kFP8 ? (pre ? pick<kFP8, true>(pair) : pick<kFP8, false>(pair))

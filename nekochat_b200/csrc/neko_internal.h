@@ -137,6 +137,11 @@ cudaError_t launch_gemv_stream(const GemvArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_gemv_fp8_tc(const GemvArgs& a, cudaStream_t st, bool pdl);
 // The tensor-core kernel for 5+ activation rows (k_mma.cu); cudaErrorNotSupported when the call does not fit.
 cudaError_t launch_gemm_tc(const GemvArgs& a, cudaStream_t st, bool pdl);
+// The warp-specialised tcgen05 kernel (k_umma_ws.cu) for 1..64 rows on activations split into f16 hi / lo
+// ([M][K] each, 16-byte aligned): the weights as the UMMA's 128-row M side; cudaErrorNotSupported when the call
+// does not fit.
+bool gemm_ws_fits(const GemvArgs& a);
+cudaError_t launch_gemm_ws(const GemvArgs& a, const __half* xh, const __half* xl, cudaStream_t st, bool pdl);
 // The tcgen05 kernel (k_umma.cu) for 128+ rows on activations split into f16 hi / lo ([M][K] each);
 // cudaErrorNotSupported when the call does not fit.
 cudaError_t launch_gemm_umma(const GemvArgs& a, const __half* xh, const __half* xl, cudaStream_t st, bool pdl);
