@@ -9,7 +9,9 @@
 // D = w_hi x_hi + w_hi x_lo + w_lo x_hi accumulated in fp32 in TMEM over all of K (w_hi x [x_hi; x_lo] as one
 // UMMA of 2 N columns, the halves added in the epilogue).
 //
-// Roles, one CTA per SM (352 threads), K in stages of 64:
+// Roles (352 threads; one CTA per SM, or two when a launch has no K split and more than two waves of tiles: the
+// ~30% of a CTA's time outside its K loop, the first copies and the epilogue, then overlaps the other's K loop;
+// M = 64 LM head 211 -> 138 us), K in stages of 64:
 //  * warp 0, one lane: weight producer. Raw stages of four K stages (the code bytes of the 128 rows, 256 bytes a
 //    row for FP8, with the 128-byte swizzle, and the 16-byte scale group holding their eight block scales) into a
 //    2-deep ring with TMA tensor copies of 64-row boxes; weights never depend on the previous kernel, so this
@@ -36,6 +38,7 @@
 
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <cstdint>
 
 #include "gemv_core.cuh"
@@ -58,6 +61,7 @@ constexpr int kWActWarp = 2 + kWConv;         // the activation producer's warp
 constexpr int kWRaw = 2;                      // raw stages (4 K stages each)
 constexpr int kWOps = 2;                      // A stages (weight tiles in TMEM)
 constexpr int kWB = 6;                        // B stages (activation tiles in shared memory)
+constexpr int kWBLite = 2;                    // the same for two CTAs per SM (no K split, many waves)
 constexpr int kWMaxSplit = 8;                 // CTAs of a split-K cluster (portable limit)
 constexpr int kWMaxRows = 64;                 // activation rows (UMMA N <= 64)
 // TMEM columns: the accumulators in [0, 2 NT) (column n < NT: w_hi x_hi + w_lo x_hi of activation row n,
@@ -84,25 +88,29 @@ constexpr int ws_recv_floats(int nt) {  // the largest ks x 128 x pitch over ks 
 // Dynamic shared memory (1024-byte aligned base): B stages (activations hi / lo) | raw stages | receive buffer |
 // barriers | flags | epilogue scratch. A raw stage holds [kRP / 128 column boxes][128 rows][128 bytes] of codes
 // with the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r % 8)), then [128 rows][16] scale groups.
-template <int FMT, int NT>
+// LITE (two CTAs per SM, no K split): a 2-deep B ring and the receive buffer over the rings, which are free once
+// every UMMA has completed.
+template <int FMT, int NT, bool LITE = false>
 struct WsLayout {
+    static constexpr int kB = LITE ? kWBLite : kWB;
     static constexpr int kCB = FMT == kFP8 ? kWK : kWK / 2;  // code bytes per row per K stage
     static constexpr int kRP = kWSub * kCB;                   // code bytes per row per raw stage (256 / 128)
     static constexpr int kBTile = NT * kWK * 2;               // one f16 B tile (activations)
     static constexpr int kOp = 2 * kBTile;                    // B hi, B lo (one 2 NT-row operand)
     static constexpr int kRawCodes = kWM * kRP;
     static constexpr int kRaw = kRawCodes + kWM * 16;
-    static constexpr int kRawOff = kWB * kOp;
-    static constexpr int kRecvOff = kRawOff + kWRaw * kRaw;   // [source split][128 tile rows][pitch]
-    static constexpr int kRecv = ws_recv_floats(NT) * 4;
-    static constexpr int kBarOff = kRecvOff + kRecv;
-    static constexpr int kNBar = 2 * kWRaw + 2 * kWOps + 2 * kWB + 1;  // raw, A, B full / empty; done
+    static constexpr int kRawOff = kB * kOp;
+    static constexpr int kRecvOff = LITE ? 0 : kRawOff + kWRaw * kRaw;  // [source split][128 tile rows][pitch]
+    static constexpr int kRecv = LITE ? kWM * ws_recv_pitch(NT) * 4 : ws_recv_floats(NT) * 4;
+    static constexpr int kBarOff = LITE ? kRawOff + kWRaw * kRaw : kRecvOff + kRecv;
+    static constexpr int kNBar = 2 * kWRaw + 2 * kWOps + 2 * kB + 1;  // raw, A, B full / empty; done
     static constexpr int kMiscOff = kBarOff + kNBar * 8;      // TMEM address, failure flag
     static constexpr int kKeysOff = (kMiscOff + 8 + 15) / 16 * 16;
     static constexpr int kRsOff = kKeysOff + NT * 8;          // row scales
     static constexpr int kSspOff = kRsOff + NT * 4;           // [NT][4] sums of squares per 32 columns
     static constexpr int kBytes = kSspOff + NT * 4 * 4;
     static_assert(kOp % 1024 == 0 && kRaw % 1024 == 0 && kRecv % 16 == 0, "tile and copy alignment");
+    static_assert(!LITE || kRecv <= kRawOff + kWRaw * kRaw, "the receive buffer fits over the rings");
 };
 
 struct WsPlan {
@@ -190,12 +198,13 @@ __device__ __forceinline__ void ws_convert(const uint8_t* raw, int r, int j, int
     }
 }
 
-template <int FMT, int NT, bool PAIR>
-__global__ void __launch_bounds__(kWThreads, 1)
+template <int FMT, int NT, bool PAIR, bool LITE>
+__global__ void __launch_bounds__(kWThreads, LITE ? 2 : 1)
     umma_ws_kernel(const GemvArgs a, const WsPlan pl, const __grid_constant__ CUtensorMap t_code,
                    const __grid_constant__ CUtensorMap t_scale, const __grid_constant__ CUtensorMap t_xh,
                    const __grid_constant__ CUtensorMap t_xl) {
-    using L = WsLayout<FMT, NT>;
+    using L = WsLayout<FMT, NT, LITE>;
+    constexpr int kWB = L::kB;
     extern __shared__ uint8_t wsm_raw[];
     uint8_t* sm = wsm_raw + ((1024 - (smem_u32(wsm_raw) & 1023)) & 1023);
     uint64_t* raw_full = reinterpret_cast<uint64_t*>(sm + L::kBarOff);
@@ -251,7 +260,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
         // the descriptors and swizzled copies assume 1024-byte aligned tiles and the tensor maps 64-byte aligned
         // parameters: a failure is recorded and nothing is issued
         *fail = ((smem_u32(sm) & 1023u) || (reinterpret_cast<uintptr_t>(&t_code) & 63u) ||
-                 (reinterpret_cast<uintptr_t>(&t_xh) & 63u) || nst <= 0)
+                 (reinterpret_cast<uintptr_t>(&t_xh) & 63u) || nst <= 0 || (LITE && ks != 1))
                     ? 1
                     : 0;
     }
@@ -486,22 +495,22 @@ __global__ void __launch_bounds__(kWThreads, 1)
             if (keys[m]) atomicMax(a.argmax + m, keys[m]);
 }
 
-template <int FMT, int NT, bool PAIR>
+template <int FMT, int NT, bool LITE>
 size_t ws_smem() {
-    return size_t(WsLayout<FMT, NT>::kBytes) + 1024;
+    return size_t(WsLayout<FMT, NT, LITE>::kBytes) + 1024;
 }
 
 using WsFn = void (*)(const GemvArgs, const WsPlan, const CUtensorMap, const CUtensorMap, const CUtensorMap,
                       const CUtensorMap);
 
-template <int FMT>
+template <int FMT, bool LITE>
 WsFn ws_pick(int nt, bool pair, size_t* smem) {
     if (nt == 32) {
-        *smem = pair ? ws_smem<FMT, 32, true>() : ws_smem<FMT, 32, false>();
-        return pair ? umma_ws_kernel<FMT, 32, true> : umma_ws_kernel<FMT, 32, false>;
+        *smem = ws_smem<FMT, 32, LITE>();
+        return pair ? umma_ws_kernel<FMT, 32, true, LITE> : umma_ws_kernel<FMT, 32, false, LITE>;
     }
-    *smem = pair ? ws_smem<FMT, 64, true>() : ws_smem<FMT, 64, false>();
-    return pair ? umma_ws_kernel<FMT, 64, true> : umma_ws_kernel<FMT, 64, false>;
+    *smem = ws_smem<FMT, 64, LITE>();
+    return pair ? umma_ws_kernel<FMT, 64, true, LITE> : umma_ws_kernel<FMT, 64, false, LITE>;
 }
 
 // K splits (1, 2, 4 or 8, whole raw stages of 4 K stages each, so each split starts on a scale group): one CTA
@@ -548,7 +557,15 @@ cudaError_t launch_gemm_ws(const GemvArgs& a, const __half* xh, const __half* xl
     const int outs = pair ? kWM / 2 : kWM, ntile = (a.rows + outs - 1) / outs, nst = a.K / kWK;
     const WsPlan pl = ws_plan(ntile, nst);
     size_t smem = 0;
-    const WsFn k = a.fmt == kFP8 ? ws_pick<kFP8>(nt, pair, &smem) : ws_pick<kFP4>(nt, pair, &smem);
+    // no K split and more tiles than two waves: two CTAs per SM, so that one's fill and epilogue overlap the
+    // other's K loop (NEKO_GEMM_WS_LITE=0 in the environment keeps one per SM)
+    static const bool lite_on = [] {
+        const char* v = std::getenv("NEKO_GEMM_WS_LITE");
+        return !(v && v[0] == '0');
+    }();
+    const bool lite = lite_on && pl.ksplit == 1 && ntile > 2 * num_sms();
+    const WsFn k = a.fmt == kFP8 ? (lite ? ws_pick<kFP8, true>(nt, pair, &smem) : ws_pick<kFP8, false>(nt, pair, &smem))
+                                 : (lite ? ws_pick<kFP4, true>(nt, pair, &smem) : ws_pick<kFP4, false>(nt, pair, &smem));
     if (const cudaError_t e = ensure_dyn_smem(k, smem); e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(ntile, 1, pl.ksplit);

@@ -120,3 +120,33 @@ def test_ws_matmul_deterministic(torch, R, fmt):
     first = ops.matmul(fmt, xt, qt, K).cpu().numpy()
     for _ in range(4):
         assert np.array_equal(ops.matmul(fmt, xt, qt, K).cpu().numpy(), first)
+
+
+@pytest.mark.parametrize("fmt", [FP8, FP4])
+@pytest.mark.parametrize("M", [17, 64])
+def test_ws_two_per_sm(torch, R, fmt, M):
+    """More weight tiles than two waves and no K split (the LM-head shape class): two CTAs per SM, the receive
+    buffer over the drained rings."""
+    from nekochat_b200 import ops
+    rng = np.random.default_rng(M + 100 * fmt)
+    K, N = 1024, 40000
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    q = R.quantize(fmt, w)
+    y = ops.matmul(fmt, cu(torch, x), cu(torch, q), K)
+    torch.cuda.synchronize()
+    close(y.cpu().numpy(), R.matmul(fmt, x, q, K))
+
+
+@pytest.mark.parametrize("fmt", [FP8, FP4])
+def test_ws_two_per_sm_swiglu(torch, R, fmt):
+    """The SwiGLU pair at more than two waves of tiles (64 gate + 64 up rows each), two CTAs per SM."""
+    from nekochat_b200 import ops
+    rng = np.random.default_rng(9 + fmt)
+    M, K, F = 40, 1024, 20000
+    w = (rng.standard_normal((2 * F, K)) * 0.05).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    q = R.quantize(fmt, w)
+    y = ops.matmul_fused(fmt, cu(torch, x), cu(torch, q), K, F, 0, None, None, 1e-6, swiglu=True)
+    torch.cuda.synchronize()
+    close(y.cpu().numpy(), R.silu_mul(R.matmul(fmt, x, q, K), F))
