@@ -9,9 +9,10 @@
 // D = w_hi x_hi + w_hi x_lo + w_lo x_hi accumulated in fp32 in TMEM over all of K (w_hi x [x_hi; x_lo] as one
 // UMMA of 2 N columns, the halves added in the epilogue).
 //
-// Roles (352 threads; one CTA per SM, or two when a launch has no K split and more than two waves of tiles: the
-// ~30% of a CTA's time outside its K loop, the first copies and the epilogue, then overlaps the other's K loop;
-// M = 64 LM head 211 -> 138 us), K in stages of 64:
+// Roles (352 threads; one CTA per SM, or two: when a launch has no K split and more than two waves of tiles, the
+// ~30% of a CTA's time outside its K loop, the first copies and the epilogue, then overlaps the other's K loop
+// (M = 64 LM head 211 -> 138 us); when one raw stage per split fits every tile in one wave of two per SM, K is
+// split further and each K loop is shorter (batch-64 SwiGLU matmul), K in stages of 64:
 //  * warp 0, one lane: weight producer. Raw stages of four K stages (the code bytes of the 128 rows, 256 bytes a
 //    row for FP8, with the 128-byte swizzle, and the 16-byte scale group holding their eight block scales) into a
 //    2-deep ring with TMA tensor copies of 64-row boxes; weights never depend on the previous kernel, so this
@@ -61,7 +62,7 @@ constexpr int kWActWarp = 2 + kWConv;         // the activation producer's warp
 constexpr int kWRaw = 2;                      // raw stages (4 K stages each)
 constexpr int kWOps = 2;                      // A stages (weight tiles in TMEM)
 constexpr int kWB = 6;                        // B stages (activation tiles in shared memory)
-constexpr int kWBLite = 2;                    // the same for two CTAs per SM (no K split, many waves)
+constexpr int kWBLite = 2;                    // the same for two CTAs per SM
 constexpr int kWMaxSplit = 8;                 // CTAs of a split-K cluster (portable limit)
 constexpr int kWMaxRows = 64;                 // activation rows (UMMA N <= 64)
 // TMEM columns: the accumulators in [0, 2 NT) (column n < NT: w_hi x_hi + w_lo x_hi of activation row n,
@@ -76,9 +77,9 @@ static_assert(kWAcol + 64 * kWOps <= kWTmemCols, "TMEM columns");
 // over all banks.
 __host__ __device__ constexpr int ws_rows_per_owner(int nt, int ks) { return nt / ks; }
 __host__ __device__ constexpr int ws_recv_pitch(int mb) { return mb + ((mb / 4) % 2 == 0 ? 4 : 8); }
-constexpr int ws_recv_floats(int nt) {  // the largest ks x 128 x pitch over ks = 1, 2, 4, 8
+constexpr int ws_recv_floats(int nt, int kmax = kWMaxSplit) {  // the largest ks x 128 x pitch, ks = 1, 2, .. kmax
     int m = 0;
-    for (int k = 1; k <= kWMaxSplit; k *= 2) {
+    for (int k = 1; k <= kmax; k *= 2) {
         const int v = k * ws_recv_pitch(ws_rows_per_owner(nt, k));
         m = m > v ? m : v;
     }
@@ -88,11 +89,15 @@ constexpr int ws_recv_floats(int nt) {  // the largest ks x 128 x pitch over ks 
 // Dynamic shared memory (1024-byte aligned base): B stages (activations hi / lo) | raw stages | receive buffer |
 // barriers | flags | epilogue scratch. A raw stage holds [kRP / 128 column boxes][128 rows][128 bytes] of codes
 // with the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r % 8)), then [128 rows][16] scale groups.
-// LITE (two CTAs per SM, no K split): a 2-deep B ring and the receive buffer over the rings, which are free once
-// every UMMA has completed.
-template <int FMT, int NT, bool LITE = false>
+// Layout modes. kFull: one CTA per SM. kLite (two CTAs per SM, no K split): a 2-deep B ring and the receive buffer
+// over the rings, which are free once every UMMA has completed. kLite2 (two CTAs per SM, 2 or 4 K splits of one raw
+// stage each): a 2-deep B ring, one raw stage, a receive buffer of its own (peers push into it while this CTA may
+// still be in its K loop) sized for up to 4 splits.
+enum WsMode : int { kFull = 0, kLite = 1, kLite2 = 2 };
+template <int FMT, int NT, int MODE = kFull>
 struct WsLayout {
-    static constexpr int kB = LITE ? kWBLite : kWB;
+    static constexpr int kB = MODE == kFull ? kWB : kWBLite;
+    static constexpr int kRawN = MODE == kLite2 ? 1 : kWRaw;   // raw ring depth
     static constexpr int kCB = FMT == kFP8 ? kWK : kWK / 2;  // code bytes per row per K stage
     static constexpr int kRP = kWSub * kCB;                   // code bytes per row per raw stage (256 / 128)
     static constexpr int kBTile = NT * kWK * 2;               // one f16 B tile (activations)
@@ -100,17 +105,20 @@ struct WsLayout {
     static constexpr int kRawCodes = kWM * kRP;
     static constexpr int kRaw = kRawCodes + kWM * 16;
     static constexpr int kRawOff = kB * kOp;
-    static constexpr int kRecvOff = LITE ? 0 : kRawOff + kWRaw * kRaw;  // [source split][128 tile rows][pitch]
-    static constexpr int kRecv = LITE ? kWM * ws_recv_pitch(NT) * 4 : ws_recv_floats(NT) * 4;
-    static constexpr int kBarOff = LITE ? kRawOff + kWRaw * kRaw : kRecvOff + kRecv;
-    static constexpr int kNBar = 2 * kWRaw + 2 * kWOps + 2 * kB + 1;  // raw, A, B full / empty; done
+    static constexpr int kRingEnd = kRawOff + kRawN * kRaw;
+    static constexpr int kRecvOff = MODE == kLite ? 0 : kRingEnd;  // [source split][128 tile rows][pitch]
+    static constexpr int kRecv = MODE == kLite    ? kWM * ws_recv_pitch(NT) * 4
+                                 : MODE == kLite2 ? ws_recv_floats(NT, 4) * 4
+                                                  : ws_recv_floats(NT) * 4;
+    static constexpr int kBarOff = MODE == kLite ? kRingEnd : kRecvOff + kRecv;
+    static constexpr int kNBar = 2 * kRawN + 2 * kWOps + 2 * kB + 1;  // raw, A, B full / empty; done
     static constexpr int kMiscOff = kBarOff + kNBar * 8;      // TMEM address, failure flag
     static constexpr int kKeysOff = (kMiscOff + 8 + 15) / 16 * 16;
     static constexpr int kRsOff = kKeysOff + NT * 8;          // row scales
     static constexpr int kSspOff = kRsOff + NT * 4;           // [NT][4] sums of squares per 32 columns
     static constexpr int kBytes = kSspOff + NT * 4 * 4;
     static_assert(kOp % 1024 == 0 && kRaw % 1024 == 0 && kRecv % 16 == 0, "tile and copy alignment");
-    static_assert(!LITE || kRecv <= kRawOff + kWRaw * kRaw, "the receive buffer fits over the rings");
+    static_assert(MODE != kLite || kRecv <= kRingEnd, "the receive buffer fits over the rings");
 };
 
 struct WsPlan {
@@ -198,13 +206,13 @@ __device__ __forceinline__ void ws_convert(const uint8_t* raw, int r, int j, int
     }
 }
 
-template <int FMT, int NT, bool PAIR, bool LITE>
-__global__ void __launch_bounds__(kWThreads, LITE ? 2 : 1)
+template <int FMT, int NT, bool PAIR, int MODE>
+__global__ void __launch_bounds__(kWThreads, MODE == kFull ? 1 : 2)
     umma_ws_kernel(const GemvArgs a, const WsPlan pl, const __grid_constant__ CUtensorMap t_code,
                    const __grid_constant__ CUtensorMap t_scale, const __grid_constant__ CUtensorMap t_xh,
                    const __grid_constant__ CUtensorMap t_xl) {
-    using L = WsLayout<FMT, NT, LITE>;
-    constexpr int kWB = L::kB;
+    using L = WsLayout<FMT, NT, MODE>;
+    constexpr int kWB = L::kB, kWRaw = L::kRawN;
     extern __shared__ uint8_t wsm_raw[];
     uint8_t* sm = wsm_raw + ((1024 - (smem_u32(wsm_raw) & 1023)) & 1023);
     uint64_t* raw_full = reinterpret_cast<uint64_t*>(sm + L::kBarOff);
@@ -260,7 +268,7 @@ __global__ void __launch_bounds__(kWThreads, LITE ? 2 : 1)
         // the descriptors and swizzled copies assume 1024-byte aligned tiles and the tensor maps 64-byte aligned
         // parameters: a failure is recorded and nothing is issued
         *fail = ((smem_u32(sm) & 1023u) || (reinterpret_cast<uintptr_t>(&t_code) & 63u) ||
-                 (reinterpret_cast<uintptr_t>(&t_xh) & 63u) || nst <= 0 || (LITE && ks != 1))
+                 (reinterpret_cast<uintptr_t>(&t_xh) & 63u) || nst <= 0 || (MODE == kLite && ks != 1) || (MODE == kLite2 && (ks > 4 || nraw > 1)))
                     ? 1
                     : 0;
     }
@@ -495,22 +503,28 @@ __global__ void __launch_bounds__(kWThreads, LITE ? 2 : 1)
             if (keys[m]) atomicMax(a.argmax + m, keys[m]);
 }
 
-template <int FMT, int NT, bool LITE>
+template <int FMT, int NT, int MODE>
 size_t ws_smem() {
-    return size_t(WsLayout<FMT, NT, LITE>::kBytes) + 1024;
+    return size_t(WsLayout<FMT, NT, MODE>::kBytes) + 1024;
 }
 
 using WsFn = void (*)(const GemvArgs, const WsPlan, const CUtensorMap, const CUtensorMap, const CUtensorMap,
                       const CUtensorMap);
 
-template <int FMT, bool LITE>
-WsFn ws_pick(int nt, bool pair, size_t* smem) {
+template <int FMT, int MODE>
+WsFn ws_pick_mode(int nt, bool pair, size_t* smem) {
     if (nt == 32) {
-        *smem = ws_smem<FMT, 32, LITE>();
-        return pair ? umma_ws_kernel<FMT, 32, true, LITE> : umma_ws_kernel<FMT, 32, false, LITE>;
+        *smem = ws_smem<FMT, 32, MODE>();
+        return pair ? umma_ws_kernel<FMT, 32, true, MODE> : umma_ws_kernel<FMT, 32, false, MODE>;
     }
-    *smem = ws_smem<FMT, 64, LITE>();
-    return pair ? umma_ws_kernel<FMT, 64, true, LITE> : umma_ws_kernel<FMT, 64, false, LITE>;
+    *smem = ws_smem<FMT, 64, MODE>();
+    return pair ? umma_ws_kernel<FMT, 64, true, MODE> : umma_ws_kernel<FMT, 64, false, MODE>;
+}
+template <int FMT>
+WsFn ws_pick(int mode, int nt, bool pair, size_t* smem) {
+    return mode == kLite    ? ws_pick_mode<FMT, kLite>(nt, pair, smem)
+           : mode == kLite2 ? ws_pick_mode<FMT, kLite2>(nt, pair, smem)
+                            : ws_pick_mode<FMT, kFull>(nt, pair, smem);
 }
 
 // K splits (1, 2, 4 or 8, whole raw stages of 4 K stages each, so each split starts on a scale group): one CTA
@@ -555,17 +569,25 @@ cudaError_t launch_gemm_ws(const GemvArgs& a, const __half* xh, const __half* xl
         !encode_f16_2d_sw128(&t_xl, xl, uint64_t(a.K), uint64_t(a.M), uint64_t(a.K) * 2, kWK, uint32_t(nt)))
         return cudaErrorNotSupported;
     const int outs = pair ? kWM / 2 : kWM, ntile = (a.rows + outs - 1) / outs, nst = a.K / kWK;
-    const WsPlan pl = ws_plan(ntile, nst);
-    size_t smem = 0;
-    // no K split and more tiles than two waves: two CTAs per SM, so that one's fill and epilogue overlap the
-    // other's K loop (NEKO_GEMM_WS_LITE=0 in the environment keeps one per SM)
+    WsPlan pl = ws_plan(ntile, nst);
+    // Two CTAs per SM (NEKO_GEMM_WS_LITE=0 in the environment keeps one): with no K split and more tiles than two
+    // waves, so that one CTA's fill and epilogue overlap the other's K loop; or, where one raw stage per split
+    // (2 or 4 splits) fits every tile in one wave of two per SM and splits K further than one per SM can, so that
+    // each CTA's K loop is shorter.
     static const bool lite_on = [] {
         const char* v = std::getenv("NEKO_GEMM_WS_LITE");
         return !(v && v[0] == '0');
     }();
-    const bool lite = lite_on && pl.ksplit == 1 && ntile > 2 * num_sms();
-    const WsFn k = a.fmt == kFP8 ? (lite ? ws_pick<kFP8, true>(nt, pair, &smem) : ws_pick<kFP8, false>(nt, pair, &smem))
-                                 : (lite ? ws_pick<kFP4, true>(nt, pair, &smem) : ws_pick<kFP4, false>(nt, pair, &smem));
+    const int sms = num_sms(), nraw = (nst + kWSub - 1) / kWSub;
+    int mode = kFull;
+    if (lite_on && pl.ksplit == 1 && ntile > 2 * sms) {
+        mode = kLite;
+    } else if (lite_on && (nraw == 2 || nraw == 4) && nraw > pl.ksplit && int64_t(ntile) * nraw <= 2 * sms) {
+        mode = kLite2;
+        pl.ksplit = nraw;
+    }
+    size_t smem = 0;
+    const WsFn k = a.fmt == kFP8 ? ws_pick<kFP8>(mode, nt, pair, &smem) : ws_pick<kFP4>(mode, nt, pair, &smem);
     if (const cudaError_t e = ensure_dyn_smem(k, smem); e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(ntile, 1, pl.ksplit);

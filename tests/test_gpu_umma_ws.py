@@ -150,3 +150,20 @@ def test_ws_two_per_sm_swiglu(torch, R, fmt):
     y = ops.matmul_fused(fmt, cu(torch, x), cu(torch, q), K, F, 0, None, None, 1e-6, swiglu=True)
     torch.cuda.synchronize()
     close(y.cpu().numpy(), R.silu_mul(R.matmul(fmt, x, q, K), F))
+
+
+@pytest.mark.parametrize("fmt", [FP8, FP4])
+@pytest.mark.parametrize("M", [17, 64])
+def test_ws_two_per_sm_split(torch, R, fmt, M):
+    """A single wave of tiles that two CTAs per SM let split K further (one raw stage of 4 K stages per split,
+    4 splits): the split two-per-SM layout, partials pushed into a receive buffer of its own."""
+    from nekochat_b200 import ops
+    rng = np.random.default_rng(M + 200 * fmt)
+    K, N = 1024, 8192
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    q = R.quantize(fmt, w)
+    y = ops.matmul(fmt, cu(torch, x), cu(torch, q), K, bias=cu(torch, bias), flags=GELU)
+    torch.cuda.synchronize()
+    close(y.cpu().numpy(), R.matmul(fmt, x, q, K, bias, None, None, GELU))
