@@ -15,10 +15,10 @@
 // split further and each K loop is shorter (batch-64 SwiGLU matmul), K in stages of 64:
 //  * warp 0, one lane: weight producer. Raw stages of four K stages (the code bytes of the 128 rows, 256 bytes a
 //    row for FP8, with the 128-byte swizzle, and the 16-byte scale group holding their eight block scales) into a
-//    2-deep ring with TMA tensor copies of 64-row boxes; weights never depend on the previous kernel, so this
-//    lane never waits for it;
+//    2-deep ring (1-deep in the split two-per-SM layout) with TMA tensor copies of 64-row boxes; weights never
+//    depend on the previous kernel, so this lane never waits for it;
 //  * warp 10, one lane: activation producer. The activations' hi / lo tiles (128-byte swizzled, K-major) of each
-//    stage into a 6-deep ring, after the dependency wait;
+//    stage into a 6-deep ring (2-deep at two CTAs per SM), after the dependency wait;
 //  * warps 2..9: converters, one tile row (TMEM lane) and half a stage's K each. Raw stage -> the A stage's
 //    w_hi / w_lo tiles in TMEM (tcgen05.st; the weights never pass through shared memory again, which leaves its
 //    bandwidth to the copies); one arrival per warp on the A stage's barrier, one on the raw stage's release
