@@ -160,12 +160,20 @@ def dist_setup(args):
     return world, rank, local
 
 
+def prompt_seed(rank, i):
+    """The seed of sequence i's prompt on a rank: replicas decode disjoint sequences (i < 100000)."""
+    return 1 + rank * 100000 + i
+
+
 def reduce_max(x, world):
+    """The largest x over the ranks (the job's time is its slowest rank's); on the GPU under NCCL, on the host
+    under gloo."""
     if world == 1:
         return x
     import torch
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -367,7 +375,7 @@ def run_ours(args):
     # prefill every sequence (different prompts per rank and sequence)
     first = np.zeros(B, np.int32)
     for i in range(B):
-        p = workload.prompt(s, prompt_len, seed=1 + rank * 100000 + i)
+        p = workload.prompt(s, prompt_len, seed=prompt_seed(rank, i))
         first[i] = int(np.argmax(m.prefill(p, slot=i)))
     slots = np.arange(B, dtype=np.int32)
     pos = np.full(B, prompt_len, np.int32)
