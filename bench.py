@@ -1,5 +1,5 @@
-"""Decode throughput of the B200 backend on BASELINE's headline workload: Qwen3-0.6B shape, FP8 weights in the
-engine's format, a 512-token random prompt, then greedy decode (BASELINE.json configs[1]).
+"""Decode throughput of the B200 backend on the headline workload: Qwen3-0.6B shape, FP8 weights in the
+engine's format, a 512-token random prompt, then greedy decode.
 
 A step is one greedy decode step of every sequence on the GPU (batch 1 by default, --batch 64 for the batched
 variant). One process per GPU; sequences are independent, so N GPUs run N replicas with the same per-GPU work
@@ -13,9 +13,10 @@ oracle/_ref) on this host's cores.
 
     python bench.py [--gpus N --steps K --warmup W --batch B --impl ours|reference --model M]
 
---model selects another BASELINE configuration: gpt2-fp8 (configs[0]: GPT-2 small, FP8, 32-token prompt),
-qwen3-1.7b-fp4 (configs[2]: Qwen3-1.7B shape, the engine's FP4 weights, a 1024-token prompt), qwen3-4b-fp8 /
-qwen3-4b-fp4 (configs[3]'s per-GPU batch: run with --batch 512); the default is the headline configuration above.
+--model selects another benchmark configuration: gpt2-fp8 (GPT-2 small, FP8, 32-token prompt), qwen3-1.7b-fp4
+(Qwen3-1.7B shape, the engine's FP4 weights, a 1024-token prompt), qwen3-4b-fp8 / qwen3-4b-fp4 (the per-GPU
+batch of the data-parallel Qwen3-4B configuration: run with --batch 512); the default is the headline
+configuration above.
 """
 import argparse
 import json
@@ -31,11 +32,11 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-# --model: the headline configuration (BASELINE configs[1]) and the other measured configurations
+# --model: the headline configuration and the other measured configurations
 MODELS = {"qwen3-0.6b-fp8": ("qwen3-0.6b", 1, 512, "Qwen3-0.6B FP8 decode tok/s"),
           "gpt2-fp8": ("gpt2", 1, 32, "GPT-2 small FP8 decode tok/s"),
           "qwen3-1.7b-fp4": ("qwen3-1.7b", 2, 1024, "Qwen3-1.7B FP4 decode tok/s"),
-          # BASELINE's data-parallel config: 512 sequences of a 256-token prompt + 128 steps per GPU
+          # the data-parallel Qwen3-4B configuration: 512 sequences of a 256-token prompt + 128 steps per GPU
           "qwen3-4b-fp8": ("qwen3-4b", 1, 256, "Qwen3-4B FP8 decode tok/s"),
           "qwen3-4b-fp4": ("qwen3-4b", 2, 256, "Qwen3-4B FP4 decode tok/s")}
 SHAPE, FMT, PROMPT, METRIC = MODELS["qwen3-0.6b-fp8"]
@@ -51,7 +52,7 @@ def parse():
     p.add_argument("--model", choices=sorted(MODELS), default="qwen3-0.6b-fp8",
                    help="qwen3-0.6b-fp8 (512-token prompt, the headline), gpt2-fp8 (32-token prompt), "
                         "qwen3-1.7b-fp4 (1024-token prompt), "
-                        "qwen3-4b-fp8 / qwen3-4b-fp4 (256-token prompt; BASELINE runs them at --batch 512 "
+                        "qwen3-4b-fp8 / qwen3-4b-fp4 (256-token prompt; measured at --batch 512 "
                         "--steps 128)")
     p.add_argument("--prompt", type=int, default=None,
                    help="prompt tokens (default: the model's, 512 / 1024 / 256; 32 with --profile)")

@@ -9,10 +9,10 @@ qwen3_model.cpp:16-40).
 import numpy as np
 
 SHAPES = {
-    # GPT-2 small
+    # GPT-2 small (the CPU-runnable benchmark configuration)
     "gpt2": dict(arch="gpt2", vocab=50257, embd=768, layers=12, heads=12, kv_heads=12, head_dim=64, ff=3072,
                  max_pos=1024, eps=1e-5, rope_theta=0.0),
-    # Qwen3 shapes
+    # Qwen3 shapes (the other benchmark configurations)
     "qwen3-0.6b": dict(arch="qwen3", vocab=151936, embd=1024, layers=28, heads=16, kv_heads=8, head_dim=128,
                        ff=3072, max_pos=40960, eps=1e-6, rope_theta=1e6),
     "qwen3-1.7b": dict(arch="qwen3", vocab=151936, embd=2048, layers=28, heads=16, kv_heads=8, head_dim=128,

@@ -6,7 +6,7 @@ sampler) compiled from its sources, with the B200 backend (``nekochat_b200/csrc/
 ``loadModel(..., backend=Auto)`` runs the engine's own compatibility check, its ``gpu::selfTest``, its GPU
 loader and every ``forwardGpu`` dispatch (qwen3/cpp/qwen3_model.cpp:278-341, gpt2/cpp/gpt2_model.cpp:220-278)
 on CUDA. Its logits are compared with the same engine's CPU backend (``backend=CPU``, forwardCpu) reading the
-same checkpoint, at the north_star tolerance (max-abs 2e-2, rel 1e-2 + 2e-3), with the greedy tokens
+same checkpoint, at the engine's GPU-vs-CPU tolerance (max-abs 2e-2, rel 1e-2 + 2e-3), with the greedy tokens
 teacher-forced from the CPU side and checked margin-aware.
 """
 import os

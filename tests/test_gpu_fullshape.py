@@ -1,12 +1,12 @@
-"""Model-level parity at BASELINE's own shapes, against the reference engine compiled from its sources.
+"""Model-level parity at the benchmarked models' own shapes, against the reference engine compiled from its sources.
 
 The benchmarked kernels run here at the shapes they are timed on:
-* Qwen3-0.6B FP8 at batch 1 and 4 -- the persistent ``decode_kernel`` (head_dim 128, GQA
+* Qwen3-0.6B FP8 (the headline configuration) at batch 1 and 4 -- the persistent ``decode_kernel`` (head_dim 128, GQA
   group 2, 148-CTA row partition of the 151,936-row LM head, split-KV attention with the ticket merge once the
   position passes 64) -- and at batch 64 (the tensor-core kernel chain of the batched line);
-* Qwen3-1.7B FP4 (configs[2]) at batch 1 and 32;
-* GPT-2 small FP8 (configs[0]): 32-token prompt, 128 greedy steps;
-* the Qwen3-4B layer shapes (configs[3]: C 2560, 32 Q / 8 KV heads, F 9728) at 512 sequences, the tcgen05 path,
+* Qwen3-1.7B FP4 at batch 1 and 32;
+* GPT-2 small FP8: 32-token prompt, 128 greedy steps;
+* the Qwen3-4B layer shapes (C 2560, 32 Q / 8 KV heads, F 9728) at 512 sequences, the tcgen05 path,
   with 4 of its 36 layers so the CPU side stays within seconds (every matrix shape is the full model's).
 
 The checker is ``oracle/_ref/libneko_ref.so``: the reference's own C++ engine (``loadModel`` with the CPU backend,
@@ -14,7 +14,7 @@ The checker is ``oracle/_ref/libneko_ref.so``: the reference's own C++ engine (`
 safetensors checkpoint of exactly the weights the runner was given. Weights are N(0, 0.02) from a seeded
 generator (norm gains 1, biases 0), rounded through f16 on both sides.
 
-Tolerance: every logit within max-abs 2e-2 and within rel 1e-2 (+2e-3 absolute for
+Tolerance (the engine's GPU-vs-CPU bound): every logit within max-abs 2e-2 and within rel 1e-2 (+2e-3 absolute for
 logits near zero) of the reference, and the same greedy token at every step. Steps are teacher-forced with the
 reference's own greedy tokens; a greedy mismatch only counts when the reference's top-1 / top-2 margin exceeds
 twice the observed logit error (random-init weights produce near-ties).
@@ -125,7 +125,7 @@ def q06():
 
 
 def test_qwen3_06b_fp8_b1_decode_kernel(q06):
-    """configs[1] at batch 1: a 120-token prompt, then 32 greedy steps on the persistent decode kernel, whose
+    """Qwen3-0.6B FP8 at batch 1: a 120-token prompt, then 32 greedy steps on the persistent decode kernel, whose
     attention crosses from 2 to 3 key splits at position 128 (the ticket merge)."""
     assert q06.m.set_decode_kernel(True) and q06.m.step_launches(1) == nmodel.decode_kernel_launches(q06.s, FP8) == 2
     prompt = workload.prompt(q06.s, 120, seed=1)
@@ -140,7 +140,7 @@ def test_qwen3_06b_fp8_b4_decode_kernel(q06):
 
 
 def test_qwen3_06b_fp8_b64_chain(q06):
-    """configs[1] at batch 64: the batched kernel chain (tensor-core matmuls, fused decode attention)."""
+    """Qwen3-0.6B FP8 at batch 64: the batched kernel chain (tensor-core matmuls, fused decode attention)."""
     assert q06.m.step_launches(64) > 1
     rng = np.random.default_rng(5)
     prompts = [workload.prompt(q06.s, int(n), seed=200 + i) for i, n in enumerate(rng.integers(8, 130, 64))]
@@ -156,14 +156,14 @@ def q17():
 
 
 def test_qwen3_17b_fp4_b1_decode_kernel(q17):
-    """configs[2] at batch 1 (FP4 nibbles + f16 block scales, C 2048, F 6144): 70-token prompt, 32 steps."""
+    """Qwen3-1.7B FP4 at batch 1 (FP4 nibbles + f16 block scales, C 2048, F 6144): 70-token prompt, 32 steps."""
     assert q17.m.set_decode_kernel(True) and q17.m.step_launches(1) == nmodel.decode_kernel_launches(q17.s, FP4) == 1
     prompt = workload.prompt(q17.s, 70, seed=1)
     run_batch(q17, [prompt], 32, [0], "qwen3-1.7b fp4 b1")
 
 
 def test_qwen3_17b_fp4_b32_chain(q17):
-    """configs[2] at batch 32."""
+    """Qwen3-1.7B FP4 at batch 32."""
     rng = np.random.default_rng(6)
     prompts = [workload.prompt(q17.s, int(n), seed=300 + i) for i, n in enumerate(rng.integers(8, 90, 32))]
     run_batch(q17, prompts, 6, [7], "qwen3-1.7b fp4 b32")
@@ -171,7 +171,7 @@ def test_qwen3_17b_fp4_b32_chain(q17):
 
 # ---------------------------------------------------------------------------------------------- GPT-2 small FP8
 def test_gpt2_small_fp8_128_steps():
-    """configs[0] exactly: GPT-2 small, FP8, 32-token prompt, 128 greedy steps (decode kernel, head_dim 64)."""
+    """The CPU-runnable configuration exactly: GPT-2 small, FP8, 32-token prompt, 128 greedy steps (decode kernel, head_dim 64)."""
     p = Pair(workload.shape("gpt2"), FP8, context=256, max_seqs=1, max_rows=64)
     try:
         assert p.m.set_decode_kernel(True) and p.m.step_launches(1) == nmodel.decode_kernel_launches(p.s, FP8) == 2
@@ -184,7 +184,7 @@ def test_gpt2_small_fp8_128_steps():
 # ---------------------------------------------------------------------------------------------- Qwen3-4B shapes
 @pytest.mark.parametrize("fmt", [FP8, FP4])
 def test_qwen3_4b_shapes_512_sequences(fmt):
-    """configs[3]'s per-GPU batch: 512 sequences in one step (tcgen05 matmuls at 512 rows), on 4 layers of the
+    """The data-parallel Qwen3-4B configuration's per-GPU batch: 512 sequences in one step (tcgen05 matmuls at 512 rows), on 4 layers of the
     Qwen3-4B shape (every matrix at its full size; 4 layers keep the CPU reference to seconds per token)."""
     s = workload.shape("qwen3-4b")
     s["layers"] = 4

@@ -1,6 +1,6 @@
 """Model-level parity of the native runner (neko_model_*) with the reference CPU forward.
 
-Tolerance: logits within max-abs 2e-2 and rel 1e-2 of the reference CPU backend on the
+Tolerance (the engine's GPU-vs-CPU bound): logits within max-abs 2e-2 and rel 1e-2 of the reference CPU backend on the
 same seeded inputs, and identical greedy tokens. Greedy identity is checked teacher-forced: both sides are fed
 the reference's token, and a step only counts as a mismatch when the reference's top-1/top-2 margin exceeds the
 observed logit error (random-init weights give near-ties; ties are reported, not counted).

@@ -1,4 +1,4 @@
-"""Operator parity through the C ABI (neko_op_*) against the oracle: dequant matmul over the BASELINE shapes and
+"""Operator parity through the C ABI (neko_op_*) against the oracle: dequant matmul over the benchmarked shapes and
 odd shapes (tolerance |gpu - cpu| <= 2e-3 (1 + |cpu|), the engine's self-test bound for matmuls), norms,
 softmax, argmax and attention."""
 import numpy as np
@@ -65,7 +65,7 @@ def test_matmul_epilogues(torch, R, fmt, flags):
 @pytest.mark.parametrize("fmt", [FP8, FP4])
 @pytest.mark.parametrize("K,N", [(1024, 3072), (3072, 1024), (2048, 6144), (2560, 9728), (9728, 2560), (1024, 151936)])
 def test_matmul_baseline_sweep_m1(torch, R, fmt, K, N):
-    """The BASELINE operator sweep shapes at M = 1 (decode), weights quantized on the GPU, checked against an
+    """The reference's operator sweep shapes at M = 1 (decode), weights quantized on the GPU, checked against an
     fp64 product of the exactly dequantized weights (the oracle's sequential sum is too slow at 152K rows)."""
     from nekochat_b200 import ops
     g = torch.Generator(device="cuda").manual_seed(K * 7 + N)

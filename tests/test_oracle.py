@@ -44,7 +44,7 @@ def test_codec_golden(R, g, tag, fmt):
 
 
 def test_row_bytes(R):
-    # quantRowBytes values listed for the BASELINE shapes
+    # quantRowBytes values for the benchmarked models' K dimensions
     for K, f8, f4 in ((1024, 1088, 576), (2048, 2176, 1152), (3072, 3264, 1728), (768, 816, 432),
                       (2560, 2720, 1440), (9728, 10336, 5472)):
         assert R.row_bytes(FP8, K) == f8 == workload.row_bytes(FP8, K)
