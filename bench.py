@@ -173,7 +173,7 @@ def reduce_max(x, world):
         return x
     import torch
     import torch.distributed as dist
-    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    dev = "cuda" if "nccl" in str(dist.get_backend()) else "cpu"
     t = torch.tensor([x], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
